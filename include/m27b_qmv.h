@@ -1,0 +1,151 @@
+/*
+ * m27b_qmv.h — C ABI of the B200 (sm_100a) quantized weight-streaming kernels.
+ *
+ * This is the seam the reference executor's matvec dispatch calls through.
+ * It replaces, one for one:
+ *
+ *   m27b_act_quant      <- l_quant_q8_n + k_quant_q8_1          src/mono27b_executor.cu:2022-2030, :84-107
+ *                          (activations are quantized to ggml's q8_K / q8_0, not q8_1,
+ *                          so that results follow ggml's CPU vec_dot semantics)
+ *   m27b_act_quant_gated<- k_quant_q8_1_fused_gate              src/mono27b_executor.cu:109-138, :2460
+ *   m27b_qmv            <- l_mv_q8_on / l_mv_quant_residual     src/mono27b_executor.cu:2054-2102
+ *                          (k_q4k_mv_q8_dp4a :320-364, k_q6k_mv_q8_dp4a :630-645,
+ *                          k_q80_mv_q8_dp4a :533-580)
+ *   m27b_qmv_swiglu     <- l_ffn_gate_up_swiglu                 src/mono27b_executor.cu:2239-2261
+ *                          (k_q4k_q4k_swiglu_dp4a :369-417)
+ *   m27b_qmv_argmax     <- lm_head block + k_argmax             src/mono27b_executor.cu:2577-2593, :209-239
+ *   m27b_dequant_rows   <- k_q4k_embed / mono27b_engine_embed   src/mono27b_executor.cu:1233-1254, :2641-2664
+ *   m27b_repack         <- (new) optional load-time repack of q6_K / q8_0 rows
+ *                          into 16-byte aligned planes; lossless.
+ *
+ * Conventions (kept from the reference, include/mono27b_config.h:155-184):
+ *   - every entry returns bool; on failure it writes a message into
+ *     err[0..err_cap) and returns false; on success err[0] is set to '\0'.
+ *   - every pointer argument that names tensor data is a DEVICE pointer on the
+ *     current CUDA device; the work is enqueued on `stream` (0 = the default
+ *     stream) and nothing is synchronised, so every entry is usable inside CUDA
+ *     graph capture.  No entry allocates device memory.
+ *
+ * Weight rows: a WeightView {ptr, ggml_type, row_blocks, row_count} as the
+ * reference loader fills it (include/mono27b_config.h:63-68, filled at
+ * src/mono27b_executor.cu:1695-1716): row_count rows of row_blocks blocks.
+ * q4_K rows are read in their GGUF layout.  q6_K and q8_0 rows must first be
+ * repacked with m27b_repack; the repacked view carries
+ * ggml_type | M27B_LAYOUT_PLANAR.  ptr must be 16-byte aligned (cudaMalloc
+ * gives 256).
+ *
+ * Activations: m27b_act_quant writes n_tok rows of m27b_act_bytes(type, k)
+ * bytes, ggml block_q8_K (for q4_K / q6_K weights) or block_q8_0 (for q8_0
+ * weights), bit for bit what ggml's quantize_row_q8_K_ref / q8_0_ref produce.
+ */
+#ifndef M27B_QMV_H
+#define M27B_QMV_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <cuda_runtime_api.h>
+
+#include "m27b_blocks.h"
+
+#if defined(__GNUC__)
+#define M27B_API __attribute__((visibility("default")))
+#else
+#define M27B_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef M27B_EXTERNAL_WEIGHTVIEW
+/* Identical layout to the reference's WeightView (include/mono27b_config.h:63-68).
+ * Define M27B_EXTERNAL_WEIGHTVIEW after including the reference's header to
+ * use its declaration instead. */
+struct WeightView {
+    void *ptr;
+    uint32_t ggml_type;
+    uint32_t row_blocks;
+    uint32_t row_count;
+};
+#endif
+
+/* Largest batch (tokens per call) the matvec entries accept. */
+#define M27B_MAX_TOKENS 16
+
+/* Library version string. */
+M27B_API const char *m27b_version(void);
+
+/* Bytes of one quantized activation row of k values: k/256*292 for
+ * M27B_TYPE_Q8_K, k/32*34 for M27B_TYPE_Q8_0; 0 if k is not a multiple of
+ * the block size or the type is not an activation type. */
+M27B_API size_t m27b_act_bytes(uint32_t act_type, int k);
+
+/* Activation type a weight type is multiplied against (q8_0 for q8_0 weights,
+ * q8_K for k-quants); 0 for an unsupported weight type. */
+M27B_API uint32_t m27b_act_type_for(uint32_t ggml_type);
+
+/* Quantize n_tok rows of k fp32 values (row stride ldx floats) into
+ * n_tok * m27b_act_bytes(act_type, k) contiguous bytes at xq. */
+M27B_API bool m27b_act_quant(const float *x, int k, int n_tok, int ldx, uint32_t act_type, void *xq,
+                    cudaStream_t stream, char *err, size_t err_cap);
+
+/* As m27b_act_quant, of x[i] * sigmoid(gate[i]) — the gated attention output
+ * that feeds o_proj. */
+M27B_API bool m27b_act_quant_gated(const float *x, const float *gate, int k, int n_tok, int ldx,
+                          uint32_t act_type, void *xq, cudaStream_t stream, char *err, size_t err_cap);
+
+/* As m27b_act_quant, of RMSNorm(x) * w (w may be NULL for weight 1.0) with
+ * the given eps; the norm is taken over each row of k values. */
+M27B_API bool m27b_act_quant_rmsnorm(const float *x, const float *w, float eps, int k, int n_tok, int ldx,
+                            uint32_t act_type, void *xq, cudaStream_t stream, char *err, size_t err_cap);
+
+/* Bytes m27b_repack writes for a tensor (0 if the type is not repackable). */
+M27B_API size_t m27b_repacked_bytes(uint32_t ggml_type, uint32_t row_blocks, uint32_t row_count);
+
+/* Repack row_count GGUF rows of q6_K or q8_0 (row_blocks blocks each) from
+ * `raw` into the planar layout at `out` (m27b_repacked_bytes bytes, 16-byte
+ * aligned).  The view for the result is {out, ggml_type | M27B_LAYOUT_PLANAR,
+ * row_blocks, row_count}.  q6_K rows become [ql | qh | scales | d, padded to
+ * 16 B]; q8_0 rows become [qs | d, padded to 16 B]. */
+M27B_API bool m27b_repack(const void *raw, uint32_t ggml_type, uint32_t row_blocks, uint32_t row_count,
+                 void *out, cudaStream_t stream, char *err, size_t err_cap);
+
+/* y[t*ldy + r] = W[r] . x[t] (+ residual[t*ldy + r] when residual != NULL)
+ * for t < n_tok (1..M27B_MAX_TOKENS), r < row_count.  xq holds n_tok
+ * activation rows from m27b_act_quant of type m27b_act_type_for(W type) and
+ * k = row_blocks * block size.  residual may alias y. */
+M27B_API bool m27b_qmv(const struct WeightView *w, const void *xq, int n_tok, float *y, int ldy,
+              const float *residual, cudaStream_t stream, char *err, size_t err_cap);
+
+/* y[t*ldy + r] = silu(G[r] . x[t]) * (U[r] . x[t]); gate and up must have the
+ * same type and shape. */
+M27B_API bool m27b_qmv_swiglu(const struct WeightView *gate, const struct WeightView *up, const void *xq,
+                     int n_tok, float *y, int ldy, cudaStream_t stream, char *err, size_t err_cap);
+
+/* Matvec with a fused argmax over rows: best[t] receives a packed key whose
+ * index m27b_argmax_key_index() decodes (largest value, ties to the smallest
+ * row index); logits (may be NULL) receive the values with stride ldl.
+ * row_offset is added to every index, so that ranks holding a slice of the
+ * vocabulary produce keys comparable across ranks. */
+M27B_API bool m27b_qmv_argmax(const struct WeightView *w, const void *xq, int n_tok, float *logits, int ldl,
+                     unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
+                     size_t err_cap);
+
+/* out[i*ldo + j] = dequant(W[rows[i]])[j] for i < n, j < k; rows is a device
+ * array of n row indices; an index outside [0, row_count) yields a zero row
+ * (the reference embed zeroes the hidden state for such tokens). */
+M27B_API bool m27b_dequant_rows(const struct WeightView *w, const int32_t *rows, int n, float *out, int ldo,
+                       cudaStream_t stream, char *err, size_t err_cap);
+
+/* Packed argmax key helpers (host side). */
+static inline int64_t m27b_argmax_key_index(unsigned long long key) {
+    return (int64_t)(0xffffffffull - (key & 0xffffffffull));
+}
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M27B_QMV_H */

@@ -1,0 +1,263 @@
+// capi.cu — extern "C" entry points of libm27b (declared in include/m27b_qmv.h).
+//
+// Error convention kept from the reference executor (include/mono27b_config.h:
+// 155-184, e.g. src/mono27b_executor.cu:1711): bool return, message written
+// with snprintf into the caller's buffer, err[0] == '\0' on success.
+#include <cstdarg>
+#include <cstdio>
+
+#include "m27b_device.cuh"
+#include "m27b_qmv.h"
+#include "qmv_kernels.cuh"
+
+#include "m27b_launch.cuh"
+
+using namespace m27b;
+
+namespace {
+
+bool fail(char *err, size_t cap, const char *fmt, ...) {
+    if (err && cap) {
+        va_list ap;
+        va_start(ap, fmt);
+        std::vsnprintf(err, cap, fmt, ap);
+        va_end(ap);
+    }
+    return false;
+}
+
+bool ok(char *err, size_t cap) {
+    if (err && cap) err[0] = '\0';
+    return true;
+}
+
+bool cuda_ok(cudaError_t e, const char *what, char *err, size_t cap) {
+    if (e == cudaSuccess) return ok(err, cap);
+    return fail(err, cap, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int sm_count_current() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+    if (dev < 64 && cache[dev]) return cache[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    if (dev < 64) cache[dev] = n;
+    return n;
+}
+
+int block_elems(uint32_t base_type) {
+    switch (base_type) {
+    case M27B_TYPE_Q4_K:
+    case M27B_TYPE_Q6_K:
+    case M27B_TYPE_Q8_K: return 256;
+    case M27B_TYPE_Q8_0: return 32;
+    default: return 0;
+    }
+}
+
+// Validated description of a weight view for the matvec kernels.
+struct WDesc {
+    int kind;       // W_Q4K / W_Q6KP / W_Q80P
+    int base;       // base ggml type
+    int k;
+    int passes;
+    size_t row_stride;
+};
+
+bool describe(const WeightView *w, WDesc &d, const char *what, char *err, size_t cap) {
+    if (!w) return fail(err, cap, "%s: null WeightView", what);
+    if (!w->ptr) return fail(err, cap, "%s: null weight pointer", what);
+    if (((uintptr_t)w->ptr & 15u) != 0) return fail(err, cap, "%s: weight pointer must be 16-byte aligned", what);
+    if (w->row_blocks == 0 || w->row_count == 0) return fail(err, cap, "%s: empty weight (row_blocks=%u row_count=%u)", what,
+                                                             w->row_blocks, w->row_count);
+    if (w->row_count > 0x7fffffffu || w->row_blocks > 0x7fffffffu / 256u)
+        return fail(err, cap, "%s: weight too large", what);
+    const uint32_t base = w->ggml_type & M27B_TYPE_MASK;
+    const bool planar = (w->ggml_type & M27B_LAYOUT_PLANAR) != 0;
+    if ((w->ggml_type & ~(M27B_TYPE_MASK | M27B_LAYOUT_PLANAR)) != 0)
+        return fail(err, cap, "%s: unknown layout flags in ggml_type 0x%x", what, w->ggml_type);
+    d.base = (int)base;
+    if (base == M27B_TYPE_Q4_K && !planar) {
+        d.kind = W_Q4K;
+        d.row_stride = (size_t)w->row_blocks * 144;
+        d.passes = (int)((w->row_blocks + 3) / 4);
+    } else if (base == M27B_TYPE_Q6_K && planar) {
+        d.kind = W_Q6KP;
+        d.row_stride = planar_row_bytes(M27B_TYPE_Q6_K, (int)w->row_blocks);
+        d.passes = (int)((w->row_blocks + 3) / 4);
+    } else if (base == M27B_TYPE_Q8_0 && planar) {
+        d.kind = W_Q80P;
+        d.row_stride = planar_row_bytes(M27B_TYPE_Q8_0, (int)w->row_blocks);
+        d.passes = (int)((w->row_blocks + 31) / 32);
+    } else if ((base == M27B_TYPE_Q6_K || base == M27B_TYPE_Q8_0) && !planar) {
+        return fail(err, cap, "%s: ggml type %u must be repacked with m27b_repack before the matvec", what, base);
+    } else {
+        return fail(err, cap, "%s: unsupported weight type 0x%x (q4_K, planar q6_K and planar q8_0 are supported)", what,
+                    w->ggml_type);
+    }
+    d.k = (int)w->row_blocks * block_elems(base);
+    return true;
+}
+
+size_t act_bytes(uint32_t act_type, int k) {
+    if (k <= 0) return 0;
+    if (act_type == M27B_TYPE_Q8_K) return (k % 256) ? 0 : (size_t)(k / 256) * sizeof(m27b_block_q8_K);
+    if (act_type == M27B_TYPE_Q8_0) return (k % 32) ? 0 : (size_t)(k / 32) * sizeof(m27b_block_q8_0);
+    return 0;
+}
+
+bool act_quant_common(int mode, const float *x, const float *gate, const float *w, float eps, int k, int n_tok, int ldx,
+                      uint32_t act_type, void *xq, cudaStream_t stream, char *err, size_t cap, const char *what) {
+    if (!x || !xq) return fail(err, cap, "%s: null pointer", what);
+    if (mode == ACT_GATED && !gate) return fail(err, cap, "%s: null gate", what);
+    if (n_tok < 1) return fail(err, cap, "%s: n_tok must be >= 1 (got %d)", what, n_tok);
+    if (ldx < k) return fail(err, cap, "%s: ldx (%d) < k (%d)", what, ldx, k);
+    if (act_bytes(act_type, k) == 0) return fail(err, cap, "%s: k=%d is not a multiple of the block size of type %u", what, k, act_type);
+    if (((uintptr_t)xq & 3u) != 0) return fail(err, cap, "%s: output must be 4-byte aligned", what);
+    if (n_tok > 65535) return fail(err, cap, "%s: n_tok too large", what);
+    ActArgs a{x, gate, w, eps, k, ldx, xq};
+    return cuda_ok(launch_act_quant((int)act_type, mode, a, n_tok, stream), what, err, cap);
+}
+
+bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void *xq, int n_tok, float *y, int ldy,
+                const float *residual, unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
+                size_t cap, const char *what) {
+    WDesc d0{}, d1{};
+    if (!describe(w0, d0, what, err, cap)) return false;
+    if (epi == EPI_SWIGLU) {
+        if (!describe(w1, d1, what, err, cap)) return false;
+        if (w1->ggml_type != w0->ggml_type || w1->row_blocks != w0->row_blocks || w1->row_count != w0->row_count)
+            return fail(err, cap, "%s: gate and up must have the same type and shape", what);
+    }
+    if (!xq) return fail(err, cap, "%s: null activation pointer", what);
+    if (n_tok < 1 || n_tok > M27B_MAX_TOKENS)
+        return fail(err, cap, "%s: n_tok must be in [1, %d] (got %d)", what, M27B_MAX_TOKENS, n_tok);
+    if (epi != EPI_ARGMAX && !y) return fail(err, cap, "%s: null output", what);
+    if (epi == EPI_ARGMAX && !best) return fail(err, cap, "%s: null argmax output", what);
+    if ((y || residual) && ldy < (int)w0->row_count && n_tok > 1)
+        return fail(err, cap, "%s: ldy (%d) < row_count (%u)", what, ldy, w0->row_count);
+    const uint32_t at = d0.base == M27B_TYPE_Q8_0 ? M27B_TYPE_Q8_0 : M27B_TYPE_Q8_K;
+    const size_t xb = act_bytes(at, d0.k);
+    if (((uintptr_t)xq & (at == M27B_TYPE_Q8_K ? 3u : 1u)) != 0) return fail(err, cap, "%s: misaligned activations", what);
+    const size_t smem = qmv_smem_bytes(d0.base, d0.k, n_tok < 4 ? n_tok : 4);
+    if (smem > 200 * 1024)
+        return fail(err, cap, "%s: activation staging needs %zu bytes of shared memory (k=%d too large)", what, smem, d0.k);
+    const int sms = sm_count_current();
+    if (sms <= 0) return fail(err, cap, "%s: no CUDA device", what);
+    if (epi == EPI_ARGMAX) {
+        cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long) * (size_t)n_tok, stream);
+        if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
+    }
+    for (int t0 = 0; t0 < n_tok; t0 += 4) {
+        const int nt = n_tok - t0 < 4 ? n_tok - t0 : 4;
+        QmvArgs a{};
+        a.w0 = (const uint8_t *)w0->ptr;
+        a.w1 = epi == EPI_SWIGLU ? (const uint8_t *)w1->ptr : nullptr;
+        a.xq = (const uint8_t *)xq + (size_t)t0 * xb;
+        a.y = y ? y + (size_t)t0 * ldy : nullptr;
+        a.residual = residual ? residual + (size_t)t0 * ldy : nullptr;
+        a.best = best ? best + t0 : nullptr;
+        a.row_stride = d0.row_stride;
+        a.ldy = ldy;
+        a.rows = (int)w0->row_count;
+        a.rb = (int)w0->row_blocks;
+        a.k = d0.k;
+        a.passes = d0.passes;
+        a.row_offset = row_offset;
+        cudaError_t e = launch_qmv(d0.kind, epi, a, nt, sms, stream);
+        if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
+    }
+    return ok(err, cap);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *m27b_version(void) { return "m27b-b200 0.1 (sm_100a)"; }
+
+size_t m27b_act_bytes(uint32_t act_type, int k) { return act_bytes(act_type, k); }
+
+uint32_t m27b_act_type_for(uint32_t ggml_type) {
+    const uint32_t b = ggml_type & M27B_TYPE_MASK;
+    if (b == M27B_TYPE_Q8_0) return M27B_TYPE_Q8_0;
+    if (b == M27B_TYPE_Q4_K || b == M27B_TYPE_Q6_K) return M27B_TYPE_Q8_K;
+    return 0;
+}
+
+bool m27b_act_quant(const float *x, int k, int n_tok, int ldx, uint32_t act_type, void *xq, cudaStream_t stream, char *err,
+                    size_t err_cap) {
+    return act_quant_common(ACT_PLAIN, x, nullptr, nullptr, 0.0f, k, n_tok, ldx, act_type, xq, stream, err, err_cap,
+                            "m27b_act_quant");
+}
+
+bool m27b_act_quant_gated(const float *x, const float *gate, int k, int n_tok, int ldx, uint32_t act_type, void *xq,
+                          cudaStream_t stream, char *err, size_t err_cap) {
+    return act_quant_common(ACT_GATED, x, gate, nullptr, 0.0f, k, n_tok, ldx, act_type, xq, stream, err, err_cap,
+                            "m27b_act_quant_gated");
+}
+
+bool m27b_act_quant_rmsnorm(const float *x, const float *w, float eps, int k, int n_tok, int ldx, uint32_t act_type,
+                            void *xq, cudaStream_t stream, char *err, size_t err_cap) {
+    return act_quant_common(ACT_RMSNORM, x, nullptr, w, eps, k, n_tok, ldx, act_type, xq, stream, err, err_cap,
+                            "m27b_act_quant_rmsnorm");
+}
+
+size_t m27b_repacked_bytes(uint32_t ggml_type, uint32_t row_blocks, uint32_t row_count) {
+    const uint32_t b = ggml_type & M27B_TYPE_MASK;
+    if (b != M27B_TYPE_Q6_K && b != M27B_TYPE_Q8_0) return 0;
+    return planar_row_bytes((int)b, (int)row_blocks) * (size_t)row_count;
+}
+
+bool m27b_repack(const void *raw, uint32_t ggml_type, uint32_t row_blocks, uint32_t row_count, void *out,
+                 cudaStream_t stream, char *err, size_t err_cap) {
+    const uint32_t b = ggml_type & M27B_TYPE_MASK;
+    if (!raw || !out) return fail(err, err_cap, "m27b_repack: null pointer");
+    if (ggml_type != M27B_TYPE_Q6_K && ggml_type != M27B_TYPE_Q8_0)
+        return fail(err, err_cap, "m27b_repack: only raw q6_K and q8_0 are repacked (got type 0x%x)", ggml_type);
+    if (row_blocks == 0 || row_count == 0) return fail(err, err_cap, "m27b_repack: empty tensor");
+    if (row_blocks > 65535u || row_count > 0x7fffffffu) return fail(err, err_cap, "m27b_repack: tensor too large");
+    if (((uintptr_t)out & 15u) != 0) return fail(err, err_cap, "m27b_repack: output must be 16-byte aligned");
+    return cuda_ok(launch_repack((int)b, raw, (int)row_blocks, (int)row_count, out, stream), "m27b_repack", err, err_cap);
+}
+
+bool m27b_qmv(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual, cudaStream_t stream,
+              char *err, size_t err_cap) {
+    return qmv_common(EPI_STORE, w, nullptr, xq, n_tok, y, ldy, residual, nullptr, 0, stream, err, err_cap, "m27b_qmv");
+}
+
+bool m27b_qmv_swiglu(const WeightView *gate, const WeightView *up, const void *xq, int n_tok, float *y, int ldy,
+                     cudaStream_t stream, char *err, size_t err_cap) {
+    return qmv_common(EPI_SWIGLU, gate, up, xq, n_tok, y, ldy, nullptr, nullptr, 0, stream, err, err_cap,
+                      "m27b_qmv_swiglu");
+}
+
+bool m27b_qmv_argmax(const WeightView *w, const void *xq, int n_tok, float *logits, int ldl, unsigned long long *best,
+                     uint32_t row_offset, cudaStream_t stream, char *err, size_t err_cap) {
+    return qmv_common(EPI_ARGMAX, w, nullptr, xq, n_tok, logits, ldl, nullptr, best, row_offset, stream, err, err_cap,
+                      "m27b_qmv_argmax");
+}
+
+bool m27b_dequant_rows(const WeightView *w, const int32_t *rows, int n, float *out, int ldo, cudaStream_t stream, char *err,
+                       size_t err_cap) {
+    if (!w || !w->ptr || !rows || !out) return fail(err, err_cap, "m27b_dequant_rows: null pointer");
+    if (n < 1) return fail(err, err_cap, "m27b_dequant_rows: n must be >= 1");
+    const uint32_t base = w->ggml_type & M27B_TYPE_MASK;
+    const bool planar = (w->ggml_type & M27B_LAYOUT_PLANAR) != 0;
+    const int be = block_elems(base);
+    if (be == 0 || base == M27B_TYPE_Q8_K || (planar && base == M27B_TYPE_Q4_K))
+        return fail(err, err_cap, "m27b_dequant_rows: unsupported weight type 0x%x", w->ggml_type);
+    if (w->row_blocks == 0 || w->row_blocks > 0x7fffffffu / 256u) return fail(err, err_cap, "m27b_dequant_rows: bad row_blocks");
+    const int k = (int)w->row_blocks * be;
+    if (ldo < k) return fail(err, err_cap, "m27b_dequant_rows: ldo (%d) < k (%d)", ldo, k);
+    size_t stride;
+    if (planar) stride = planar_row_bytes((int)base, (int)w->row_blocks);
+    else stride = (size_t)w->row_blocks * (base == M27B_TYPE_Q4_K ? 144 : base == M27B_TYPE_Q6_K ? 210 : 34);
+    return cuda_ok(launch_dequant_rows((int)base, planar, w->ptr, stride, (int)w->row_blocks, (int)w->row_count, k, rows, n,
+                                       out, ldo, stream),
+                   "m27b_dequant_rows", err, err_cap);
+}
+
+}  // extern "C"

@@ -1,0 +1,67 @@
+// m27b_device.cuh — device helpers shared by the sm_100a quantized matvec kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "m27b_blocks.h"
+
+#define M27B_DI __device__ __forceinline__
+
+namespace m27b {
+
+// Streaming 128-bit load of weight bytes: read-only path, no L1 allocation
+// (each weight byte is used once per call), 256-byte L2 prefetch hint so that
+// the DRAM bursts stay full while the warp walks a row.
+M27B_DI uint4 ldg_stream16(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+M27B_DI uint2 ldg_stream8(const void *p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+
+M27B_DI uint32_t ldg_stream_u16(const void *p) {
+    unsigned short r;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+
+M27B_DI float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu))); }
+
+M27B_DI int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// Sum of the four byte-lanes products of two uint4 (16 x int8 . int8).
+M27B_DI int dot16(uint4 a, uint4 b) {
+    int s = dp4a((int)a.x, (int)b.x, 0);
+    s = dp4a((int)a.y, (int)b.y, s);
+    s = dp4a((int)a.z, (int)b.z, s);
+    return dp4a((int)a.w, (int)b.w, s);
+}
+
+M27B_DI float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Monotone map of a float to uint32 (total order on non-NaN values).
+M27B_DI uint32_t float_order_key(float v) {
+    uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Packed argmax key: larger value wins; on equal values the smaller index
+// wins (the index is stored complemented in the low word).
+M27B_DI unsigned long long argmax_key(float v, uint32_t idx) {
+    return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xffffffffu - idx);
+}
+
+}  // namespace m27b

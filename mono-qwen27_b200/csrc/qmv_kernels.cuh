@@ -1,0 +1,334 @@
+// qmv_kernels.cuh — the persistent streaming matvec kernel and its per-format
+// slice arithmetic (see qmv.cu for the design).
+#pragma once
+
+#include "m27b_device.cuh"
+
+namespace m27b {
+
+constexpr int QMV_WARPS = 8;
+constexpr int QMV_THREADS = QMV_WARPS * 32;
+
+enum WeightKind { W_Q4K = 0, W_Q6KP = 1, W_Q80P = 2 };
+enum Epilogue { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ARGMAX = 2 };
+
+struct QmvArgs {
+    const uint8_t *w0;         // weight rows (gate for SWIGLU)
+    const uint8_t *w1;         // up rows (SWIGLU only)
+    const void *xq;            // NT activation rows (q8_K or q8_0 blocks)
+    float *y;                  // [NT][ldy] output (ARGMAX: logits, may be null)
+    const float *residual;     // [NT][ldy] added to y (STORE only; may be null)
+    unsigned long long *best;  // [NT] packed argmax keys (ARGMAX)
+    size_t row_stride;         // bytes per weight row in its layout
+    int ldy;
+    int rows;
+    int rb;                    // blocks per row
+    int k;                     // values per row
+    int passes;                // 1024-value passes per row
+    uint32_t row_offset;       // added to argmax indices
+};
+
+// Planar view of the staged activations in shared memory.
+struct XStage {
+    const int8_t *q;   // [NT][k] codes
+    const int16_t *bs; // [NT][k/16] bsums (q8_K only)
+    const float *d;    // [NT][nb] block scales
+    int k;
+    int nb;
+};
+
+// ---------------------------------------------------------------------------
+// q4_K, GGUF layout (144-byte blocks).  Pass p, lane L: block b = 4p + L/8,
+// 16-byte nibble chunk c = L%8 = 2g + h of qs: the low nibbles are values
+// 64g + 16h + [0,16) of sub-block 2g, the high nibbles values 64g + 32 + 16h
+// + [0,16) of sub-block 2g+1 (reference :930-942 / official_dequant.c:57-61).
+struct WQ4K {
+    static constexpr int NL = 2;
+    static constexpr int PER_PASS = 4;  // blocks per pass
+    M27B_DI static void load(const uint8_t *row, int rb, int p, int lane, uint4 (&v)[NL]) {
+        const int b = PER_PASS * p + (lane >> 3);
+        if (b < rb) {
+            const uint8_t *blk = row + (size_t)b * 144;
+            v[0] = ldg_stream16(blk + 16 + 16 * (lane & 7));
+            v[1] = ldg_stream16(blk);
+        } else {
+            v[0] = make_uint4(0, 0, 0, 0);
+            v[1] = make_uint4(0, 0, 0, 0);
+        }
+    }
+    template <int NT>
+    M27B_DI static void mac(const uint4 (&v)[NL], int rb, int p, int lane, const XStage &xs, float (&acc)[NT]) {
+        const int b = PER_PASS * p + (lane >> 3);
+        if (b >= rb) return;
+        const int c = lane & 7, g = c >> 1, h = c & 1;
+        const uint4 q = v[0], hd = v[1];
+        // 6-bit scale/min of sub-blocks 2g and 2g+1 as byte pairs
+        // (get_scale_min_k4, reference :690-693).
+        const int sh = 16 * (g & 1);
+        const uint32_t A = (hd.y >> sh) & 0xffffu, B = (hd.z >> sh) & 0xffffu, C = (hd.w >> sh) & 0xffffu;
+        uint32_t scp, mnp;
+        if (g < 2) {
+            scp = A & 0x3f3fu;
+            mnp = B & 0x3f3fu;
+        } else {
+            scp = (C & 0x0f0fu) | ((A >> 2) & 0x3030u);
+            mnp = ((C >> 4) & 0x0f0fu) | ((B >> 2) & 0x3030u);
+        }
+        const int sc_lo = (int)(scp & 0xffu), sc_hi = (int)(scp >> 8);
+        const int m_lo = (int)(mnp & 0xffu), m_hi = (int)(mnp >> 8);
+        const float dw = h2f(hd.x), dmw = h2f(hd.x >> 16);
+        const uint4 lo = make_uint4(q.x & 0x0f0f0f0fu, q.y & 0x0f0f0f0fu, q.z & 0x0f0f0f0fu, q.w & 0x0f0f0f0fu);
+        const uint4 hi = make_uint4((q.x >> 4) & 0x0f0f0f0fu, (q.y >> 4) & 0x0f0f0f0fu, (q.z >> 4) & 0x0f0f0f0fu,
+                                    (q.w >> 4) & 0x0f0f0f0fu);
+        const int e0 = b * 256 + 64 * g + 16 * h;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const int8_t *xt = xs.q + (size_t)t * xs.k;
+            const uint4 xa = *(const uint4 *)(xt + e0);
+            const uint4 xb = *(const uint4 *)(xt + e0 + 32);
+            const int16_t *bs = xs.bs + (size_t)t * (xs.k / 16) + (e0 >> 4);
+            const int isum = sc_lo * dot16(lo, xa) + sc_hi * dot16(hi, xb);
+            const int msum = m_lo * (int)bs[0] + m_hi * (int)bs[2];
+            const float dx = xs.d[t * xs.nb + b];
+            acc[t] = fmaf(dw * dx, (float)isum, acc[t]);
+            acc[t] = fmaf(-(dmw * dx), (float)msum, acc[t]);
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
+// q6_K, planar layout from m27b_repack: row = [ql rb*128 | qh rb*64 |
+// scales rb*16 | d rb*2, padded to 16].  Pass p, lane L: block b = 4p + L/8,
+// c = L%8 = 4*half + 2*rr + lsub: ql chunk c holds, in its low nibbles,
+// values 128*half + 32*rr + 16*lsub + [0,16) and, in its high nibbles, the
+// same + 64; their high bits are bits 2rr and 2rr+4 of qh chunk 2*half+lsub
+// (q6k_val, reference :1026-1048).
+struct WQ6KP {
+    static constexpr int NL = 3;
+    static constexpr int PER_PASS = 4;
+    M27B_DI static void load(const uint8_t *row, int rb, int p, int lane, uint4 (&v)[NL]) {
+        const int b = PER_PASS * p + (lane >> 3);
+        if (b < rb) {
+            const int c = lane & 7, half = c >> 2, lsub = c & 1;
+            v[0] = ldg_stream16(row + (size_t)b * 128 + 16 * c);
+            v[1] = ldg_stream16(row + (size_t)rb * 128 + (size_t)b * 64 + 16 * (2 * half + lsub));
+            const uint2 s = ldg_stream8(row + (size_t)rb * 192 + (size_t)b * 16 + 8 * half);
+            v[2] = make_uint4(s.x, s.y, ldg_stream_u16(row + (size_t)rb * 208 + 2 * b), 0u);
+        } else {
+            v[0] = v[1] = v[2] = make_uint4(0, 0, 0, 0);
+        }
+    }
+    template <int NT>
+    M27B_DI static void mac(const uint4 (&v)[NL], int rb, int p, int lane, const XStage &xs, float (&acc)[NT]) {
+        const int b = PER_PASS * p + (lane >> 3);
+        if (b >= rb) return;
+        const int c = lane & 7, half = c >> 2, rr = (c >> 1) & 1, lsub = c & 1;
+        const int sb = 8 * (2 * rr + lsub);
+        const int sc_lo = (int)(int8_t)((v[2].x >> sb) & 0xffu);
+        const int sc_hi = (int)(int8_t)((v[2].y >> sb) & 0xffu);
+        const float dw = h2f(v[2].z);
+        const uint4 ql = v[0], qh = v[1];
+        const int s_lo = 2 * rr, s_hi = 2 * rr + 4;
+        uint4 lo, hi;
+        lo.x = (ql.x & 0x0f0f0f0fu) | (((qh.x >> s_lo) & 0x03030303u) << 4);
+        lo.y = (ql.y & 0x0f0f0f0fu) | (((qh.y >> s_lo) & 0x03030303u) << 4);
+        lo.z = (ql.z & 0x0f0f0f0fu) | (((qh.z >> s_lo) & 0x03030303u) << 4);
+        lo.w = (ql.w & 0x0f0f0f0fu) | (((qh.w >> s_lo) & 0x03030303u) << 4);
+        hi.x = ((ql.x >> 4) & 0x0f0f0f0fu) | (((qh.x >> s_hi) & 0x03030303u) << 4);
+        hi.y = ((ql.y >> 4) & 0x0f0f0f0fu) | (((qh.y >> s_hi) & 0x03030303u) << 4);
+        hi.z = ((ql.z >> 4) & 0x0f0f0f0fu) | (((qh.z >> s_hi) & 0x03030303u) << 4);
+        hi.w = ((ql.w >> 4) & 0x0f0f0f0fu) | (((qh.w >> s_hi) & 0x03030303u) << 4);
+        const int e_lo = b * 256 + 128 * half + 32 * rr + 16 * lsub;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const int8_t *xt = xs.q + (size_t)t * xs.k;
+            const uint4 xa = *(const uint4 *)(xt + e_lo);
+            const uint4 xb = *(const uint4 *)(xt + e_lo + 64);
+            const int16_t *bs = xs.bs + (size_t)t * (xs.k / 16) + (e_lo >> 4);
+            // codes are stored +32: <q-32, x> = <q, x> - 32 * bsum
+            const int isum = sc_lo * (dot16(lo, xa) - 32 * (int)bs[0]) + sc_hi * (dot16(hi, xb) - 32 * (int)bs[4]);
+            const float dx = xs.d[t * xs.nb + b];
+            acc[t] = fmaf(dw * dx, (float)isum, acc[t]);
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
+// q8_0, planar layout from m27b_repack: row = [qs rb*32 | d rb*2, padded to
+// 16].  Pass p, lane L: block b = 32p + L, all 32 codes.
+struct WQ80P {
+    static constexpr int NL = 3;
+    static constexpr int PER_PASS = 32;
+    M27B_DI static void load(const uint8_t *row, int rb, int p, int lane, uint4 (&v)[NL]) {
+        const int b = PER_PASS * p + lane;
+        if (b < rb) {
+            v[0] = ldg_stream16(row + (size_t)b * 32);
+            v[1] = ldg_stream16(row + (size_t)b * 32 + 16);
+            v[2] = make_uint4(ldg_stream_u16(row + (size_t)rb * 32 + 2 * b), 0u, 0u, 0u);
+        } else {
+            v[0] = v[1] = v[2] = make_uint4(0, 0, 0, 0);
+        }
+    }
+    template <int NT>
+    M27B_DI static void mac(const uint4 (&v)[NL], int rb, int p, int lane, const XStage &xs, float (&acc)[NT]) {
+        const int b = PER_PASS * p + lane;
+        if (b >= rb) return;
+        const float dw = h2f(v[2].x);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const int8_t *xt = xs.q + (size_t)t * xs.k + b * 32;
+            const int dot = dot16(v[0], *(const uint4 *)xt) + dot16(v[1], *(const uint4 *)(xt + 16));
+            acc[t] = fmaf((float)dot, dw * xs.d[t * xs.nb + b], acc[t]);
+        }
+    }
+};
+
+template <int WT> struct WTraits;
+template <> struct WTraits<W_Q4K> { using T = WQ4K; };
+template <> struct WTraits<W_Q6KP> { using T = WQ6KP; };
+template <> struct WTraits<W_Q80P> { using T = WQ80P; };
+
+// Passes of loads kept in flight per register buffer.
+template <int WT, int NM> struct PipeDepth { static constexpr int value = (WT == W_Q4K && NM == 1) ? 4 : 2; };
+
+// Copy NT activation rows into shared memory in planar form.
+template <int WT, int NT>
+M27B_DI XStage stage_x(const QmvArgs &a, uint8_t *smem) {
+    XStage xs;
+    xs.k = a.k;
+    if (WT == W_Q80P) {
+        const int nb = a.k / 32;
+        int8_t *q = (int8_t *)smem;
+        float *d = (float *)(smem + (size_t)NT * a.k);
+        const uint16_t *src = (const uint16_t *)a.xq;  // 17 halfwords per block
+        const int total = NT * nb * 17;
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            const int blk = i / 17, o = i - blk * 17;
+            const uint16_t h = src[i];
+            if (o == 0) d[blk] = h2f(h);
+            else *(uint16_t *)(q + (size_t)blk * 32 + 2 * (o - 1)) = h;
+        }
+        xs.q = q;
+        xs.bs = nullptr;
+        xs.d = d;
+        xs.nb = nb;
+    } else {
+        const int nb = a.k / 256;
+        int8_t *q = (int8_t *)smem;
+        int16_t *bs = (int16_t *)(smem + (size_t)NT * a.k);
+        float *d = (float *)(smem + (size_t)NT * a.k + (size_t)NT * nb * 32);
+        const uint32_t *src = (const uint32_t *)a.xq;  // 73 words per block
+        const int total = NT * nb * 73;
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            const int blk = i / 73, o = i - blk * 73;
+            const uint32_t w = src[i];
+            if (o == 0) d[blk] = __uint_as_float(w);
+            else if (o <= 64) ((uint32_t *)q)[(size_t)blk * 64 + (o - 1)] = w;
+            else ((uint32_t *)bs)[(size_t)blk * 8 + (o - 65)] = w;
+        }
+        xs.q = q;
+        xs.bs = bs;
+        xs.d = d;
+        xs.nb = nb;
+    }
+    return xs;
+}
+
+template <int EPI, int NT, int NM>
+M27B_DI void finish_row(const QmvArgs &a, int row, float (&acc)[NM][NT], int lane, unsigned long long &best) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        float s0 = warp_sum(acc[0][t]);
+        float s1 = 0.0f;
+        if constexpr (NM == 2) s1 = warp_sum(acc[1][t]);
+        if (lane == t) {
+            const size_t o = (size_t)t * a.ldy + row;
+            if constexpr (EPI == EPI_STORE) {
+                a.y[o] = a.residual ? s0 + a.residual[o] : s0;
+            } else if constexpr (EPI == EPI_SWIGLU) {
+                a.y[o] = s0 / (1.0f + expf(-s0)) * s1;
+            } else {
+                if (a.y) a.y[o] = s0;
+                const unsigned long long key = argmax_key(s0, (uint32_t)row + a.row_offset);
+                best = key > best ? key : best;
+            }
+        }
+        acc[0][t] = 0.0f;
+        if constexpr (NM == 2) acc[1][t] = 0.0f;
+    }
+}
+
+template <int WT, int NT, int EPI>
+__global__ void __launch_bounds__(QMV_THREADS, 2) k_qmv(const QmvArgs a) {
+    using T = typename WTraits<WT>::T;
+    constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
+    constexpr int PM = PipeDepth<WT, NM>::value;
+    extern __shared__ __align__(16) uint8_t smem[];
+
+    const int lane = threadIdx.x & 31;
+    const int wg = blockIdx.x * QMV_WARPS + (threadIdx.x >> 5);
+    const int W = gridDim.x * QMV_WARPS;
+    const int P = a.passes;
+    const int my_rows = wg < a.rows ? (a.rows - 1 - wg) / W + 1 : 0;
+
+    uint4 bufA[PM][NM][T::NL];
+    uint4 bufB[PM][NM][T::NL];
+    int lrow = 0, lp = 0;  // load cursor (row ordinal, pass)
+    int crow = 0, cp = 0;  // compute cursor
+
+    auto load_chunk = [&](uint4 (&buf)[PM][NM][T::NL]) {
+#pragma unroll
+        for (int j = 0; j < PM; ++j) {
+            if (lrow < my_rows) {
+                const size_t r = (size_t)wg + (size_t)lrow * W;
+                T::load(a.w0 + r * a.row_stride, a.rb, lp, lane, buf[j][0]);
+                if constexpr (NM == 2) T::load(a.w1 + r * a.row_stride, a.rb, lp, lane, buf[j][1]);
+                if (++lp == P) { lp = 0; ++lrow; }
+            }
+        }
+    };
+
+    // First loads go out before the activations are staged.
+    load_chunk(bufA);
+    const XStage xs = stage_x<WT, NT>(a, smem);
+    __syncthreads();
+
+    float acc[NM][NT];
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[m][t] = 0.0f;
+    unsigned long long best = 0ull;
+
+    auto compute_chunk = [&](const uint4 (&buf)[PM][NM][T::NL]) {
+#pragma unroll
+        for (int j = 0; j < PM; ++j) {
+            if (crow < my_rows) {
+                T::template mac<NT>(buf[j][0], a.rb, cp, lane, xs, acc[0]);
+                if constexpr (NM == 2) T::template mac<NT>(buf[j][1], a.rb, cp, lane, xs, acc[1]);
+                if (++cp == P) {
+                    finish_row<EPI, NT, NM>(a, wg + crow * W, acc, lane, best);
+                    cp = 0;
+                    ++crow;
+                }
+            }
+        }
+    };
+
+    while (crow < my_rows) {
+        load_chunk(bufB);
+        compute_chunk(bufA);
+        if (crow >= my_rows) break;
+        load_chunk(bufA);
+        compute_chunk(bufB);
+    }
+
+    if constexpr (EPI == EPI_ARGMAX) {
+        if (lane < NT && best != 0ull) atomicMax(a.best + lane, best);
+    }
+}
+
+size_t qmv_smem_bytes(int wtype, int k, int ntok);
+cudaError_t launch_qmv(int wt, int epi, const QmvArgs &a, int nt, int sm_count, cudaStream_t st);
+
+}  // namespace m27b

@@ -1,0 +1,202 @@
+"""ctypes binding of libm27b.so, the C ABI declared in include/m27b_qmv.h.
+
+This is the Python mirror of the reference's matvec seam (WeightView +
+quantize/matvec calls, src/mono27b_executor.cu:1989-2261) used by the tests and
+the benchmark.  PyTorch only provides device memory and streams; every
+computation goes through the CUDA library.  There is no fallback: if
+libm27b.so is missing or fails to load, every call raises.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libm27b.so")
+
+# ggml type codes (reference include/mono27b_gguf.h:28-44)
+Q8_0, Q4_K, Q6_K, Q8_K = 8, 12, 14, 15
+LAYOUT_PLANAR = 0x100
+MAX_TOKENS = 16
+BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292)}
+
+ERR_CAP = 512
+
+
+class WeightView(ctypes.Structure):
+    """Same layout as the reference's WeightView (include/mono27b_config.h:63-68)."""
+    _fields_ = [("ptr", ctypes.c_void_p), ("ggml_type", ctypes.c_uint32), ("row_blocks", ctypes.c_uint32),
+                ("row_count", ctypes.c_uint32)]
+
+
+class M27BError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib():
+    """Load libm27b.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise M27BError(f"libm27b.so is not built ({LIB_PATH}); run __graft_entry__.build()")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, u32, i32, sz, cp = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_size_t, ctypes.c_char_p
+    fp, b = ctypes.c_float, ctypes.c_bool
+    wvp = ctypes.POINTER(WeightView)
+    sig = {
+        "m27b_version": (cp, []),
+        "m27b_act_bytes": (sz, [u32, i32]),
+        "m27b_act_type_for": (u32, [u32]),
+        "m27b_act_quant": (b, [vp, i32, i32, i32, u32, vp, vp, cp, sz]),
+        "m27b_act_quant_gated": (b, [vp, vp, i32, i32, i32, u32, vp, vp, cp, sz]),
+        "m27b_act_quant_rmsnorm": (b, [vp, vp, fp, i32, i32, i32, u32, vp, vp, cp, sz]),
+        "m27b_repacked_bytes": (sz, [u32, u32, u32]),
+        "m27b_repack": (b, [vp, u32, u32, u32, vp, vp, cp, sz]),
+        "m27b_qmv": (b, [wvp, vp, i32, vp, i32, vp, vp, cp, sz]),
+        "m27b_qmv_swiglu": (b, [wvp, wvp, vp, i32, vp, i32, vp, cp, sz]),
+        "m27b_qmv_argmax": (b, [wvp, vp, i32, vp, i32, vp, u32, vp, cp, sz]),
+        "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def version():
+    return lib().m27b_version().decode()
+
+
+def row_bytes(qtype, k):
+    be, bb = BLOCK[qtype & 0xff]
+    assert k % be == 0
+    return k // be * bb
+
+
+def act_type_for(qtype):
+    return Q8_0 if (qtype & 0xff) == Q8_0 else Q8_K
+
+
+def act_bytes(act_type, k):
+    return lib().m27b_act_bytes(act_type, k)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(stream):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _check(ok, err, what):
+    if not ok:
+        raise M27BError(f"{what}: {err.value.decode(errors='replace')}")
+
+
+class QWeight:
+    """A quantized weight matrix resident on the device.
+
+    Holds the device bytes (a torch uint8 tensor) and the WeightView the C ABI
+    consumes.  q6_K and q8_0 are repacked to the planar layout on upload.
+    """
+
+    def __init__(self, raw_u8, qtype, k, rows, device="cuda", stream=None, keep_raw=False):
+        import torch
+        self.qtype, self.k, self.rows = qtype, k, rows
+        be = BLOCK[qtype][0]
+        self.row_blocks = k // be
+        raw = torch.as_tensor(raw_u8).reshape(-1)
+        assert raw.numel() == rows * row_bytes(qtype, k), (raw.numel(), rows, row_bytes(qtype, k))
+        raw_dev = raw.to(device) if raw.device.type != "cuda" else raw
+        if qtype in (Q6_K, Q8_0):
+            n = lib().m27b_repacked_bytes(qtype, self.row_blocks, rows)
+            self.data = torch.empty(n, dtype=torch.uint8, device=raw_dev.device)
+            err = ctypes.create_string_buffer(ERR_CAP)
+            _check(lib().m27b_repack(_ptr(raw_dev), qtype, self.row_blocks, rows, _ptr(self.data), _stream(stream), err,
+                                     ERR_CAP), err, "m27b_repack")
+            self.view = WeightView(self.data.data_ptr(), qtype | LAYOUT_PLANAR, self.row_blocks, rows)
+            self.raw = raw_dev if keep_raw else None
+        else:
+            self.data = raw_dev.contiguous()
+            self.view = WeightView(self.data.data_ptr(), qtype, self.row_blocks, rows)
+            self.raw = self.data
+        self.nbytes = rows * row_bytes(qtype, k)  # stored GGUF bytes (algorithmic)
+
+    @property
+    def act_type(self):
+        return act_type_for(self.qtype)
+
+
+def act_quant(x, act_type, out=None, stream=None, gate=None, norm_w=None, eps=None):
+    """Quantize fp32 rows x [n, k] (device) to q8_K / q8_0 blocks (device uint8)."""
+    import torch
+    x = x if x.dim() == 2 else x.reshape(1, -1)
+    n, k = x.shape
+    nb = act_bytes(act_type, k)
+    if nb == 0:
+        raise M27BError(f"act_quant: bad k={k} for type {act_type}")
+    if out is None:
+        out = torch.empty(n * nb, dtype=torch.uint8, device=x.device)
+    err = ctypes.create_string_buffer(ERR_CAP)
+    L = lib()
+    if gate is not None:
+        ok = L.m27b_act_quant_gated(_ptr(x), _ptr(gate), k, n, x.stride(0), act_type, _ptr(out), _stream(stream), err,
+                                    ERR_CAP)
+    elif eps is not None:
+        ok = L.m27b_act_quant_rmsnorm(_ptr(x), _ptr(norm_w), ctypes.c_float(eps), k, n, x.stride(0), act_type, _ptr(out),
+                                      _stream(stream), err, ERR_CAP)
+    else:
+        ok = L.m27b_act_quant(_ptr(x), k, n, x.stride(0), act_type, _ptr(out), _stream(stream), err, ERR_CAP)
+    _check(ok, err, "m27b_act_quant")
+    return out
+
+
+def qmv(w, xq, n_tok, y, residual=None, stream=None, ldy=None):
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ldy = ldy if ldy is not None else w.rows
+    _check(lib().m27b_qmv(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(y), ldy, _ptr(residual), _stream(stream), err,
+                          ERR_CAP), err, "m27b_qmv")
+    return y
+
+
+def qmv_swiglu(gate, up, xq, n_tok, y, stream=None, ldy=None):
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ldy = ldy if ldy is not None else gate.rows
+    _check(lib().m27b_qmv_swiglu(ctypes.byref(gate.view), ctypes.byref(up.view), _ptr(xq), n_tok, _ptr(y), ldy,
+                                 _stream(stream), err, ERR_CAP), err, "m27b_qmv_swiglu")
+    return y
+
+
+def qmv_argmax(w, xq, n_tok, best, logits=None, row_offset=0, stream=None, ldl=None):
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ldl = ldl if ldl is not None else w.rows
+    _check(lib().m27b_qmv_argmax(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(logits), ldl, _ptr(best), row_offset,
+                                 _stream(stream), err, ERR_CAP), err, "m27b_qmv_argmax")
+    return best
+
+
+def argmax_key_index(key):
+    return 0xffffffff - (int(key) & 0xffffffff)
+
+
+def dequant_rows(w, rows_dev, out, stream=None, view=None):
+    err = ctypes.create_string_buffer(ERR_CAP)
+    v = view if view is not None else w.view
+    k = v.row_blocks * BLOCK[v.ggml_type & 0xff][0]
+    _check(lib().m27b_dequant_rows(ctypes.byref(v), _ptr(rows_dev), rows_dev.numel(), _ptr(out), k, _stream(stream), err,
+                                   ERR_CAP), err, "m27b_dequant_rows")
+    return out
+
+
+def call_raw(name, *args):
+    """Call a C-ABI function with an error buffer appended; returns (ok, message)."""
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ok = getattr(lib(), name)(*args, err, ERR_CAP)
+    return bool(ok), err.value.decode(errors="replace")

@@ -1,0 +1,52 @@
+"""Build recipe for the CPU oracle (test infrastructure only).
+
+* ``liboracle.so`` — the C restatement of ggml's k-quant semantics
+  (``ggml_semantics.c``), compiled with ``-ffp-contract=off`` so that every
+  dequantized value is an unfused ``fl(fl(d*sc)*q) - fl(dmin*m)``.
+* ``_ref/official_dequant`` — the reference's own q4_K dequant known-answer
+  program, compiled from ``debug/official_dequant.c`` where it lies in the
+  reference checkout (only when that checkout is present; the built binary is
+  git-ignored but travels with the tree).  Nothing is copied out of the
+  reference: gcc reads the file in place.
+"""
+import os
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+REF_DIR = os.path.join(HERE, "_ref")
+REF_KAT = os.path.join(REF_DIR, "official_dequant")
+REFERENCE_ROOT = os.environ.get("M27B_REFERENCE_ROOT", "/root/reference")
+
+
+def _stale(out, srcs):
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(s) > t for s in srcs)
+
+
+def build_oracle(force=False):
+    src = os.path.join(HERE, "ggml_semantics.c")
+    if force or _stale(LIB, [src, __file__]):
+        cmd = ["gcc", "-O2", "-march=x86-64-v2", "-fopenmp", "-ffp-contract=off", "-fPIC",
+               "-shared", "-std=c11", "-Wall", "-Wextra", "-o", LIB, src, "-lm"]
+        subprocess.run(cmd, check=True)
+    return LIB
+
+
+def build_reference_kat(force=False):
+    """Compile the reference's q4_K dequant KAT program, if the reference is mounted."""
+    src = os.path.join(REFERENCE_ROOT, "debug", "official_dequant.c")
+    if not os.path.exists(src):
+        return REF_KAT if os.path.exists(REF_KAT) else None
+    os.makedirs(REF_DIR, exist_ok=True)
+    if force or _stale(REF_KAT, [src]):
+        subprocess.run(["gcc", "-O0", "-ffp-contract=off", "-fno-strict-aliasing", "-o", REF_KAT, src, "-lm"],
+                       check=True)
+    return REF_KAT
+
+
+if __name__ == "__main__":
+    print(build_oracle(force=True))
+    print(build_reference_kat(force=True))
