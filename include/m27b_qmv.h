@@ -77,6 +77,13 @@ struct WeightView {
 /* Library version string. */
 M27B_API const char *m27b_version(void);
 
+/* Read the current device's status word (synchronous): 0 when every bounded
+ * wait inside the kernels completed; non-zero when a kernel gave up waiting
+ * for its own shared-memory copies (the results of that launch are invalid).
+ * clear != 0 resets it.  No counterpart in the reference, whose kernels have
+ * no waits. */
+M27B_API bool m27b_device_status(int *status, int clear, char *err, size_t err_cap);
+
 /* Bytes of one quantized activation row of k values: k/256*292 for
  * M27B_TYPE_Q8_K, k/32*34 for M27B_TYPE_Q8_0; 0 if k is not a multiple of
  * the block size or the type is not an activation type. */

@@ -14,7 +14,23 @@
 
 using namespace m27b;
 
+// Library status word, one per device: kernels set it non-zero when one of
+// their bounded waits runs out (1: a stage never filled, 2: draining after
+// such a failure).  Read and cleared with m27b_device_status().
+__device__ int g_m27b_status;
+
 namespace {
+
+int *status_ptr_current() {
+    static int *cache[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return nullptr;
+    if (dev < 64 && cache[dev]) return cache[dev];
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_m27b_status) != cudaSuccess) return nullptr;
+    if (dev < 64) cache[dev] = (int *)p;
+    return (int *)p;
+}
 
 bool fail(char *err, size_t cap, const char *fmt, ...) {
     if (err && cap) {
@@ -142,10 +158,12 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
     const size_t xb = act_bytes(at, d0.k);
     if (((uintptr_t)xq & (at == M27B_TYPE_Q8_K ? 3u : 1u)) != 0) return fail(err, cap, "%s: misaligned activations", what);
     const size_t smem = qmv_smem_bytes(d0.base, d0.k, n_tok < 4 ? n_tok : 4);
-    if (smem > 200 * 1024)
-        return fail(err, cap, "%s: activation staging needs %zu bytes of shared memory (k=%d too large)", what, smem, d0.k);
+    if (smem == 0 || smem > 227 * 1024)
+        return fail(err, cap, "%s: activation staging does not fit in shared memory (k=%d too large)", what, d0.k);
     const int sms = sm_count_current();
     if (sms <= 0) return fail(err, cap, "%s: no CUDA device", what);
+    int *status = status_ptr_current();
+    if (!status) return fail(err, cap, "%s: cannot resolve the device status word", what);
     if (epi == EPI_ARGMAX) {
         cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long) * (size_t)n_tok, stream);
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
@@ -166,6 +184,7 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         a.k = d0.k;
         a.passes = d0.passes;
         a.row_offset = row_offset;
+        a.status = status;
         cudaError_t e = launch_qmv(d0.kind, epi, a, nt, sms, stream);
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
     }
@@ -177,6 +196,20 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
 extern "C" {
 
 const char *m27b_version(void) { return "m27b-b200 0.1 (sm_100a)"; }
+
+bool m27b_device_status(int *status, int clear, char *err, size_t err_cap) {
+    if (!status) return fail(err, err_cap, "m27b_device_status: null output");
+    int *p = status_ptr_current();
+    if (!p) return fail(err, err_cap, "m27b_device_status: no CUDA device");
+    cudaError_t e = cudaMemcpy(status, p, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_ok(e, "m27b_device_status", err, err_cap);
+    if (clear && *status) {
+        const int zero = 0;
+        e = cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_ok(e, "m27b_device_status", err, err_cap);
+    }
+    return ok(err, err_cap);
+}
 
 size_t m27b_act_bytes(uint32_t act_type, int k) { return act_bytes(act_type, k); }
 

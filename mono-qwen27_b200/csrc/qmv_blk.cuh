@@ -1,0 +1,348 @@
+// qmv_blk.cuh — q4_K matvec with one super-block per lane, weights streamed
+// through shared memory with coalesced asynchronous copies.
+//
+// Mapping: a warp owns groups of 8 consecutive rows; lane L works on row slot
+// L/4 of the group and, in pass p, on super-block 4p + L%4 of that row.  A
+// lane holds a whole 144-byte block, so the per-block work — the fp16 scales,
+// the twelve packed bytes of 6-bit scales/mins (reference get_scale_min_k4,
+// src/mono27b_executor.cu:690-693), and the min correction against the
+// activation's bsums — is done once per 256 weights.  The four lanes of a row
+// reduce with two shuffles at the end of the row.
+//
+// Streaming: one "item" of a warp is pass p of one group — the 4 consecutive
+// blocks (576 contiguous bytes) of each of the 8 rows.  Lane 0 of the warp
+// copies an item into the warp's shared-memory stage with ONE 2-D TMA tensor
+// copy (cp.async.bulk.tensor.2d, box 8 rows x 576 bytes over a uint32 view of
+// the weight rows, no multicast) that completes on the stage's mbarrier.
+// Rows past the end and blocks past the end of a row read as zeros (the
+// tensor map's bounds), so ragged tails need no special case; the copies of item i+1 are in flight while item i is
+// multiplied (three stages per warp, 16 warps in one CTA per SM).  Every mbarrier wait is bounded by the
+// global timer (M27B_WAIT_NS); a wait that runs out records an error in the
+// library's device status word and the kernel drains its own copies before
+// it returns.  Lanes read their block from the stage: the 576-byte slot
+// stride and 144-byte block stride put the 8 lanes of each shared-memory
+// phase on distinct banks.
+//
+// Activations are staged per CTA as 272-byte records per (token, block):
+// 256 codes | 8 int16 sums of each 32-value sub-block (bsum[2j]+bsum[2j+1]);
+// the fp32 block scales follow in their own array.  The 272-byte stride puts
+// the four blocks a phase reads on disjoint banks.
+#pragma once
+
+#include <cuda.h>
+
+#include "qmv_kernels.cuh"
+
+namespace m27b {
+
+constexpr int BLK_XREC = 272;                 // bytes per staged (token, block) activation record
+constexpr int BLK_ITEM = 8 * 4 * 144;         // 4608 bytes: one item (8 rows x 4 blocks)
+constexpr int BLK_STAGES = 2;                 // stages per warp
+constexpr int BLK_WARPS = 8;                  // most warps per CTA (two CTAs per SM)
+constexpr int BLK_THREADS = BLK_WARPS * 32;
+constexpr size_t BLK_SMEM_MAX = 112 * 1024;   // two CTAs per SM within the 228 KB of shared memory
+
+inline size_t blk_x_bytes(int k, int nt) { return (size_t)nt * ((size_t)k / 256) * (BLK_XREC + 4); }
+constexpr size_t BLK_WARP_BYTES = (size_t)BLK_STAGES * BLK_ITEM + (size_t)BLK_STAGES * 8;  // stages + barriers
+
+// Warps per CTA: as many as the shared memory left after the staged
+// activations holds stages for (at most BLK_WARPS); 0 if not even one fits.
+inline int blk_warps(int k, int nt) {
+    const size_t x = blk_x_bytes(k, nt);
+    if (x + 16 >= BLK_SMEM_MAX) return 0;
+    const size_t w = (BLK_SMEM_MAX - x - 16) / BLK_WARP_BYTES;
+    return (int)(w < (size_t)BLK_WARPS ? w : (size_t)BLK_WARPS);
+}
+
+inline size_t blk_smem_bytes(int k, int nt) { return (size_t)blk_warps(k, nt) * BLK_WARP_BYTES + blk_x_bytes(k, nt) + 16; }
+
+// ---- mbarrier + bulk-copy helpers (sm_90+ PTX; no cluster multicast) ----
+constexpr unsigned long long M27B_WAIT_NS = 2000000000ull;  // 2 s bound on any wait
+
+M27B_DI uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+M27B_DI void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+M27B_DI void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+M27B_DI void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+M27B_DI void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+M27B_DI void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 2-D tiled TMA load of the box at (x, y) of the tensor map into shared memory.
+M27B_DI void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"((unsigned long long)tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Test the phase; if it is not complete the thread may sleep in hardware for
+// up to ~20 us (suspend-time hint) before the test returns false.
+M27B_DI bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(20000)
+        : "memory");
+    return ok != 0;
+}
+
+M27B_DI unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase with the given parity to complete, for at most
+// M27B_WAIT_NS; returns false (and records `code` in *status) on timeout.
+M27B_DI bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *status, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 8; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > M27B_WAIT_NS) {
+            if (status) atomicCAS(status, 0, code);
+            return false;
+        }
+    }
+}
+
+template <int NT>
+M27B_DI void stage_x_blk(const QmvArgs &a, uint8_t *xrec, float *xd) {
+    const int nb = a.k / 256;
+    const uint8_t *src = (const uint8_t *)a.xq;  // NT*nb blocks of 292 bytes
+    for (int i = threadIdx.x; i < NT * nb * 64; i += blockDim.x) {
+        const int blk = i >> 6, w = i & 63;
+        ((uint32_t *)(xrec + (size_t)blk * BLK_XREC))[w] = ((const uint32_t *)(src + (size_t)blk * 292 + 4))[w];
+    }
+    for (int i = threadIdx.x; i < NT * nb * 9; i += blockDim.x) {
+        const int blk = i / 9, j = i - blk * 9;
+        const uint8_t *sb = src + (size_t)blk * 292;
+        if (j < 8) {
+            const int16_t *bs = (const int16_t *)(sb + 260);
+            ((int16_t *)(xrec + (size_t)blk * BLK_XREC + 256))[j] = (int16_t)(bs[2 * j] + bs[2 * j + 1]);
+        } else {
+            xd[blk] = *(const float *)sb;
+        }
+    }
+}
+
+// One block (held in registers) times NT staged activation blocks.
+template <int NT>
+M27B_DI void q4k_block_mac(const uint4 (&v)[9], const uint8_t *xrec0, const float *xd0, int nb, float (&acc)[NT]) {
+    const uint4 hd = v[0];
+    // all eight 6-bit scales and mins of the block, one byte each
+    const uint32_t sc03 = hd.y & 0x3f3f3f3fu;
+    const uint32_t mn03 = hd.z & 0x3f3f3f3fu;
+    const uint32_t sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
+    const uint32_t mn47 = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
+    const float dw = h2f(hd.x), dmw = h2f(hd.x >> 16);
+    int isum[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) isum[t] = 0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const uint4 qa = v[1 + 2 * g], qb = v[2 + 2 * g];  // qs bytes 32g .. 32g+31
+        const uint32_t lo[8] = {qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu, qa.w & 0x0f0f0f0fu,
+                                qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu, qb.w & 0x0f0f0f0fu};
+        const uint32_t hi[8] = {qa.x & 0xf0f0f0f0u, qa.y & 0xf0f0f0f0u, qa.z & 0xf0f0f0f0u, qa.w & 0xf0f0f0f0u,
+                                qb.x & 0xf0f0f0f0u, qb.y & 0xf0f0f0f0u, qb.z & 0xf0f0f0f0u, qb.w & 0xf0f0f0f0u};
+        const uint32_t scw = g < 2 ? sc03 : sc47;
+        const int sh = 16 * (g & 1);
+        const int s_lo = (int)((scw >> sh) & 0xffu), s_hi = (int)((scw >> (sh + 8)) & 0xffu);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const uint8_t *xr = xrec0 + (size_t)t * nb * BLK_XREC + 64 * g;
+            const int4 x0 = *(const int4 *)(xr);
+            const int4 x1 = *(const int4 *)(xr + 16);
+            const int4 x2 = *(const int4 *)(xr + 32);
+            const int4 x3 = *(const int4 *)(xr + 48);
+            int dl = dp4a_us(lo[0], x0.x, 0);
+            dl = dp4a_us(lo[1], x0.y, dl);
+            dl = dp4a_us(lo[2], x0.z, dl);
+            dl = dp4a_us(lo[3], x0.w, dl);
+            dl = dp4a_us(lo[4], x1.x, dl);
+            dl = dp4a_us(lo[5], x1.y, dl);
+            dl = dp4a_us(lo[6], x1.z, dl);
+            dl = dp4a_us(lo[7], x1.w, dl);
+            int dh = dp4a_us(hi[0], x2.x, 0);  // 16 x the high-nibble dot
+            dh = dp4a_us(hi[1], x2.y, dh);
+            dh = dp4a_us(hi[2], x2.z, dh);
+            dh = dp4a_us(hi[3], x2.w, dh);
+            dh = dp4a_us(hi[4], x3.x, dh);
+            dh = dp4a_us(hi[5], x3.y, dh);
+            dh = dp4a_us(hi[6], x3.z, dh);
+            dh = dp4a_us(hi[7], x3.w, dh);
+            isum[t] += s_lo * dl + s_hi * (dh >> 4);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const uint8_t *xr = xrec0 + (size_t)t * nb * BLK_XREC;
+        const int4 bs = *(const int4 *)(xr + 256);  // sub-block bsum pairs
+        int msum = __dp2a_lo(bs.x, (int)mn03, 0);
+        msum = __dp2a_hi(bs.y, (int)mn03, msum);
+        msum = __dp2a_lo(bs.z, (int)mn47, msum);
+        msum = __dp2a_hi(bs.w, (int)mn47, msum);
+        const float dx = xd0[t * nb];
+        acc[t] = fmaf(dw * dx, (float)isum[t], acc[t]);
+        acc[t] = fmaf(-(dmw * dx), (float)msum, acc[t]);
+    }
+}
+
+// Work of a warp: items (group, pass, matrix) in that order, matrix fastest
+// (SWIGLU streams the gate blocks, then the up blocks, of the same pass).
+template <int NT, int EPI>
+__global__ void __launch_bounds__(BLK_THREADS, 2)
+    k_qmv_q4k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1) {
+    constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int slot = lane >> 2, qd = lane & 3;
+    const int nwarps = blockDim.x >> 5;
+    const int wg = blockIdx.x * nwarps + warp;
+    const int W = gridDim.x * nwarps;
+    const int ngroups = (a.rows + 7) >> 3;
+    const int P = (a.rb + 3) >> 2;  // passes per row
+    const int nb = a.rb;
+    const int my_groups = wg < ngroups ? (ngroups - 1 - wg) / W + 1 : 0;
+
+    // [stages of all warps | activation records | block scales | barriers]
+    uint8_t *stage0 = smem + (size_t)warp * BLK_STAGES * BLK_ITEM;
+    uint8_t *xrec = smem + (size_t)nwarps * BLK_STAGES * BLK_ITEM;
+    float *xd = (float *)(xrec + (size_t)NT * nb * BLK_XREC);
+    uint64_t *bar = (uint64_t *)(((uintptr_t)(xd + NT * nb) + 15) & ~(uintptr_t)15) + (size_t)warp * BLK_STAGES;
+    if (lane == 0) {
+        for (int s = 0; s < BLK_STAGES; ++s) mbar_init(&bar[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    // copy cursor: lane 0 issues one tensor copy per item; all lanes track it
+    int lg = 0, lp = 0, lm = 0, li = 0, ls = 0;  // ls = li % BLK_STAGES
+    auto issue_item = [&]() {
+        if (lg < my_groups) {
+            if (lane == 0) {
+                uint64_t *b = &bar[ls];
+                fence_proxy_async();  // the stage's previous reads precede the async writes
+                mbar_arrive_expect_tx(b, BLK_ITEM);
+                tma_load_2d(stage0 + ls * BLK_ITEM, (NM == 2 && lm == 1) ? &tm1 : &tm0, lp * 144, (wg + lg * W) * 8, b);
+            }
+            ++li;
+            if (++ls == BLK_STAGES) ls = 0;
+            if (++lm == NM) {
+                lm = 0;
+                if (++lp == P) { lp = 0; ++lg; }
+            }
+        }
+    };
+
+    // all stages' copies go out before the activations are staged
+    for (int i = 0; i < BLK_STAGES; ++i) issue_item();
+    stage_x_blk<NT>(a, xrec, xd);
+    __syncthreads();
+
+    float acc[NM][NT];
+#pragma unroll
+    for (int m = 0; m < NM; ++m)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[m][t] = 0.0f;
+    unsigned long long best[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) best[t] = 0ull;
+
+    int cg = 0, cp = 0, cm = 0, ci = 0, cs = 0;  // compute cursor; cs = ci % BLK_STAGES
+    uint32_t cph = 0;                             // phase parity of stage cs
+    bool ok = true;
+    while (cg < my_groups) {
+        // every lane waits (bounded); the warp leaves together if any lane gave up
+        const bool landed = mbar_wait_bounded(&bar[cs], cph, a.status, 1);
+        if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
+        const int row = (wg + cg * W) * 8 + slot;
+        const int b = 4 * cp + qd;
+        // take this lane's block into registers, then hand the stage back to
+        // the copy engine: item ci+2 streams in while this one is multiplied
+        uint4 v[9];
+        const uint8_t *blk = stage0 + cs * BLK_ITEM + slot * 576 + qd * 144;
+#pragma unroll
+        for (int j = 0; j < 9; ++j) v[j] = *(const uint4 *)(blk + 16 * j);
+        __syncwarp();
+        issue_item();
+        if (row < a.rows && b < nb) {
+            if (NM == 1 || cm == 0) q4k_block_mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[0]);
+            else q4k_block_mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[NM - 1]);
+        }
+        ++ci;
+        if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
+        if (++cm < NM) continue;
+        cm = 0;
+        if (++cp < P) continue;
+        cp = 0;
+        ++cg;
+        // row done: reduce the four lanes of each row (lane slot*4 keeps it)
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                float s = acc[m][t];
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                s += __shfl_xor_sync(0xffffffffu, s, 2);
+                acc[m][t] = s;
+            }
+        if (qd == 0 && row < a.rows) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const size_t o = (size_t)t * a.ldy + row;
+                const float s0 = acc[0][t];
+                if constexpr (EPI == EPI_STORE) {
+                    a.y[o] = a.residual ? s0 + a.residual[o] : s0;
+                } else if constexpr (EPI == EPI_SWIGLU) {
+                    a.y[o] = s0 / (1.0f + expf(-s0)) * acc[NM - 1][t];
+                } else {
+                    if (a.y) a.y[o] = s0;
+                    const unsigned long long key = argmax_key(s0, (uint32_t)row + a.row_offset);
+                    best[t] = key > best[t] ? key : best[t];
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+#pragma unroll
+            for (int t = 0; t < NT; ++t) acc[m][t] = 0.0f;
+    }
+    if (!ok) {
+        // a wait ran out: let every copy this warp issued land (bounded again)
+        // before the CTA's shared memory is released
+        for (; ci < li; ++ci) {
+            mbar_wait_bounded(&bar[cs], cph, a.status, 2);
+            if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
+        }
+        return;
+    }
+
+    if constexpr (EPI == EPI_ARGMAX) {
+        if (qd == 0) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                if (best[t] != 0ull) atomicMax(a.best + t, best[t]);
+        }
+    }
+}
+
+}  // namespace m27b

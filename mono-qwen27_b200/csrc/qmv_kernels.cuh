@@ -25,17 +25,26 @@ struct QmvArgs {
     int rb;                    // blocks per row
     int k;                     // values per row
     int passes;                // 1024-value passes per row
+    int segs;                  // units per row = ceil(passes / PS)
     uint32_t row_offset;       // added to argmax indices
+    int *status;               // device status word: set non-zero if a bounded wait runs out
 };
 
 // Planar view of the staged activations in shared memory.
 struct XStage {
-    const int8_t *q;   // [NT][k] codes
-    const int16_t *bs; // [NT][k/16] bsums (q8_K only)
-    const float *d;    // [NT][nb] block scales
+    const int8_t *q;     // [NT][k] codes
+    const uint32_t *pk;  // [NT][nb*8] the two bsums each lane slice needs, packed as int16 pairs (q8_K only)
+    const float *d;      // [NT][nb] block scales
     int k;
     int nb;
 };
+
+// u8 x s8 four-way dot product (dp4a.u32.s32): a's bytes unsigned, b's signed.
+M27B_DI int dp4a_us(uint32_t a, int b, int c) {
+    int r;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
 
 // ---------------------------------------------------------------------------
 // q4_K, GGUF layout (144-byte blocks).  Pass p, lane L: block b = 4p + L/8,
@@ -45,15 +54,15 @@ struct XStage {
 struct WQ4K {
     static constexpr int NL = 2;
     static constexpr int PER_PASS = 4;  // blocks per pass
+    // index of the first of the two bsums lane slice c needs (second is +2)
+    M27B_DI static int bsum_lo(int c) { return 2 * c - (c & 1); }
+    static constexpr int BSUM_GAP = 2;
     M27B_DI static void load(const uint8_t *row, int rb, int p, int lane, uint4 (&v)[NL]) {
         const int b = PER_PASS * p + (lane >> 3);
         if (b < rb) {
             const uint8_t *blk = row + (size_t)b * 144;
             v[0] = ldg_stream16(blk + 16 + 16 * (lane & 7));
             v[1] = ldg_stream16(blk);
-        } else {
-            v[0] = make_uint4(0, 0, 0, 0);
-            v[1] = make_uint4(0, 0, 0, 0);
         }
     }
     template <int NT>
@@ -62,10 +71,10 @@ struct WQ4K {
         if (b >= rb) return;
         const int c = lane & 7, g = c >> 1, h = c & 1;
         const uint4 q = v[0], hd = v[1];
-        // 6-bit scale/min of sub-blocks 2g and 2g+1 as byte pairs
-        // (get_scale_min_k4, reference :690-693).
+        // 6-bit scale/min of sub-blocks 2g and 2g+1 as byte pairs in the low
+        // 16 bits (get_scale_min_k4, reference :690-693).
         const int sh = 16 * (g & 1);
-        const uint32_t A = (hd.y >> sh) & 0xffffu, B = (hd.z >> sh) & 0xffffu, C = (hd.w >> sh) & 0xffffu;
+        const uint32_t A = hd.y >> sh, B = hd.z >> sh, C = hd.w >> sh;
         uint32_t scp, mnp;
         if (g < 2) {
             scp = A & 0x3f3fu;
@@ -74,24 +83,29 @@ struct WQ4K {
             scp = (C & 0x0f0fu) | ((A >> 2) & 0x3030u);
             mnp = ((C >> 4) & 0x0f0fu) | ((B >> 2) & 0x3030u);
         }
-        const int sc_lo = (int)(scp & 0xffu), sc_hi = (int)(scp >> 8);
-        const int m_lo = (int)(mnp & 0xffu), m_hi = (int)(mnp >> 8);
         const float dw = h2f(hd.x), dmw = h2f(hd.x >> 16);
-        const uint4 lo = make_uint4(q.x & 0x0f0f0f0fu, q.y & 0x0f0f0f0fu, q.z & 0x0f0f0f0fu, q.w & 0x0f0f0f0fu);
-        const uint4 hi = make_uint4((q.x >> 4) & 0x0f0f0f0fu, (q.y >> 4) & 0x0f0f0f0fu, (q.z >> 4) & 0x0f0f0f0fu,
-                                    (q.w >> 4) & 0x0f0f0f0fu);
+        const uint32_t l0 = q.x & 0x0f0f0f0fu, l1 = q.y & 0x0f0f0f0fu, l2 = q.z & 0x0f0f0f0fu, l3 = q.w & 0x0f0f0f0fu;
+        const uint32_t h0 = q.x & 0xf0f0f0f0u, h1 = q.y & 0xf0f0f0f0u, h2 = q.z & 0xf0f0f0f0u, h3 = q.w & 0xf0f0f0f0u;
         const int e0 = b * 256 + 64 * g + 16 * h;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             const int8_t *xt = xs.q + (size_t)t * xs.k;
-            const uint4 xa = *(const uint4 *)(xt + e0);
-            const uint4 xb = *(const uint4 *)(xt + e0 + 32);
-            const int16_t *bs = xs.bs + (size_t)t * (xs.k / 16) + (e0 >> 4);
-            const int isum = sc_lo * dot16(lo, xa) + sc_hi * dot16(hi, xb);
-            const int msum = m_lo * (int)bs[0] + m_hi * (int)bs[2];
-            const float dx = xs.d[t * xs.nb + b];
-            acc[t] = fmaf(dw * dx, (float)isum, acc[t]);
-            acc[t] = fmaf(-(dmw * dx), (float)msum, acc[t]);
+            const int4 xa = *(const int4 *)(xt + e0);
+            const int4 xb = *(const int4 *)(xt + e0 + 32);
+            int dl = dp4a_us(l0, xa.x, 0);
+            dl = dp4a_us(l1, xa.y, dl);
+            dl = dp4a_us(l2, xa.z, dl);
+            dl = dp4a_us(l3, xa.w, dl);
+            int dh = dp4a_us(h0, xb.x, 0);  // 16 x the high-nibble dot
+            dh = dp4a_us(h1, xb.y, dh);
+            dh = dp4a_us(h2, xb.z, dh);
+            dh = dp4a_us(h3, xb.w, dh);
+            // |dl|, |dh>>4| <= 16*15*127 fit int16: pack and weight by the byte-pair scales
+            const int pair = (dl & 0xffff) | ((dh >> 4) << 16);
+            const int isum = __dp2a_lo(pair, (int)scp, 0);
+            const int msum = __dp2a_lo((int)xs.pk[t * xs.nb * 8 + b * 8 + c], (int)mnp, 0);
+            const float v2 = fmaf(dw, (float)isum, -dmw * (float)msum);
+            acc[t] = fmaf(v2, xs.d[t * xs.nb + b], acc[t]);
         }
     }
 };
@@ -106,6 +120,8 @@ struct WQ4K {
 struct WQ6KP {
     static constexpr int NL = 3;
     static constexpr int PER_PASS = 4;
+    M27B_DI static int bsum_lo(int c) { return c + 4 * (c >> 2); }
+    static constexpr int BSUM_GAP = 4;
     M27B_DI static void load(const uint8_t *row, int rb, int p, int lane, uint4 (&v)[NL]) {
         const int b = PER_PASS * p + (lane >> 3);
         if (b < rb) {
@@ -114,8 +130,6 @@ struct WQ6KP {
             v[1] = ldg_stream16(row + (size_t)rb * 128 + (size_t)b * 64 + 16 * (2 * half + lsub));
             const uint2 s = ldg_stream8(row + (size_t)rb * 192 + (size_t)b * 16 + 8 * half);
             v[2] = make_uint4(s.x, s.y, ldg_stream_u16(row + (size_t)rb * 208 + 2 * b), 0u);
-        } else {
-            v[0] = v[1] = v[2] = make_uint4(0, 0, 0, 0);
         }
     }
     template <int NT>
@@ -142,13 +156,22 @@ struct WQ6KP {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             const int8_t *xt = xs.q + (size_t)t * xs.k;
-            const uint4 xa = *(const uint4 *)(xt + e_lo);
-            const uint4 xb = *(const uint4 *)(xt + e_lo + 64);
-            const int16_t *bs = xs.bs + (size_t)t * (xs.k / 16) + (e_lo >> 4);
-            // codes are stored +32: <q-32, x> = <q, x> - 32 * bsum
-            const int isum = sc_lo * (dot16(lo, xa) - 32 * (int)bs[0]) + sc_hi * (dot16(hi, xb) - 32 * (int)bs[4]);
-            const float dx = xs.d[t * xs.nb + b];
-            acc[t] = fmaf(dw * dx, (float)isum, acc[t]);
+            const int4 xa = *(const int4 *)(xt + e_lo);
+            const int4 xb = *(const int4 *)(xt + e_lo + 64);
+            int dl = dp4a_us(lo.x, xa.x, 0);
+            dl = dp4a_us(lo.y, xa.y, dl);
+            dl = dp4a_us(lo.z, xa.z, dl);
+            dl = dp4a_us(lo.w, xa.w, dl);
+            int dh = dp4a_us(hi.x, xb.x, 0);
+            dh = dp4a_us(hi.y, xb.y, dh);
+            dh = dp4a_us(hi.z, xb.z, dh);
+            dh = dp4a_us(hi.w, xb.w, dh);
+            // codes are stored +32: <q-32, x> = <q, x> - 32 * bsum (up to 16*32*127 in
+            // magnitude, so kept in 32-bit integers)
+            const uint32_t pr = xs.pk[t * xs.nb * 8 + b * 8 + c];
+            const int blo = (int)(int16_t)(pr & 0xffffu), bhi = (int)(int16_t)(pr >> 16);
+            const int isum = sc_lo * (dl - 32 * blo) + sc_hi * (dh - 32 * bhi);
+            acc[t] = fmaf(dw * xs.d[t * xs.nb + b], (float)isum, acc[t]);
         }
     }
 };
@@ -164,9 +187,7 @@ struct WQ80P {
         if (b < rb) {
             v[0] = ldg_stream16(row + (size_t)b * 32);
             v[1] = ldg_stream16(row + (size_t)b * 32 + 16);
-            v[2] = make_uint4(ldg_stream_u16(row + (size_t)rb * 32 + 2 * b), 0u, 0u, 0u);
-        } else {
-            v[0] = v[1] = v[2] = make_uint4(0, 0, 0, 0);
+            v[2].x = ldg_stream_u16(row + (size_t)rb * 32 + 2 * b);
         }
     }
     template <int NT>
@@ -188,15 +209,13 @@ template <> struct WTraits<W_Q4K> { using T = WQ4K; };
 template <> struct WTraits<W_Q6KP> { using T = WQ6KP; };
 template <> struct WTraits<W_Q80P> { using T = WQ80P; };
 
-// Passes of loads kept in flight per register buffer.
-template <int WT, int NM> struct PipeDepth { static constexpr int value = (WT == W_Q4K && NM == 1) ? 4 : 2; };
-
-// Copy NT activation rows into shared memory in planar form.
+// Copy NT activation rows into shared memory in planar form: codes, the
+// bsum pair of every (block, lane slice), block scales.
 template <int WT, int NT>
 M27B_DI XStage stage_x(const QmvArgs &a, uint8_t *smem) {
     XStage xs;
     xs.k = a.k;
-    if (WT == W_Q80P) {
+    if constexpr (WT == W_Q80P) {
         const int nb = a.k / 32;
         int8_t *q = (int8_t *)smem;
         float *d = (float *)(smem + (size_t)NT * a.k);
@@ -204,30 +223,35 @@ M27B_DI XStage stage_x(const QmvArgs &a, uint8_t *smem) {
         const int total = NT * nb * 17;
         for (int i = threadIdx.x; i < total; i += blockDim.x) {
             const int blk = i / 17, o = i - blk * 17;
-            const uint16_t h = src[i];
-            if (o == 0) d[blk] = h2f(h);
-            else *(uint16_t *)(q + (size_t)blk * 32 + 2 * (o - 1)) = h;
+            const uint16_t hw = src[i];
+            if (o == 0) d[blk] = h2f(hw);
+            else *(uint16_t *)(q + (size_t)blk * 32 + 2 * (o - 1)) = hw;
         }
         xs.q = q;
-        xs.bs = nullptr;
+        xs.pk = nullptr;
         xs.d = d;
         xs.nb = nb;
     } else {
+        using T = typename WTraits<WT>::T;
         const int nb = a.k / 256;
         int8_t *q = (int8_t *)smem;
-        int16_t *bs = (int16_t *)(smem + (size_t)NT * a.k);
+        uint32_t *pk = (uint32_t *)(smem + (size_t)NT * a.k);
         float *d = (float *)(smem + (size_t)NT * a.k + (size_t)NT * nb * 32);
-        const uint32_t *src = (const uint32_t *)a.xq;  // 73 words per block
-        const int total = NT * nb * 73;
+        const uint8_t *src = (const uint8_t *)a.xq;  // 292-byte blocks
+        const int total = NT * nb * 65;                // d + 64 code words per block
         for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            const int blk = i / 73, o = i - blk * 73;
-            const uint32_t w = src[i];
+            const int blk = i / 65, o = i - blk * 65;
+            const uint32_t w = ((const uint32_t *)(src + (size_t)blk * 292))[o];
             if (o == 0) d[blk] = __uint_as_float(w);
-            else if (o <= 64) ((uint32_t *)q)[(size_t)blk * 64 + (o - 1)] = w;
-            else ((uint32_t *)bs)[(size_t)blk * 8 + (o - 65)] = w;
+            else ((uint32_t *)q)[(size_t)blk * 64 + (o - 1)] = w;
+        }
+        for (int i = threadIdx.x; i < NT * nb * 8; i += blockDim.x) {
+            const int blk = i >> 3, c = i & 7, lo = T::bsum_lo(c);
+            const int16_t *bs = (const int16_t *)(src + (size_t)blk * 292 + 260);
+            pk[i] = (uint32_t)(uint16_t)bs[lo] | ((uint32_t)(uint16_t)bs[lo + T::BSUM_GAP] << 16);
         }
         xs.q = q;
-        xs.bs = bs;
+        xs.pk = pk;
         xs.d = d;
         xs.nb = nb;
     }
@@ -258,38 +282,45 @@ M27B_DI void finish_row(const QmvArgs &a, int row, float (&acc)[NM][NT], int lan
     }
 }
 
-template <int WT, int NT, int EPI>
+// The warp's work is a sequence of units (row, segment); a segment is PS
+// passes of a row.  Units are double-buffered in registers: the loads of unit
+// u+1 are issued before unit u is multiplied.
+template <int WT, int NT, int EPI, int PS>
 __global__ void __launch_bounds__(QMV_THREADS, 2) k_qmv(const QmvArgs a) {
     using T = typename WTraits<WT>::T;
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
-    constexpr int PM = PipeDepth<WT, NM>::value;
     extern __shared__ __align__(16) uint8_t smem[];
 
     const int lane = threadIdx.x & 31;
     const int wg = blockIdx.x * QMV_WARPS + (threadIdx.x >> 5);
     const int W = gridDim.x * QMV_WARPS;
-    const int P = a.passes;
+    const int P = a.passes, S = a.segs;
     const int my_rows = wg < a.rows ? (a.rows - 1 - wg) / W + 1 : 0;
 
-    uint4 bufA[PM][NM][T::NL];
-    uint4 bufB[PM][NM][T::NL];
-    int lrow = 0, lp = 0;  // load cursor (row ordinal, pass)
-    int crow = 0, cp = 0;  // compute cursor
+    uint4 bufA[PS][NM][T::NL];
+    uint4 bufB[PS][NM][T::NL];
+    int lrow = 0, lseg = 0;  // load cursor
+    int crow = 0, cseg = 0;  // compute cursor
 
-    auto load_chunk = [&](uint4 (&buf)[PM][NM][T::NL]) {
+    auto load_unit = [&](uint4 (&buf)[PS][NM][T::NL]) {
+        if (lrow < my_rows) {
+            const size_t r = (size_t)wg + (size_t)lrow * W;
+            const uint8_t *r0 = a.w0 + r * a.row_stride;
+            const uint8_t *r1 = NM == 2 ? a.w1 + r * a.row_stride : nullptr;
 #pragma unroll
-        for (int j = 0; j < PM; ++j) {
-            if (lrow < my_rows) {
-                const size_t r = (size_t)wg + (size_t)lrow * W;
-                T::load(a.w0 + r * a.row_stride, a.rb, lp, lane, buf[j][0]);
-                if constexpr (NM == 2) T::load(a.w1 + r * a.row_stride, a.rb, lp, lane, buf[j][1]);
-                if (++lp == P) { lp = 0; ++lrow; }
+            for (int j = 0; j < PS; ++j) {
+                const int p = lseg * PS + j;
+                if (p < P) {
+                    T::load(r0, a.rb, p, lane, buf[j][0]);
+                    if constexpr (NM == 2) T::load(r1, a.rb, p, lane, buf[j][1]);
+                }
             }
+            if (++lseg == S) { lseg = 0; ++lrow; }
         }
     };
 
     // First loads go out before the activations are staged.
-    load_chunk(bufA);
+    load_unit(bufA);
     const XStage xs = stage_x<WT, NT>(a, smem);
     __syncthreads();
 
@@ -300,27 +331,28 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) k_qmv(const QmvArgs a) {
         for (int t = 0; t < NT; ++t) acc[m][t] = 0.0f;
     unsigned long long best = 0ull;
 
-    auto compute_chunk = [&](const uint4 (&buf)[PM][NM][T::NL]) {
+    auto compute_unit = [&](const uint4 (&buf)[PS][NM][T::NL]) {
 #pragma unroll
-        for (int j = 0; j < PM; ++j) {
-            if (crow < my_rows) {
-                T::template mac<NT>(buf[j][0], a.rb, cp, lane, xs, acc[0]);
-                if constexpr (NM == 2) T::template mac<NT>(buf[j][1], a.rb, cp, lane, xs, acc[1]);
-                if (++cp == P) {
-                    finish_row<EPI, NT, NM>(a, wg + crow * W, acc, lane, best);
-                    cp = 0;
-                    ++crow;
-                }
+        for (int j = 0; j < PS; ++j) {
+            const int p = cseg * PS + j;
+            if (p < P) {
+                T::template mac<NT>(buf[j][0], a.rb, p, lane, xs, acc[0]);
+                if constexpr (NM == 2) T::template mac<NT>(buf[j][1], a.rb, p, lane, xs, acc[1]);
             }
+        }
+        if (++cseg == S) {
+            finish_row<EPI, NT, NM>(a, wg + crow * W, acc, lane, best);
+            cseg = 0;
+            ++crow;
         }
     };
 
     while (crow < my_rows) {
-        load_chunk(bufB);
-        compute_chunk(bufA);
+        load_unit(bufB);
+        compute_unit(bufA);
         if (crow >= my_rows) break;
-        load_chunk(bufA);
-        compute_chunk(bufB);
+        load_unit(bufA);
+        compute_unit(bufB);
     }
 
     if constexpr (EPI == EPI_ARGMAX) {
@@ -328,7 +360,29 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) k_qmv(const QmvArgs a) {
     }
 }
 
+// Largest unit (passes held per register buffer) that double-buffers
+// without spilling: per pass and lane a q4_K slice holds 8 registers, a q6_K
+// slice 11, a q8_0 slice 9; SWIGLU holds two matrices.
+constexpr int max_ps(int wt, int epi, int nt) {
+    return epi == EPI_SWIGLU ? (wt == W_Q4K ? (nt == 1 ? 3 : nt == 2 ? 2 : 1) : (nt == 1 ? 2 : 1))
+         : wt == W_Q4K ? (nt <= 2 ? 6 : nt == 3 ? 5 : 4)
+         : wt == W_Q6KP ? (nt <= 2 ? 4 : 3)
+         : (nt <= 3 ? 5 : 4);
+}
+
+// Passes per unit for a row of P passes: the whole row when it fits the cap,
+// else the unit size <= cap with the fewest idle passes (then the largest).
+inline int pick_ps(int P, int cap) {
+    if (P <= cap) return P;
+    int best = cap, waste = 1 << 30;
+    for (int ps = cap; ps >= 1; --ps) {
+        const int s = (P + ps - 1) / ps, w = s * ps - P;
+        if (w < waste) { waste = w; best = ps; }
+    }
+    return best;
+}
+
 size_t qmv_smem_bytes(int wtype, int k, int ntok);
-cudaError_t launch_qmv(int wt, int epi, const QmvArgs &a, int nt, int sm_count, cudaStream_t st);
+cudaError_t launch_qmv(int wt, int epi, QmvArgs a, int nt, int sm_count, cudaStream_t st);
 
 }  // namespace m27b

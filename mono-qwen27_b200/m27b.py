@@ -47,6 +47,7 @@ def lib():
     wvp = ctypes.POINTER(WeightView)
     sig = {
         "m27b_version": (cp, []),
+        "m27b_device_status": (b, [ctypes.POINTER(ctypes.c_int), i32, cp, sz]),
         "m27b_act_bytes": (sz, [u32, i32]),
         "m27b_act_type_for": (u32, [u32]),
         "m27b_act_quant": (b, [vp, i32, i32, i32, u32, vp, vp, cp, sz]),
@@ -69,6 +70,14 @@ def lib():
 
 def version():
     return lib().m27b_version().decode()
+
+
+def device_status(clear=True):
+    """The device status word (0 = every bounded kernel wait completed)."""
+    v = ctypes.c_int(0)
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(lib().m27b_device_status(ctypes.byref(v), 1 if clear else 0, err, ERR_CAP), err, "m27b_device_status")
+    return v.value
 
 
 def row_bytes(qtype, k):

@@ -310,3 +310,9 @@ def test_config3_ffn_block_full_size(torch, orc, m27b, n):
     m27b.qmv(Dn, aq, n, y)
     err = orc.rel_l2(host(y), want)
     assert err <= TOL, err
+
+
+def test_device_status_is_clean(torch, m27b):
+    """No bounded wait inside any kernel ran out during the runs above."""
+    torch.cuda.synchronize()
+    assert m27b.device_status(clear=True) == 0
