@@ -112,10 +112,12 @@ M27B_API bool m27b_act_quant_rmsnorm(const float *x, const float *w, float eps, 
 M27B_API size_t m27b_repacked_bytes(uint32_t ggml_type, uint32_t row_blocks, uint32_t row_count);
 
 /* Repack row_count GGUF rows of q6_K or q8_0 (row_blocks blocks each) from
- * `raw` into the planar layout at `out` (m27b_repacked_bytes bytes, 16-byte
- * aligned).  The view for the result is {out, ggml_type | M27B_LAYOUT_PLANAR,
- * row_blocks, row_count}.  q6_K rows become [ql | qh | scales | d, padded to
- * 16 B]; q8_0 rows become [qs | d, padded to 16 B]. */
+ * `raw` into the aligned layout at `out` (m27b_repacked_bytes bytes, 16-byte
+ * aligned); lossless.  The view for the result is {out, ggml_type |
+ * M27B_LAYOUT_PLANAR, row_blocks, row_count}.  A q6_K row becomes
+ * ceil(row_blocks/4) tiles of 848 bytes, each holding 4 blocks as
+ * ql[4][128] | qh[4][64] | scales[4][16] | d[4] (fp16 + 2 zero bytes), blocks
+ * past the row end zero; a q8_0 row becomes [qs | d, padded to 16 B]. */
 M27B_API bool m27b_repack(const void *raw, uint32_t ggml_type, uint32_t row_blocks, uint32_t row_count,
                  void *out, cudaStream_t stream, char *err, size_t err_cap);
 

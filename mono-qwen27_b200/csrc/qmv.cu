@@ -30,15 +30,44 @@
 // q6_K and q8_0 tensors are read in the planar layout written by m27b_repack
 // (repack.cu), because their GGUF blocks (210 B / 34 B) are only 2-byte
 // aligned; q4_K blocks (144 B) are read in place.
+#include <cudaTypedefs.h>
+
 #include "qmv_blk.cuh"
 #include "qmv_launch.cuh"
+#include "qmv_q6k_tile.cuh"
 
 namespace m27b {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows, int box_u32) {
+    auto enc = tensor_map_encoder();
+    if (!enc || (row_bytes & 15) != 0 || ((uintptr_t)w & 15) != 0) return false;
+    const cuuint64_t gdim[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)box_u32, 8};
+    const cuuint32_t estride[2] = {1, 1};
+    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(w), gdim, gstride, box, estride,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 // Dynamic shared memory bytes for the staged activations.
 size_t qmv_smem_bytes(int wtype, int k, int ntok) {
     if (wtype == M27B_TYPE_Q8_0) return (size_t)ntok * k + (size_t)ntok * (k / 32) * 4;
     if (wtype == M27B_TYPE_Q4_K) return blk_warps(k, ntok) > 0 ? blk_smem_bytes(k, ntok) : 0;  // qmv_blk.cuh
+    if (wtype == M27B_TYPE_Q6_K) return q6t_warps(k, ntok) > 0 ? q6t_smem_bytes(k, ntok) : 0;   // qmv_q6k_tile.cuh
     return (size_t)ntok * k + (size_t)ntok * (k / 256) * 32 + (size_t)ntok * (k / 256) * 4;
 }
 

@@ -1,38 +1,9 @@
 // qmv_q4k.cu — q4_K matvec instantiations: one super-block per lane
 // (qmv_blk.cuh), batch 1..4, store / SwiGLU / argmax epilogues.
-#include <cudaTypedefs.h>
-
 #include "qmv_blk.cuh"
 #include "qmv_launch.cuh"
 
 namespace m27b {
-
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-    }
-    return fn;
-}
-
-// Tensor map over q4_K rows viewed as [rows][row_bytes/4] uint32 with a box of
-// 8 rows x 144 uint32 (4 blocks): one TMA copy per (8-row group, pass).
-static bool encode_rows(CUtensorMap *tm, const void *w, size_t row_bytes, int rows) {
-    auto enc = tensor_map_encoder();
-    if (!enc) return false;
-    const cuuint64_t gdim[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)rows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {144, 8};
-    const cuuint32_t estride[2] = {1, 1};
-    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(w), gdim, gstride, box, estride,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 template <int NT, int EPI>
 static cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
@@ -67,9 +38,9 @@ static cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     const long warps = (groups + gpw - 1) / gpw;
     const long grid = (warps + nw - 1) / nw;
     CUtensorMap tm0, tm1;
-    if (!encode_rows(&tm0, a.w0, a.row_stride, a.rows)) return cudaErrorInvalidValue;
+    if (!encode_rows_u32(&tm0, a.w0, a.row_stride, a.rows, 144)) return cudaErrorInvalidValue;
     if (EPI == EPI_SWIGLU) {
-        if (!encode_rows(&tm1, a.w1, a.row_stride, a.rows)) return cudaErrorInvalidValue;
+        if (!encode_rows_u32(&tm1, a.w1, a.row_stride, a.rows, 144)) return cudaErrorInvalidValue;
     } else {
         tm1 = tm0;
     }

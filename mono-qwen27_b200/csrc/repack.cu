@@ -2,12 +2,14 @@
 // row dequantization (the embedding gather).
 //
 // GGUF q6_K blocks are 210 bytes and q8_0 blocks 34 bytes, so their fields
-// are only 2-byte aligned and cannot be streamed with 128-bit loads.  The
-// repack is a lossless permutation of each row into planes:
-//   q6_K: [ql rb*128 | qh rb*64 | scales rb*16 | d rb*2 | zero pad to 16]
-//   q8_0: [qs rb*32 | d rb*2 | zero pad to 16]
-// which adds at most 14 bytes per row (4208 vs 4200 bytes for K=5120 q6_K,
-// 0 bytes for q8_0 rows of 32k values).
+// are only 2-byte aligned and cannot be streamed with 128-bit loads or TMA.
+// The repack is a lossless rearrangement of each row:
+//   q6_K: ceil(rb/4) tiles of 848 bytes, tile t holding blocks 4t..4t+3 as
+//         ql[4][128] | qh[4][64] | scales[4][16] | d[4] (fp16 + 2 zero bytes);
+//         blocks past the end of the row are zero (4240 vs 4200 bytes for a
+//         K=5120 row, 14416 vs 14280 for K=17408);
+//   q8_0: [qs rb*32 | d rb*2 | zero pad to 16] (0 extra bytes for rows of
+//         32k values).
 //
 // Dequant follows ggml's dequantize_row_q4_K / q6_K / q8_0 (as restated in
 // debug/official_dequant.c:47-65 and src/mono27b_executor.cu:1026-1048,
@@ -20,28 +22,25 @@
 namespace m27b {
 
 size_t planar_row_bytes(int type, int rb) {
-    if (type == M27B_TYPE_Q6_K) return (size_t)rb * 208 + (((size_t)rb * 2 + 15) & ~(size_t)15);
+    if (type == M27B_TYPE_Q6_K) return (size_t)((rb + 3) / 4) * 848;
     if (type == M27B_TYPE_Q8_0) return (size_t)rb * 32 + (((size_t)rb * 2 + 15) & ~(size_t)15);
     return 0;
 }
 
-// grid (rb, rows), block 64: one block of one row per CTA.
+// grid (rb, rows), block 64: one block of one row per CTA (the output was
+// zeroed first, so padding blocks and pad bytes stay zero).
 __global__ void k_repack_q6K(const uint8_t *raw, uint8_t *out, int rb, size_t out_row) {
     const int b = blockIdx.x;
     const size_t r = blockIdx.y;
     const uint8_t *src = raw + (r * rb + b) * 210;
-    uint8_t *dst = out + r * out_row;
+    uint8_t *tile = out + r * out_row + (size_t)(b >> 2) * 848;
+    const int j = b & 3;
     for (int i = threadIdx.x; i < 210; i += blockDim.x) {
         const uint8_t v = src[i];
-        if (i < 128) dst[(size_t)b * 128 + i] = v;
-        else if (i < 192) dst[(size_t)rb * 128 + (size_t)b * 64 + (i - 128)] = v;
-        else if (i < 208) dst[(size_t)rb * 192 + (size_t)b * 16 + (i - 192)] = v;
-        else dst[(size_t)rb * 208 + (size_t)b * 2 + (i - 208)] = v;
-    }
-    // zero the pad of the d plane (last block of the row only)
-    if (b == rb - 1) {
-        const size_t pad0 = (size_t)rb * 210, pad1 = out_row;
-        for (size_t i = pad0 + threadIdx.x; i < pad1; i += blockDim.x) dst[i] = 0;
+        if (i < 128) tile[j * 128 + i] = v;
+        else if (i < 192) tile[512 + j * 64 + (i - 128)] = v;
+        else if (i < 208) tile[768 + j * 16 + (i - 192)] = v;
+        else tile[832 + j * 4 + (i - 208)] = v;
     }
 }
 
@@ -62,6 +61,10 @@ __global__ void k_repack_q80(const uint8_t *raw, uint8_t *out, int rb, size_t ou
 
 cudaError_t launch_repack(int type, const void *raw, int rb, int rows, void *out, cudaStream_t st) {
     const size_t orow = planar_row_bytes(type, rb);
+    if (type == M27B_TYPE_Q6_K) {
+        cudaError_t e = cudaMemsetAsync(out, 0, orow * (size_t)rows, st);
+        if (e != cudaSuccess) return e;
+    }
     // grid.y is limited to 65535: walk the rows in slices.
     for (int r0 = 0; r0 < rows; r0 += 65535) {
         const int n = rows - r0 < 65535 ? rows - r0 : 65535;
@@ -113,10 +116,12 @@ M27B_DI float dq_q6K(const uint8_t *row, int rb, int e, bool planar) {
     int8_t sc;
     uint16_t dbits;
     if (planar) {
-        ql = row + (size_t)b * 128 + 64 * half;
-        qh = row + (size_t)rb * 128 + (size_t)b * 64 + 32 * half;
-        sc = (int8_t)row[(size_t)rb * 192 + (size_t)b * 16 + (i >> 4)];
-        dbits = (uint16_t)(row[(size_t)rb * 208 + 2 * b] | (row[(size_t)rb * 208 + 2 * b + 1] << 8));
+        const uint8_t *tile = row + (size_t)(b >> 2) * 848;
+        const int j = b & 3;
+        ql = tile + j * 128 + 64 * half;
+        qh = tile + 512 + j * 64 + 32 * half;
+        sc = (int8_t)tile[768 + j * 16 + (i >> 4)];
+        dbits = (uint16_t)(tile[832 + j * 4] | (tile[832 + j * 4 + 1] << 8));
     } else {
         const uint8_t *blk = row + (size_t)b * 210;
         ql = blk + 64 * half;

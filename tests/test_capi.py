@@ -50,9 +50,10 @@ def test_size_helpers(m27b):
     assert L.m27b_act_type_for(m27b.Q6_K | m27b.LAYOUT_PLANAR) == m27b.Q8_K
     assert L.m27b_act_type_for(m27b.Q8_0) == m27b.Q8_0
     assert L.m27b_act_type_for(1) == 0
-    # planar q6_K rows: 208 B per block + d plane padded to 16 B
-    assert L.m27b_repacked_bytes(m27b.Q6_K, 20, 3) == 3 * (20 * 208 + 48)
-    assert L.m27b_repacked_bytes(m27b.Q6_K, 68, 1) == 68 * 208 + 144
+    # repacked q6_K rows: 4-block tiles of 848 bytes; q8_0 rows: codes then the d plane padded to 16 B
+    assert L.m27b_repacked_bytes(m27b.Q6_K, 20, 3) == 3 * 5 * 848  # 4-block tiles of 848 bytes
+    assert L.m27b_repacked_bytes(m27b.Q6_K, 68, 1) == 17 * 848
+    assert L.m27b_repacked_bytes(m27b.Q6_K, 17, 1) == 5 * 848  # padded to whole tiles
     assert L.m27b_repacked_bytes(m27b.Q8_0, 32, 5) == 5 * (32 * 32 + 64)
     assert L.m27b_repacked_bytes(m27b.Q4_K, 20, 1) == 0
 
