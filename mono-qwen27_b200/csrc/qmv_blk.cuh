@@ -16,7 +16,8 @@
 // the weight rows, no multicast) that completes on the stage's mbarrier.
 // Rows past the end and blocks past the end of a row read as zeros (the
 // tensor map's bounds), so ragged tails need no special case; the copies of item i+1 are in flight while item i is
-// multiplied (three stages per warp, 16 warps in one CTA per SM).  Every mbarrier wait is bounded by the
+// multiplied (two stages per warp; the block is copied to registers and the
+// stage handed back before the math).  Every mbarrier wait is bounded by the
 // global timer (M27B_WAIT_NS); a wait that runs out records an error in the
 // library's device status word and the kernel drains its own copies before
 // it returns.  Lanes read their block from the stage: the 576-byte slot
@@ -47,14 +48,19 @@ constexpr size_t BLK_WARP_BYTES = (size_t)BLK_STAGES * BLK_ITEM + (size_t)BLK_ST
 
 // Warps per CTA: as many as the shared memory left after the staged
 // activations holds stages for (at most BLK_WARPS); 0 if not even one fits.
+inline size_t blk_part_bytes(int nt) { return (size_t)BLK_WARPS * 8 * 2 * nt * 4; }
+
 inline int blk_warps(int k, int nt) {
-    const size_t x = blk_x_bytes(k, nt);
+    const size_t x = blk_x_bytes(k, nt) + blk_part_bytes(nt);
     if (x + 16 >= BLK_SMEM_MAX) return 0;
     const size_t w = (BLK_SMEM_MAX - x - 16) / BLK_WARP_BYTES;
     return (int)(w < (size_t)BLK_WARPS ? w : (size_t)BLK_WARPS);
 }
 
-inline size_t blk_smem_bytes(int k, int nt) { return (size_t)blk_warps(k, nt) * BLK_WARP_BYTES + blk_x_bytes(k, nt) + 16; }
+inline size_t blk_smem_for(int nwarps, int k, int nt) {
+    return (size_t)nwarps * BLK_WARP_BYTES + blk_x_bytes(k, nt) + blk_part_bytes(nt) + 16;
+}
+inline size_t blk_smem_bytes(int k, int nt) { return blk_smem_for(blk_warps(k, nt), k, nt); }
 
 // ---- mbarrier + bulk-copy helpers (sm_90+ PTX; no cluster multicast) ----
 constexpr unsigned long long M27B_WAIT_NS = 2000000000ull;  // 2 s bound on any wait
@@ -210,24 +216,33 @@ M27B_DI void q4k_block_mac(const uint4 (&v)[9], const uint8_t *xrec0, const floa
 // (SWIGLU streams the gate blocks, then the up blocks, of the same pass).
 template <int NT, int EPI>
 __global__ void __launch_bounds__(BLK_THREADS, 2)
-    k_qmv_q4k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1) {
+    k_qmv_q4k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
+                  int split) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int slot = lane >> 2, qd = lane & 3;
     const int nwarps = blockDim.x >> 5;
-    const int wg = blockIdx.x * nwarps + warp;
-    const int W = gridDim.x * nwarps;
     const int ngroups = (a.rows + 7) >> 3;
     const int P = (a.rb + 3) >> 2;  // passes per row
     const int nb = a.rb;
-    const int my_groups = wg < ngroups ? (ngroups - 1 - wg) / W + 1 : 0;
 
-    // [stages of all warps | activation records | block scales | barriers]
+    // split == 1: warp wg owns groups wg, wg+W, ...; all passes of each.
+    // split == nwarps: the CTA owns groups blockIdx.x, +gridDim.x, ...; warp
+    // w takes passes [w*P/split, (w+1)*P/split) of each and the partial sums
+    // are combined in warp order (deterministic).
+    const int wg = split == 1 ? blockIdx.x * nwarps + warp : blockIdx.x;
+    const int W = split == 1 ? gridDim.x * nwarps : gridDim.x;
+    const int my_groups = wg < ngroups ? (ngroups - 1 - wg) / W + 1 : 0;
+    const int p_lo = split == 1 ? 0 : (warp * P) / split;
+    const int my_passes = (split == 1 ? P : ((warp + 1) * P) / split) - p_lo;
+
+    // [stages of all warps | activation records | block scales | partials | barriers]
     uint8_t *stage0 = smem + (size_t)warp * BLK_STAGES * BLK_ITEM;
     uint8_t *xrec = smem + (size_t)nwarps * BLK_STAGES * BLK_ITEM;
     float *xd = (float *)(xrec + (size_t)NT * nb * BLK_XREC);
-    uint64_t *bar = (uint64_t *)(((uintptr_t)(xd + NT * nb) + 15) & ~(uintptr_t)15) + (size_t)warp * BLK_STAGES;
+    float *part = (float *)(((uintptr_t)(xd + NT * nb) + 15) & ~(uintptr_t)15);  // [BLK_WARPS][8][2][NT]
+    uint64_t *bar = (uint64_t *)(part + (size_t)BLK_WARPS * 8 * 2 * NT) + (size_t)warp * BLK_STAGES;
     if (lane == 0) {
         for (int s = 0; s < BLK_STAGES; ++s) mbar_init(&bar[s], 1);
         fence_mbar_init();
@@ -237,23 +252,24 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
     // copy cursor: lane 0 issues one tensor copy per item; all lanes track it
     int lg = 0, lp = 0, lm = 0, li = 0, ls = 0;  // ls = li % BLK_STAGES
     auto issue_item = [&]() {
-        if (lg < my_groups) {
+        if (lg < my_groups && my_passes > 0) {
             if (lane == 0) {
                 uint64_t *b = &bar[ls];
                 fence_proxy_async();  // the stage's previous reads precede the async writes
                 mbar_arrive_expect_tx(b, BLK_ITEM);
-                tma_load_2d(stage0 + ls * BLK_ITEM, (NM == 2 && lm == 1) ? &tm1 : &tm0, lp * 144, (wg + lg * W) * 8, b);
+                tma_load_2d(stage0 + ls * BLK_ITEM, (NM == 2 && lm == 1) ? &tm1 : &tm0, (p_lo + lp) * 144,
+                            (wg + lg * W) * 8, b);
             }
             ++li;
             if (++ls == BLK_STAGES) ls = 0;
             if (++lm == NM) {
                 lm = 0;
-                if (++lp == P) { lp = 0; ++lg; }
+                if (++lp == my_passes) { lp = 0; ++lg; }
             }
         }
     };
 
-    // all stages' copies go out before the activations are staged
+    // the stages' copies go out before the activations are staged
     for (int i = 0; i < BLK_STAGES; ++i) issue_item();
     stage_x_blk<NT>(a, xrec, xd);
     __syncthreads();
@@ -267,35 +283,36 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
 #pragma unroll
     for (int t = 0; t < NT; ++t) best[t] = 0ull;
 
-    int cg = 0, cp = 0, cm = 0, ci = 0, cs = 0;  // compute cursor; cs = ci % BLK_STAGES
-    uint32_t cph = 0;                             // phase parity of stage cs
+    int ci = 0, cs = 0;  // items consumed; cs = ci % BLK_STAGES
+    uint32_t cph = 0;     // phase parity of stage cs
     bool ok = true;
-    while (cg < my_groups) {
-        // every lane waits (bounded); the warp leaves together if any lane gave up
-        const bool landed = mbar_wait_bounded(&bar[cs], cph, a.status, 1);
-        if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
-        const int row = (wg + cg * W) * 8 + slot;
-        const int b = 4 * cp + qd;
-        // take this lane's block into registers, then hand the stage back to
-        // the copy engine: item ci+2 streams in while this one is multiplied
-        uint4 v[9];
-        const uint8_t *blk = stage0 + cs * BLK_ITEM + slot * 576 + qd * 144;
+    int g = 0;
+    for (; g < my_groups; ++g) {
+        const int row = (wg + g * W) * 8 + slot;
+        for (int pt = 0; pt < my_passes; ++pt) {
+            const int b = 4 * (p_lo + pt) + qd;
 #pragma unroll
-        for (int j = 0; j < 9; ++j) v[j] = *(const uint4 *)(blk + 16 * j);
-        __syncwarp();
-        issue_item();
-        if (row < a.rows && b < nb) {
-            if (NM == 1 || cm == 0) q4k_block_mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[0]);
-            else q4k_block_mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[NM - 1]);
+            for (int m = 0; m < NM; ++m) {
+                // every lane waits (bounded); the warp leaves together if any lane gave up
+                const bool landed = mbar_wait_bounded(&bar[cs], cph, a.status, 1);
+                if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
+                // take this lane's block into registers, then hand the stage back
+                // to the copy engine: a later item streams in during the math
+                uint4 v[9];
+                const uint8_t *blk = stage0 + cs * BLK_ITEM + slot * 576 + qd * 144;
+#pragma unroll
+                for (int j = 0; j < 9; ++j) v[j] = *(const uint4 *)(blk + 16 * j);
+                __syncwarp();
+                issue_item();
+                ++ci;
+                if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
+                if (row < a.rows && b < nb) q4k_block_mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[m]);
+            }
+            if (!ok) break;
         }
-        ++ci;
-        if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
-        if (++cm < NM) continue;
-        cm = 0;
-        if (++cp < P) continue;
-        cp = 0;
-        ++cg;
-        // row done: reduce the four lanes of each row (lane slot*4 keeps it)
+        if (!ok) break;
+
+        // group done: reduce the four lanes of each row (lane slot*4 keeps it)
 #pragma unroll
         for (int m = 0; m < NM; ++m)
 #pragma unroll
@@ -305,7 +322,28 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
                 s += __shfl_xor_sync(0xffffffffu, s, 2);
                 acc[m][t] = s;
             }
-        if (qd == 0 && row < a.rows) {
+        if (split > 1) {
+            // combine the warps' partial sums in warp order
+            if (qd == 0) {
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) part[(((size_t)warp * 8 + slot) * 2 + m) * NT + t] = acc[m][t];
+            }
+            __syncthreads();
+            if (warp == 0 && qd == 0) {
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        float v = 0.0f;
+                        for (int w = 0; w < split; ++w) v += part[(((size_t)w * 8 + slot) * 2 + m) * NT + t];
+                        acc[m][t] = v;
+                    }
+            }
+            __syncthreads();
+        }
+        if ((split == 1 || warp == 0) && qd == 0 && row < a.rows) {
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 const size_t o = (size_t)t * a.ldy + row;
@@ -333,6 +371,12 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
             mbar_wait_bounded(&bar[cs], cph, a.status, 2);
             if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
         }
+        // keep the CTA-wide barriers of the cooperative split balanced
+        if (split > 1)
+            for (; g < my_groups; ++g) {
+                __syncthreads();
+                __syncthreads();
+            }
         return;
     }
 

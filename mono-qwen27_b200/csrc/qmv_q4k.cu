@@ -15,28 +15,36 @@ static cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     static size_t opted[64] = {0};
-    static size_t occ_smem[64] = {0};
-    static int occ_val[64] = {0};
     if (smem > 48 * 1024 && (dev >= 64 || smem > opted[dev])) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         if (dev < 64) opted[dev] = smem;
     }
-    int occ = 0;
-    if (dev < 64 && occ_val[dev] > 0 && occ_smem[dev] == smem) {
-        occ = occ_val[dev];
-    } else {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, nw * 32, smem);
-        if (e != cudaSuccess) return e;
-        if (dev < 64) { occ_smem[dev] = smem; occ_val[dev] = occ; }
-    }
-    if (occ < 1) return cudaErrorInvalidConfiguration;
-    // balanced persistent grid over groups of 8 rows
+    // two resident CTAs per SM by construction (shared memory <= 112 KB each)
     const long groups = (a.rows + 7) / 8;
-    const long max_warps = (long)sm_count * occ * nw;
-    const long gpw = (groups + max_warps - 1) / max_warps;
-    const long warps = (groups + gpw - 1) / gpw;
-    const long grid = (warps + nw - 1) / nw;
+    const int P = (a.rb + 3) / 4;
+    const long slots = (long)sm_count * 2;
+    int split, nthreads;
+    long grid;
+    size_t smem_launch;
+    if (2 * groups >= slots * nw || P < 2) {
+        // every warp streams whole row groups: the fewest groups per warp
+        // that the resident warps allow, then just enough warps
+        split = 1;
+        const long max_warps = slots * nw;
+        const long gpw = (groups + max_warps - 1) / max_warps;
+        const long warps = (groups + gpw - 1) / gpw;
+        grid = (warps + nw - 1) / nw;
+        nthreads = nw * 32;
+        smem_launch = smem;
+    } else {
+        // few row groups: the warps of a CTA split each group's passes
+        split = P < nw ? P : nw;
+        const long gpc = (groups + slots - 1) / slots;
+        grid = (groups + gpc - 1) / gpc;
+        nthreads = split * 32;
+        smem_launch = blk_smem_for(split, a.k, NT);
+    }
     CUtensorMap tm0, tm1;
     if (!encode_rows_u32(&tm0, a.w0, a.row_stride, a.rows, 144)) return cudaErrorInvalidValue;
     if (EPI == EPI_SWIGLU) {
@@ -44,7 +52,7 @@ static cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     } else {
         tm1 = tm0;
     }
-    kern<<<(unsigned)grid, nw * 32, smem, st>>>(a, tm0, tm1);
+    kern<<<(unsigned)grid, nthreads, smem_launch, st>>>(a, tm0, tm1, split);
     return cudaGetLastError();
 }
 

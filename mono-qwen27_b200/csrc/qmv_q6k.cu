@@ -31,7 +31,7 @@ static cudaError_t run_q6t(const QmvArgs &a, int sm_count, cudaStream_t st) {
     int split, nthreads;
     long grid;
     size_t smem;
-    if (groups >= slots * nw || P < 2) {
+    if (2 * groups >= slots * nw || P < 2) {
         // every warp streams whole row groups
         split = 1;
         const long max_warps = slots * nw;
