@@ -54,6 +54,8 @@ M27B_DI float act_value(const ActArgs &a, const float *xr, const float *gr, int 
 // super-block 8c + w of token blockIdx.y.
 template <int MODE>
 __global__ void __launch_bounds__(256) k_act_quant_q8K(ActArgs a) {
+    pdl_trigger();
+    pdl_wait();  // x is produced by the previous kernel
     const int t = blockIdx.y;
     const float *xr = a.x + (size_t)t * a.ldx;
     const float *gr = a.gate ? a.gate + (size_t)t * a.ldx : nullptr;
@@ -108,6 +110,8 @@ __global__ void __launch_bounds__(256) k_act_quant_q8K(ActArgs a) {
 // block 8c + w (32 values, one per lane).
 template <int MODE>
 __global__ void __launch_bounds__(256) k_act_quant_q80(ActArgs a) {
+    pdl_trigger();
+    pdl_wait();  // x is produced by the previous kernel
     const int t = blockIdx.y;
     const float *xr = a.x + (size_t)t * a.ldx;
     const float *gr = a.gate ? a.gate + (size_t)t * a.ldx : nullptr;
@@ -131,15 +135,13 @@ cudaError_t launch_act_quant(int act_type, int mode, const ActArgs &a, int n_tok
     const int nb = act_type == M27B_TYPE_Q8_K ? a.k / 256 : a.k / 32;
     dim3 grid((nb + 7) / 8, n_tok);
     if (act_type == M27B_TYPE_Q8_K) {
-        if (mode == ACT_PLAIN) k_act_quant_q8K<ACT_PLAIN><<<grid, 256, 0, st>>>(a);
-        else if (mode == ACT_GATED) k_act_quant_q8K<ACT_GATED><<<grid, 256, 0, st>>>(a);
-        else k_act_quant_q8K<ACT_RMSNORM><<<grid, 256, 0, st>>>(a);
-    } else {
-        if (mode == ACT_PLAIN) k_act_quant_q80<ACT_PLAIN><<<grid, 256, 0, st>>>(a);
-        else if (mode == ACT_GATED) k_act_quant_q80<ACT_GATED><<<grid, 256, 0, st>>>(a);
-        else k_act_quant_q80<ACT_RMSNORM><<<grid, 256, 0, st>>>(a);
+        if (mode == ACT_PLAIN) return launch_pdl(k_act_quant_q8K<ACT_PLAIN>, grid, dim3(256), 0, st, a);
+        if (mode == ACT_GATED) return launch_pdl(k_act_quant_q8K<ACT_GATED>, grid, dim3(256), 0, st, a);
+        return launch_pdl(k_act_quant_q8K<ACT_RMSNORM>, grid, dim3(256), 0, st, a);
     }
-    return cudaGetLastError();
+    if (mode == ACT_PLAIN) return launch_pdl(k_act_quant_q80<ACT_PLAIN>, grid, dim3(256), 0, st, a);
+    if (mode == ACT_GATED) return launch_pdl(k_act_quant_q80<ACT_GATED>, grid, dim3(256), 0, st, a);
+    return launch_pdl(k_act_quant_q80<ACT_RMSNORM>, grid, dim3(256), 0, st, a);
 }
 
 }  // namespace m27b

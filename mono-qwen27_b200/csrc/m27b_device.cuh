@@ -64,4 +64,13 @@ M27B_DI unsigned long long argmax_key(float v, uint32_t idx) {
     return ((unsigned long long)float_order_key(v) << 32) | (unsigned long long)(0xffffffffu - idx);
 }
 
+// Programmatic dependent launch (sm_90+).  A kernel launched with the
+// programmatic-stream-serialization attribute may start while the previous
+// kernel in the stream is still running, once that kernel has executed
+// pdl_trigger() in every CTA (or exited).  pdl_wait() blocks until the
+// previous kernel has completed and its memory writes are visible: every read
+// of data a previous kernel produced, and every global write, comes after it.
+M27B_DI void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+M27B_DI void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace m27b

@@ -271,7 +271,11 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
 
     // the stages' copies go out before the activations are staged
     for (int i = 0; i < BLK_STAGES; ++i) issue_item();
+    // the weights are not produced by the previous kernel: their copies are
+    // already in flight; the activations (and every global write) wait for it
+    pdl_wait();
     stage_x_blk<NT>(a, xrec, xd);
+    pdl_trigger();
     __syncthreads();
 
     float acc[NM][NT];

@@ -319,9 +319,12 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) k_qmv(const QmvArgs a) {
         }
     };
 
-    // First loads go out before the activations are staged.
+    // First loads go out before the activations are staged (weights are not
+    // produced by the previous kernel; activations and writes wait for it).
     load_unit(bufA);
+    pdl_wait();
     const XStage xs = stage_x<WT, NT>(a, smem);
+    pdl_trigger();
     __syncthreads();
 
     float acc[NM][NT];

@@ -4,6 +4,7 @@
 
 #include <cuda.h>
 
+#include "m27b_launch.cuh"
 #include "qmv_kernels.cuh"
 
 namespace m27b {
@@ -46,8 +47,7 @@ cudaError_t run_qmv(const QmvArgs &a, int sm_count, cudaStream_t st) {
     const long rpw = (a.rows + max_warps - 1) / max_warps;
     const long warps = (a.rows + rpw - 1) / rpw;
     const long grid = (warps + QMV_WARPS - 1) / QMV_WARPS;
-    kern<<<(unsigned)grid, QMV_THREADS, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(QMV_THREADS), smem, st, a);
 }
 
 template <int WT, int NT, int EPI, int PS>

@@ -1,6 +1,7 @@
 // qmv_q4k.cu — q4_K matvec instantiations: one super-block per lane
 // (qmv_blk.cuh), batch 1..4, store / SwiGLU / argmax epilogues.
 #include "qmv_blk.cuh"
+#include "m27b_launch.cuh"
 #include "qmv_launch.cuh"
 
 namespace m27b {
@@ -52,8 +53,7 @@ static cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     } else {
         tm1 = tm0;
     }
-    kern<<<(unsigned)grid, nthreads, smem_launch, st>>>(a, tm0, tm1, split);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(nthreads), smem_launch, st, a, tm0, tm1, split);
 }
 
 template <int EPI>

@@ -1,5 +1,6 @@
 // qmv_q6k.cu — q6_K matvec instantiations over the tiled layout
 // (qmv_q6k_tile.cuh), batch 1..4, store / SwiGLU / argmax epilogues.
+#include "m27b_launch.cuh"
 #include "qmv_launch.cuh"
 #include "qmv_q6k_tile.cuh"
 
@@ -55,8 +56,7 @@ static cudaError_t run_q6t(const QmvArgs &a, int sm_count, cudaStream_t st) {
     } else {
         tm1 = tm0;
     }
-    kern<<<(unsigned)grid, nthreads, smem, st>>>(a, tm0, tm1, split);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(nthreads), smem, st, a, tm0, tm1, split);
 }
 
 template <int EPI>

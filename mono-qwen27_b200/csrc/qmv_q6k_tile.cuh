@@ -138,7 +138,11 @@ __global__ void __launch_bounds__(Q6T_WARPS * 32, 2)
     };
 
     for (int i = 0; i < Q6T_STAGES; ++i) issue_item();
+    // the weights are not produced by the previous kernel: their copies are
+    // already in flight; the activations (and every global write) wait for it
+    pdl_wait();
     stage_x_q6t<NT>(a, xrec, xd);
+    pdl_trigger();
     __syncthreads();
 
     float acc[NM][8][NT];
