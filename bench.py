@@ -1,26 +1,31 @@
 #!/usr/bin/env python
-"""Benchmark: q4_K batch-1 matvec HBM GB/s on B200 (BASELINE cfg0 shape).
+"""Benchmark: quantized weight-streaming matvec on B200, HBM GB/s.
 
-One step = one pass of the quantized matvec path over one batch: for each of
-C=6 distinct q4_K weight matrices of 17408 x 5120 (the config-0 shape; 6 x
-50.1 MB = 301 MB rotate so the working set exceeds the 126 MB L2), quantize a
+Default workload (the driver's line) — cfg0, the q4_K matvec BASELINE's
+metric is quoted on: one step = one pass of the matvec path over one batch:
+for each of C=6 distinct q4_K weight matrices of 17408 x 5120 (6 x 50.1 MB =
+301 MB rotate, so the working set exceeds the 126 MB L2), quantize a
 5120-long fp32 activation to q8_K and multiply.  Steps are replayed through
 CUDA graphs of the C-ABI calls (m27b_act_quant + m27b_qmv), timed with CUDA
 events on the launching stream, bracketed by a barrier and a synchronize.
 
-value  = algorithmic bytes of all ranks' steps / max-over-ranks time, where a
-         matvec's algorithmic bytes are W 50,135,040 + x 20,480 + y 69,632.
-e2e    = the same through the C ABI with host buffers: per matvec a pinned
-         host->device copy of x and a device->host copy of y inside the
-         timed region.
-roofline = the matvec kernel alone (graphs of m27b_qmv over the rotating
-         weights), bytes per launch / mean launch time, against the measured
-         HBM copy bandwidth in MEASURED_PEAKS.json.
-cpu_baseline = the CPU oracle (restatement of ggml's vec_dot_q4_K_q8_K,
-         OpenMP over rows) timed on this host's cores on a bounded sample.
+  value    algorithmic bytes of all ranks' steps / max-over-ranks time; a
+           matvec's algorithmic bytes are W 50,135,040 + x 20,480 + y 69,632.
+  e2e      the same through the C ABI with host buffers: per matvec a pinned
+           host->device copy of x and a device->host copy of y are inside the
+           timed region.
+  roofline the matvec kernel alone (graphs of m27b_qmv over the rotating
+           weights): bytes per launch / mean launch time, against the
+           measured HBM copy bandwidth in MEASURED_PEAKS.json.
+  cpu_baseline  the CPU oracle (restatement of ggml's vec_dot_q4_K_q8_K,
+           OpenMP over rows) on this host's cores, a bounded sample.
 
---impl reference times that CPU path (the reference ships no CPU path of its
-own and its ggml dependency is absent) on the same metric.
+Other workloads (--workload, for profiling and the design notes; not the
+driver's line): cfg1 = q6_K lm_head 248320 x 5120 with fused argmax; cfg3 =
+the FFN block down(silu(gate.x) * up.x) with RMSNormed input.
+
+--impl reference times the ggml-semantics CPU path on the same metric (the
+reference has no CPU path of its own and its ggml dependency is absent).
 
 Multi-GPU (torchrun): each rank runs its own replica (the matvec shards by
 matrix with no exchange), scaling "weak", value summed over ranks.
@@ -40,31 +45,30 @@ for _p in (ROOT, PKG, os.path.join(ROOT, "tests")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-ROWS, K = 17408, 5120
-Q4_K = 12
-W_BYTES = ROWS * (K // 256) * 144          # 50,135,040
-X_BYTES = K * 4                            # fp32 activation in
-Y_BYTES = ROWS * 4                         # fp32 output
-MV_BYTES = W_BYTES + X_BYTES + Y_BYTES     # 50,225,152 algorithmic bytes per matvec
-COPIES = 6
+Q8_0, Q4_K, Q6_K, Q8_K = 8, 12, 14, 15
+BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34)}
 GRAPH_STEPS = 16
-METRIC = "q4_K matvec HBM GB/s"
+
+
+def wbytes(qt, rows, k):
+    be, bb = BLOCK[qt]
+    return rows * (k // be) * bb
 
 
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=40000)
+    p.add_argument("--steps", type=int, default=None)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg3"], default="cfg0")
+    p.add_argument("--rows", type=int, default=None, help="override the row count (smaller profiling cases)")
+    p.add_argument("--ntok", type=int, default=1, help="tokens per step (cfg3)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    return p.parse_args()
-
-
-def random_q4K(seed):
-    import numpy as np
-    from _data import random_valid_blocks
-    return random_valid_blocks(Q4_K, ROWS, K, seed)
+    a = p.parse_args()
+    if a.steps is None:
+        a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg3": 8000}[a.workload]
+    return a
 
 
 def measured_peak():
@@ -76,9 +80,9 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def ncu_traffic_per_launch():
-    """DRAM bytes per launch of the q4_K matvec from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "qmv_q4K_cfg0.md")
+def ncu_traffic_per_launch(name):
+    """DRAM bytes per launch of the named kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", open(path).read())
         return int(m.group(1)) if m else None
@@ -140,58 +144,201 @@ class ClockSampler:
         return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_oracle_gbs(w_host, seconds, nthreads=0, rows=None):
-    """GB/s of the CPU oracle's q4_K.q8_K matvec on (a row sample of) w_host."""
-    import numpy as np
+# --------------------------------------------------------------------------
+# workloads
+
+
+class Workload:
+    """A step made of C-ABI calls; bytes are the algorithmic bytes per step."""
+
+    def __init__(self, args, dev, rank):
+        import numpy as np
+        import torch
+        import m27b
+        from _data import random_valid_blocks
+        self.m27b, self.torch, self.dev = m27b, torch, dev
+        gen = np.random.default_rng(7 + rank)
+        w = args.workload
+        self.name = w
+        if w == "cfg0":
+            rows, k, copies = args.rows or 17408, 5120, 6
+            self.host_w0 = random_valid_blocks(Q4_K, rows, k, 1000 * rank)
+            self.W = [m27b.QWeight(self.host_w0 if c == 0 else random_valid_blocks(Q4_K, rows, k, 1000 * rank + c),
+                                   Q4_K, k, rows) for c in range(copies)]
+            self.x = [torch.from_numpy(gen.standard_normal((1, k)).astype(np.float32)).to(dev) for _ in range(copies)]
+            self.xq = [torch.empty(m27b.act_bytes(Q8_K, k), dtype=torch.uint8, device=dev) for _ in range(copies)]
+            self.y = [torch.empty((1, rows), dtype=torch.float32, device=dev) for _ in range(copies)]
+            self.mv_bytes = wbytes(Q4_K, rows, k) + k * 4 + rows * 4
+            self.step_bytes = copies * self.mv_bytes
+            self.metric = "q4_K matvec HBM GB/s"
+            self.config = {"workload": f"cfg0: q4_K matvec {rows}x{k}, batch 1, q8_K activations", "rows": rows, "k": k,
+                           "matvecs_per_step": copies, "bytes_per_matvec": self.mv_bytes,
+                           "l2": f"inputs larger than L2: {copies} rotating weight matrices "
+                                 f"({copies * wbytes(Q4_K, rows, k) / 1e6:.0f} MB)"}
+            self.kernel = "k_qmv_q4k_blk<1,STORE>"
+            self.profile = "qmv_q4K_cfg0.md"
+            self.launches_per_step = 2 * copies
+            self.copies, self.rows, self.k = copies, rows, k
+            self.h2d = copies * k * 4
+            self.d2h = copies * rows * 4
+        elif w == "cfg1":
+            rows, k = args.rows or 248320, 5120
+            self.W = [m27b.QWeight(random_valid_blocks(Q6_K, rows, k, 2 + 1000 * rank), Q6_K, k, rows)]
+            self.x = [torch.from_numpy(gen.standard_normal((1, k)).astype(np.float32)).to(dev)]
+            self.xq = [torch.empty(m27b.act_bytes(Q8_K, k), dtype=torch.uint8, device=dev)]
+            self.y = [torch.empty((1, rows), dtype=torch.float32, device=dev)]
+            self.best = torch.empty(1, dtype=torch.int64, device=dev)
+            self.mv_bytes = wbytes(Q6_K, rows, k) + k * 4 + rows * 4
+            self.step_bytes = self.mv_bytes
+            self.metric = "q6_K lm_head matvec+argmax HBM GB/s"
+            self.config = {"workload": f"cfg1: q6_K lm_head {rows}x{k} with fused argmax, batch 1", "rows": rows, "k": k,
+                           "l2": f"inputs larger than L2: {wbytes(Q6_K, rows, k) / 1e6:.0f} MB of weights"}
+            self.kernel = "k_qmv_q6k_tile<1,ARGMAX>"
+            self.profile = "qmv_q6K_lm_head.md"
+            self.launches_per_step = 2
+            self.copies, self.rows, self.k = 1, rows, k
+            self.h2d, self.d2h = k * 4, rows * 4 + 8
+        else:  # cfg3
+            H, F, n = 5120, args.rows or 17408, args.ntok
+            self.sets = []
+            for c in range(2):
+                G = m27b.QWeight(random_valid_blocks(Q4_K, F, H, 10 + 3 * c + 1000 * rank), Q4_K, H, F)
+                U = m27b.QWeight(random_valid_blocks(Q4_K, F, H, 11 + 3 * c + 1000 * rank), Q4_K, H, F)
+                D = m27b.QWeight(random_valid_blocks(Q6_K, H, F, 12 + 3 * c + 1000 * rank), Q6_K, F, H)
+                self.sets.append((G, U, D))
+            self.h = [torch.from_numpy(gen.standard_normal((n, H)).astype(np.float32)).to(dev) for _ in range(2)]
+            self.hq = torch.empty(n * m27b.act_bytes(Q8_K, H), dtype=torch.uint8, device=dev)
+            self.a = torch.empty((n, F), dtype=torch.float32, device=dev)
+            self.aq = torch.empty(n * m27b.act_bytes(Q8_K, F), dtype=torch.uint8, device=dev)
+            self.out = [torch.empty((n, H), dtype=torch.float32, device=dev) for _ in range(2)]
+            self.n, self.H, self.F = n, H, F
+            self.mv_bytes = 2 * wbytes(Q4_K, F, H) + wbytes(Q6_K, H, F) + n * (H * 4 * 2 + F * 4 * 2)
+            self.step_bytes = 2 * self.mv_bytes
+            self.metric = "q4_k_m FFN block HBM GB/s"
+            self.config = {"workload": f"cfg3: FFN block gate/up {F}x{H} q4_K, down {H}x{F} q6_K, {n} token(s)",
+                           "hidden": H, "ffn": F, "ntok": n, "l2": "inputs larger than L2: 2 rotating FFN weight sets "
+                           f"({2 * (2 * wbytes(Q4_K, F, H) + wbytes(Q6_K, H, F)) / 1e6:.0f} MB)"}
+            self.kernel = "k_qmv_q4k_blk<n,SWIGLU> + k_qmv_q6k_tile<n,STORE>"
+            self.profile = "ffn_block_cfg3.md"
+            self.launches_per_step = 8
+            self.copies = 2
+            self.hh = [x.cpu().pin_memory() for x in self.h]
+            self.oh = [torch.empty((n, H), dtype=torch.float32).pin_memory() for _ in range(2)]
+            self.h2d, self.d2h = 2 * n * H * 4, 2 * n * H * 4
+        if w in ("cfg0", "cfg1"):
+            self.xh = [x.cpu().pin_memory() for x in self.x]
+            self.yh = [torch.empty_like(y, device="cpu").pin_memory() for y in self.y]
+
+    def _mv(self, c):
+        m = self.m27b
+        if self.name == "cfg1":
+            m.qmv_argmax(self.W[c], self.xq[c], 1, self.best, logits=self.y[c])
+        else:
+            m.qmv(self.W[c], self.xq[c], 1, self.y[c])
+
+    def step(self):
+        m = self.m27b
+        if self.name == "cfg3":
+            for c in range(2):
+                self._ffn(c)
+            return
+        for c in range(self.copies):
+            m.act_quant(self.x[c], Q8_K, out=self.xq[c])
+            self._mv(c)
+
+    def _ffn(self, c):
+        m = self.m27b
+        G, U, D = self.sets[c]
+        m.act_quant(self.h[c], Q8_K, out=self.hq, eps=1e-6)
+        m.qmv_swiglu(G, U, self.hq, self.n, self.a)
+        m.act_quant(self.a, Q8_K, out=self.aq)
+        m.qmv(D, self.aq, self.n, self.out[c])
+
+    def kernel_only(self):
+        if self.name == "cfg3":
+            m = self.m27b
+            for c in range(2):
+                G, U, D = self.sets[c]
+                m.qmv_swiglu(G, U, self.hq, self.n, self.a)
+                m.qmv(D, self.aq, self.n, self.out[c])
+            return
+        for c in range(self.copies):
+            self._mv(c)
+
+    def step_e2e(self):
+        if self.name == "cfg3":
+            for c in range(2):
+                self.h[c].copy_(self.hh[c], non_blocking=True)
+                self._ffn(c)
+                self.oh[c].copy_(self.out[c], non_blocking=True)
+            return
+        for c in range(self.copies):
+            self.x[c].copy_(self.xh[c], non_blocking=True)
+            self.m27b.act_quant(self.x[c], Q8_K, out=self.xq[c])
+            self._mv(c)
+            self.yh[c].copy_(self.y[c], non_blocking=True)
+
+    def kernel_bytes(self):
+        return self.step_bytes / (1 if self.name == "cfg3" else self.copies)
+
+    def kernel_launches(self):
+        # cfg3: the step's matvec kernels are timed as one unit
+        return 1 if self.name == "cfg3" else self.copies
+
+
+def cpu_oracle_gbs(w_host, k, seconds, nthreads=0):
+    """GB/s of the CPU oracle's q4_K.q8_K matvec on w_host (rows x row bytes)."""
     from oracle import oracle as orc
     from _data import gauss_act
-    w = w_host if rows is None else w_host[:rows]
-    n = w.shape[0]
-    xq = orc.quantize_q8_K(gauss_act(1, K, 1))
-    orc.matvec(Q4_K, w, K, xq, nthreads)  # warm
+    n = w_host.shape[0]
+    xq = orc.quantize_q8_K(gauss_act(1, k, 1))
+    orc.matvec(Q4_K, w_host, k, xq, nthreads)  # warm
     reps, t0 = 0, time.perf_counter()
     while True:
-        orc.matvec(Q4_K, w, K, xq, nthreads)
+        orc.matvec(Q4_K, w_host, k, xq, nthreads)
         reps += 1
         el = time.perf_counter() - t0
         if el >= seconds and reps >= 3:
             break
-    bytes_per = n * (K // 256) * 144 + X_BYTES + n * 4
-    return bytes_per * reps / el / 1e9, reps, n, (nthreads or orc.max_threads())
+    bytes_per = wbytes(Q4_K, n, k) + k * 4 + n * 4
+    return bytes_per * reps / el / 1e9, reps, (nthreads or orc.max_threads())
 
 
 def run_reference(args, world, rank):
-    """CPU reference arm: the ggml-semantics CPU path on all host threads."""
+    """CPU reference arm: the ggml-semantics CPU path on all host threads (cfg0)."""
     if rank != 0:
         return 0
     from oracle import oracle as orc
-    w = random_q4K(0)
+    from _data import gauss_act, random_valid_blocks
+    rows, k = args.rows or 17408, 5120
+    w = random_valid_blocks(Q4_K, rows, k, 0)
     threads = orc.max_threads()
     # calibrate one full matvec, then size each step's row sample so that
     # warmup + steps take about a minute of CPU time in total
+    xq = orc.quantize_q8_K(gauss_act(1, k, 1))
+    orc.matvec(Q4_K, w, k, xq)
     t0 = time.perf_counter()
-    cpu_oracle_gbs(w, 0.0)
-    full = max(1e-4, (time.perf_counter() - t0) / 4)
+    for _ in range(3):
+        orc.matvec(Q4_K, w, k, xq)
+    full = max(1e-4, (time.perf_counter() - t0) / 3)
     budget = 60.0 / max(1, args.steps + args.warmup)
-    rows = int(min(ROWS, max(64, ROWS * budget / full)))
-    from _data import gauss_act
-    xq = orc.quantize_q8_K(gauss_act(1, K, 1))
-    ws = w[:rows]
+    srows = int(min(rows, max(64, rows * budget / full)))
+    ws = w[:srows]
     for _ in range(args.warmup):
-        orc.matvec(Q4_K, ws, K, xq)
+        orc.matvec(Q4_K, ws, k, xq)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        orc.matvec(Q4_K, ws, K, xq)
+        orc.matvec(Q4_K, ws, k, xq)
     el = time.perf_counter() - t0
-    step_bytes = rows * (K // 256) * 144 + X_BYTES + rows * 4
+    step_bytes = wbytes(Q4_K, srows, k) + k * 4 + srows * 4
     gbs = step_bytes * args.steps / el / 1e9
-    sample = f"{rows} of {ROWS} rows of one cfg0 q4_K matrix per step, x quantized to q8_K"
+    sample = f"{srows} of {rows} rows of one cfg0 q4_K matrix per step, x quantized to q8_K"
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "impl": "reference", "metric": "q4_K matvec HBM GB/s", "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_K*q8_K int32->f32",
         "data": "synthetic (seeded random valid q4_K blocks)",
-        "config": {"workload": "cfg0: q4_K matvec 17408x5120, batch 1", "rows": ROWS, "k": K},
+        "config": {"workload": f"cfg0: q4_K matvec {rows}x{k}, batch 1", "rows": rows, "k": k},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "CPU restatement of ggml's vec_dot_q4_K_q8_K (ggml itself is absent from the reference checkout)",
@@ -208,9 +355,7 @@ def main():
     if args.impl == "reference":
         return run_reference(args, world, rank)
 
-    import numpy as np
     import torch
-    import m27b
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -224,40 +369,9 @@ def main():
         if dist:
             dist.barrier()
 
-    # ---- inputs resident in HBM
-    host_w0 = None
-    Ws = []
-    for c in range(COPIES):
-        wh = random_q4K(1000 * rank + c)
-        if c == 0:
-            host_w0 = wh
-        Ws.append(m27b.QWeight(wh, Q4_K, K, ROWS))
-    gen = np.random.default_rng(7 + rank)
-    xs = [torch.from_numpy(gen.standard_normal((1, K)).astype(np.float32)).to(dev) for _ in range(COPIES)]
-    xq = [torch.empty(m27b.act_bytes(m27b.Q8_K, K), dtype=torch.uint8, device=dev) for _ in range(COPIES)]
-    ys = [torch.empty((1, ROWS), dtype=torch.float32, device=dev) for _ in range(COPIES)]
-    # host buffers for the end-to-end variant
-    xh = [x.cpu().pin_memory() for x in xs]
-    yh = [torch.empty((1, ROWS), dtype=torch.float32).pin_memory() for _ in range(COPIES)]
-
-    def step_dev():
-        for c in range(COPIES):
-            m27b.act_quant(xs[c], m27b.Q8_K, out=xq[c])
-            m27b.qmv(Ws[c], xq[c], 1, ys[c])
-
-    def step_qmv_only():
-        for c in range(COPIES):
-            m27b.qmv(Ws[c], xq[c], 1, ys[c])
-
-    def step_e2e():
-        for c in range(COPIES):
-            xs[c].copy_(xh[c], non_blocking=True)
-            m27b.act_quant(xs[c], m27b.Q8_K, out=xq[c])
-            m27b.qmv(Ws[c], xq[c], 1, ys[c])
-            yh[c].copy_(ys[c], non_blocking=True)
-
+    wl = Workload(args, dev, rank)
     # eager pass: validates the calls and warms per-kernel state before capture
-    step_e2e()
+    wl.step_e2e()
     torch.cuda.synchronize()
 
     def capture(fn, n):
@@ -307,58 +421,54 @@ def main():
         return ms, clocks
 
     warm = max(3, args.warmup)
-    # pre-capture all graphs outside the timed regions
-    for fn in (step_dev, step_qmv_only, step_e2e):
+    for fn in (wl.step, wl.kernel_only, wl.step_e2e):  # capture every graph outside the timed regions
         run_steps(fn, GRAPH_STEPS + (args.steps % GRAPH_STEPS))
     torch.cuda.synchronize()
 
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
     uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    ms, clocks = timed(step_dev, args.steps, warm, ClockSampler(uuid))
-    ms_k, _ = timed(step_qmv_only, args.steps, warm)
-    ms_e2e, _ = timed(step_e2e, args.steps, warm)
+    ms, clocks = timed(wl.step, args.steps, warm, ClockSampler(uuid))
+    ms_k, _ = timed(wl.kernel_only, args.steps, warm)
+    ms_e2e, _ = timed(wl.step_e2e, args.steps, warm)
 
-    step_bytes = COPIES * MV_BYTES
-    value = world * step_bytes * args.steps / (ms / 1e3) / 1e9
-    e2e = world * step_bytes * args.steps / (ms_e2e / 1e3) / 1e9
-    kern_us = ms_k * 1e3 / (args.steps * COPIES)
-    achieved = MV_BYTES / (kern_us * 1e-6) / 1e9
+    value = world * wl.step_bytes * args.steps / (ms / 1e3) / 1e9
+    e2e = world * wl.step_bytes * args.steps / (ms_e2e / 1e3) / 1e9
+    kern_us = ms_k * 1e3 / (args.steps * wl.kernel_launches())
+    achieved = wl.kernel_bytes() / (kern_us * 1e-6) / 1e9
     peak, peak_kind = measured_peak()
+    status = wl.m27b.device_status(clear=True)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, reps, nrows, threads = cpu_oracle_gbs(host_w0, 10.0)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "cfg0":
+        gbs, reps, threads = cpu_oracle_gbs(wl.host_w0, wl.k, 10.0)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{reps} full cfg0 matvecs (17408x5120 q4_K . q8_K), OpenMP over rows"}
+               "sample": f"{reps} full cfg0 matvecs ({wl.rows}x{wl.k} q4_K . q8_K), OpenMP over rows"}
 
     if rank == 0:
+        cfg = dict(wl.config)
+        cfg["parallelism"] = f"replica x{world}"
+        cfg["pct_of_8TBps"] = round(100 * value / world / 8000, 1)
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": wl.metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": warm, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_K*q8_K int8 dp4a, f32 accumulate",
-            "data": "synthetic (seeded random valid q4_K blocks, N(0,1) activations)",
-            "config": {"workload": "cfg0: q4_K matvec 17408x5120, batch 1, q8_K activations", "rows": ROWS, "k": K,
-                       "matvecs_per_step": COPIES, "bytes_per_matvec": MV_BYTES,
-                       "l2": f"inputs larger than L2: {COPIES} rotating weight matrices ({COPIES * W_BYTES / 1e6:.0f} MB)",
-                       "parallelism": f"replica x{world}", "pct_of_8TBps": round(100 * value / world / 8000, 1)},
+            "vs_baseline": None, "dtype": "q4_K/q6_K * q8_K, int8 dp4a, f32 accumulate",
+            "data": "synthetic (seeded random valid k-quant blocks, N(0,1) activations)",
+            "config": cfg,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic_per_launch(),
-                         "kernel": "k_qmv<W_Q4K,1,STORE>", "mean_launch_us": round(kern_us, 3),
-                         "peak_kind": peak_kind},
-            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": COPIES * X_BYTES,
-                    "d2h_bytes_per_step": COPIES * Y_BYTES},
-            "gpu_launches": 2 * COPIES * args.steps,
+                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic_per_launch(wl.profile),
+                         "kernel": wl.kernel, "mean_launch_us": round(kern_us, 3), "peak_kind": peak_kind},
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
+            "gpu_launches": wl.launches_per_step * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "device_status": status,
         }
         print(json.dumps(line), flush=True)
-    for g in graphs.values():
-        del g
     graphs.clear()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-    return 0
+    return 0 if status == 0 else 1
 
 
 if __name__ == "__main__":
