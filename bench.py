@@ -61,13 +61,17 @@ def parse_args():
     p.add_argument("--steps", type=int, default=None)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg3"], default="cfg0")
+    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg3", "decode"], default="cfg0")
     p.add_argument("--rows", type=int, default=None, help="override the row count (smaller profiling cases)")
     p.add_argument("--ntok", type=int, default=1, help="tokens per step (cfg3)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-decode", action="store_true", help="skip the whole-model decode figures of the default line")
+    p.add_argument("--prompt", type=int, default=512, help="decode: prompt tokens before generation")
+    p.add_argument("--gen", type=int, default=256, help="decode: generated tokens (timed)")
+    p.add_argument("--layers", type=int, default=64, help="decode: layers (64 = the Qwen-27B shape)")
     a = p.parse_args()
     if a.steps is None:
-        a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg3": 8000}[a.workload]
+        a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg3": 8000, "decode": a.gen}[a.workload]
     return a
 
 
@@ -286,6 +290,124 @@ class Workload:
         return 1 if self.name == "cfg3" else self.copies
 
 
+# --------------------------------------------------------------------------
+# whole-model decode (cfg4): the engine's tensor-parallel greedy decode
+
+
+def decode_bench(args, world, rank, dev, dist, uuid):
+    """Qwen-27B-shaped synthetic model (seeded random valid q4_K / q6_K blocks,
+    norms 1), tensor-parallel over `world` ranks.  The prompt is fed token by
+    token (untimed), then args.gen tokens are generated twice from the same
+    state: on the device (m27b_engine_generate: graph replays with no host
+    round trip) and through m27b_engine_decode_step (one host call per token:
+    16 B host->device, 8 B device->host).  Both are timed with CUDA events on
+    the engine's stream, max over ranks; the two token sequences must agree."""
+    import numpy as np
+    import torch
+    import m27b
+    cfg = m27b.model_config(max_ctx=args.prompt + args.gen + 8, tp_rank=rank, tp_size=world, n_layers=args.layers)
+    e = m27b.Engine(cfg)
+    try:
+        if world > 1:
+            uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(m27b.nccl_unique_id()), dtype=torch.uint8))
+            dist.broadcast(uid, 0)
+            e.set_nccl(bytes(uid.cpu().numpy()))
+        t0 = time.perf_counter()
+        e.random_weights(seed=0, sigma=0.02)
+        t_load = time.perf_counter() - t0
+        prompt = np.random.default_rng(4).integers(0, cfg.vocab, args.prompt)
+        for pos in range(args.prompt - 1):
+            e.decode_step(int(prompt[pos]), pos)
+        start, p0 = int(prompt[-1]), args.prompt - 1
+        st = torch.cuda.ExternalStream(e.stream(), device=dev)
+        warm = max(3, min(args.warmup, 16))
+        e.generate(start, p0, warm)  # warm-up (rewritten by the timed runs)
+
+        def timed(fn, sampler=None):
+            torch.cuda.synchronize()
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            if sampler:
+                sampler.start()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            out = fn()
+            b.record(st)
+            b.synchronize()
+            clk = sampler.stop() if sampler else None
+            ms = a.elapsed_time(b)
+            if dist:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            return ms, out, clk
+
+        ms, gen, clocks = timed(lambda: e.generate(start, p0, args.gen), ClockSampler(uuid))
+
+        def host_loop():
+            tok, out = start, []
+            for i in range(args.gen):
+                tok = e.decode_step(tok, p0 + i)
+                out.append(tok)
+            return out
+
+        ms_e2e, gen_e2e, _ = timed(host_loop)
+        wb = e.weight_bytes_per_token()
+        kv_bytes = 2 * args.layers * (p0 + 1 + args.gen / 2) * e_kv_heads(cfg) * cfg.head_dim * 4
+        tps = args.gen / (ms / 1e3)
+        peak, peak_kind = measured_peak()
+        per_rank_gbs = wb * tps / 1e9
+        return {
+            "tokens_per_s": round(tps, 2), "ms_per_token": round(ms / args.gen, 4), "tp": world,
+            "e2e_tokens_per_s": round(args.gen / (ms_e2e / 1e3), 2),
+            "weight_bytes_per_token_per_rank": wb, "kv_bytes_per_token_per_rank": int(kv_bytes),
+            "weight_gbs_per_rank": round(per_rank_gbs, 1), "weight_gbs_total": round(per_rank_gbs * world, 1),
+            "roofline_frac": round(per_rank_gbs / peak, 4), "peak_gbs": peak, "peak_kind": peak_kind,
+            "tokens_match": list(map(int, gen)) == list(map(int, gen_e2e)),
+            "layers": args.layers, "prompt": args.prompt, "gen": args.gen, "weights_init_s": round(t_load, 1),
+            "clocks": clocks,
+        }
+    finally:
+        e.close()
+
+
+def decode_main(args, world, rank, dev, dist, uuid):
+    """--workload decode: the decode figures as the line's own metric."""
+    import m27b
+    d = decode_bench(args, world, rank, dev, dist, uuid)
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s", "value": d["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.gen, "warmup": max(3, min(args.warmup, 16)), "ms_per_step": d["ms_per_token"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q4_K/q6_K * q8_K, int8 dp4a, f32 accumulate; fp32 KV cache",
+            "data": "synthetic (seeded random valid q4_K/q6_K blocks, random 512-token prompt, seed 4)",
+            "config": {"workload": f"cfg4: {args.layers}-layer Qwen-27B-shaped decode, TP={world}, "
+                                   f"{args.prompt}-token prompt, {args.gen} generated tokens",
+                       "parallelism": f"tp{world}", "l2": "weights per token >> L2 (16 GB / TP)"},
+            "roofline": {"bound": "hbm", "achieved": d["weight_gbs_per_rank"], "peak": d["peak_gbs"], "unit": "GB/s",
+                         "frac": d["roofline_frac"], "traffic": None, "kernel": "whole decode step (weight bytes / time)",
+                         "peak_kind": d["peak_kind"]},
+            "e2e": {"value": d["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 8},
+            "gpu_launches": (11 * args.layers + 4) * args.gen,
+            "clocks": d["clocks"], "cpu_baseline": None,
+            "device_status": m27b.device_status(clear=True), "decode": d,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def e_kv_heads(cfg):
+    import m27b
+    return m27b.partition(cfg).n_kv
+
+
 def cpu_oracle_gbs(w_host, k, seconds, nthreads=0):
     """GB/s of the CPU oracle's q4_K.q8_K matvec on w_host (rows x row bytes)."""
     from oracle import oracle as orc
@@ -369,6 +491,11 @@ def main():
         if dist:
             dist.barrier()
 
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    if args.workload == "decode":
+        return decode_main(args, world, rank, dev, dist, uuid)
+
     wl = Workload(args, dev, rank)
     # eager pass: validates the calls and warms per-kernel state before capture
     wl.step_e2e()
@@ -425,8 +552,6 @@ def main():
         run_steps(fn, GRAPH_STEPS + (args.steps % GRAPH_STEPS))
     torch.cuda.synchronize()
 
-    uuid = str(torch.cuda.get_device_properties(dev).uuid)
-    uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
     ms, clocks = timed(wl.step, args.steps, warm, ClockSampler(uuid))
     ms_k, _ = timed(wl.kernel_only, args.steps, warm)
     ms_e2e, _ = timed(wl.step_e2e, args.steps, warm)
@@ -437,6 +562,8 @@ def main():
     achieved = wl.kernel_bytes() / (kern_us * 1e-6) / 1e9
     peak, peak_kind = measured_peak()
     status = wl.m27b.device_status(clear=True)
+    wl_config, wl_metric, wl_profile, wl_kernel = wl.config, wl.metric, wl.profile, wl.kernel
+    wl_h2d, wl_d2h, wl_launches = wl.h2d, wl.d2h, wl.launches_per_step
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "cfg0":
@@ -444,27 +571,34 @@ def main():
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"{reps} full cfg0 matvecs ({wl.rows}x{wl.k} q4_K . q8_K), OpenMP over rows"}
 
+    graphs.clear()
+    decode = None
+    if not args.no_decode and wl.name == "cfg0":
+        del wl  # release the matvec workload's buffers before the model is loaded
+        torch.cuda.empty_cache()
+        decode = decode_bench(args, world, rank, dev, dist, uuid)
+
     if rank == 0:
-        cfg = dict(wl.config)
+        cfg = dict(wl_config)
         cfg["parallelism"] = f"replica x{world}"
         cfg["pct_of_8TBps"] = round(100 * value / world / 8000, 1)
         line = {
-            "metric": wl.metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": wl_metric, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": warm, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q4_K/q6_K * q8_K, int8 dp4a, f32 accumulate",
             "data": "synthetic (seeded random valid k-quant blocks, N(0,1) activations)",
             "config": cfg,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic_per_launch(wl.profile),
-                         "kernel": wl.kernel, "mean_launch_us": round(kern_us, 3), "peak_kind": peak_kind},
-            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
-            "gpu_launches": wl.launches_per_step * args.steps,
+                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic_per_launch(wl_profile),
+                         "kernel": wl_kernel, "mean_launch_us": round(kern_us, 3), "peak_kind": peak_kind},
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": wl_h2d, "d2h_bytes_per_step": wl_d2h},
+            "gpu_launches": wl_launches * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "device_status": status,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
-    graphs.clear()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

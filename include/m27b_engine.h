@@ -1,0 +1,130 @@
+/*
+ * m27b_engine.h — decode engine around the quantized matvec C ABI.
+ *
+ * Mirrors the lifecycle of the reference executor's C API
+ * (include/mono27b_config.h:155-184: load_weights / init_state / embed /
+ * decode_step / argmax / free_*) for a Qwen-27B-shaped attention model:
+ * every layer is RMSNorm -> fused q/gate/k/v projection (q4_K) -> q/k head
+ * RMSNorm + rotary embedding -> decode attention over an fp32 KV cache ->
+ * sigmoid(gate)-gated o_proj (q4_K) + residual -> RMSNorm -> gate/up SwiGLU
+ * (q4_K) -> down (q6_K) + residual; then output RMSNorm -> lm_head (q6_K) with
+ * fused argmax (greedy).  Tensor names are the reference loader's
+ * (src/mono27b_executor.cu:1739-1831): token_embd.weight, output_norm.weight,
+ * output.weight, blk.N.{attn_norm, attn_q, attn_k, attn_v, attn_output,
+ * attn_q_norm, attn_k_norm, post_attention_norm, ffn_gate, ffn_up,
+ * ffn_down}.weight.
+ *
+ * Tensor parallelism over tp_size GPUs (one process per GPU): q/gate by
+ * heads, k/v by the kv heads the local q heads use (replicated when
+ * tp_size > n_kv_head), gate/up by 256-value blocks of the FFN dimension,
+ * o_proj and down split along their input dimension, lm_head by vocabulary
+ * rows.  The 5120-wide hidden state is summed with an NCCL all-reduce after
+ * o_proj and after down (rank 0 adds the residual), and the argmax keys with
+ * an NCCL max all-reduce.  The reference itself is single-GPU.
+ *
+ * Same conventions as m27b_qmv.h: bool + error buffer; no exceptions.
+ */
+#ifndef M27B_ENGINE_H
+#define M27B_ENGINE_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "m27b_qmv.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct M27BModelConfig {
+    int n_layers;     /* 64 */
+    int hidden;       /* 5120 */
+    int ffn;          /* 17408 */
+    int n_head;       /* 24 */
+    int n_kv_head;    /* 4 */
+    int head_dim;     /* 256 (<= 256, multiple of 32) */
+    int vocab;        /* 248320 */
+    int n_rot;        /* rotary dims per head, 64 */
+    float rope_theta; /* 1e7 */
+    float rms_eps;    /* 1e-6 */
+    int max_ctx;      /* KV cache positions */
+    int tp_rank;      /* this process's tensor-parallel rank */
+    int tp_size;      /* 1, 2, 4 or 8 */
+} M27BModelConfig;
+
+typedef struct M27BEngine M27BEngine;
+
+/* The slice of the model one tensor-parallel rank holds (pure host logic). */
+typedef struct M27BPartition {
+    int q_lo, n_q;    /* local query heads [q_lo, q_lo + n_q) */
+    int kv_lo, n_kv;  /* local kv heads (the ones those query heads use) */
+    int f_lo, n_f;    /* local FFN values (whole 256-value blocks) */
+    int v_lo, n_v;    /* local vocabulary rows */
+} M27BPartition;
+
+/* Compute rank cfg->tp_rank's partition; false (with a message) if the shape
+ * cannot be split over cfg->tp_size ranks.  No CUDA call. */
+M27B_API bool m27b_engine_partition(const M27BModelConfig *cfg, M27BPartition *out, char *err, size_t err_cap);
+
+/* Size of an NCCL unique id (bytes). */
+#define M27B_NCCL_ID_BYTES 128
+
+/* Fill `id` (M27B_NCCL_ID_BYTES bytes) with a new NCCL unique id; rank 0
+ * calls this and distributes the bytes to the other ranks. */
+M27B_API bool m27b_nccl_unique_id(void *id, char *err, size_t err_cap);
+
+/* Create an engine on the current CUDA device: validates the shapes, and
+ * allocates this rank's weight shards, the KV cache and the workspace. */
+M27B_API bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err, size_t err_cap);
+
+/* Join the tensor-parallel group (tp_size > 1): id from m27b_nccl_unique_id. */
+M27B_API bool m27b_engine_set_nccl(M27BEngine *e, const void *id, char *err, size_t err_cap);
+
+/* Load one FULL tensor (host bytes in GGUF layout, or fp32 for norms) by its
+ * GGUF name; the engine keeps this rank's shard (and repacks it). */
+M27B_API bool m27b_engine_load_tensor(M27BEngine *e, const char *name, uint32_t ggml_type, uint32_t row_elems,
+                                      uint32_t row_count, const void *host, char *err, size_t err_cap);
+
+/* Fill every weight with seeded synthetic GGUF blocks generated on the GPU
+ * in global coordinates (identical tensors for every tp_size); norms = 1.
+ * The q4_K / q6_K values have standard deviation ~ sigma. */
+M27B_API bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char *err, size_t err_cap);
+
+/* Bytes of weights this rank streams per token (its shards, as stored). */
+M27B_API size_t m27b_engine_weight_bytes_per_token(const M27BEngine *e);
+
+/* Forget the KV cache (next position 0). */
+M27B_API bool m27b_engine_reset(M27BEngine *e, char *err, size_t err_cap);
+
+/* One decode step for `token` at position `pos` (pos == number of tokens
+ * already in the cache).  Writes the greedy next token to *next (all ranks
+ * agree).  If logits != NULL (tp_size == 1 only) the vocabulary logits are
+ * copied to the host buffer.  The first step captures the step into a CUDA
+ * graph that later steps replay; synchronises before returning. */
+M27B_API bool m27b_engine_decode_step(M27BEngine *e, int token, int pos, int *next, float *logits, char *err,
+                                      size_t err_cap);
+
+/* Greedy generation of n tokens on the device: step i (position pos + i)
+ * consumes the token step i-1 produced (`token` for i = 0), with no host
+ * round trip between steps (the captured step ends by writing its argmax as
+ * the next token and advancing the position).  tokens[i] receives the token
+ * step i produced.  Needs pos + n <= max_ctx; synchronises before returning. */
+M27B_API bool m27b_engine_generate(M27BEngine *e, int token, int pos, int n, int *tokens, char *err, size_t err_cap);
+
+/* Copy the current hidden state (after the last decode step, before the
+ * output norm) to the host (hidden floats). */
+M27B_API bool m27b_engine_hidden(M27BEngine *e, float *host, char *err, size_t err_cap);
+
+/* The CUDA stream every engine call enqueues on (a cudaStream_t), so that a
+ * caller can order its own work after the engine's or time the engine's work
+ * with events recorded on it. */
+M27B_API void *m27b_engine_stream(M27BEngine *e);
+
+M27B_API void m27b_engine_destroy(M27BEngine *e);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M27B_ENGINE_H */

@@ -21,9 +21,26 @@ LIB = os.path.join(LIBDIR, "libm27b.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
+
+
+def _nccl_dirs():
+    """NCCL headers and library: the copy torch ships (nvidia-nccl wheel), so
+    that one libnccl is loaded per process; else the system one."""
+    try:
+        import nvidia.nccl
+        base = list(nvidia.nccl.__path__)[0]
+        inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
+        if os.path.exists(os.path.join(inc, "nccl.h")):
+            return inc, lib
+    except ImportError:
+        pass
+    return "/usr/include", "/usr/lib/x86_64-linux-gnu"
+
+
+NCCL_INC, NCCL_LIB = _nccl_dirs()
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-           "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
+           "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC, "-I", NCCL_INC]
 
 
 def _sources():
@@ -68,7 +85,8 @@ def build(force=False, verbose=False, ptxas_info=False):
         for o in outs:
             sys.stdout.write(o)
     if jobs or force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs
+        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + [
+            "-L", NCCL_LIB, "-lnccl", "-Xlinker", "-rpath=" + NCCL_LIB]
         run(cmd)
     return LIB
 

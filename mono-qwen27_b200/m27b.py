@@ -209,3 +209,139 @@ def call_raw(name, *args):
     err = ctypes.create_string_buffer(ERR_CAP)
     ok = getattr(lib(), name)(*args, err, ERR_CAP)
     return bool(ok), err.value.decode(errors="replace")
+
+
+# --------------------------------------------------------------------------
+# decode engine (include/m27b_engine.h)
+
+
+class ModelConfig(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("ffn", ctypes.c_int), ("n_head", ctypes.c_int),
+                ("n_kv_head", ctypes.c_int), ("head_dim", ctypes.c_int), ("vocab", ctypes.c_int), ("n_rot", ctypes.c_int),
+                ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("max_ctx", ctypes.c_int),
+                ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int)]
+
+
+class Partition(ctypes.Structure):
+    _fields_ = [("q_lo", ctypes.c_int), ("n_q", ctypes.c_int), ("kv_lo", ctypes.c_int), ("n_kv", ctypes.c_int),
+                ("f_lo", ctypes.c_int), ("n_f", ctypes.c_int), ("v_lo", ctypes.c_int), ("n_v", ctypes.c_int)]
+
+
+QWEN27 = dict(n_layers=64, hidden=5120, ffn=17408, n_head=24, n_kv_head=4, head_dim=256, vocab=248320, n_rot=64,
+              rope_theta=1e7, rms_eps=1e-6)
+F32 = 0
+
+
+def model_config(max_ctx=1024, tp_rank=0, tp_size=1, **kw):
+    d = dict(QWEN27)
+    d.update(kw)
+    return ModelConfig(max_ctx=max_ctx, tp_rank=tp_rank, tp_size=tp_size, **d)
+
+
+def _engine_lib():
+    L = lib()
+    if getattr(L, "_engine_sigs", False):
+        return L
+    vp, cp, sz, i32, u32, b = ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_bool
+    sig = {
+        "m27b_engine_partition": (b, [ctypes.POINTER(ModelConfig), ctypes.POINTER(Partition), cp, sz]),
+        "m27b_nccl_unique_id": (b, [vp, cp, sz]),
+        "m27b_engine_create": (b, [ctypes.POINTER(ModelConfig), ctypes.POINTER(vp), cp, sz]),
+        "m27b_engine_set_nccl": (b, [vp, vp, cp, sz]),
+        "m27b_engine_load_tensor": (b, [vp, cp, u32, u32, u32, vp, cp, sz]),
+        "m27b_engine_random_weights": (b, [vp, ctypes.c_uint64, ctypes.c_float, cp, sz]),
+        "m27b_engine_weight_bytes_per_token": (sz, [vp]),
+        "m27b_engine_reset": (b, [vp, cp, sz]),
+        "m27b_engine_decode_step": (b, [vp, i32, i32, ctypes.POINTER(ctypes.c_int), vp, cp, sz]),
+        "m27b_engine_generate": (b, [vp, i32, i32, i32, vp, cp, sz]),
+        "m27b_engine_hidden": (b, [vp, vp, cp, sz]),
+        "m27b_engine_stream": (vp, [vp]),
+        "m27b_engine_destroy": (None, [vp]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    L._engine_sigs = True
+    return L
+
+
+def partition(cfg):
+    p = Partition()
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(_engine_lib().m27b_engine_partition(ctypes.byref(cfg), ctypes.byref(p), err, ERR_CAP), err,
+           "m27b_engine_partition")
+    return p
+
+
+def nccl_unique_id():
+    buf = ctypes.create_string_buffer(128)
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(_engine_lib().m27b_nccl_unique_id(buf, err, ERR_CAP), err, "m27b_nccl_unique_id")
+    return buf.raw
+
+
+class Engine:
+    """One tensor-parallel rank of the decode engine on the current device."""
+
+    def __init__(self, cfg):
+        self.cfg = cfg
+        self.L = _engine_lib()
+        self.h = ctypes.c_void_p()
+        self._call("m27b_engine_create", ctypes.byref(cfg), ctypes.byref(self.h))
+
+    def _call(self, name, *args):
+        err = ctypes.create_string_buffer(ERR_CAP)
+        _check(getattr(self.L, name)(*args, err, ERR_CAP), err, name)
+
+    def set_nccl(self, uid):
+        buf = ctypes.create_string_buffer(bytes(uid), 128)
+        self._call("m27b_engine_set_nccl", self.h, buf)
+
+    def load_tensor(self, name, ggml_type, row_elems, row_count, data):
+        import numpy as np
+        a = np.ascontiguousarray(data)
+        self._call("m27b_engine_load_tensor", self.h, name.encode(), ggml_type, row_elems, row_count,
+                   ctypes.c_void_p(a.ctypes.data))
+
+    def random_weights(self, seed=0, sigma=0.02):
+        self._call("m27b_engine_random_weights", self.h, seed, ctypes.c_float(sigma))
+
+    def weight_bytes_per_token(self):
+        return self.L.m27b_engine_weight_bytes_per_token(self.h)
+
+    def decode_step(self, token, pos, logits=False):
+        import numpy as np
+        nxt = ctypes.c_int(-1)
+        lg = np.empty(self.cfg.vocab, dtype=np.float32) if logits else None
+        self._call("m27b_engine_decode_step", self.h, int(token), int(pos), ctypes.byref(nxt),
+                   ctypes.c_void_p(lg.ctypes.data) if logits else None)
+        return (nxt.value, lg) if logits else nxt.value
+
+    def generate(self, token, pos, n):
+        """Greedy tokens of steps pos..pos+n-1 (step i consumes step i-1's token), all on the device."""
+        import numpy as np
+        out = np.empty(n, dtype=np.int32)
+        self._call("m27b_engine_generate", self.h, int(token), int(pos), int(n), ctypes.c_void_p(out.ctypes.data))
+        return out
+
+    def stream(self):
+        """The engine's cudaStream_t as an integer handle."""
+        return self.L.m27b_engine_stream(self.h)
+
+    def hidden(self):
+        import numpy as np
+        out = np.empty(self.cfg.hidden, dtype=np.float32)
+        self._call("m27b_engine_hidden", self.h, ctypes.c_void_p(out.ctypes.data))
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.m27b_engine_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
