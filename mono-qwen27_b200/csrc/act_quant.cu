@@ -26,9 +26,28 @@ template <int MODE>
 M27B_DI float row_norm_scale(const ActArgs &a, const float *xr) {
     if (MODE != ACT_RMSNORM) return 1.0f;
     __shared__ float red[32];
-    float s = 0.0f;
-    for (int i = threadIdx.x; i < a.k; i += blockDim.x) s = fmaf(xr[i], xr[i], s);
-    s = warp_sum(s);
+    // independent partial sums over 16-byte loads keep several loads in flight
+    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+    const int bd = blockDim.x;
+    if ((a.k & 3) == 0 && ((uintptr_t)xr & 15) == 0) {
+        const float4 *x4 = (const float4 *)xr;
+        const int n4 = a.k >> 2;
+        int i = threadIdx.x;
+        for (; i + 3 * bd < n4; i += 4 * bd) {
+            const float4 v0 = x4[i], v1 = x4[i + bd], v2 = x4[i + 2 * bd], v3 = x4[i + 3 * bd];
+            s0 = fmaf(v0.x, v0.x, fmaf(v0.y, v0.y, fmaf(v0.z, v0.z, fmaf(v0.w, v0.w, s0))));
+            s1 = fmaf(v1.x, v1.x, fmaf(v1.y, v1.y, fmaf(v1.z, v1.z, fmaf(v1.w, v1.w, s1))));
+            s2 = fmaf(v2.x, v2.x, fmaf(v2.y, v2.y, fmaf(v2.z, v2.z, fmaf(v2.w, v2.w, s2))));
+            s3 = fmaf(v3.x, v3.x, fmaf(v3.y, v3.y, fmaf(v3.z, v3.z, fmaf(v3.w, v3.w, s3))));
+        }
+        for (; i < n4; i += bd) {
+            const float4 v0 = x4[i];
+            s0 = fmaf(v0.x, v0.x, fmaf(v0.y, v0.y, fmaf(v0.z, v0.z, fmaf(v0.w, v0.w, s0))));
+        }
+    } else {
+        for (int i = threadIdx.x; i < a.k; i += bd) s0 = fmaf(xr[i], xr[i], s0);
+    }
+    float s = warp_sum((s0 + s1) + (s2 + s3));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
     float tot = 0.0f;

@@ -10,6 +10,7 @@
 // (k_attn_decode_split_partial / _reduce :1339-1484) — here a plain
 // max-subtracted softmax with no score clamp.
 #include "m27b_device.cuh"
+#include "m27b_launch.cuh"
 
 namespace m27b {
 
@@ -62,68 +63,100 @@ __global__ void k_qk_norm_rope_cache(const float *qkv, const float *q_norm, cons
 }
 
 // ---------------------------------------------------------------------------
-// Decode attention, split over positions.  Grid (nkv, splits), 256 threads:
-// CTA (j, s) handles the G = nq/nkv query heads of kv head j over positions
-// [s*L/S, (s+1)*L/S) of the L = *pos + 1 cached positions; warp w takes every
-// 8th position, lanes hold hd/32 dims.  Partials (max, sum, acc[hd]) per
-// (split, q head) go to `part`; k_attn_reduce combines them.
-constexpr int ATT_G = 8;  // most query heads per kv head
+// Decode attention, split over positions (flash-decoding).
+//
+// k_attn_partial: grid (nkv, S), 256 threads.  CTA (j, s) handles the
+// G = nq/nkv query heads of kv head j over split s of the L = *pos + 1 cached
+// positions; the number of active splits adapts to L on the device
+// (att_splits: at least ATT_MIN_POS positions per split) so one captured graph
+// serves every position.  Warp w takes every 8th position of the split; lane l
+// holds dims [l*DPL, (l+1)*DPL) of a K/V row (vector loads), the query heads
+// sit in shared memory.  Per (split, head) the partial record is
+// acc[hd], max, sum (record stride hd + 4 keeps records 16-byte aligned).
+// k_attn_reduce: grid nq, 256 threads: warp w combines splits w, w+8, ...
+// rescaled to the global max, then the 8 warps are summed in shared memory.
+constexpr int ATT_G = 8;         // most query heads per kv head
+constexpr int ATT_MIN_POS = 16;  // fewest positions per split
 
+M27B_DI int att_splits(int L, int smax) {
+    const int s = (L + ATT_MIN_POS - 1) / ATT_MIN_POS;
+    return s < smax ? s : smax;
+}
+
+template <int DPL>
+M27B_DI void ld_dims(const float *p, float (&v)[DPL]) {
+    if constexpr (DPL % 4 == 0) {
+#pragma unroll
+        for (int c = 0; c < DPL / 4; ++c) {
+            const float4 t = reinterpret_cast<const float4 *>(p)[c];
+            v[4 * c] = t.x; v[4 * c + 1] = t.y; v[4 * c + 2] = t.z; v[4 * c + 3] = t.w;
+        }
+    } else if constexpr (DPL % 2 == 0) {
+#pragma unroll
+        for (int c = 0; c < DPL / 2; ++c) {
+            const float2 t = reinterpret_cast<const float2 *>(p)[c];
+            v[2 * c] = t.x; v[2 * c + 1] = t.y;
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) v[c] = p[c];
+    }
+}
+
+template <int DPL>
 __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const float *kc, const float *vc, float *part,
-                                                      const int *pos_p, int nq, int nkv, int hd, float scale) {
+                                                      const int *pos_p, int nq, int nkv, float scale) {
     pdl_wait();
     pdl_trigger();
-    const int j = blockIdx.x, s = blockIdx.y, S = gridDim.y;
+    constexpr int hd = DPL * 32, rec = hd + 4;
+    const int j = blockIdx.x, s = blockIdx.y;
     const int G = nq / nkv;
     const int L = *pos_p + 1;
+    const int S = att_splits(L, gridDim.y);
+    if (s >= S) return;
     const int p0 = (int)(((long)L * s) / S), p1 = (int)(((long)L * (s + 1)) / S);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int DPL = hd / 32;  // dims per lane (<= 8)
-    float qr[ATT_G][8], acc[ATT_G][8], m[ATT_G], l[ATT_G];
+    extern __shared__ __align__(16) float sh[];  // q [G][hd] (pre-scaled), then [8 warps][G][rec]
+    float *qs = sh;
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[(size_t)j * G * hd + i] * scale;
+    __syncthreads();
+    float acc[ATT_G][DPL], m[ATT_G], l[ATT_G];
 #pragma unroll
     for (int g = 0; g < ATT_G; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            acc[g][i] = 0.0f;
-            qr[g][i] = (g < G && i < DPL) ? q[(size_t)(j * G + g) * hd + lane * DPL + i] * scale : 0.0f;
-        }
+        for (int i = 0; i < DPL; ++i) acc[g][i] = 0.0f;
     }
     for (int p = p0 + warp; p < p1; p += 8) {
-        const float *kr = kc + ((size_t)p * nkv + j) * hd + lane * DPL;
-        const float *vr = vc + ((size_t)p * nkv + j) * hd + lane * DPL;
-        float kv[8], vv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            kv[i] = i < DPL ? kr[i] : 0.0f;
-            vv[i] = i < DPL ? vr[i] : 0.0f;
-        }
+        float kv[DPL], vv[DPL];
+        ld_dims<DPL>(kc + ((size_t)p * nkv + j) * hd + lane * DPL, kv);
+        ld_dims<DPL>(vc + ((size_t)p * nkv + j) * hd + lane * DPL, vv);
 #pragma unroll
         for (int g = 0; g < ATT_G; ++g) {
-            if (g >= G) continue;
-            float d = 0.0f;
+            if (g < G) {
+                float qv[DPL];
+                ld_dims<DPL>(qs + g * hd + lane * DPL, qv);
+                float d = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) d = fmaf(qr[g][i], kv[i], d);
-            d = warp_sum(d);
-            const float mn = fmaxf(m[g], d);
-            const float a = expf(m[g] - mn), b = expf(d - mn);
-            l[g] = l[g] * a + b;
+                for (int i = 0; i < DPL; ++i) d = fmaf(qv[i], kv[i], d);
+                d = warp_sum(d);
+                const float mn = fmaxf(m[g], d);
+                const float a = expf(m[g] - mn), b = expf(d - mn);
+                l[g] = l[g] * a + b;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[g][i] = acc[g][i] * a + b * vv[i];
-            m[g] = mn;
+                for (int i = 0; i < DPL; ++i) acc[g][i] = acc[g][i] * a + b * vv[i];
+                m[g] = mn;
+            }
         }
     }
-    // combine the 8 warps in shared memory: per warp (m, l, acc[hd]) per head
-    extern __shared__ float sh[];  // [8 warps][G][hd + 2]
-    const int rec = hd + 2;
+    float *cb = sh + G * hd;
 #pragma unroll
     for (int g = 0; g < ATT_G; ++g) {
         if (g < G) {
-            float *r = sh + ((size_t)warp * G + g) * rec;
+            float *r = cb + ((size_t)warp * G + g) * rec;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (i < DPL) r[lane * DPL + i] = acc[g][i];
+            for (int i = 0; i < DPL; ++i) r[lane * DPL + i] = acc[g][i];
             if (lane == 0) {
                 r[hd] = m[g];
                 r[hd + 1] = l[g];
@@ -134,10 +167,12 @@ __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const floa
     for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
         const int g = idx / hd, dd = idx - g * hd;
         float M = -INFINITY;
-        for (int w = 0; w < 8; ++w) M = fmaxf(M, sh[((size_t)w * G + g) * rec + hd]);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, cb[((size_t)w * G + g) * rec + hd]);
         float Lsum = 0.0f, A = 0.0f;
+#pragma unroll
         for (int w = 0; w < 8; ++w) {
-            const float *r = sh + ((size_t)w * G + g) * rec;
+            const float *r = cb + ((size_t)w * G + g) * rec;
             const float f = r[hd] == -INFINITY ? 0.0f : expf(r[hd] - M);
             Lsum += r[hd + 1] * f;
             A += r[dd] * f;
@@ -151,22 +186,90 @@ __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const floa
     }
 }
 
-// Combine the split partials: out[h][d] = sum_s e^(m_s-M) acc_s / sum_s e^(m_s-M) l_s.
-__global__ void k_attn_reduce(const float *part, float *out, int nq, int hd, int S) {
+template <int DPL>
+__global__ void __launch_bounds__(256) k_attn_reduce(const float *part, float *out, const int *pos_p, int nq, int smax) {
     pdl_wait();
     pdl_trigger();
-    const int h = blockIdx.x, d = threadIdx.x;
-    const int rec = hd + 2;
+    constexpr int hd = DPL * 32, rec = hd + 4;
+    __shared__ __align__(16) float red[8][rec];
+    __shared__ float wmax[8];
+    const int h = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int S = att_splits(*pos_p + 1, smax);
     float M = -INFINITY;
-    for (int s = 0; s < S; ++s) M = fmaxf(M, part[((size_t)s * nq + h) * rec + hd]);
-    float Lsum = 0.0f, A = 0.0f;
-    for (int s = 0; s < S; ++s) {
+    for (int s = warp; s < S; s += 8) M = fmaxf(M, part[((size_t)s * nq + h) * rec + hd]);
+    if (lane == 0) wmax[warp] = M;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, wmax[w]);
+    float A[DPL], Ls = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) A[i] = 0.0f;
+    for (int s = warp; s < S; s += 8) {
         const float *r = part + ((size_t)s * nq + h) * rec;
-        const float f = r[hd] == -INFINITY ? 0.0f : expf(r[hd] - M);
-        Lsum += r[hd + 1] * f;
-        A += r[d] * f;
+        const float f = expf(r[hd] - M);  // every active split holds at least one position
+        Ls = fmaf(f, r[hd + 1], Ls);
+        float v[DPL];
+        ld_dims<DPL>(r + lane * DPL, v);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) A[i] = fmaf(f, v[i], A[i]);
     }
-    out[(size_t)h * hd + d] = A / Lsum;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) red[warp][lane * DPL + i] = A[i];
+    if (lane == 0) red[warp][hd] = Ls;
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.0f, L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            o += red[w][d];
+            L += red[w][hd];
+        }
+        out[(size_t)h * hd + d] = o / L;
+    }
+}
+
+size_t attn_smem_bytes(int G, int hd) { return (size_t)(G * hd + 8 * G * (hd + 4)) * sizeof(float); }
+
+template <int DPL>
+static cudaError_t attn_run(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
+                            int nq, int nkv, int S, float scale, cudaStream_t st) {
+    const size_t smem = attn_smem_bytes(nq / nkv, DPL * 32);
+    cudaError_t e = launch_pdl(k_attn_partial<DPL>, dim3(nkv, S), dim3(256), smem, st, q, kc, vc, part, pos, nq, nkv, scale);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_attn_reduce<DPL>, dim3(nq), dim3(256), 0, st, (const float *)part, out, pos, nq, S);
+}
+
+template <int DPL>
+static cudaError_t attn_opt_in() {
+    return cudaFuncSetAttribute(k_attn_partial<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)attn_smem_bytes(ATT_G, DPL * 32));
+}
+
+// Raise the shared-memory limit of every attention instantiation (once per
+// device, before any capture).
+cudaError_t attn_prepare() {
+    cudaError_t e = cudaSuccess;
+    for (cudaError_t r : {attn_opt_in<1>(), attn_opt_in<2>(), attn_opt_in<3>(), attn_opt_in<4>(), attn_opt_in<5>(),
+                          attn_opt_in<6>(), attn_opt_in<7>(), attn_opt_in<8>()})
+        if (r != cudaSuccess) e = r;
+    return e;
+}
+
+// Enqueue decode attention: out[h][:] for the nq local query heads.  part
+// holds S * nq * (hd + 4) floats; hd is a multiple of 32, at most 256.
+cudaError_t attn_launch(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
+                        int nq, int nkv, int hd, int S, float scale, cudaStream_t st) {
+    switch (hd / 32) {
+        case 1: return attn_run<1>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 2: return attn_run<2>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 3: return attn_run<3>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 4: return attn_run<4>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 5: return attn_run<5>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 6: return attn_run<6>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 7: return attn_run<7>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 8: return attn_run<8>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 // ---------------------------------------------------------------------------

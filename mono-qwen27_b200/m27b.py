@@ -212,6 +212,36 @@ def call_raw(name, *args):
 
 
 # --------------------------------------------------------------------------
+# decode attention (include/m27b_attn.h)
+
+
+def _attn_lib():
+    L = lib()
+    if getattr(L, "_attn_sigs", False):
+        return L
+    vp, i32, sz, cp, fp, b = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_char_p, ctypes.c_float, ctypes.c_bool
+    L.m27b_attn_part_bytes.restype = sz
+    L.m27b_attn_part_bytes.argtypes = [i32, i32, i32]
+    L.m27b_attn_decode.restype = b
+    L.m27b_attn_decode.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, fp, vp, vp, vp, cp, sz]
+    L._attn_sigs = True
+    return L
+
+
+def attn_part_bytes(n_q, head_dim, splits):
+    return _attn_lib().m27b_attn_part_bytes(n_q, head_dim, splits)
+
+
+def attn_decode(q, k_cache, v_cache, pos, n_q, n_kv, head_dim, splits, scale, part, out, stream=None):
+    """Decode attention of n_q heads over cache positions [0, pos[0]] (all device tensors)."""
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ok = _attn_lib().m27b_attn_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), n_q, n_kv, head_dim, splits,
+                                      ctypes.c_float(scale), _ptr(part), _ptr(out), _stream(stream), err, ERR_CAP)
+    _check(ok, err, "m27b_attn_decode")
+    return out
+
+
+# --------------------------------------------------------------------------
 # decode engine (include/m27b_engine.h)
 
 

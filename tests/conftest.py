@@ -33,3 +33,10 @@ def m27b():
     import m27b as M
     M.lib()
     return M
+
+
+@pytest.fixture(scope="session")
+def torch():
+    import torch as T
+    assert T.cuda.is_available(), "GPU tests need a CUDA device"
+    return T
