@@ -45,6 +45,35 @@ M27B_API bool m27b_attn_decode(const float *q, const float *k_cache, const float
                                int n_kv, int head_dim, int splits, float scale, float *part, float *out,
                                cudaStream_t stream, char *err, size_t err_cap);
 
+/* Capacity of the static scratch m27b_attn_decode_noalloc uses (1 MiB): enough
+ * for 24 query heads of 256 values over 37 splits (921,600 bytes, the
+ * single-GPU Qwen-27B shape). */
+#define M27B_ATTN_NOALLOC_SCRATCH_BYTES (1u << 20)
+
+/* m27b_attn_decode without the `part` argument: the split partials live in a
+ * file-scope __device__ array of M27B_ATTN_NOALLOC_SCRATCH_BYTES inside the
+ * library, so neither the caller nor the library allocates device memory
+ * (no cudaMalloc, cudaFree or allocating library routine).  This entry has no
+ * counterpart in the reference; it is for callers that have no scratch
+ * buffer to pass: a call site with a fixed signature (the reference's
+ * attention call passes only q, the caches and out), or a host that plans all
+ * device memory once at load time and cannot allocate on the decode path.
+ * Results equal m27b_attn_decode's for the same arguments.
+ *   - Shapes whose m27b_attn_part_bytes(n_q, head_dim, splits) exceeds
+ *     M27B_ATTN_NOALLOC_SCRATCH_BYTES are rejected with an error (use fewer
+ *     splits, or m27b_attn_decode with a larger buffer).
+ *   - The first call on a device does the set-up (looks up the scratch's
+ *     device address with cudaGetSymbolAddress and raises the kernels'
+ *     shared-memory limit); make it before any stream capture.
+ *   - Nothing in the scratch needs to start at zero: every active split writes
+ *     its record before the reduction reads it.
+ *   - There is one scratch per device: calls on the same device whose
+ *     executions overlap (other streams, other host threads) race on it and
+ *     give wrong results.  Order them on one stream. */
+M27B_API bool m27b_attn_decode_noalloc(const float *q, const float *k_cache, const float *v_cache, const int *pos,
+                                       int n_q, int n_kv, int head_dim, int splits, float scale, float *out,
+                                       cudaStream_t stream, char *err, size_t err_cap);
+
 #ifdef __cplusplus
 }
 #endif

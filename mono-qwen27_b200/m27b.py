@@ -224,6 +224,8 @@ def _attn_lib():
     L.m27b_attn_part_bytes.argtypes = [i32, i32, i32]
     L.m27b_attn_decode.restype = b
     L.m27b_attn_decode.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, fp, vp, vp, vp, cp, sz]
+    L.m27b_attn_decode_noalloc.restype = b
+    L.m27b_attn_decode_noalloc.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, fp, vp, vp, cp, sz]
     L._attn_sigs = True
     return L
 
@@ -238,6 +240,18 @@ def attn_decode(q, k_cache, v_cache, pos, n_q, n_kv, head_dim, splits, scale, pa
     ok = _attn_lib().m27b_attn_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), n_q, n_kv, head_dim, splits,
                                       ctypes.c_float(scale), _ptr(part), _ptr(out), _stream(stream), err, ERR_CAP)
     _check(ok, err, "m27b_attn_decode")
+    return out
+
+
+ATTN_NOALLOC_SCRATCH_BYTES = 1 << 20
+
+
+def attn_decode_noalloc(q, k_cache, v_cache, pos, n_q, n_kv, head_dim, splits, scale, out, stream=None):
+    """m27b_attn_decode with the library's static scratch (no scratch argument, no allocation)."""
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ok = _attn_lib().m27b_attn_decode_noalloc(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(pos), n_q, n_kv, head_dim,
+                                              splits, ctypes.c_float(scale), _ptr(out), _stream(stream), err, ERR_CAP)
+    _check(ok, err, "m27b_attn_decode_noalloc")
     return out
 
 
