@@ -69,6 +69,8 @@ def parse_args():
     p.add_argument("--prompt", type=int, default=512, help="decode: prompt tokens before generation")
     p.add_argument("--gen", type=int, default=256, help="decode: generated tokens (timed)")
     p.add_argument("--layers", type=int, default=64, help="decode: layers (64 = the Qwen-27B shape)")
+    p.add_argument("--comm", choices=["p2p", "nccl"], default="p2p",
+                   help="decode, N>1: fused NVLink all-reduce (p2p) or NCCL all-reduce")
     a = p.parse_args()
     if a.steps is None:
         a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg3": 8000, "decode": a.gen}[a.workload]
@@ -314,6 +316,8 @@ def decode_bench(args, world, rank, dev, dist, uuid):
                 uid.copy_(torch.frombuffer(bytearray(m27b.nccl_unique_id()), dtype=torch.uint8))
             dist.broadcast(uid, 0)
             e.set_nccl(bytes(uid.cpu().numpy()))
+            if args.comm == "p2p":
+                e.enable_p2p()
         t0 = time.perf_counter()
         e.random_weights(seed=0, sigma=0.02)
         t_load = time.perf_counter() - t0
@@ -368,6 +372,8 @@ def decode_bench(args, world, rank, dev, dist, uuid):
             "roofline_frac": round(per_rank_gbs / peak, 4), "peak_gbs": peak, "peak_kind": peak_kind,
             "tokens_match": list(map(int, gen)) == list(map(int, gen_e2e)),
             "layers": args.layers, "prompt": args.prompt, "gen": args.gen, "weights_init_s": round(t_load, 1),
+            "allreduce": "none" if world == 1 else ("fused NVLink push (P2P stores + release flags)" if args.comm == "p2p"
+                                                   else "NCCL all-reduce"),
             "clocks": clocks,
         }
     finally:
@@ -392,7 +398,7 @@ def decode_main(args, world, rank, dev, dist, uuid):
                          "frac": d["roofline_frac"], "traffic": None, "kernel": "whole decode step (weight bytes / time)",
                          "peak_kind": d["peak_kind"]},
             "e2e": {"value": d["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 8},
-            "gpu_launches": (11 * args.layers + 4) * args.gen,
+            "gpu_launches": ((10 if world > 1 and args.comm == "p2p" else 11) * args.layers + 3) * args.gen,
             "clocks": d["clocks"], "cpu_baseline": None,
             "device_status": m27b.device_status(clear=True), "decode": d,
         }

@@ -18,9 +18,10 @@
  * heads, k/v by the kv heads the local q heads use (replicated when
  * tp_size > n_kv_head), gate/up by 256-value blocks of the FFN dimension,
  * o_proj and down split along their input dimension, lm_head by vocabulary
- * rows.  The 5120-wide hidden state is summed with an NCCL all-reduce after
- * o_proj and after down (rank 0 adds the residual), and the argmax keys with
- * an NCCL max all-reduce.  The reference itself is single-GPU.
+ * rows.  The 5120-wide hidden state is summed after o_proj and after down
+ * (rank 0 adds the residual) with an NCCL all-reduce, or with the fused
+ * NVLink path of m27b_engine_enable_p2p; the argmax keys likewise.  The
+ * reference itself is single-GPU.
  *
  * Same conventions as m27b_qmv.h: bool + error buffer; no exceptions.
  */
@@ -80,6 +81,16 @@ M27B_API bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, c
 
 /* Join the tensor-parallel group (tp_size > 1): id from m27b_nccl_unique_id. */
 M27B_API bool m27b_engine_set_nccl(M27BEngine *e, const void *id, char *err, size_t err_cap);
+
+/* Switch the hidden-state all-reduces to the fused NVLink path (tp_size 2..8,
+ * after m27b_engine_set_nccl, before the first decode step; all ranks call
+ * it).  o_proj and ffn_down then store their output rows straight into every
+ * rank's receive window (CUDA IPC mappings, exchanged once over NCCL) and
+ * publish an epoch with a system-scope release store; the next kernel waits
+ * (bounded) for every rank's epoch, sums the partials in rank order and
+ * applies the following RMSNorm + q8_K quantization.  The argmax keys are
+ * exchanged the same way.  No NCCL call remains in the decode step. */
+M27B_API bool m27b_engine_enable_p2p(M27BEngine *e, char *err, size_t err_cap);
 
 /* Load one FULL tensor (host bytes in GGUF layout, or fp32 for norms) by its
  * GGUF name; the engine keeps this rank's shard (and repacks it). */

@@ -21,33 +21,15 @@
 
 namespace m27b {
 
-// Row scale for ACT_RMSNORM: 1/sqrt(mean(x^2) + eps), block-wide reduction.
+// Row scale for ACT_RMSNORM: 1/sqrt(mean(x^2) + eps), block-wide reduction
+// (used when the row cannot be staged in shared memory).
 template <int MODE>
 M27B_DI float row_norm_scale(const ActArgs &a, const float *xr) {
     if (MODE != ACT_RMSNORM) return 1.0f;
     __shared__ float red[32];
-    // independent partial sums over 16-byte loads keep several loads in flight
-    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-    const int bd = blockDim.x;
-    if ((a.k & 3) == 0 && ((uintptr_t)xr & 15) == 0) {
-        const float4 *x4 = (const float4 *)xr;
-        const int n4 = a.k >> 2;
-        int i = threadIdx.x;
-        for (; i + 3 * bd < n4; i += 4 * bd) {
-            const float4 v0 = x4[i], v1 = x4[i + bd], v2 = x4[i + 2 * bd], v3 = x4[i + 3 * bd];
-            s0 = fmaf(v0.x, v0.x, fmaf(v0.y, v0.y, fmaf(v0.z, v0.z, fmaf(v0.w, v0.w, s0))));
-            s1 = fmaf(v1.x, v1.x, fmaf(v1.y, v1.y, fmaf(v1.z, v1.z, fmaf(v1.w, v1.w, s1))));
-            s2 = fmaf(v2.x, v2.x, fmaf(v2.y, v2.y, fmaf(v2.z, v2.z, fmaf(v2.w, v2.w, s2))));
-            s3 = fmaf(v3.x, v3.x, fmaf(v3.y, v3.y, fmaf(v3.z, v3.z, fmaf(v3.w, v3.w, s3))));
-        }
-        for (; i < n4; i += bd) {
-            const float4 v0 = x4[i];
-            s0 = fmaf(v0.x, v0.x, fmaf(v0.y, v0.y, fmaf(v0.z, v0.z, fmaf(v0.w, v0.w, s0))));
-        }
-    } else {
-        for (int i = threadIdx.x; i < a.k; i += bd) s0 = fmaf(xr[i], xr[i], s0);
-    }
-    float s = warp_sum((s0 + s1) + (s2 + s3));
+    float s0 = 0.0f;
+    for (int i = threadIdx.x; i < a.k; i += blockDim.x) s0 = fmaf(xr[i], xr[i], s0);
+    float s = warp_sum(s0);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();
     float tot = 0.0f;
@@ -69,28 +51,14 @@ M27B_DI float act_value(const ActArgs &a, const float *xr, const float *gr, int 
     return v;
 }
 
-// grid (ceil(nblocks/8), n_tok), block 256: warp w of CTA c quantizes
-// super-block 8c + w of token blockIdx.y.
-template <int MODE>
-__global__ void __launch_bounds__(256) k_act_quant_q8K(ActArgs a) {
-    pdl_trigger();
-    pdl_wait();  // x is produced by the previous kernel
-    const int t = blockIdx.y;
-    const float *xr = a.x + (size_t)t * a.ldx;
-    const float *gr = a.gate ? a.gate + (size_t)t * a.ldx : nullptr;
-    const float ns = row_norm_scale<MODE>(a, xr);
-    const int nb = a.k / 256;
-    const int lane = threadIdx.x & 31;
-    const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (b >= nb) return;
-    m27b_block_q8_K *ob = (m27b_block_q8_K *)a.out + (size_t)t * nb + b;
-
-    float v[8];
+// ggml q8_K of one super-block, 8 values per lane (lane l holds values
+// 8l..8l+7): m = signed value of largest |x| (first one on ties),
+// iscale = -127/m, q = min(127, rne(iscale*x)), d = 1/iscale, bsums of 16.
+M27B_DI void quant_q8K_warp(const float (&v)[8], int lane, m27b_block_q8_K *ob) {
     float best_a = 0.0f, best_v = 0.0f;
     int best_i = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        v[j] = act_value<MODE>(a, xr, gr, b * 256 + lane * 8 + j, ns);
         const float av = fabsf(v[j]);
         if (av > best_a) { best_a = av; best_v = v[j]; best_i = lane * 8 + j; }
     }
@@ -125,6 +93,158 @@ __global__ void __launch_bounds__(256) k_act_quant_q8K(ActArgs a) {
     if (lane == 0) ob->d = d;
 }
 
+// grid (ceil(nblocks/8), n_tok), block 256: warp w of CTA c quantizes
+// super-block 8c + w of token blockIdx.y.
+template <int MODE>
+__global__ void __launch_bounds__(256) k_act_quant_q8K(ActArgs a) {
+    pdl_trigger();
+    pdl_wait();  // x is produced by the previous kernel
+    const int t = blockIdx.y;
+    const float *xr = a.x + (size_t)t * a.ldx;
+    const float *gr = a.gate ? a.gate + (size_t)t * a.ldx : nullptr;
+    const float ns = row_norm_scale<MODE>(a, xr);
+    const int nb = a.k / 256;
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (b >= nb) return;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = act_value<MODE>(a, xr, gr, b * 256 + lane * 8 + j, ns);
+    quant_q8K_warp(v, lane, (m27b_block_q8_K *)a.out + (size_t)t * nb + b);
+}
+
+// RMSNorm(x) * w -> q8_K with the row staged once in shared memory: every
+// value is read from global memory once (all loads issued up front), the sum
+// of squares reduced over the CTA, and each warp quantizes a super-block from
+// shared memory.  grid (ceil(nblocks/8), n_tok), block 256.
+constexpr int NQ_MAX_K = 16384;  // largest row staged in shared memory (64 KB)
+constexpr int M27B_MAX_SRC = 8;   // most source ranks of the fused all-reduce
+
+__global__ void __launch_bounds__(256) k_norm_quant_q8K(ActArgs a) {
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float red[8];
+    pdl_trigger();
+    pdl_wait();  // x is produced by the previous kernel
+    const int t = blockIdx.y;
+    const float4 *x4 = (const float4 *)(a.x + (size_t)t * a.ldx);
+    float4 *xs4 = (float4 *)xs;
+    const int n4 = a.k >> 2;
+    float ss = 0.0f;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += 256) {
+        const float4 v = x4[i];
+        xs4[i] = v;
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+    ss = warp_sum(ss);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += red[w];
+    const float ns = 1.0f / sqrtf(tot / (float)a.k + a.eps);
+    const int nb = a.k / 256;
+    const int b = blockIdx.x * 8 + warp;
+    if (b >= nb) return;
+    float v[8];
+    const float4 *p = (const float4 *)(xs + b * 256 + lane * 8);
+    const float4 p0 = p[0], p1 = p[1];
+    const float raw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        float u = raw[j] * ns;
+        if (a.w) u = u * a.w[b * 256 + lane * 8 + j];
+        v[j] = u;
+    }
+    quant_q8K_warp(v, lane, (m27b_block_q8_K *)a.out + (size_t)t * nb + b);
+}
+
+// Consumer half of the fused all-reduce (ACT_RMSNORM_SUM): grid k/256, block
+// 256; CTA b owns super-block b, thread i value 256b + i.  Each thread reads
+// its value's word from every source rank (all loads in flight), re-reads any
+// word whose epoch has not arrived yet (bounded), and sums them in rank order.
+// The CTA's sum of squares goes to ss_words[b] as an epoch-tagged word; every
+// CTA waits for all of them and adds them in CTA order, so every CTA (and
+// every rank) computes the same norm.  Then warp 0 quantizes the super-block.
+// The words order everything this kernel reads and writes against the
+// producing matvec (which has staged its activations and read its residual
+// before storing a row), so it does not wait for that grid to retire: it
+// starts once the grid has triggered, when every producer CTA is resident.
+// It triggers its own dependents at once; they launch only after all of its
+// CTAs are resident, so none of them can be starved of an SM.
+__global__ void __launch_bounds__(256) k_allreduce_norm_quant_q8K(ActArgs a) {
+    __shared__ __align__(16) float xs[256];
+    __shared__ float red[8];
+    __shared__ float css[256];
+    pdl_trigger();
+    const uint32_t ep = *a.epoch_base * a.epoch_mul + a.epoch_add;
+    const int b = blockIdx.x, nb = gridDim.x, i = b * 256 + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint2 w[M27B_MAX_SRC];
+#pragma unroll
+    for (int s = 0; s < M27B_MAX_SRC; ++s)
+        if (s < a.nsrc) w[s] = ld_word(a.words + (size_t)s * a.src_stride + i);
+    float v = 0.0f;
+#pragma unroll
+    for (int s = 0; s < M27B_MAX_SRC; ++s)
+        if (s < a.nsrc) {
+            w[s] = wait_word(a.words + (size_t)s * a.src_stride + i, w[s], ep, a.status, 3);
+            v = s == 0 ? __uint_as_float(w[s].x) : v + __uint_as_float(w[s].x);
+        }
+    a.x_out[i] = v;
+    xs[threadIdx.x] = v;
+    const float sq = warp_sum(v * v);
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float c = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) c += red[k];
+        st_word(a.ss_words + b, __float_as_uint(c), ep);
+    }
+    if ((int)threadIdx.x < nb) {
+        const uint2 *q = a.ss_words + threadIdx.x;
+        css[threadIdx.x] = __uint_as_float(wait_word(q, ld_word(q), ep, a.status, 3).x);
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    float tot = 0.0f;
+    for (int k = 0; k < nb; ++k) tot += css[k];
+    const float ns = 1.0f / sqrtf(tot / (float)a.k + a.eps);
+    const float4 *p = (const float4 *)(xs + lane * 8);
+    const float4 p0 = p[0], p1 = p[1];
+    const float raw[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    float q[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        float u = raw[j] * ns;
+        if (a.w) u = u * a.w[b * 256 + lane * 8 + j];
+        q[j] = u;
+    }
+    quant_q8K_warp(q, lane, (m27b_block_q8_K *)a.out + b);
+}
+
+bool norm_quant_staged(const ActArgs &a) {
+    return a.k <= NQ_MAX_K && (a.k & 3) == 0 && (a.ldx & 3) == 0 && ((uintptr_t)a.x & 15) == 0;
+}
+
+cudaError_t launch_norm_quant(const ActArgs &a, int n_tok, cudaStream_t st) {
+    const int nb = a.k / 256;
+    const dim3 grid((nb + 7) / 8, n_tok);
+    const size_t smem = (size_t)a.k * sizeof(float);
+    static bool opted[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (smem > 48 * 1024 && (dev >= 64 || !opted[dev])) {
+        e = cudaFuncSetAttribute(k_norm_quant_q8K, cudaFuncAttributeMaxDynamicSharedMemorySize, NQ_MAX_K * 4);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) opted[dev] = true;
+    }
+    return launch_pdl(k_norm_quant_q8K, grid, dim3(256), smem, st, a);
+}
+
 // grid (ceil(nblocks/8), n_tok), block 256: warp w of CTA c quantizes q8_0
 // block 8c + w (32 values, one per lane).
 template <int MODE>
@@ -156,8 +276,16 @@ cudaError_t launch_act_quant(int act_type, int mode, const ActArgs &a, int n_tok
     if (act_type == M27B_TYPE_Q8_K) {
         if (mode == ACT_PLAIN) return launch_pdl(k_act_quant_q8K<ACT_PLAIN>, grid, dim3(256), 0, st, a);
         if (mode == ACT_GATED) return launch_pdl(k_act_quant_q8K<ACT_GATED>, grid, dim3(256), 0, st, a);
+        if (mode == ACT_RMSNORM_SUM) {
+            if (n_tok != 1 || a.nsrc < 1 || a.nsrc > M27B_MAX_SRC || !a.words || !a.ss_words || !a.epoch_base ||
+                !a.x_out || nb > 256)
+                return cudaErrorInvalidValue;
+            return launch_pdl(k_allreduce_norm_quant_q8K, dim3(nb), dim3(256), 0, st, a);
+        }
+        if (norm_quant_staged(a)) return launch_norm_quant(a, n_tok, st);
         return launch_pdl(k_act_quant_q8K<ACT_RMSNORM>, grid, dim3(256), 0, st, a);
     }
+    if (mode == ACT_RMSNORM_SUM) return cudaErrorInvalidValue;
     if (mode == ACT_PLAIN) return launch_pdl(k_act_quant_q80<ACT_PLAIN>, grid, dim3(256), 0, st, a);
     if (mode == ACT_GATED) return launch_pdl(k_act_quant_q80<ACT_GATED>, grid, dim3(256), 0, st, a);
     return launch_pdl(k_act_quant_q80<ACT_RMSNORM>, grid, dim3(256), 0, st, a);

@@ -16,11 +16,11 @@ using namespace m27b;
 
 // Library status word, one per device: kernels set it non-zero when one of
 // their bounded waits runs out (1: a stage never filled, 2: draining after
-// such a failure).  Read and cleared with m27b_device_status().
+// such a failure, 3: a rank's all-reduce partial never arrived, 4: a rank's
+// argmax key never arrived).  Read and cleared with m27b_device_status().
 __device__ int g_m27b_status;
 
-namespace {
-
+namespace m27b {
 int *status_ptr_current() {
     static int *cache[64] = {nullptr};
     int dev = 0;
@@ -31,6 +31,9 @@ int *status_ptr_current() {
     if (dev < 64) cache[dev] = (int *)p;
     return (int *)p;
 }
+}  // namespace m27b
+
+namespace {
 
 bool fail(char *err, size_t cap, const char *fmt, ...) {
     if (err && cap) {
@@ -139,7 +142,7 @@ bool act_quant_common(int mode, const float *x, const float *gate, const float *
 
 bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void *xq, int n_tok, float *y, int ldy,
                 const float *residual, unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
-                size_t cap, const char *what) {
+                size_t cap, const char *what, const PushArgs *push = nullptr) {
     WDesc d0{}, d1{};
     if (!describe(w0, d0, what, err, cap)) return false;
     if (epi == EPI_SWIGLU) {
@@ -150,7 +153,14 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
     if (!xq) return fail(err, cap, "%s: null activation pointer", what);
     if (n_tok < 1 || n_tok > M27B_MAX_TOKENS)
         return fail(err, cap, "%s: n_tok must be in [1, %d] (got %d)", what, M27B_MAX_TOKENS, n_tok);
-    if (epi != EPI_ARGMAX && !y) return fail(err, cap, "%s: null output", what);
+    if (epi == EPI_PUSH) {
+        if (!push || push->npeers < 1 || push->npeers > M27B_MAX_PEERS || !push->epoch_base)
+            return fail(err, cap, "%s: bad push descriptor", what);
+        if (n_tok != 1) return fail(err, cap, "%s: the fused all-reduce takes one token", what);
+        if (d0.kind == W_Q80P) return fail(err, cap, "%s: the fused all-reduce takes q4_K or q6_K weights", what);
+    } else if (epi != EPI_ARGMAX && !y) {
+        return fail(err, cap, "%s: null output", what);
+    }
     if (epi == EPI_ARGMAX && !best) return fail(err, cap, "%s: null argmax output", what);
     if ((y || residual) && ldy < (int)w0->row_count && n_tok > 1)
         return fail(err, cap, "%s: ldy (%d) < row_count (%u)", what, ldy, w0->row_count);
@@ -185,6 +195,7 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         a.passes = d0.passes;
         a.row_offset = row_offset;
         a.status = status;
+        if (push) a.push = *push;
         cudaError_t e = launch_qmv(d0.kind, epi, a, nt, sms, stream);
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
     }
@@ -192,6 +203,16 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
 }
 
 }  // namespace
+
+namespace m27b {
+// Matvec whose rows go to every rank's receive window (fused all-reduce,
+// producer side); used by the tensor-parallel decode engine.
+bool qmv_push(const WeightView *w, const void *xq, const float *residual, const PushArgs &push, cudaStream_t stream,
+              char *err, size_t cap) {
+    return qmv_common(EPI_PUSH, w, nullptr, xq, 1, nullptr, (int)(w ? w->row_count : 0), residual, nullptr, 0, stream,
+                      err, cap, "qmv_push", &push);
+}
+}  // namespace m27b
 
 extern "C" {
 

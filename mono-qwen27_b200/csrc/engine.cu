@@ -20,6 +20,7 @@
 #include "m27b_device.cuh"
 #include "m27b_engine.h"
 #include "m27b_launch.cuh"
+#include "qmv_kernels.cuh"
 
 namespace m27b {
 __global__ void k_qk_norm_rope_cache(const float *qkv, const float *q_norm, const float *k_norm, float *q, float *gate,
@@ -32,6 +33,15 @@ __global__ void k_fill_blocks(uint8_t *out, int type, int rows, int nblk, long r
                               float sigma);
 __global__ void k_fill_f32(float *out, long n, float v);
 __global__ void k_advance(const unsigned long long *best, int *ctl, int *hist, int cap);
+struct BestExchange {
+    uint2 *dst[8];
+    const uint2 *slots;
+    int npeers;
+    int *status;
+};
+__global__ void k_advance_p2p(unsigned long long *best, int *ctl, int *hist, int cap, BestExchange b);
+bool qmv_push(const WeightView *w, const void *xq, const float *residual, const PushArgs &push, cudaStream_t stream,
+              char *err, size_t cap);
 }  // namespace m27b
 
 using namespace m27b;
@@ -66,6 +76,31 @@ bool efail(char *err, size_t cap, const char *fmt, ...) {
 
 size_t block_bytes(uint32_t t) { return t == M27B_TYPE_Q4_K ? 144 : t == M27B_TYPE_Q6_K ? 210 : t == M27B_TYPE_Q8_0 ? 34 : 0; }
 int block_elems(uint32_t t) { return t == M27B_TYPE_Q8_0 ? 32 : 256; }
+
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// Receive window of the fused all-reduce (same layout on every rank), in
+// epoch-tagged 8-byte words {value bits, epoch}:
+//   recv  [2 parities][N source ranks][hidden]  partial rows
+//   ss    [2 parities][hidden / 256]             the consumer CTAs' sums of squares
+//   best  [N][2]                                 argmax keys (low word, high word)
+// o_proj uses parity 0 and ffn_down parity 1, so a rank that runs one
+// all-reduce ahead never overwrites words a slower rank is still reading.
+struct WinLayout {
+    size_t recv, ss, best, total;
+};
+WinLayout win_layout(int N, int hidden) {
+    WinLayout w;
+    size_t off = 0;
+    w.recv = off;
+    off = align256(off + (size_t)2 * N * hidden * sizeof(uint2));
+    w.ss = off;
+    off = align256(off + (size_t)2 * (hidden / 256) * sizeof(uint2));
+    w.best = off;
+    off = align256(off + (size_t)N * 2 * sizeof(uint2));
+    w.total = off;
+    return w;
+}
 
 // A quantized matrix resident on the device (repacked when its type needs it).
 struct QMat {
@@ -110,6 +145,10 @@ struct M27BEngine {
     cudaStream_t st = nullptr;
     cudaGraphExec_t gexec = nullptr;
     ncclComm_t comm = nullptr;
+    // fused all-reduce over NVLink (m27b_engine_enable_p2p)
+    bool p2p = false;
+    uint8_t *win = nullptr;         // this rank's receive window (exported by CUDA IPC)
+    uint8_t *peer_win[8] = {};      // every rank's window as mapped here (own: win)
     std::vector<void *> allocs;
 };
 
@@ -215,17 +254,58 @@ bool allreduce_hidden(M27BEngine *e, float *buf, char *err, size_t err_cap) {
     return true;
 }
 
+// Producer half of the fused all-reduce: rows of `m` (+ residual) to every
+// rank's window, parity `par`, instance `idx` of the step.
+PushArgs push_args(M27BEngine *e, int par, unsigned idx) {
+    const int N = e->c.tp_size, r = e->c.tp_rank;
+    const WinLayout lay = win_layout(N, e->c.hidden);
+    PushArgs p{};
+    for (int q = 0; q < N; ++q) p.dst[q] = (uint2 *)(e->peer_win[q] + lay.recv) + ((size_t)par * N + r) * e->c.hidden;
+    p.epoch_base = (const unsigned *)(e->ctl + 3);
+    p.epoch_mul = 2u * (unsigned)e->c.n_layers;
+    p.epoch_add = idx + 1u;
+    p.npeers = N;
+    return p;
+}
+
+// Consumer half: every rank's rows of parity `par`, summed in rank order into
+// x_out (the replicated hidden state), then RMSNorm with `norm_w` and q8_K
+// for the next matvec.
+bool consume(M27BEngine *e, int par, unsigned idx, const float *norm_w, float *x_out, char *err, size_t err_cap) {
+    const int N = e->c.tp_size;
+    const WinLayout lay = win_layout(N, e->c.hidden);
+    ActArgs a{};
+    a.w = norm_w;
+    a.eps = e->c.rms_eps;
+    a.k = e->c.hidden;
+    a.ldx = e->c.hidden;
+    a.out = e->xq;
+    a.words = (const uint2 *)(e->win + lay.recv) + (size_t)par * N * e->c.hidden;
+    a.nsrc = N;
+    a.src_stride = e->c.hidden;
+    a.ss_words = (uint2 *)(e->win + lay.ss) + (size_t)par * (e->c.hidden / 256);
+    a.epoch_base = (const unsigned *)(e->ctl + 3);
+    a.epoch_mul = 2u * (unsigned)e->c.n_layers;
+    a.epoch_add = idx + 1u;
+    a.x_out = x_out;
+    a.status = status_ptr_current();
+    if (!a.status) return efail(err, err_cap, "cannot resolve the device status word");
+    ECUDA(launch_act_quant(M27B_TYPE_Q8_K, ACT_RMSNORM_SUM, a, 1, e->st));
+    return true;
+}
+
 // Enqueue one decode step on e->st (token / position read from device memory).
 bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
     const M27BModelConfig &c = e->c;
     const int hd = c.head_dim;
     const bool r0 = c.tp_rank == 0;
+    const bool p2p = e->p2p;
     const int *pos = e->ctl + 1;
     ECALL(m27b_dequant_rows(&e->embd.v, e->ctl, 1, e->h, c.hidden, e->st, err, err_cap));
+    ECALL(m27b_act_quant_rmsnorm(e->h, e->L[0].attn_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq,
+                                 e->st, err, err_cap));
     for (int l = 0; l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
-        ECALL(m27b_act_quant_rmsnorm(e->h, Ly.attn_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq, e->st,
-                                     err, err_cap));
         ECALL(mv(e, Ly.wqkv, e->xq, e->qkv, nullptr, err, err_cap));
         ECUDA(launch_pdl(k_qk_norm_rope_cache, dim3(e->H + e->KV), dim3(hd), (size_t)(hd + 32) * 4, e->st,
                          (const float *)e->qkv, (const float *)Ly.q_norm, (const float *)Ly.k_norm, e->q, e->gate, Ly.kc,
@@ -233,23 +313,47 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         ECUDA(attn_launch(e->q, Ly.kc, Ly.vc, e->part, e->o, pos, e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd),
                           e->st));
         ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, 1, e->H * hd, M27B_TYPE_Q8_K, e->xq, e->st, err, err_cap));
-        // o_proj partial (+ residual on rank 0), summed over ranks -> h2
-        ECALL(mv(e, Ly.wo, e->xq, e->h2, r0 ? e->h : nullptr, err, err_cap));
-        ECALL(allreduce_hidden(e, e->h2, err, err_cap));
-        ECALL(m27b_act_quant_rmsnorm(e->h2, Ly.post_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq,
-                                     e->st, err, err_cap));
+        // o_proj partial (+ residual on rank 0), summed over ranks -> h2, then post-attention RMSNorm -> xq
+        if (p2p) {
+            ECALL(qmv_push(&Ly.wo.v, e->xq, r0 ? e->h : nullptr, push_args(e, 0, 2u * l), e->st, err, err_cap));
+            ECALL(consume(e, 0, 2u * l, Ly.post_norm, e->h2, err, err_cap));
+        } else {
+            ECALL(mv(e, Ly.wo, e->xq, e->h2, r0 ? e->h : nullptr, err, err_cap));
+            ECALL(allreduce_hidden(e, e->h2, err, err_cap));
+            ECALL(m27b_act_quant_rmsnorm(e->h2, Ly.post_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq,
+                                         e->st, err, err_cap));
+        }
         ECALL(m27b_qmv_swiglu(&Ly.wg.v, &Ly.wu.v, e->xq, 1, e->a, e->F, e->st, err, err_cap));
         ECALL(m27b_act_quant(e->a, e->F, 1, e->F, M27B_TYPE_Q8_K, e->xq, e->st, err, err_cap));
-        // down partial (+ residual on rank 0), summed over ranks -> h
-        ECALL(mv(e, Ly.wd, e->xq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
-        ECALL(allreduce_hidden(e, e->h, err, err_cap));
+        // down partial (+ residual on rank 0), summed over ranks -> h, then the
+        // next layer's input RMSNorm (the output norm after the last layer) -> xq
+        const float *next_norm = l + 1 < c.n_layers ? e->L[l + 1].attn_norm : e->out_norm;
+        if (p2p) {
+            ECALL(qmv_push(&Ly.wd.v, e->xq, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), e->st, err, err_cap));
+            ECALL(consume(e, 1, 2u * l + 1u, next_norm, e->h, err, err_cap));
+        } else {
+            ECALL(mv(e, Ly.wd, e->xq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
+            ECALL(allreduce_hidden(e, e->h, err, err_cap));
+            ECALL(m27b_act_quant_rmsnorm(e->h, next_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq, e->st,
+                                         err, err_cap));
+        }
     }
-    ECALL(m27b_act_quant_rmsnorm(e->h, e->out_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq, e->st, err,
-                                 err_cap));
     ECALL(m27b_qmv_argmax(&e->lmh.v, e->xq, 1, e->logits, e->V, e->best, (uint32_t)e->v_lo, e->st, err, err_cap));
-    if (c.tp_size > 1) ENCCL(ncclAllReduce(e->best, e->best, 1, ncclUint64, ncclMax, e->comm, e->st));
     // next token and position for the following step (greedy generation on the device)
-    k_advance<<<1, 32, 0, e->st>>>(e->best, e->ctl, e->hist, c.max_ctx);
+    if (p2p) {
+        const int N = c.tp_size, r = c.tp_rank;
+        const WinLayout lay = win_layout(N, c.hidden);
+        BestExchange b{};
+        for (int q = 0; q < N; ++q) b.dst[q] = (uint2 *)(e->peer_win[q] + lay.best) + 2 * r;
+        b.slots = (const uint2 *)(e->win + lay.best);
+        b.npeers = N;
+        b.status = status_ptr_current();
+        if (!b.status) return efail(err, err_cap, "cannot resolve the device status word");
+        k_advance_p2p<<<1, 32, 0, e->st>>>(e->best, e->ctl, e->hist, c.max_ctx, b);
+    } else {
+        if (c.tp_size > 1) ENCCL(ncclAllReduce(e->best, e->best, 1, ncclUint64, ncclMax, e->comm, e->st));
+        k_advance<<<1, 32, 0, e->st>>>(e->best, e->ctl, e->hist, c.max_ctx);
+    }
     ECUDA(cudaGetLastError());
     return true;
 }
@@ -258,8 +362,8 @@ bool set_ctl(M27BEngine *e, int token, int pos, char *err, size_t err_cap) {
     e->h_ctl[0] = token;
     e->h_ctl[1] = pos;
     e->h_ctl[2] = 0;
-    e->h_ctl[3] = 0;
-    ECUDA(cudaMemcpyAsync(e->ctl, e->h_ctl, 16, cudaMemcpyHostToDevice, e->st));
+    // ctl[3] (the step counter, the fused all-reduce's epoch) is left alone
+    ECUDA(cudaMemcpyAsync(e->ctl, e->h_ctl, 12, cudaMemcpyHostToDevice, e->st));
     return true;
 }
 
@@ -404,6 +508,7 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
         ok = A((void **)&e->L[l].kc, kvb) && A((void **)&e->L[l].vc, kvb) &&
              cudaMemset(e->L[l].kc, 0, kvb) == cudaSuccess && cudaMemset(e->L[l].vc, 0, kvb) == cudaSuccess;
     }
+    ok = ok && cudaMemset(e->ctl, 0, 16) == cudaSuccess;
     if (!ok) return bail(efail(err, err_cap, "%s", e2));
     if (cudaMallocHost((void **)&e->h_ctl, 16) != cudaSuccess || cudaMallocHost((void **)&e->h_best, 8) != cudaSuccess ||
         cudaMallocHost((void **)&e->h_hist, (size_t)c.max_ctx * 4) != cudaSuccess)
@@ -421,6 +526,56 @@ bool m27b_engine_set_nccl(M27BEngine *e, const void *id, char *err, size_t err_c
     ncclUniqueId u;
     std::memcpy(&u, id, sizeof(u));
     ENCCL(ncclCommInitRank(&e->comm, e->c.tp_size, u, e->c.tp_rank));
+    if (err && err_cap) err[0] = '\0';
+    return true;
+}
+
+bool m27b_engine_enable_p2p(M27BEngine *e, char *err, size_t err_cap) {
+    if (!e) return efail(err, err_cap, "m27b_engine_enable_p2p: null engine");
+    const int N = e->c.tp_size, r = e->c.tp_rank;
+    if (N < 2) return efail(err, err_cap, "m27b_engine_enable_p2p: tp_size is 1");
+    if (N > 8) return efail(err, err_cap, "m27b_engine_enable_p2p: at most 8 ranks");
+    if (!e->comm) return efail(err, err_cap, "m27b_engine_enable_p2p: call m27b_engine_set_nccl first");
+    if (e->gexec) return efail(err, err_cap, "m27b_engine_enable_p2p: call it before the first decode step");
+    if (e->p2p) return efail(err, err_cap, "m27b_engine_enable_p2p: already enabled");
+    const WinLayout lay = win_layout(N, e->c.hidden);
+    ECUDA(cudaMalloc(&e->win, lay.total));
+    ECUDA(cudaMemset(e->win, 0, lay.total));  // epochs start at 1: a zero word is "nothing yet"
+    // every rank's IPC handle, gathered over the NCCL communicator
+    cudaIpcMemHandle_t mine;
+    ECUDA(cudaIpcGetMemHandle(&mine, e->win));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    uint8_t *dh = nullptr;
+    ECUDA(cudaMalloc(&dh, (size_t)N * 64));
+    std::vector<uint8_t> all((size_t)N * 64);
+    bool ok = cudaMemcpyAsync(dh + (size_t)r * 64, &mine, 64, cudaMemcpyHostToDevice, e->st) == cudaSuccess &&
+              ncclAllGather(dh + (size_t)r * 64, dh, 64, ncclUint8, e->comm, e->st) == ncclSuccess &&
+              cudaMemcpyAsync(all.data(), dh, all.size(), cudaMemcpyDeviceToHost, e->st) == cudaSuccess &&
+              cudaStreamSynchronize(e->st) == cudaSuccess;
+    cudaFree(dh);
+    if (!ok) return efail(err, err_cap, "m27b_engine_enable_p2p: exchanging IPC handles failed");
+    for (int q = 0; q < N; ++q) {
+        if (q == r) {
+            e->peer_win[q] = e->win;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + (size_t)q * 64, 64);
+        void *p = nullptr;
+        const cudaError_t ie = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (ie != cudaSuccess)
+            return efail(err, err_cap, "m27b_engine_enable_p2p: mapping rank %d's window: %s", q, cudaGetErrorString(ie));
+        e->peer_win[q] = (uint8_t *)p;
+    }
+    // every rank has mapped every window before any rank stores into one
+    int *one = nullptr;
+    ECUDA(cudaMalloc(&one, sizeof(int)));
+    ok = cudaMemsetAsync(one, 0, sizeof(int), e->st) == cudaSuccess &&
+         ncclAllReduce(one, one, 1, ncclInt32, ncclSum, e->comm, e->st) == ncclSuccess &&
+         cudaStreamSynchronize(e->st) == cudaSuccess;
+    cudaFree(one);
+    if (!ok) return efail(err, err_cap, "m27b_engine_enable_p2p: barrier failed");
+    e->p2p = true;
     if (err && err_cap) err[0] = '\0';
     return true;
 }
@@ -606,6 +761,9 @@ void m27b_engine_destroy(M27BEngine *e) {
     if (!e) return;
     if (e->st) cudaStreamSynchronize(e->st);
     if (e->gexec) cudaGraphExecDestroy(e->gexec);  // before the communicator it holds
+    for (int q = 0; q < 8; ++q)
+        if (e->peer_win[q] && e->peer_win[q] != e->win) cudaIpcCloseMemHandle(e->peer_win[q]);
+    if (e->win) cudaFree(e->win);
     if (e->comm) ncclCommDestroy(e->comm);
     for (void *p : e->allocs) cudaFree(p);
     if (e->scratch) cudaFree(e->scratch);

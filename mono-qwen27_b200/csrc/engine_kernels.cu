@@ -318,7 +318,7 @@ __global__ void k_fill_blocks(uint8_t *out, int type, int rows, int nblk, long r
 
 // End of a decode step: the argmax key becomes the next step's token, the
 // position advances, and the token is appended to hist (greedy generation
-// without a host round trip).  ctl = [token, pos, count].
+// without a host round trip).  ctl = [token, pos, count, step].
 __global__ void k_advance(const unsigned long long *best, int *ctl, int *hist, int cap) {
     if (threadIdx.x != 0) return;
     const int next = (int)(0xffffffffu - (uint32_t)(*best & 0xffffffffull));
@@ -327,6 +327,44 @@ __global__ void k_advance(const unsigned long long *best, int *ctl, int *hist, i
     ctl[0] = next;
     ctl[1] += 1;
     ctl[2] = c + 1;
+    ctl[3] += 1;
+}
+
+// Tensor-parallel variant of k_advance: exchange the ranks' argmax keys over
+// NVLink as two epoch-tagged words per rank (each rank stores its key into
+// slot `rank` of every rank's window), wait for every rank's key (bounded),
+// and take the largest.  ctl[3] counts steps.
+struct BestExchange {
+    uint2 *dst[8];       // slot `rank` ([2] words) in every rank's window
+    const uint2 *slots;  // this rank's slots [npeers][2]
+    int npeers;
+    int *status;
+};
+
+__global__ void k_advance_p2p(unsigned long long *best, int *ctl, int *hist, int cap, BestExchange b) {
+    if (threadIdx.x != 0) return;
+    const uint32_t ep = (uint32_t)ctl[3] + 1u;
+    const unsigned long long key = *best;
+    for (int p = 0; p < b.npeers; ++p) {
+        st_word(b.dst[p], (uint32_t)key, ep);
+        st_word(b.dst[p] + 1, (uint32_t)(key >> 32), ep);
+    }
+    unsigned long long m = 0ull;
+    for (int s = 0; s < b.npeers; ++s) {
+        const uint2 *q = b.slots + 2 * s;
+        const uint2 lo = wait_word(q, ld_word(q), ep, b.status, 4);
+        const uint2 hi = wait_word(q + 1, ld_word(q + 1), ep, b.status, 4);
+        const unsigned long long v = ((unsigned long long)hi.x << 32) | lo.x;
+        m = v > m ? v : m;
+    }
+    *best = m;  // the global key, as the NCCL max all-reduce leaves it
+    const int next = (int)(0xffffffffu - (uint32_t)(m & 0xffffffffull));
+    const int c = ctl[2];
+    if (c < cap) hist[c] = next;
+    ctl[0] = next;
+    ctl[1] += 1;
+    ctl[2] = c + 1;
+    ctl[3] += 1;
 }
 
 __global__ void k_fill_f32(float *out, long n, float v) {

@@ -73,4 +73,73 @@ M27B_DI unsigned long long argmax_key(float v, uint32_t idx) {
 M27B_DI void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 M27B_DI void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ---- bounded waits and cross-GPU signalling ----
+constexpr unsigned long long M27B_WAIT_NS = 2000000000ull;  // 2 s bound on any wait
+
+M27B_DI unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+M27B_DI unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+M27B_DI void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+M27B_DI void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// ---- epoch-tagged words ----
+// A value travels with its epoch in one aligned 8-byte word {bits, epoch},
+// written by a single 8-byte store and read by a single 8-byte load, so a
+// reader sees either the old word or the new one, never a mix: a word whose
+// epoch matches is complete, and no fence or separate flag is needed.  Reads
+// bypass L1 (the word is rewritten by another SM or another GPU).
+M27B_DI void st_word(uint2 *p, uint32_t bits, uint32_t ep) {
+    asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(bits), "r"(ep) : "memory");
+}
+M27B_DI uint2 ld_word(const uint2 *p) {
+    uint2 w;
+    asm volatile("ld.global.cv.v2.b32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
+    return w;
+}
+// Re-read *p until its epoch is `ep`, for at most M27B_WAIT_NS (or until an
+// earlier wait has failed: *status non-zero); on failure record `code` and
+// return the last word read.
+M27B_DI uint2 wait_word(const uint2 *p, uint2 w, uint32_t ep, int *status, int code) {
+    if (w.y == ep) return w;
+    const unsigned long long t0 = global_ns();
+    for (unsigned it = 0;; ++it) {
+        w = ld_word(p);
+        if (w.y == ep) return w;
+        if ((it & 31u) == 31u &&
+            (global_ns() - t0 > M27B_WAIT_NS || (status && *(volatile int *)status != 0))) {
+            if (status) atomicCAS(status, 0, code);
+            return w;
+        }
+    }
+}
+
+// Wait (acquire, system scope) until the monotonic counter *f reaches epoch
+// `ep` (wrap-safe compare), for at most M27B_WAIT_NS.  On timeout, or when
+// *status is already non-zero (an earlier wait gave up), record `code` and
+// return false instead of waiting.
+M27B_DI bool wait_epoch_sys(const unsigned *f, unsigned ep, int *status, int code) {
+    if ((int)(ld_acquire_sys(f) - ep) >= 0) return true;
+    const unsigned long long t0 = global_ns();
+    for (unsigned it = 0;; ++it) {
+        if ((int)(ld_acquire_sys(f) - ep) >= 0) return true;
+        if ((it & 63u) == 63u) {
+            if (global_ns() - t0 > M27B_WAIT_NS || (status && *(volatile int *)status != 0)) {
+                if (status) atomicCAS(status, 0, code);
+                return false;
+            }
+        }
+        __nanosleep(64);
+    }
+}
+
 }  // namespace m27b

@@ -63,8 +63,6 @@ inline size_t blk_smem_for(int nwarps, int k, int nt) {
 inline size_t blk_smem_bytes(int k, int nt) { return blk_smem_for(blk_warps(k, nt), k, nt); }
 
 // ---- mbarrier + bulk-copy helpers (sm_90+ PTX; no cluster multicast) ----
-constexpr unsigned long long M27B_WAIT_NS = 2000000000ull;  // 2 s bound on any wait
-
 M27B_DI uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 M27B_DI void mbar_init(uint64_t *bar, uint32_t count) {
@@ -106,12 +104,6 @@ M27B_DI bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "r"(smem_u32(bar)), "r"(parity), "r"(20000)
         : "memory");
     return ok != 0;
-}
-
-M27B_DI unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 
 // Wait for the phase with the given parity to complete, for at most
@@ -354,6 +346,8 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
                 const float s0 = acc[0][t];
                 if constexpr (EPI == EPI_STORE) {
                     a.y[o] = a.residual ? s0 + a.residual[o] : s0;
+                } else if constexpr (EPI == EPI_PUSH) {
+                    push_row(a.push, o, a.residual ? s0 + a.residual[o] : s0);
                 } else if constexpr (EPI == EPI_SWIGLU) {
                     a.y[o] = s0 / (1.0f + expf(-s0)) * acc[NM - 1][t];
                 } else {
@@ -381,11 +375,10 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
                 __syncthreads();
                 __syncthreads();
             }
-        return;
     }
 
     if constexpr (EPI == EPI_ARGMAX) {
-        if (qd == 0) {
+        if (ok && qd == 0) {
 #pragma unroll
             for (int t = 0; t < NT; ++t)
                 if (best[t] != 0ull) atomicMax(a.best + t, best[t]);

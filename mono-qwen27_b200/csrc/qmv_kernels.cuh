@@ -10,7 +10,20 @@ constexpr int QMV_WARPS = 8;
 constexpr int QMV_THREADS = QMV_WARPS * 32;
 
 enum WeightKind { W_Q4K = 0, W_Q6KP = 1, W_Q80P = 2 };
-enum Epilogue { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ARGMAX = 2 };
+enum Epilogue { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ARGMAX = 2, EPI_PUSH = 3 };
+
+// EPI_PUSH: the matvec half of a fused matvec + all-reduce over NVLink.  Row
+// r of token t (plus the residual, if any) goes, as the epoch-tagged word
+// {value, epoch}, to dst[p][t * ldy + r] for every rank p < npeers (dst[p]
+// lies in rank p's receive window, mapped into this process).  The consumer
+// polls the words themselves; nothing else signals completion.
+constexpr int M27B_MAX_PEERS = 8;
+struct PushArgs {
+    uint2 *dst[M27B_MAX_PEERS];
+    const unsigned *epoch_base;  // epoch = *epoch_base * epoch_mul + epoch_add
+    unsigned epoch_mul, epoch_add;
+    int npeers;
+};
 
 struct QmvArgs {
     const uint8_t *w0;         // weight rows (gate for SWIGLU)
@@ -28,7 +41,16 @@ struct QmvArgs {
     int segs;                  // units per row = ceil(passes / PS)
     uint32_t row_offset;       // added to argmax indices
     int *status;               // device status word: set non-zero if a bounded wait runs out
+    PushArgs push;             // EPI_PUSH only
 };
+
+// EPI_PUSH row store: one epoch-tagged value to every rank's receive window.
+M27B_DI void push_row(const PushArgs &p, size_t o, float v) {
+    const uint32_t ep = *p.epoch_base * p.epoch_mul + p.epoch_add;
+#pragma unroll
+    for (int i = 0; i < M27B_MAX_PEERS; ++i)
+        if (i < p.npeers) st_word(p.dst[i] + o, __float_as_uint(v), ep);
+}
 
 // Planar view of the staged activations in shared memory.
 struct XStage {

@@ -73,6 +73,7 @@ cudaError_t run_qmv_format<W_Q4K>(int epi, int nt, const QmvArgs &a, int sm_coun
     case EPI_STORE: return run_blk_nt<EPI_STORE>(nt, a, sm_count, st);
     case EPI_SWIGLU: return run_blk_nt<EPI_SWIGLU>(nt, a, sm_count, st);
     case EPI_ARGMAX: return run_blk_nt<EPI_ARGMAX>(nt, a, sm_count, st);
+    case EPI_PUSH: return nt == 1 ? run_blk<1, EPI_PUSH>(a, sm_count, st) : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
     }
 }

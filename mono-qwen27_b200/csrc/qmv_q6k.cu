@@ -76,6 +76,7 @@ cudaError_t run_qmv_format<W_Q6KP>(int epi, int nt, const QmvArgs &a, int sm_cou
     case EPI_STORE: return run_q6t_nt<EPI_STORE>(nt, a, sm_count, st);
     case EPI_SWIGLU: return run_q6t_nt<EPI_SWIGLU>(nt, a, sm_count, st);
     case EPI_ARGMAX: return run_q6t_nt<EPI_ARGMAX>(nt, a, sm_count, st);
+    case EPI_PUSH: return nt == 1 ? run_q6t<1, EPI_PUSH>(a, sm_count, st) : cudaErrorInvalidValue;
     default: return cudaErrorInvalidValue;
     }
 }

@@ -281,6 +281,8 @@ __global__ void __launch_bounds__(Q6T_WARPS * 32, 2)
                 const float s0 = fin[0][t];
                 if constexpr (EPI == EPI_STORE) {
                     a.y[o] = a.residual ? s0 + a.residual[o] : s0;
+                } else if constexpr (EPI == EPI_PUSH) {
+                    push_row(a.push, o, a.residual ? s0 + a.residual[o] : s0);
                 } else if constexpr (EPI == EPI_SWIGLU) {
                     a.y[o] = s0 / (1.0f + expf(-s0)) * fin[NM - 1][t];
                 } else {
@@ -310,10 +312,9 @@ __global__ void __launch_bounds__(Q6T_WARPS * 32, 2)
                 __syncthreads();
                 __syncthreads();
             }
-        return;
     }
     if constexpr (EPI == EPI_ARGMAX) {
-        if (lane < 8) {
+        if (ok && lane < 8) {
 #pragma unroll
             for (int t = 0; t < NT; ++t)
                 if (best[t] != 0ull) atomicMax(a.best + t, best[t]);

@@ -292,6 +292,7 @@ def _engine_lib():
         "m27b_nccl_unique_id": (b, [vp, cp, sz]),
         "m27b_engine_create": (b, [ctypes.POINTER(ModelConfig), ctypes.POINTER(vp), cp, sz]),
         "m27b_engine_set_nccl": (b, [vp, vp, cp, sz]),
+        "m27b_engine_enable_p2p": (b, [vp, cp, sz]),
         "m27b_engine_load_tensor": (b, [vp, cp, u32, u32, u32, vp, cp, sz]),
         "m27b_engine_random_weights": (b, [vp, ctypes.c_uint64, ctypes.c_float, cp, sz]),
         "m27b_engine_weight_bytes_per_token": (sz, [vp]),
@@ -341,6 +342,10 @@ class Engine:
     def set_nccl(self, uid):
         buf = ctypes.create_string_buffer(bytes(uid), 128)
         self._call("m27b_engine_set_nccl", self.h, buf)
+
+    def enable_p2p(self):
+        """Fused NVLink all-reduce instead of NCCL (tp_size > 1; after set_nccl)."""
+        self._call("m27b_engine_enable_p2p", self.h)
 
     def load_tensor(self, name, ggml_type, row_elems, row_count, data):
         import numpy as np
