@@ -178,8 +178,10 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long) * (size_t)n_tok, stream);
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
     }
+    // 5..16 tokens of a q4_K matrix: one pass on the tensor cores
+    const bool mma = d0.kind == W_Q4K && epi == EPI_STORE && q4k_mma_supported((int)w0->row_blocks, n_tok);
     for (int t0 = 0; t0 < n_tok; t0 += 4) {
-        const int nt = n_tok - t0 < 4 ? n_tok - t0 : 4;
+        const int nt = mma ? n_tok : (n_tok - t0 < 4 ? n_tok - t0 : 4);
         QmvArgs a{};
         a.w0 = (const uint8_t *)w0->ptr;
         a.w1 = epi == EPI_SWIGLU ? (const uint8_t *)w1->ptr : nullptr;
@@ -196,8 +198,9 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         a.row_offset = row_offset;
         a.status = status;
         if (push) a.push = *push;
-        cudaError_t e = launch_qmv(d0.kind, epi, a, nt, sms, stream);
+        cudaError_t e = mma ? launch_q4k_mma(a, nt, sms, stream) : launch_qmv(d0.kind, epi, a, nt, sms, stream);
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
+        if (mma) break;
     }
     return ok(err, cap);
 }

@@ -409,5 +409,8 @@ inline int pick_ps(int P, int cap) {
 
 size_t qmv_smem_bytes(int wtype, int k, int ntok);
 cudaError_t launch_qmv(int wt, int epi, QmvArgs a, int nt, int sm_count, cudaStream_t st);
+// q4_K x 5..16 tokens on the tensor cores (qmv_q4k_mma.cu), store epilogue.
+bool q4k_mma_supported(int rb, int n_tok);
+cudaError_t launch_q4k_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st);
 
 }  // namespace m27b

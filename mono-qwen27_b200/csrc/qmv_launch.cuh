@@ -12,8 +12,8 @@ namespace m27b {
 size_t qmv_smem_bytes(int wtype, int k, int ntok);
 
 // Tensor map over weight rows viewed as [rows][row_bytes/4] uint32 with a box
-// of 8 rows x box_u32 words (one TMA copy per (8-row group, tile)).
-bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows, int box_u32);
+// of box_rows rows x box_u32 words (one TMA copy per (row group, tile)).
+bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows, int box_u32, int box_rows = 8);
 
 template <int WT, int NT, int EPI, int PS>
 cudaError_t run_qmv(const QmvArgs &a, int sm_count, cudaStream_t st) {
