@@ -61,9 +61,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=None)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg3", "decode"], default="cfg0")
+    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "decode"], default="cfg0")
     p.add_argument("--rows", type=int, default=None, help="override the row count (smaller profiling cases)")
-    p.add_argument("--ntok", type=int, default=1, help="tokens per step (cfg3)")
+    p.add_argument("--ntok", type=int, default=None, help="tokens per matvec (cfg2: 16, cfg3: 1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-decode", action="store_true", help="skip the whole-model decode figures of the default line")
     p.add_argument("--prompt", type=int, default=512, help="decode: prompt tokens before generation")
@@ -73,7 +73,9 @@ def parse_args():
                    help="decode, N>1: fused NVLink all-reduce (p2p) or NCCL all-reduce")
     a = p.parse_args()
     if a.steps is None:
-        a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg3": 8000, "decode": a.gen}[a.workload]
+        a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg2": 20000, "cfg3": 8000, "decode": a.gen}[a.workload]
+    if a.ntok is None:
+        a.ntok = 16 if a.workload == "cfg2" else 1
     return a
 
 
@@ -166,27 +168,38 @@ class Workload:
         gen = np.random.default_rng(7 + rank)
         w = args.workload
         self.name = w
-        if w == "cfg0":
+        if w in ("cfg0", "cfg2"):
+            n = args.ntok if w == "cfg2" else 1
             rows, k, copies = args.rows or 17408, 5120, 6
             self.host_w0 = random_valid_blocks(Q4_K, rows, k, 1000 * rank)
             self.W = [m27b.QWeight(self.host_w0 if c == 0 else random_valid_blocks(Q4_K, rows, k, 1000 * rank + c),
                                    Q4_K, k, rows) for c in range(copies)]
-            self.x = [torch.from_numpy(gen.standard_normal((1, k)).astype(np.float32)).to(dev) for _ in range(copies)]
-            self.xq = [torch.empty(m27b.act_bytes(Q8_K, k), dtype=torch.uint8, device=dev) for _ in range(copies)]
-            self.y = [torch.empty((1, rows), dtype=torch.float32, device=dev) for _ in range(copies)]
-            self.mv_bytes = wbytes(Q4_K, rows, k) + k * 4 + rows * 4
+            self.x = [torch.from_numpy(gen.standard_normal((n, k)).astype(np.float32)).to(dev) for _ in range(copies)]
+            self.xq = [torch.empty(n * m27b.act_bytes(Q8_K, k), dtype=torch.uint8, device=dev) for _ in range(copies)]
+            self.y = [torch.empty((n, rows), dtype=torch.float32, device=dev) for _ in range(copies)]
+            self.mv_bytes = wbytes(Q4_K, rows, k) + n * (k * 4 + rows * 4)
             self.step_bytes = copies * self.mv_bytes
-            self.metric = "q4_K matvec HBM GB/s"
-            self.config = {"workload": f"cfg0: q4_K matvec {rows}x{k}, batch 1, q8_K activations", "rows": rows, "k": k,
-                           "matvecs_per_step": copies, "bytes_per_matvec": self.mv_bytes,
-                           "l2": f"inputs larger than L2: {copies} rotating weight matrices "
-                                 f"({copies * wbytes(Q4_K, rows, k) / 1e6:.0f} MB)"}
-            self.kernel = "k_qmv_q4k_blk<1,STORE>"
-            self.profile = "qmv_q4K_cfg0.md"
+            self.n = n
+            l2 = f"inputs larger than L2: {copies} rotating weight matrices ({copies * wbytes(Q4_K, rows, k) / 1e6:.0f} MB)"
+            if w == "cfg0":
+                self.metric = "q4_K matvec HBM GB/s"
+                self.config = {"workload": f"cfg0: q4_K matvec {rows}x{k}, batch 1, q8_K activations", "rows": rows,
+                               "k": k, "matvecs_per_step": copies, "bytes_per_matvec": self.mv_bytes, "l2": l2}
+                self.kernel = "k_qmv_q4k_blk<1,STORE>"
+                self.profile = "qmv_q4K_cfg0.md"
+            else:
+                self.metric = f"q4_K verify matvec HBM GB/s ({n} tokens)"
+                self.config = {"workload": f"cfg2: q4_K matvec {rows}x{k}, {n} tokens per matvec, q8_K activations",
+                               "rows": rows, "k": k, "ntok": n, "matvecs_per_step": copies,
+                               "bytes_per_matvec": self.mv_bytes, "l2": l2,
+                               "int_ops_per_matvec": 2 * rows * k * n}
+                self.kernel = ("k_qmv_q4k_mma<%d> (tcgen05 kind::i8)" % (8 if n <= 8 else 16)) if n >= 5 else \
+                    "k_qmv_q4k_blk<%d,STORE>" % n
+                self.profile = "qmv_q4K_mma_cfg2.md"
             self.launches_per_step = 2 * copies
             self.copies, self.rows, self.k = copies, rows, k
-            self.h2d = copies * k * 4
-            self.d2h = copies * rows * 4
+            self.h2d = copies * n * k * 4
+            self.d2h = copies * n * rows * 4
         elif w == "cfg1":
             rows, k = args.rows or 248320, 5120
             self.W = [m27b.QWeight(random_valid_blocks(Q6_K, rows, k, 2 + 1000 * rank), Q6_K, k, rows)]
@@ -204,6 +217,7 @@ class Workload:
             self.launches_per_step = 2
             self.copies, self.rows, self.k = 1, rows, k
             self.h2d, self.d2h = k * 4, rows * 4 + 8
+            self.n = 1
         else:  # cfg3
             H, F, n = 5120, args.rows or 17408, args.ntok
             self.sets = []
@@ -231,7 +245,8 @@ class Workload:
             self.hh = [x.cpu().pin_memory() for x in self.h]
             self.oh = [torch.empty((n, H), dtype=torch.float32).pin_memory() for _ in range(2)]
             self.h2d, self.d2h = 2 * n * H * 4, 2 * n * H * 4
-        if w in ("cfg0", "cfg1"):
+            self.n = n
+        if w in ("cfg0", "cfg1", "cfg2"):
             self.xh = [x.cpu().pin_memory() for x in self.x]
             self.yh = [torch.empty_like(y, device="cpu").pin_memory() for y in self.y]
 
@@ -240,7 +255,7 @@ class Workload:
         if self.name == "cfg1":
             m.qmv_argmax(self.W[c], self.xq[c], 1, self.best, logits=self.y[c])
         else:
-            m.qmv(self.W[c], self.xq[c], 1, self.y[c])
+            m.qmv(self.W[c], self.xq[c], self.n, self.y[c])
 
     def step(self):
         m = self.m27b

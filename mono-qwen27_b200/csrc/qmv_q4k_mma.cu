@@ -11,32 +11,31 @@
 // and y += d*dx*isum - dmin*dx*msum in fp32.
 //
 // Mapping onto the tensor cores.  One MMA of shape M=128 rows x N tokens x
-// K=32 is exactly one q4_K sub-block.  The 6-bit scale cannot multiply the
-// 4-bit weights inside an 8-bit operand (up to 945), so each sub-block is
-// split into two 8-bit planes, q4 * (sc >> 3) and q4 * (sc & 7) (at most 105:
-// a plain 32-bit multiply of four packed nibbles by the small factor forms
-// them without carries between bytes).  The 16 MMAs of a super-block (8
-// sub-blocks x 2 planes) accumulate into two TMEM accumulators D_hi, D_lo,
-// and isum = 8 * D_hi + D_lo exactly.  The min term uses dp2a against the
-// activation's bsums on the CUDA cores.
+// K=32 is exactly one q4_K sub-block: A = the sub-block's 4-bit values as
+// bytes, B = the tokens' q8 codes, D = the 32-term integer dot products of
+// every (row, token), each sub-block into its own TMEM accumulator.  The
+// epilogue applies the 6-bit scales in integers (isum = sum_s sc_s * D_s,
+// exactly ggml's), the min term with dp2a against the activation's bsums, and
+// the fp16/fp32 block scales.  The A operand lives in TMEM: the thread that
+// owns a row writes its bytes into its own TMEM lane (tcgen05.st), so the
+// narrow MMAs (N = 8 or 16) do not re-read a 4 KB A tile from shared memory.
 //
-// Pipeline per CTA (one 128-row tile at a time, persistent over tiles; one
-// CTA per SM):
-//   * TMA streams one raw 128-row x 144-byte block column per stage (2-D
-//     tensor map, no multicast) into a ring of stages;
-//   * the activations (all K, all tokens) are staged once in the canonical
-//     K-major no-swizzle UMMA layout, with their scales and bsum pairs;
-//   * work advances in half-blocks (4 sub-blocks): all 256 threads unpack a
-//     half-block into one of two A buffers (32 KB each: 4 sub-blocks x 2
-//     planes x 128 rows x 32 bytes), one thread issues its 8 MMAs and
-//     commits them to that buffer's mbarrier; the next half-block is
-//     unpacked into the other buffer meanwhile;
-//   * D accumulators are double-buffered per block: the epilogue of block b
-//     (tcgen05.ld of D_hi / D_lo, one row per thread, eight tokens per
-//     thread) runs while block b + 1 is in the tensor cores.
-// Every wait is bounded (2 s); a timeout records status 5, the CTA leaves
-// together, waits (bounded) for its own copies and MMAs, frees its TMEM and
-// returns.
+// Pipeline per CTA (one 128-row tile at a time, persistent over tiles, one
+// CTA per SM), warp-specialized and synchronised only by mbarriers:
+//   * warp 8 issues: TMA copies of one raw 128-row x 144-byte block column per
+//     stage (2-D tensor map, no multicast), and, per half-block (4
+//     sub-blocks), the 4 MMAs plus a commit;
+//   * warps 0-7 unpack a half-block into one of two TMEM A buffers, and run
+//     the epilogue of the previous block (tcgen05.ld of its 8 accumulators,
+//     one row per thread, eight tokens per thread);
+//   * hand-offs: stage full (TMA) -> stage empty (the unpacking warps have
+//     read it), A buffer full -> MMAs done (the buffer is free again and the
+//     block's accumulators are final), accumulators free (epilogue read).
+// The activations (all K, all tokens) are staged once per CTA in the
+// canonical K-major no-swizzle UMMA layout, with their scales and bsum
+// pairs.  Every wait is bounded (2 s); a timeout records status 5 and raises
+// the CTA's abort flag, every role leaves its loop, the issuing thread waits
+// (bounded) for its own copies and MMAs, and the CTA frees its TMEM.
 #include "qmv_blk.cuh"
 #include "m27b_launch.cuh"
 #include "qmv_launch.cuh"
@@ -44,21 +43,23 @@
 namespace m27b {
 
 constexpr int MMA_ROWS = 128;
-constexpr int MMA_THREADS = 256;
-constexpr int MMA_RAW_BYTES = MMA_ROWS * 144;  // one TMA box: 128 rows x one q4_K block
-constexpr int MMA_ABUF = 8 * 4096;             // 4 sub-blocks x 2 planes x 4 KB
-constexpr int MMA_TMEM_COLS = 64;              // 2 blocks x (D_hi, D_lo) x 16 columns
+constexpr int MMA_WORKERS = 256;                 // warps 0-7: unpack + epilogue
+constexpr int MMA_THREADS = MMA_WORKERS + 32;    // warp 8: TMA + MMA issue
+constexpr int MMA_RAW_BYTES = MMA_ROWS * 144;    // one TMA box: 128 rows x one q4_K block
+constexpr int MMA_TMEM_COLS = 512;               // D: 2 blocks x 8 sub-blocks x 16; A: 2 x 32
+constexpr int MMA_ACOL = 256;                    // first TMEM column of the A buffers
+constexpr int MMA_NA = 2;                        // A buffers (half-blocks the unpacking may run ahead)
 constexpr size_t MMA_SMEM_LIMIT = 227 * 1024;
 
 struct MmaLayout {
-    size_t b, dx, bs, raw, bar, tslot, total;
+    size_t b, dx, bs, raw, bar, flag, total;
     int stages;
 };
 
 // Shared memory plan for K = 256 * rb values and an MMA N of nb_tok (8 or 16).
 __host__ __device__ inline MmaLayout mma_layout(int rb, int nb_tok, int stages) {
     MmaLayout L;
-    size_t off = 2 * (size_t)MMA_ABUF;                       // two A buffers
+    size_t off = 0;
     L.b = off;
     off += (size_t)rb * 8 * nb_tok * 32;                     // codes, UMMA layout
     L.dx = off;
@@ -68,9 +69,9 @@ __host__ __device__ inline MmaLayout mma_layout(int rb, int nb_tok, int stages) 
     off = (off + 127) & ~(size_t)127;
     L.raw = off;
     off += (size_t)stages * MMA_RAW_BYTES;
-    L.bar = off;
-    off += (size_t)(stages + 2) * 8;
-    L.tslot = off;
+    L.bar = off;  // full[stages], empty[stages], a_full[NA], mma_done[NA], d_free[2], drain
+    off += (size_t)(2 * stages + 2 * MMA_NA + 3) * 8;
+    L.flag = off;  // abort flag, TMEM address slot
     off += 16;
     L.total = off;
     L.stages = stages;
@@ -96,13 +97,13 @@ M27B_DI void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 M27B_DI void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 M27B_DI void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, s8 x s8 -> s32, one thread.
-M27B_DI void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, s8 x s8 -> s32, one thread.
+M27B_DI void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
         : "memory");
 }
 // The MMAs issued so far by this thread arrive on `bar` when they complete.
@@ -118,6 +119,14 @@ M27B_DI void tmem_ld8(uint32_t taddr, int (&v)[8]) {
                  : "memory");
 }
 M27B_DI void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Eight consecutive 32-bit TMEM columns of this thread's lane.
+M27B_DI void tmem_st8(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, uint32_t v4, uint32_t v5,
+                      uint32_t v6, uint32_t v7) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v0),
+                 "r"(v1), "r"(v2), "r"(v3), "r"(v4), "r"(v5), "r"(v6), "r"(v7)
+                 : "memory");
+}
+M27B_DI void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: K-major, no swizzle, core matrices of
 // 8 rows x 16 bytes; 128 bytes between the two 16-byte K halves of a 32-byte
@@ -134,23 +143,50 @@ constexpr uint32_t umma_idesc_i8() {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(MMA_ROWS >> 4) << 24);
 }
 
+M27B_DI void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait that gives up at once when the CTA's abort flag is raised, and
+// raises it (recording status 5) when its own 2 s run out.
+M27B_DI bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort, int *status) {
+    if (*abort) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 8; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > M27B_WAIT_NS) {
+            *abort = 1;
+            if (status) atomicCAS(status, 0, 5);
+            return false;
+        }
+    }
+}
+
 template <int NB>
 __global__ void __launch_bounds__(MMA_THREADS, 1)
     k_qmv_q4k_mma(const QmvArgs a, const __grid_constant__ CUtensorMap tm, int n_tok, int stages) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int r = tid & (MMA_ROWS - 1);  // row of the tile (TMEM lane)
-    const int h = tid >> 7;              // which half of the work on that row
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool issuer_warp = warp == 8;
+    const int r = tid & (MMA_ROWS - 1);  // workers: row of the tile (TMEM lane)
+    const int h = (tid >> 7) & 1;        // workers: which half of the row's work
     const int rb = a.rb;
     const MmaLayout L = mma_layout(rb, NB, stages);
-    uint8_t *abuf = smem;
     uint8_t *bsm = smem + L.b;
     float *dxs = (float *)(smem + L.dx);
     int4 *bss = (int4 *)(smem + L.bs);
     uint8_t *raw = smem + L.raw;
     uint64_t *full = (uint64_t *)(smem + L.bar);
-    uint64_t *mma_bar = full + stages;  // [2]: one per A buffer
-    uint32_t *tslot = (uint32_t *)(smem + L.tslot);
+    uint64_t *empty = full + stages;
+    uint64_t *a_full = empty + stages;      // [MMA_NA]
+    uint64_t *mma_done = a_full + MMA_NA;   // [MMA_NA]
+    uint64_t *d_free = mma_done + MMA_NA;   // [2]
+    uint64_t *drain = d_free + 2;
+    volatile int *abort = (volatile int *)(smem + L.flag);
+    uint32_t *tslot = (uint32_t *)(smem + L.flag + 8);
 
     const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS;
     const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -158,7 +194,18 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     const int J = 2 * nblk;          // half-block items
 
     if (tid == 0) {
-        for (int s = 0; s < stages + 2; ++s) mbar_init(&full[s], 1);
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 8);
+        }
+        for (int b = 0; b < MMA_NA; ++b) {
+            mbar_init(&a_full[b], 8);
+            mbar_init(&mma_done[b], 1);
+        }
+        mbar_init(&d_free[0], 8);
+        mbar_init(&d_free[1], 8);
+        mbar_init(drain, 1);
+        *abort = 0;
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -169,7 +216,6 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    // raw block columns go out first: the weights do not depend on the previous kernel
     auto issue_block = [&](int bi) {
         const int tl = bi / rb, k = bi - tl * rb;
         const int row0 = ((int)blockIdx.x + tl * (int)gridDim.x) * MMA_ROWS;
@@ -178,8 +224,9 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
         mbar_arrive_expect_tx(b, MMA_RAW_BYTES);
         tma_load_2d(raw + (size_t)(bi % stages) * MMA_RAW_BYTES, &tm, k * 36, row0, b);
     };
+    // the first raw block columns go out at once: weights do not depend on the previous kernel
     int issued = 0;
-    if (tid == 0)
+    if (issuer_warp && lane == 0)
         for (; issued < stages && issued < nblk; ++issued) issue_block(issued);
 
     // activations: codes into the UMMA layout (tokens >= n_tok are zero),
@@ -222,153 +269,169 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     fence_proxy_async();  // the codes are read by the tensor cores (async proxy)
     __syncthreads();
 
-    constexpr uint32_t idesc = umma_idesc_i8<NB>();
-    const uint32_t a_base = smem_u32(abuf), b_base = smem_u32(bsm);
-    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-    const bool epi_thread = NB == 16 || h == 0;
-
-    float acc[8];
+    if (issuer_warp) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_i8<NB>();
+            const uint32_t b_base = smem_u32(bsm);
+            for (int j = 0; j < J; ++j) {
+                const int bi = j >> 1, q = j & 1, ab = j % MMA_NA, db = bi & 1;
+                // a block's first MMAs overwrite accumulators whose epilogue (block bi - 2) is done
+                if (q == 0 && bi >= 2 && !wait_or_abort(&d_free[db], (uint32_t)(((bi - 2) >> 1) & 1), abort, a.status))
+                    break;
+                if (!wait_or_abort(&a_full[ab], (uint32_t)((j / MMA_NA) & 1), abort, a.status)) break;
+                tc_fence_after();
+                const int k = bi % rb;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    // scales of the block being unpacked and of the previous one (its epilogue)
-    float cur_d = 0.0f, cur_dm = 0.0f, prev_d = 0.0f, prev_dm = 0.0f;
-    uint32_t cur_m03 = 0, cur_m47 = 0, prev_m03 = 0, prev_m47 = 0, sc03 = 0, sc47 = 0;
-
-    // epilogue of block item bi (its MMAs have completed)
-    auto epilogue = [&](int bi) {
-        const int tl = bi / rb, k = bi - tl * rb;
-        if (epi_thread) {
-            int dh[8], dl[8];
-            const uint32_t col = (uint32_t)((bi & 1) * 32 + (NB == 16 ? 8 * h : 0));
-            tmem_ld8(tmem + lane_base + col, dh);
-            tmem_ld8(tmem + lane_base + col + 16, dl);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int t = (NB == 16 ? 8 * h : 0) + i;
-                const int4 bs = bss[t * rb + k];
-                int msum = __dp2a_lo(bs.x, (int)prev_m03, 0);
-                msum = __dp2a_hi(bs.y, (int)prev_m03, msum);
-                msum = __dp2a_lo(bs.z, (int)prev_m47, msum);
-                msum = __dp2a_hi(bs.w, (int)prev_m47, msum);
-                const int isum = dh[i] * 8 + dl[i];
-                const float dx = dxs[t * rb + k];
-                acc[i] = fmaf(prev_d * dx, (float)isum, acc[i]);
-                acc[i] = fmaf(-(prev_dm * dx), (float)msum, acc[i]);
+                for (int s = 0; s < 4; ++s) {
+                    const uint64_t bd = umma_desc(b_base + (uint32_t)((k * 8 + 4 * q + s) * NB * 32));
+                    umma_i8_ts(tmem + (uint32_t)(db * 128 + (4 * q + s) * 16),
+                               tmem + (uint32_t)(MMA_ACOL + ab * 32 + s * 8), bd, idesc, 0u);
+                }
+                umma_commit(&mma_done[ab]);
+                // the block's raw stage, once every worker warp has read it, takes block bi + stages
+                if (q == 1 && issued < nblk) {
+                    if (!wait_or_abort(&empty[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) break;
+                    issue_block(issued++);
+                }
             }
+            // drain: every MMA issued above, and every copy still in flight (bounded, even after an abort)
+            umma_commit(drain);
+            mbar_wait_bounded(drain, 0u, a.status, 5);
+            for (int bi = issued - stages < 0 ? 0 : issued - stages; bi < issued; ++bi)
+                mbar_wait_bounded(&full[bi % stages], (uint32_t)((bi / stages) & 1), a.status, 5);
         }
-        if (k == rb - 1) {  // the tile's last block: write its rows
-            const int row = ((int)blockIdx.x + tl * (int)gridDim.x) * MMA_ROWS + r;
-            if (epi_thread && row < a.rows) {
+        __syncwarp();
+    } else {
+        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        const bool epi_thread = NB == 16 || h == 0;
+        const int toff = NB == 16 ? 8 * h : 0;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+        // scales of the block being unpacked and of the previous one (its epilogue)
+        float cur_d = 0.0f, cur_dm = 0.0f, prev_d = 0.0f, prev_dm = 0.0f;
+        uint32_t sc03 = 0, sc47 = 0, cur_m03 = 0, cur_m47 = 0;
+        uint32_t psc03 = 0, psc47 = 0, prev_m03 = 0, prev_m47 = 0;
+
+        auto epilogue = [&](int bi) {
+            const int tl = bi / rb, k = bi - tl * rb;
+            if (epi_thread) {
+                int v[8][8];
+                const uint32_t dcol = tmem + lane_base + (uint32_t)((bi & 1) * 128 + toff);
+#pragma unroll
+                for (int s = 0; s < 8; ++s) tmem_ld8(dcol + (uint32_t)(s * 16), v[s]);
+                tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const int t = (NB == 16 ? 8 * h : 0) + i;
-                    if (t < n_tok) {
-                        const size_t o = (size_t)t * a.ldy + row;
-                        a.y[o] = a.residual ? acc[i] + a.residual[o] : acc[i];
+                    int isum = 0;
+#pragma unroll
+                    for (int s = 0; s < 8; ++s) {
+                        const int sc = (int)(((s < 4 ? psc03 : psc47) >> (8 * (s & 3))) & 0xffu);
+                        isum += sc * v[s][i];
+                    }
+                    const int t = toff + i;
+                    const int4 bs = bss[t * rb + k];
+                    int msum = __dp2a_lo(bs.x, (int)prev_m03, 0);
+                    msum = __dp2a_hi(bs.y, (int)prev_m03, msum);
+                    msum = __dp2a_lo(bs.z, (int)prev_m47, msum);
+                    msum = __dp2a_hi(bs.w, (int)prev_m47, msum);
+                    const float dx = dxs[t * rb + k];
+                    acc[i] = fmaf(prev_d * dx, (float)isum, acc[i]);
+                    acc[i] = fmaf(-(prev_dm * dx), (float)msum, acc[i]);
+                }
+            }
+            if (k == rb - 1) {  // the tile's last block: write its rows
+                const int row = ((int)blockIdx.x + tl * (int)gridDim.x) * MMA_ROWS + r;
+                if (epi_thread && row < a.rows) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int t = toff + i;
+                        if (t < n_tok) {
+                            const size_t o = (size_t)t * a.ldy + row;
+                            a.y[o] = a.residual ? acc[i] + a.residual[o] : acc[i];
+                        }
                     }
                 }
-            }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-        }
-    };
-
-    bool ok = true;
-    int waited = 0;  // block items whose raw stage has been waited for
-    int j = 0;
-    for (; j < J; ++j) {
-        const int bi = j >> 1, q = j & 1, ab = j & 1;
-        bool landed = true;
-        if (q == 0) {
-            landed = mbar_wait_bounded(&full[bi % stages], (uint32_t)((bi / stages) & 1), a.status, 5);
-            if (landed) ++waited;
-        }
-        if (j >= 2) landed = mbar_wait_bounded(&mma_bar[ab], (uint32_t)(((j - 2) >> 1) & 1), a.status, 5) && landed;
-        // unpack qs group g = 2q + h of row r: low nibbles are sub-block 2g, high 2g+1
-        const uint8_t *rw = raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144;
-        if (q == 0) {
-            const uint4 hd = *(const uint4 *)rw;
+                for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+            }
+        };
+        auto shift_scales = [&]() {
             prev_d = cur_d;
             prev_dm = cur_dm;
             prev_m03 = cur_m03;
             prev_m47 = cur_m47;
-            cur_d = h2f(hd.x);
-            cur_dm = h2f(hd.x >> 16);
-            sc03 = hd.y & 0x3f3f3f3fu;
-            cur_m03 = hd.z & 0x3f3f3f3fu;
-            sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
-            cur_m47 = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
-        }
-        {
-            const int g = 2 * q + h;
-            const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
-            const uint32_t nib[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            const uint32_t scw = g < 2 ? sc03 : sc47;
-            const int sh = 16 * (g & 1);
-            uint8_t *dst0 = abuf + (size_t)ab * MMA_ABUF + (size_t)(r >> 3) * 256 + (r & 7) * 16;
-#pragma unroll
-            for (int part = 0; part < 2; ++part) {  // 0: low nibbles (sub-block 2g), 1: high (2g+1)
-                const uint32_t sc = (scw >> (sh + 8 * part)) & 0xffu;
-                const uint32_t fh = sc >> 3, fl = sc & 7u;
-                const int sl = 2 * h + part;  // sub-block within the half-block
-                uint32_t qv[8];
-#pragma unroll
-                for (int w = 0; w < 8; ++w) qv[w] = part ? (nib[w] >> 4) & 0x0f0f0f0fu : nib[w] & 0x0f0f0f0fu;
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    *(uint4 *)(dst0 + (size_t)(0 * 4 + sl) * 4096 + c * 128) =
-                        make_uint4(qv[4 * c] * fh, qv[4 * c + 1] * fh, qv[4 * c + 2] * fh, qv[4 * c + 3] * fh);
-                    *(uint4 *)(dst0 + (size_t)(1 * 4 + sl) * 4096 + c * 128) =
-                        make_uint4(qv[4 * c] * fl, qv[4 * c + 1] * fl, qv[4 * c + 2] * fl, qv[4 * c + 3] * fl);
+            psc03 = sc03;
+            psc47 = sc47;
+        };
+
+        bool ok = true;
+        for (int j = 0; j < J; ++j) {
+            const int bi = j >> 1, q = j & 1, ab = j % MMA_NA;
+            if (q == 0 && !wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) {
+                ok = false;
+                break;
+            }
+            // A buffer ab is free once the MMAs of half-block j - MMA_NA are done
+            if (j >= MMA_NA &&
+                !wait_or_abort(&mma_done[ab], (uint32_t)(((j - MMA_NA) / MMA_NA) & 1), abort, a.status)) {
+                ok = false;
+                break;
+            }
+            const uint8_t *rw = raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144;
+            if (q == 0) {
+                const uint4 hd = *(const uint4 *)rw;
+                shift_scales();
+                cur_d = h2f(hd.x);
+                cur_dm = h2f(hd.x >> 16);
+                sc03 = hd.y & 0x3f3f3f3fu;
+                cur_m03 = hd.z & 0x3f3f3f3fu;
+                sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
+                cur_m47 = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
+            }
+            {
+                // qs group g = 2q + h of row r: low nibbles are sub-block 2g, high 2g+1,
+                // i.e. sub-blocks 2h and 2h + 1 of the half-block
+                const int g = 2 * q + h;
+                const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
+                const uint32_t acol = tmem + lane_base + (uint32_t)(MMA_ACOL + ab * 32 + 2 * h * 8);
+                tmem_st8(acol, qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu, qa.w & 0x0f0f0f0fu,
+                         qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu, qb.w & 0x0f0f0f0fu);
+                tmem_st8(acol + 8, (qa.x >> 4) & 0x0f0f0f0fu, (qa.y >> 4) & 0x0f0f0f0fu, (qa.z >> 4) & 0x0f0f0f0fu,
+                         (qa.w >> 4) & 0x0f0f0f0fu, (qb.x >> 4) & 0x0f0f0f0fu, (qb.y >> 4) & 0x0f0f0f0fu,
+                         (qb.z >> 4) & 0x0f0f0f0fu, (qb.w >> 4) & 0x0f0f0f0fu);
+                tmem_wait_st();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&a_full[ab]);
+                if (q == 1) mbar_arrive(&empty[bi % stages]);  // this warp is done with the raw stage
+            }
+            if (q == 1 && bi >= 1) {
+                // block bi - 1: its last half-block's MMAs (half-block j - 2)
+                if (!wait_or_abort(&mma_done[(j - 2) % MMA_NA], (uint32_t)(((j - 2) / MMA_NA) & 1), abort, a.status)) {
+                    ok = false;
+                    break;
                 }
+                tc_fence_after();
+                epilogue(bi - 1);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&d_free[(bi - 1) & 1]);
             }
         }
-        if (q == 1 && bi >= 1) {
-            tc_fence_after();
-            epilogue(bi - 1);
-        }
-        fence_proxy_async();
-        tc_fence_before();
-        ok = __syncthreads_and(landed) != 0;
-        if (!ok) break;
-        if (tid == 0) {
-            tc_fence_after();
-            if (q == 1 && issued < nblk) issue_block(issued++);  // this raw stage has been read
-            const uint32_t d_hi = tmem + (uint32_t)((bi & 1) * 32), d_lo = d_hi + 16;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const int k = bi % rb;
-                const uint64_t bd = umma_desc(b_base + (uint32_t)((k * 8 + 4 * q + s) * NB * 32));
-                const uint32_t acc_in = (q > 0 || s > 0) ? 1u : 0u;
-                umma_i8(d_hi, umma_desc(a_base + (uint32_t)(ab * MMA_ABUF + (0 * 4 + s) * 4096)), bd, idesc, acc_in);
-                umma_i8(d_lo, umma_desc(a_base + (uint32_t)(ab * MMA_ABUF + (1 * 4 + s) * 4096)), bd, idesc, acc_in);
+        if (ok && nblk > 0) {
+            // the last block: its two half-blocks' MMAs, then its epilogue
+            const bool done =
+                wait_or_abort(&mma_done[(J - 2) % MMA_NA], (uint32_t)(((J - 2) / MMA_NA) & 1), abort, a.status) &&
+                wait_or_abort(&mma_done[(J - 1) % MMA_NA], (uint32_t)(((J - 1) / MMA_NA) & 1), abort, a.status);
+            if (done) {
+                shift_scales();
+                tc_fence_after();
+                epilogue(nblk - 1);
             }
-            umma_commit(&mma_bar[ab]);
         }
-    }
-
-    if (ok) {
-        // the last two half-blocks' MMAs, then the last block's epilogue
-        bool landed = true;
-        if (J >= 2) landed = mbar_wait_bounded(&mma_bar[(J - 2) & 1], (uint32_t)(((J - 2) >> 1) & 1), a.status, 5);
-        if (J >= 1) landed = mbar_wait_bounded(&mma_bar[(J - 1) & 1], (uint32_t)(((J - 1) >> 1) & 1), a.status, 5) && landed;
-        if (__syncthreads_and(landed) && nblk > 0) {
-            // the last block's scales moved to prev_* only when a next block began
-            prev_d = cur_d;
-            prev_dm = cur_dm;
-            prev_m03 = cur_m03;
-            prev_m47 = cur_m47;
-            tc_fence_after();
-            epilogue(nblk - 1);
-        }
-    } else if (tid == 0) {
-        // a wait ran out: let this CTA's copies and MMAs finish (bounded) before
-        // its shared memory and TMEM are released
-        for (int bi = waited; bi < issued; ++bi)
-            mbar_wait_bounded(&full[bi % stages], (uint32_t)((bi / stages) & 1), a.status, 5);
-        if (j >= 2) mbar_wait_bounded(&mma_bar[j & 1], (uint32_t)(((j - 2) >> 1) & 1), a.status, 5);
-        if (j >= 1) mbar_wait_bounded(&mma_bar[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), a.status, 5);
     }
     tc_fence_before();
     __syncthreads();
