@@ -27,6 +27,11 @@ __global__ void k_qk_norm_rope_cache(const float *qkv, const float *q_norm, cons
                                      float *kc, float *vc, const int *pos_p, int nq, int nkv, int hd, int n_rot,
                                      float theta, float eps);
 cudaError_t attn_prepare();
+bool attn_fused_supported(int hd);
+cudaError_t attn_fused_launch(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
+                              float *part, void *xq, const int *pos, int nq, int nkv, int hd, int S, float scale,
+                              const float2 *rope, int n_rot, float eps, cudaStream_t st);
+cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float theta, cudaStream_t st);
 cudaError_t attn_launch(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
                         int nq, int nkv, int hd, int S, float scale, cudaStream_t st);
 __global__ void k_fill_blocks(uint8_t *out, int type, int rows, int nblk, long row0, int blk0, uint64_t seed, int tid,
@@ -133,6 +138,7 @@ struct M27BEngine {
     float *out_norm = nullptr;
     float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *q = nullptr, *gate = nullptr, *o = nullptr, *a = nullptr;
     float *part = nullptr, *logits = nullptr;
+    float2 *rope = nullptr;  // (cos, sin) of the step's position, n_rot/2 pairs
     uint8_t *xq = nullptr;
     unsigned long long *best = nullptr;
     int *ctl = nullptr;                      // device [token, pos, generated count, pad]
@@ -302,17 +308,25 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
     const bool p2p = e->p2p;
     const int *pos = e->ctl + 1;
     ECALL(m27b_dequant_rows(&e->embd.v, e->ctl, 1, e->h, c.hidden, e->st, err, err_cap));
+    ECUDA(rope_table_launch(e->rope, pos, c.n_rot, c.rope_theta, e->st));  // this step's rotary table
     ECALL(m27b_act_quant_rmsnorm(e->h, e->L[0].attn_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq,
                                  e->st, err, err_cap));
     for (int l = 0; l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
         ECALL(mv(e, Ly.wqkv, e->xq, e->qkv, nullptr, err, err_cap));
-        ECUDA(launch_pdl(k_qk_norm_rope_cache, dim3(e->H + e->KV), dim3(hd), (size_t)(hd + 32) * 4, e->st,
-                         (const float *)e->qkv, (const float *)Ly.q_norm, (const float *)Ly.k_norm, e->q, e->gate, Ly.kc,
-                         Ly.vc, pos, e->H, e->KV, hd, c.n_rot, c.rope_theta, c.rms_eps));
-        ECUDA(attn_launch(e->q, Ly.kc, Ly.vc, e->part, e->o, pos, e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd),
-                          e->st));
-        ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, 1, e->H * hd, M27B_TYPE_Q8_K, e->xq, e->st, err, err_cap));
+        if (attn_fused_supported(hd)) {
+            // q/k norm + RoPE + KV append + attention, then reduce + gate + q8_K for o_proj
+            ECUDA(attn_fused_launch(e->qkv, Ly.q_norm, Ly.k_norm, Ly.kc, Ly.vc, e->part, e->xq, pos, e->H, e->KV, hd,
+                                    e->S, 1.0f / sqrtf((float)hd), e->rope, c.n_rot, c.rms_eps, e->st));
+        } else {
+            ECUDA(launch_pdl(k_qk_norm_rope_cache, dim3(e->H + e->KV), dim3(hd), (size_t)(hd + 32) * 4, e->st,
+                             (const float *)e->qkv, (const float *)Ly.q_norm, (const float *)Ly.k_norm, e->q, e->gate,
+                             Ly.kc, Ly.vc, pos, e->H, e->KV, hd, c.n_rot, c.rope_theta, c.rms_eps));
+            ECUDA(attn_launch(e->q, Ly.kc, Ly.vc, e->part, e->o, pos, e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd),
+                              e->st));
+            ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, 1, e->H * hd, M27B_TYPE_Q8_K, e->xq, e->st, err,
+                                       err_cap));
+        }
         // o_proj partial (+ residual on rank 0), summed over ranks -> h2, then post-attention RMSNorm -> xq
         if (p2p) {
             ECALL(qmv_push(&Ly.wo.v, e->xq, r0 ? e->h : nullptr, push_args(e, 0, 2u * l), e->st, err, err_cap));
@@ -502,7 +516,8 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
               A((void **)&e->gate, (size_t)e->H * hd * 4) && A((void **)&e->o, (size_t)e->H * hd * 4) &&
               A((void **)&e->a, (size_t)e->F * 4) && A((void **)&e->part, (size_t)e->S * e->H * (hd + 4) * 4) &&
               A((void **)&e->logits, (size_t)e->V * 4) && A((void **)&e->xq, m27b_act_bytes(M27B_TYPE_Q8_K, xmax)) &&
-              A((void **)&e->best, 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4);
+              A((void **)&e->best, 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4) &&
+              A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2));
     for (int l = 0; ok && l < c.n_layers; ++l) {
         const size_t kvb = (size_t)c.max_ctx * e->KV * hd * 4;
         ok = A((void **)&e->L[l].kc, kvb) && A((void **)&e->L[l].vc, kvb) &&

@@ -11,6 +11,7 @@
 // max-subtracted softmax with no score clamp.
 #include "m27b_device.cuh"
 #include "m27b_launch.cuh"
+#include "q8k_warp.cuh"
 
 namespace m27b {
 
@@ -228,6 +229,227 @@ __global__ void __launch_bounds__(256) k_attn_reduce(const float *part, float *o
     }
 }
 
+// ---------------------------------------------------------------------------
+// Fused decode-layer attention for the engine: the two kernels below replace
+// k_qk_norm_rope_cache + the split attention + the gated q8_K quantizer.
+//
+// Rotary table of the step's position: rope[p] = (cos, sin) of
+// pos * theta^(-2p/n_rot) for p < n_rot/2 (the same for every layer), one
+// thread per pair, computed once per step.
+__global__ void k_rope_table(float2 *rope, const int *pos_p, int n_rot, float theta) {
+    pdl_wait();
+    pdl_trigger();
+    const int p = threadIdx.x;
+    if (p >= n_rot / 2) return;
+    const float ang = (float)(*pos_p) * powf(theta, -2.0f * (float)p / (float)n_rot);
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    rope[p] = make_float2(cs, sn);
+}
+
+// One warp applies RMSNorm (with its norm weights) and the rotary embedding
+// (table from k_rope_table) to one head of `src` (hd = DPL * 32 values, lane
+// l holding dims [l*DPL, (l+1)*DPL)) and leaves the result, times `mul`, in
+// dst (shared).
+template <int DPL>
+M27B_DI void norm_rope_warp(const float *src, const float *nw, float *dst, float mul, const float2 *rope, int n_rot,
+                            float eps, int lane) {
+    constexpr int hd = DPL * 32;
+    float v[DPL];
+    ld_dims<DPL>(src + lane * DPL, v);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) ss = fmaf(v[i], v[i], ss);
+    ss = warp_sum(ss);
+    const float sc = rsqrtf(ss / (float)hd + eps);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+        const int d = lane * DPL + i;
+        v[i] = v[i] * sc * (nw ? nw[d] : 1.0f);
+        dst[d] = v[i];
+    }
+    __syncwarp();
+    const int half = n_rot / 2;
+    float out[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+        const int d = lane * DPL + i;
+        out[i] = v[i];
+        if (d < n_rot) {
+            const float2 r = rope[d < half ? d : d - half];
+            out[i] = d < half ? v[i] * r.x - dst[d + half] * r.y : dst[d - half] * r.y + v[i] * r.x;
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) dst[lane * DPL + i] = out[i] * mul;
+    __syncwarp();
+}
+
+// Split attention with the q/k norm, RoPE and KV-cache append folded in.
+// grid (nkv, splits), 256 threads.  qkv = [nq heads of (q, gate) | nkv k
+// heads | nkv v heads].  Warp g normalises and rotates query head j*G + g
+// into shared memory.  The newest position L - 1 (= *pos) lies in the last
+// active split only: that CTA also normalises and rotates kv head j's k,
+// appends k and v at position L - 1 of the caches, and reads them back like
+// any other position (no other CTA touches it).  Then as k_attn_partial.
+template <int DPL>
+__global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, const float *q_norm, const float *k_norm,
+                                                          float *kc, float *vc, float *part, const int *pos_p, int nq,
+                                                          int nkv, float scale, const float2 *rope, int n_rot,
+                                                          float eps) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int hd = DPL * 32, rec = hd + 4;
+    const int j = blockIdx.x, s = blockIdx.y;
+    const int G = nq / nkv;
+    const int pos = *pos_p, L = pos + 1;
+    const int S = att_splits(L, gridDim.y);
+    if (s >= S) return;
+    const int p0 = (int)(((long)L * s) / S), p1 = (int)(((long)L * (s + 1)) / S);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    extern __shared__ __align__(16) float sh[];  // q [G][hd] (pre-scaled), then [8 warps][G][rec]
+    float *qs = sh;
+    float *cb = sh + G * hd;
+    if (warp < G)
+        norm_rope_warp<DPL>(qkv + (size_t)(j * G + warp) * 2 * hd, q_norm, qs + warp * hd, scale, rope, n_rot, eps,
+                            lane);
+    if (s == S - 1 && warp == 0) {
+        const size_t off = ((size_t)pos * nkv + j) * hd;
+        norm_rope_warp<DPL>(qkv + (size_t)nq * 2 * hd + (size_t)j * hd, k_norm, cb, 1.0f, rope, n_rot, eps, lane);
+        const float *vsrc = qkv + (size_t)nq * 2 * hd + (size_t)nkv * hd + (size_t)j * hd;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+            const int d = lane * DPL + i;
+            kc[off + d] = cb[d];
+            vc[off + d] = vsrc[d];
+        }
+    }
+    __syncthreads();  // q in shared memory; the appended k/v visible to this CTA
+    float acc[ATT_G][DPL], m[ATT_G], l[ATT_G];
+#pragma unroll
+    for (int g = 0; g < ATT_G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[g][i] = 0.0f;
+    }
+    for (int p = p0 + warp; p < p1; p += 8) {
+        float kv[DPL], vv[DPL];
+        ld_dims<DPL>(kc + ((size_t)p * nkv + j) * hd + lane * DPL, kv);
+        ld_dims<DPL>(vc + ((size_t)p * nkv + j) * hd + lane * DPL, vv);
+#pragma unroll
+        for (int g = 0; g < ATT_G; ++g) {
+            if (g < G) {
+                float qv[DPL];
+                ld_dims<DPL>(qs + g * hd + lane * DPL, qv);
+                float d = 0.0f;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) d = fmaf(qv[i], kv[i], d);
+                d = warp_sum(d);
+                const float mn = fmaxf(m[g], d);
+                const float a = expf(m[g] - mn), b = expf(d - mn);
+                l[g] = l[g] * a + b;
+#pragma unroll
+                for (int i = 0; i < DPL; ++i) acc[g][i] = acc[g][i] * a + b * vv[i];
+                m[g] = mn;
+            }
+        }
+    }
+    __syncthreads();  // the k scratch in cb is reused below
+#pragma unroll
+    for (int g = 0; g < ATT_G; ++g) {
+        if (g < G) {
+            float *r = cb + ((size_t)warp * G + g) * rec;
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) r[lane * DPL + i] = acc[g][i];
+            if (lane == 0) {
+                r[hd] = m[g];
+                r[hd + 1] = l[g];
+            }
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
+        const int g = idx / hd, dd = idx - g * hd;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, cb[((size_t)w * G + g) * rec + hd]);
+        float Lsum = 0.0f, A = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const float *r = cb + ((size_t)w * G + g) * rec;
+            const float f = r[hd] == -INFINITY ? 0.0f : expf(r[hd] - M);
+            Lsum += r[hd + 1] * f;
+            A += r[dd] * f;
+        }
+        float *o = part + ((size_t)s * nq + j * G + g) * rec;
+        o[dd] = A;
+        if (dd == 0) {
+            o[hd] = M;
+            o[hd + 1] = Lsum;
+        }
+    }
+}
+
+// Split reduction + sigmoid gate + q8_K quantization: grid nq*hd/256 (hd
+// divides 256), 256 threads; CTA b produces q8_K block b of the gated
+// attention output o * sigmoid(gate) (heads b*256/hd ..), the input of o_proj.
+template <int DPL>
+__global__ void __launch_bounds__(256) k_attn_reduce_gate_q8K(const float *part, const float *qkv, void *xq,
+                                                              const int *pos_p, int nq, int smax) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int hd = DPL * 32, rec = hd + 4, hpb = 256 / hd;
+    __shared__ __align__(16) float red[8][rec];
+    __shared__ float wmax[8];
+    __shared__ __align__(16) float xs[256];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int S = att_splits(*pos_p + 1, smax);
+    for (int hh = 0; hh < hpb; ++hh) {
+        const int h = blockIdx.x * hpb + hh;
+        float M = -INFINITY;
+        for (int s = warp; s < S; s += 8) M = fmaxf(M, part[((size_t)s * nq + h) * rec + hd]);
+        if (lane == 0) wmax[warp] = M;
+        __syncthreads();
+#pragma unroll
+        for (int w = 0; w < 8; ++w) M = fmaxf(M, wmax[w]);
+        float A[DPL], Ls = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) A[i] = 0.0f;
+        for (int s = warp; s < S; s += 8) {
+            const float *r = part + ((size_t)s * nq + h) * rec;
+            const float f = expf(r[hd] - M);
+            Ls = fmaf(f, r[hd + 1], Ls);
+            float v[DPL];
+            ld_dims<DPL>(r + lane * DPL, v);
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) A[i] = fmaf(f, v[i], A[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) red[warp][lane * DPL + i] = A[i];
+        if (lane == 0) red[warp][hd] = Ls;
+        __syncthreads();
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+            float o = 0.0f, L = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                o += red[w][d];
+                L += red[w][hd];
+            }
+            const float g = qkv[(size_t)h * 2 * hd + hd + d];
+            xs[hh * hd + d] = (o / L) * (1.0f / (1.0f + expf(-g)));
+        }
+        __syncthreads();
+    }
+    if (warp == 0) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = xs[lane * 8 + i];
+        quant_q8K_warp(v, lane, (m27b_block_q8_K *)xq + blockIdx.x);
+    }
+}
+
 size_t attn_smem_bytes(int G, int hd) { return (size_t)(G * hd + 8 * G * (hd + 4)) * sizeof(float); }
 
 template <int DPL>
@@ -241,8 +463,43 @@ static cudaError_t attn_run(const float *q, const float *kc, const float *vc, fl
 
 template <int DPL>
 static cudaError_t attn_opt_in() {
-    return cudaFuncSetAttribute(k_attn_partial<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)attn_smem_bytes(ATT_G, DPL * 32));
+    const int smem = (int)attn_smem_bytes(ATT_G, DPL * 32);
+    const cudaError_t e = cudaFuncSetAttribute(k_attn_partial<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess || (DPL != 1 && DPL != 2 && DPL != 4 && DPL != 8)) return e;
+    return cudaFuncSetAttribute(k_attn_partial_qkv<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
+template <int DPL>
+static cudaError_t attn_fused_run(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
+                                  float *part, void *xq, const int *pos, int nq, int nkv, int S, float scale,
+                                  const float2 *rope, int n_rot, float eps, cudaStream_t st) {
+    const size_t smem = attn_smem_bytes(nq / nkv, DPL * 32);
+    cudaError_t e = launch_pdl(k_attn_partial_qkv<DPL>, dim3(nkv, S), dim3(256), smem, st, qkv, q_norm, k_norm, kc, vc,
+                               part, pos, nq, nkv, scale, rope, n_rot, eps);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_attn_reduce_gate_q8K<DPL>, dim3(nq * DPL * 32 / 256), dim3(256), 0, st, (const float *)part, qkv,
+                      xq, pos, nq, S);
+}
+
+// Engine attention in two kernels: q/k norm + RoPE + KV append + split
+// attention, then split reduce + gate + q8_K of o_proj's input.  head_dim
+// must divide 256 (false: use the unfused kernels).
+bool attn_fused_supported(int hd) { return hd == 32 || hd == 64 || hd == 128 || hd == 256; }
+
+cudaError_t attn_fused_launch(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
+                              float *part, void *xq, const int *pos, int nq, int nkv, int hd, int S, float scale,
+                              const float2 *rope, int n_rot, float eps, cudaStream_t st) {
+    switch (hd) {
+        case 32: return attn_fused_run<1>(qkv, q_norm, k_norm, kc, vc, part, xq, pos, nq, nkv, S, scale, rope, n_rot, eps, st);
+        case 64: return attn_fused_run<2>(qkv, q_norm, k_norm, kc, vc, part, xq, pos, nq, nkv, S, scale, rope, n_rot, eps, st);
+        case 128: return attn_fused_run<4>(qkv, q_norm, k_norm, kc, vc, part, xq, pos, nq, nkv, S, scale, rope, n_rot, eps, st);
+        case 256: return attn_fused_run<8>(qkv, q_norm, k_norm, kc, vc, part, xq, pos, nq, nkv, S, scale, rope, n_rot, eps, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float theta, cudaStream_t st) {
+    return launch_pdl(k_rope_table, dim3(1), dim3(128), 0, st, rope, pos, n_rot, theta);
 }
 
 // Raise the shared-memory limit of every attention instantiation (once per

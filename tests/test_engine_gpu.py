@@ -59,6 +59,13 @@ def test_engine_shared_kv_uneven(orc, m27b):
     _decode_compare(orc, m27b, c, seed=1, n_steps=6, prompt=[1, 2, 3, 4])
 
 
+def test_engine_unfused_head_dim(orc, m27b):
+    # head_dim 96 does not divide 256: the engine uses its unfused attention kernels
+    c = dict(n_layers=2, hidden=512, ffn=768, n_head=8, n_kv_head=2, head_dim=96, vocab=500, n_rot=32,
+             rope_theta=1e6, rms_eps=1e-6)
+    _decode_compare(orc, m27b, c, seed=6, n_steps=5, prompt=[3, 1, 4])
+
+
 def test_engine_long_context(orc, m27b):
     # enough positions that every attention split holds several of them
     c = dict(R.TINY, n_layers=1)
