@@ -5,18 +5,21 @@ Default workload (the driver's line) — cfg0, the q4_K matvec BASELINE's
 metric is quoted on: one step = one pass of the matvec path over one batch:
 for each of C=6 distinct q4_K weight matrices of 17408 x 5120 (6 x 50.1 MB =
 301 MB rotate, so the working set exceeds the 126 MB L2), quantize a
-5120-long fp32 activation to q8_K and multiply.  Steps are replayed through
-CUDA graphs of the C-ABI calls (m27b_act_quant + m27b_qmv), timed with CUDA
-events on the launching stream, bracketed by a barrier and a synchronize.
+5120-long fp32 activation to q8_K and multiply — one launch of
+m27b_qmv_f32 (the reference's l_mv_quant seam), whose kernel quantizes the
+activation in its prologue.  Steps are replayed through CUDA graphs of the
+C-ABI calls, timed with CUDA events on the launching stream, bracketed by a
+barrier and a synchronize.
 
   value    algorithmic bytes of all ranks' steps / max-over-ranks time; a
            matvec's algorithmic bytes are W 50,135,040 + x 20,480 + y 69,632.
   e2e      the same through the C ABI with host buffers: per matvec a pinned
            host->device copy of x and a device->host copy of y are inside the
            timed region.
-  roofline the matvec kernel alone (graphs of m27b_qmv over the rotating
-           weights): bytes per launch / mean launch time, against the
-           measured HBM copy bandwidth in MEASURED_PEAKS.json.
+  roofline the step's kernel (for cfg0 the step is that one kernel; for
+           cfg2 the matvec without the separate quantizer): bytes per launch
+           / mean launch time, against the measured HBM copy bandwidth in
+           MEASURED_PEAKS.json.
   cpu_baseline  the CPU oracle (restatement of ggml's vec_dot_q4_K_q8_K,
            OpenMP over rows) on this host's cores, a bounded sample.
 
@@ -185,7 +188,7 @@ class Workload:
                 self.metric = "q4_K matvec HBM GB/s"
                 self.config = {"workload": f"cfg0: q4_K matvec {rows}x{k}, batch 1, q8_K activations", "rows": rows,
                                "k": k, "matvecs_per_step": copies, "bytes_per_matvec": self.mv_bytes, "l2": l2}
-                self.kernel = "k_qmv_q4k_blk<1,STORE>"
+                self.kernel = "k_qmv_q4k_blk<1,STORE> (q8_K quantization in the prologue)"
                 self.profile = "qmv_q4K_cfg0.md"
             else:
                 self.metric = f"q4_K verify matvec HBM GB/s ({n} tokens)"
@@ -196,7 +199,8 @@ class Workload:
                 self.kernel = ("k_qmv_q4k_mma<%d> (tcgen05 kind::i8)" % (8 if n <= 8 else 16)) if n >= 5 else \
                     "k_qmv_q4k_blk<%d,STORE>" % n
                 self.profile = "qmv_q4K_mma_cfg2.md"
-            self.launches_per_step = 2 * copies
+            self.fused = w == "cfg0"  # quantize in the matvec prologue (m27b_qmv_f32)
+            self.launches_per_step = copies if self.fused else 2 * copies
             self.copies, self.rows, self.k = copies, rows, k
             self.h2d = copies * n * k * 4
             self.d2h = copies * n * rows * 4
@@ -264,6 +268,9 @@ class Workload:
                 self._ffn(c)
             return
         for c in range(self.copies):
+            if getattr(self, "fused", False):
+                m.qmv_f32(self.W[c], self.x[c], self.n, self.y[c])
+                continue
             m.act_quant(self.x[c], Q8_K, out=self.xq[c])
             self._mv(c)
 
@@ -284,7 +291,10 @@ class Workload:
                 m.qmv(D, self.aq, self.n, self.out[c])
             return
         for c in range(self.copies):
-            self._mv(c)
+            if getattr(self, "fused", False):
+                self.m27b.qmv_f32(self.W[c], self.x[c], self.n, self.y[c])
+            else:
+                self._mv(c)
 
     def step_e2e(self):
         if self.name == "cfg3":
@@ -295,8 +305,11 @@ class Workload:
             return
         for c in range(self.copies):
             self.x[c].copy_(self.xh[c], non_blocking=True)
-            self.m27b.act_quant(self.x[c], Q8_K, out=self.xq[c])
-            self._mv(c)
+            if getattr(self, "fused", False):
+                self.m27b.qmv_f32(self.W[c], self.x[c], self.n, self.y[c])
+            else:
+                self.m27b.act_quant(self.x[c], Q8_K, out=self.xq[c])
+                self._mv(c)
             self.yh[c].copy_(self.y[c], non_blocking=True)
 
     def kernel_bytes(self):

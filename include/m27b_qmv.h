@@ -142,6 +142,26 @@ M27B_API bool m27b_qmv_argmax(const struct WeightView *w, const void *xq, int n_
                      unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
                      size_t err_cap);
 
+/* fp32 activations in, like the reference's l_mv_quant(W, x, y)
+ * (src/mono27b_executor.cu:2033-2050, its quantizer k_quant_q8_1 :84-107):
+ * x rows (n_tok of them, stride ldx floats) are quantized to q8_K / q8_0 and
+ * multiplied, y = W.x (+ residual).  For a q4_K matrix and up to 4 tokens
+ * (x 16-byte aligned, ldx a multiple of 4) the matvec kernel quantizes the
+ * rows in its own prologue (one launch, same codes as m27b_act_quant);
+ * otherwise the rows are first quantized into xq_scratch
+ * (n_tok * m27b_act_bytes(m27b_act_type_for(type), k) bytes; may be NULL on
+ * the one-launch path). */
+M27B_API bool m27b_qmv_f32(const struct WeightView *w, const float *x, int ldx, int n_tok, void *xq_scratch, float *y,
+                           int ldy, const float *residual, cudaStream_t stream, char *err, size_t err_cap);
+
+/* The same with RMSNorm(x) * norm_w (eps; norm_w may be NULL: 1.0) before
+ * the quantization, the reference's l_rms + MV pair (:2139-2141).  With
+ * w_up non-NULL the epilogue is SwiGLU, y = silu(W.x) * (W_up.x) (no
+ * residual) — the FFN's gate/up after the post-attention norm. */
+M27B_API bool m27b_qmv_f32_rmsnorm(const struct WeightView *w, const struct WeightView *w_up, const float *x, int ldx,
+                                   const float *norm_w, float eps, int n_tok, void *xq_scratch, float *y, int ldy,
+                                   const float *residual, cudaStream_t stream, char *err, size_t err_cap);
+
 /* out[i*ldo + j] = dequant(W[rows[i]])[j] for i < n, j < k; rows is a device
  * array of n row indices; an index outside [0, row_count) yields a zero row
  * (the reference embed zeroes the hidden state for such tokens). */

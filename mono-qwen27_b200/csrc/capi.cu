@@ -140,9 +140,18 @@ bool act_quant_common(int mode, const float *x, const float *gate, const float *
     return cuda_ok(launch_act_quant((int)act_type, mode, a, n_tok, stream), what, err, cap);
 }
 
+// fp32 activations for the quantizing prologue of the q4_K kernel
+struct XArgs {
+    const float *xf;
+    int ldxf;
+    int norm_on;
+    const float *norm_w;
+    float eps;
+};
+
 bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void *xq, int n_tok, float *y, int ldy,
                 const float *residual, unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
-                size_t cap, const char *what, const PushArgs *push = nullptr) {
+                size_t cap, const char *what, const PushArgs *push = nullptr, const XArgs *xa = nullptr) {
     WDesc d0{}, d1{};
     if (!describe(w0, d0, what, err, cap)) return false;
     if (epi == EPI_SWIGLU) {
@@ -150,7 +159,9 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         if (w1->ggml_type != w0->ggml_type || w1->row_blocks != w0->row_blocks || w1->row_count != w0->row_count)
             return fail(err, cap, "%s: gate and up must have the same type and shape", what);
     }
-    if (!xq) return fail(err, cap, "%s: null activation pointer", what);
+    if (!xq && !xa) return fail(err, cap, "%s: null activation pointer", what);
+    if (xa && (d0.kind != W_Q4K || n_tok > 4 || !xa->xf || ((uintptr_t)xa->xf & 15) || (xa->ldxf & 3)))
+        return fail(err, cap, "%s: in-kernel quantization needs q4_K weights, <= 4 tokens, 16-byte aligned rows", what);
     if (n_tok < 1 || n_tok > M27B_MAX_TOKENS)
         return fail(err, cap, "%s: n_tok must be in [1, %d] (got %d)", what, M27B_MAX_TOKENS, n_tok);
     if (epi == EPI_PUSH) {
@@ -167,6 +178,7 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
     const uint32_t at = d0.base == M27B_TYPE_Q8_0 ? M27B_TYPE_Q8_0 : M27B_TYPE_Q8_K;
     const size_t xb = act_bytes(at, d0.k);
     if (((uintptr_t)xq & (at == M27B_TYPE_Q8_K ? 3u : 1u)) != 0) return fail(err, cap, "%s: misaligned activations", what);
+    (void)xb;
     const size_t smem = qmv_smem_bytes(d0.base, d0.k, n_tok < 4 ? n_tok : 4);
     if (smem == 0 || smem > 227 * 1024)
         return fail(err, cap, "%s: activation staging does not fit in shared memory (k=%d too large)", what, d0.k);
@@ -179,13 +191,20 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
     }
     // 5..16 tokens of a q4_K matrix: one pass on the tensor cores
-    const bool mma = d0.kind == W_Q4K && epi == EPI_STORE && q4k_mma_supported((int)w0->row_blocks, n_tok);
+    const bool mma = !xa && d0.kind == W_Q4K && epi == EPI_STORE && q4k_mma_supported((int)w0->row_blocks, n_tok);
     for (int t0 = 0; t0 < n_tok; t0 += 4) {
         const int nt = mma ? n_tok : (n_tok - t0 < 4 ? n_tok - t0 : 4);
         QmvArgs a{};
         a.w0 = (const uint8_t *)w0->ptr;
         a.w1 = epi == EPI_SWIGLU ? (const uint8_t *)w1->ptr : nullptr;
-        a.xq = (const uint8_t *)xq + (size_t)t0 * xb;
+        a.xq = xq ? (const uint8_t *)xq + (size_t)t0 * xb : nullptr;
+        if (xa) {
+            a.xf = xa->xf + (size_t)t0 * xa->ldxf;
+            a.ldxf = xa->ldxf;
+            a.xnorm_on = xa->norm_on;
+            a.xnorm = xa->norm_w;
+            a.eps = xa->eps;
+        }
         a.y = y ? y + (size_t)t0 * ldy : nullptr;
         a.residual = residual ? residual + (size_t)t0 * ldy : nullptr;
         a.best = best ? best + t0 : nullptr;
@@ -295,6 +314,44 @@ bool m27b_qmv_argmax(const WeightView *w, const void *xq, int n_tok, float *logi
                      uint32_t row_offset, cudaStream_t stream, char *err, size_t err_cap) {
     return qmv_common(EPI_ARGMAX, w, nullptr, xq, n_tok, logits, ldl, nullptr, best, row_offset, stream, err, err_cap,
                       "m27b_qmv_argmax");
+}
+
+// fp32 activations: quantized inside the q4_K kernel's prologue (<= 4 tokens),
+// otherwise into xq_scratch by a separate quantizer launch first.
+static bool qmv_f32_common(const WeightView *w, const WeightView *w_up, const float *x, int ldx, int norm_on,
+                           const float *norm_w, float eps, int n_tok, void *xq_scratch, float *y, int ldy,
+                           const float *residual, cudaStream_t stream, char *err, size_t cap, const char *what) {
+    if (!w || !x) return fail(err, cap, "%s: null argument", what);
+    if (w_up && residual) return fail(err, cap, "%s: the SwiGLU epilogue takes no residual", what);
+    const int epi = w_up ? EPI_SWIGLU : EPI_STORE;
+    const uint32_t base = w->ggml_type & M27B_TYPE_MASK;
+    const int k = (int)w->row_blocks * (base == M27B_TYPE_Q8_0 ? 32 : 256);
+    if (ldx < k) return fail(err, cap, "%s: ldx (%d) < k (%d)", what, ldx, k);
+    if (base == M27B_TYPE_Q4_K && w->ggml_type == M27B_TYPE_Q4_K && n_tok >= 1 && n_tok <= 4 &&
+        ((uintptr_t)x & 15) == 0 && (ldx & 3) == 0) {
+        XArgs xa{x, ldx, norm_on, norm_w, eps};
+        return qmv_common(epi, w, w_up, nullptr, n_tok, y, ldy, residual, nullptr, 0, stream, err, cap, what, nullptr,
+                          &xa);
+    }
+    if (!xq_scratch) return fail(err, cap, "%s: this weight type / token count needs xq_scratch", what);
+    const uint32_t at = base == M27B_TYPE_Q8_0 ? M27B_TYPE_Q8_0 : M27B_TYPE_Q8_K;
+    if (!act_quant_common(norm_on ? ACT_RMSNORM : ACT_PLAIN, x, nullptr, norm_w, eps, k, n_tok, ldx, at, xq_scratch,
+                          stream, err, cap, what))
+        return false;
+    return qmv_common(epi, w, w_up, xq_scratch, n_tok, y, ldy, residual, nullptr, 0, stream, err, cap, what);
+}
+
+bool m27b_qmv_f32(const WeightView *w, const float *x, int ldx, int n_tok, void *xq_scratch, float *y, int ldy,
+                  const float *residual, cudaStream_t stream, char *err, size_t err_cap) {
+    return qmv_f32_common(w, nullptr, x, ldx, 0, nullptr, 0.0f, n_tok, xq_scratch, y, ldy, residual, stream, err,
+                          err_cap, "m27b_qmv_f32");
+}
+
+bool m27b_qmv_f32_rmsnorm(const WeightView *w, const WeightView *w_up, const float *x, int ldx, const float *norm_w,
+                          float eps, int n_tok, void *xq_scratch, float *y, int ldy, const float *residual,
+                          cudaStream_t stream, char *err, size_t err_cap) {
+    return qmv_f32_common(w, w_up, x, ldx, 1, norm_w, eps, n_tok, xq_scratch, y, ldy, residual, stream, err, err_cap,
+                          "m27b_qmv_f32_rmsnorm");
 }
 
 bool m27b_dequant_rows(const WeightView *w, const int32_t *rows, int n, float *out, int ldo, cudaStream_t stream, char *err,

@@ -309,11 +309,19 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
     const int *pos = e->ctl + 1;
     ECALL(m27b_dequant_rows(&e->embd.v, e->ctl, 1, e->h, c.hidden, e->st, err, err_cap));
     ECUDA(rope_table_launch(e->rope, pos, c.n_rot, c.rope_theta, e->st));  // this step's rotary table
-    ECALL(m27b_act_quant_rmsnorm(e->h, e->L[0].attn_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq,
-                                 e->st, err, err_cap));
+    // with the fused all-reduce the consumer kernel hands each projection its
+    // normalised, quantized input; otherwise the projection normalises and
+    // quantizes h itself (q4_K: in its prologue)
+    if (p2p)
+        ECALL(m27b_act_quant_rmsnorm(e->h, e->L[0].attn_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq,
+                                     e->st, err, err_cap));
     for (int l = 0; l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
-        ECALL(mv(e, Ly.wqkv, e->xq, e->qkv, nullptr, err, err_cap));
+        if (p2p)
+            ECALL(mv(e, Ly.wqkv, e->xq, e->qkv, nullptr, err, err_cap));
+        else
+            ECALL(m27b_qmv_f32_rmsnorm(&Ly.wqkv.v, nullptr, e->h, c.hidden, Ly.attn_norm, c.rms_eps, 1, e->xq, e->qkv,
+                                       Ly.wqkv.rows, nullptr, e->st, err, err_cap));
         if (attn_fused_supported(hd)) {
             // q/k norm + RoPE + KV append + attention, then reduce + gate + q8_K for o_proj
             ECUDA(attn_fused_launch(e->qkv, Ly.q_norm, Ly.k_norm, Ly.kc, Ly.vc, e->part, e->xq, pos, e->H, e->KV, hd,
@@ -331,13 +339,13 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         if (p2p) {
             ECALL(qmv_push(&Ly.wo.v, e->xq, r0 ? e->h : nullptr, push_args(e, 0, 2u * l), e->st, err, err_cap));
             ECALL(consume(e, 0, 2u * l, Ly.post_norm, e->h2, err, err_cap));
+            ECALL(m27b_qmv_swiglu(&Ly.wg.v, &Ly.wu.v, e->xq, 1, e->a, e->F, e->st, err, err_cap));
         } else {
             ECALL(mv(e, Ly.wo, e->xq, e->h2, r0 ? e->h : nullptr, err, err_cap));
             ECALL(allreduce_hidden(e, e->h2, err, err_cap));
-            ECALL(m27b_act_quant_rmsnorm(e->h2, Ly.post_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq,
-                                         e->st, err, err_cap));
+            ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
+                                       nullptr, e->st, err, err_cap));
         }
-        ECALL(m27b_qmv_swiglu(&Ly.wg.v, &Ly.wu.v, e->xq, 1, e->a, e->F, e->st, err, err_cap));
         ECALL(m27b_act_quant(e->a, e->F, 1, e->F, M27B_TYPE_Q8_K, e->xq, e->st, err, err_cap));
         // down partial (+ residual on rank 0), summed over ranks -> h, then the
         // next layer's input RMSNorm (the output norm after the last layer) -> xq
@@ -348,10 +356,11 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         } else {
             ECALL(mv(e, Ly.wd, e->xq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
             ECALL(allreduce_hidden(e, e->h, err, err_cap));
-            ECALL(m27b_act_quant_rmsnorm(e->h, next_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq, e->st,
-                                         err, err_cap));
         }
     }
+    if (!p2p)
+        ECALL(m27b_act_quant_rmsnorm(e->h, e->out_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq, e->st,
+                                     err, err_cap));
     ECALL(m27b_qmv_argmax(&e->lmh.v, e->xq, 1, e->logits, e->V, e->best, (uint32_t)e->v_lo, e->st, err, err_cap));
     // next token and position for the following step (greedy generation on the device)
     if (p2p) {

@@ -33,6 +33,7 @@
 #include <cuda.h>
 
 #include "qmv_kernels.cuh"
+#include "q8k_warp.cuh"
 
 namespace m27b {
 
@@ -138,6 +139,147 @@ M27B_DI void stage_x_blk(const QmvArgs &a, uint8_t *xrec, float *xd) {
         } else {
             xd[blk] = *(const float *)sb;
         }
+    }
+}
+
+// The same records built from fp32 activations in the prologue (the fused
+// quantize + matvec entries): warp w quantizes blocks w, w + nwarps, ... of
+// the NT rows with the shared q8_K warp routine (the codes, sub-block sums
+// and scale equal those m27b_act_quant produces).  A warp loads all of its
+// blocks (up to QX_REGS) before any arithmetic, so the prologue pays one L2
+// round trip.  With a.xnorm_on the rows are first RMSNormed with weights
+// a.xnorm (may be null) and a.eps: each warp's sums of squares over the
+// values it holds are reduced over the CTA in warp order (`red`: nwarps * NT
+// floats).
+constexpr int QX_REGS = 4;
+
+M27B_DI void quant_x_rec(float (&v)[8], int lane, uint8_t *rec8, float *dslot) {
+    uint32_t packed[2];
+    int sum;
+    float d;
+    quant_q8K_lane(v, lane, packed, sum, d);
+    uint32_t *rec = (uint32_t *)rec8;
+    rec[2 * lane] = packed[0];
+    rec[2 * lane + 1] = packed[1];
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);  // lanes 4s..4s+3 hold sub-block s
+    if ((lane & 3) == 0) ((int16_t *)(rec8 + 256))[lane >> 2] = (int16_t)sum;
+    if (lane == 0) *dslot = d;
+}
+
+template <int NT>
+M27B_DI void quant_x_blk(const QmvArgs &a, uint8_t *xrec, float *xd, float *red) {
+    const int nb = a.k / 256;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int total = NT * nb;
+    if ((total + nw - 1) / nw <= QX_REGS) {
+        float v[QX_REGS][8];
+#pragma unroll
+        for (int r = 0; r < QX_REGS; ++r) {
+            const int i = warp + r * nw;
+            if (i < total) {
+                const int t = i / nb, b = i - t * nb;
+                const float4 *xr = (const float4 *)(a.xf + (size_t)t * a.ldxf + b * 256 + lane * 8);
+                const float4 p0 = xr[0], p1 = xr[1];
+                v[r][0] = p0.x; v[r][1] = p0.y; v[r][2] = p0.z; v[r][3] = p0.w;
+                v[r][4] = p1.x; v[r][5] = p1.y; v[r][6] = p1.z; v[r][7] = p1.w;
+            }
+        }
+        if (a.xnorm_on) {
+            float ss[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) ss[t] = 0.0f;
+#pragma unroll
+            for (int r = 0; r < QX_REGS; ++r) {
+                const int i = warp + r * nw;
+                if (i < total) {
+                    float s2 = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) s2 = fmaf(v[r][j], v[r][j], s2);
+                    const int t = i / nb;
+#pragma unroll
+                    for (int t2 = 0; t2 < NT; ++t2)
+                        if (t2 == t) ss[t2] += s2;
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                const float w = warp_sum(ss[t]);
+                if (lane == 0) red[warp * NT + t] = w;
+            }
+            __syncthreads();
+            float ns[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+                float tot = 0.0f;
+                for (int w = 0; w < nw; ++w) tot += red[w * NT + t];
+                ns[t] = 1.0f / sqrtf(tot / (float)a.k + a.eps);
+            }
+            __syncthreads();  // red is reused by the caller
+#pragma unroll
+            for (int r = 0; r < QX_REGS; ++r) {
+                const int i = warp + r * nw;
+                if (i < total) {
+                    const int t = i / nb, b = i - t * nb;
+                    float nst = ns[0];
+#pragma unroll
+                    for (int t2 = 1; t2 < NT; ++t2)
+                        if (t2 == t) nst = ns[t2];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        v[r][j] = v[r][j] * nst;
+                        if (a.xnorm) v[r][j] = v[r][j] * a.xnorm[b * 256 + lane * 8 + j];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < QX_REGS; ++r) {
+            const int i = warp + r * nw;
+            if (i < total) quant_x_rec(v[r], lane, xrec + (size_t)i * BLK_XREC, xd + i);
+        }
+        return;
+    }
+    // long rows: two passes (sum of squares, then quantize), block by block
+    float ns[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) ns[t] = 1.0f;
+    if (a.xnorm_on) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const float4 *x4 = (const float4 *)(a.xf + (size_t)t * a.ldxf);
+            float ss = 0.0f;
+#pragma unroll 4
+            for (int i = threadIdx.x; i < a.k / 4; i += blockDim.x) {
+                const float4 q = x4[i];
+                ss = fmaf(q.x, q.x, fmaf(q.y, q.y, fmaf(q.z, q.z, fmaf(q.w, q.w, ss))));
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            __syncthreads();
+            float tot = 0.0f;
+            for (int w = 0; w < nw; ++w) tot += red[w];
+            ns[t] = 1.0f / sqrtf(tot / (float)a.k + a.eps);
+            __syncthreads();
+        }
+    }
+    for (int i = warp; i < total; i += nw) {
+        const int t = i / nb, b = i - t * nb;
+        const float4 *xr = (const float4 *)(a.xf + (size_t)t * a.ldxf + b * 256 + lane * 8);
+        const float4 p0 = xr[0], p1 = xr[1];
+        float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        if (a.xnorm_on) {
+            float nst = ns[0];
+#pragma unroll
+            for (int t2 = 1; t2 < NT; ++t2)
+                if (t2 == t) nst = ns[t2];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                v[j] = v[j] * nst;
+                if (a.xnorm) v[j] = v[j] * a.xnorm[b * 256 + lane * 8 + j];
+            }
+        }
+        quant_x_rec(v, lane, xrec + (size_t)i * BLK_XREC, xd + i);
     }
 }
 
@@ -266,7 +408,10 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
     // the weights are not produced by the previous kernel: their copies are
     // already in flight; the activations (and every global write) wait for it
     pdl_wait();
-    stage_x_blk<NT>(a, xrec, xd);
+    if (a.xf)
+        quant_x_blk<NT>(a, xrec, xd, part);
+    else
+        stage_x_blk<NT>(a, xrec, xd);
     pdl_trigger();
     __syncthreads();
 

@@ -42,6 +42,13 @@ struct QmvArgs {
     uint32_t row_offset;       // added to argmax indices
     int *status;               // device status word: set non-zero if a bounded wait runs out
     PushArgs push;             // EPI_PUSH only
+    // activations quantized in the prologue (q4_K kernel) instead of read as
+    // q8_K blocks from xq: fp32 rows xf (stride ldxf), optionally RMSNormed
+    const float *xf;
+    int ldxf;
+    int xnorm_on;
+    const float *xnorm;        // RMSNorm weights (may be null: 1.0)
+    float eps;
 };
 
 // EPI_PUSH row store: one epoch-tagged value to every rank's receive window.

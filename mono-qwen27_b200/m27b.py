@@ -58,6 +58,8 @@ def lib():
         "m27b_qmv": (b, [wvp, vp, i32, vp, i32, vp, vp, cp, sz]),
         "m27b_qmv_swiglu": (b, [wvp, wvp, vp, i32, vp, i32, vp, cp, sz]),
         "m27b_qmv_argmax": (b, [wvp, vp, i32, vp, i32, vp, u32, vp, cp, sz]),
+        "m27b_qmv_f32": (b, [wvp, vp, i32, i32, vp, vp, i32, vp, vp, cp, sz]),
+        "m27b_qmv_f32_rmsnorm": (b, [wvp, wvp, vp, i32, vp, fp, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
@@ -189,6 +191,25 @@ def qmv_argmax(w, xq, n_tok, best, logits=None, row_offset=0, stream=None, ldl=N
     _check(lib().m27b_qmv_argmax(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(logits), ldl, _ptr(best), row_offset,
                                  _stream(stream), err, ERR_CAP), err, "m27b_qmv_argmax")
     return best
+
+
+def qmv_f32(w, x, n_tok, y, residual=None, xq_scratch=None, norm_w=None, eps=None, up=None, stream=None, ldy=None):
+    """y = W . q8(x) (+ residual) from fp32 rows x [n_tok, k] (device); with eps
+    given, x is RMSNormed (weights norm_w) first; with `up`, SwiGLU epilogue."""
+    err = ctypes.create_string_buffer(ERR_CAP)
+    L = lib()
+    ldx = x.stride(0) if x.dim() == 2 else x.shape[-1]
+    ldy = ldy if ldy is not None else w.view.row_count
+    if eps is None and up is None:
+        ok = L.m27b_qmv_f32(ctypes.byref(w.view), _ptr(x), ldx, n_tok, _ptr(xq_scratch), _ptr(y), ldy, _ptr(residual),
+                            _stream(stream), err, ERR_CAP)
+        _check(ok, err, "m27b_qmv_f32")
+    else:
+        ok = L.m27b_qmv_f32_rmsnorm(ctypes.byref(w.view), ctypes.byref(up.view) if up is not None else None, _ptr(x),
+                                    ldx, _ptr(norm_w), ctypes.c_float(1e-6 if eps is None else eps), n_tok,
+                                    _ptr(xq_scratch), _ptr(y), ldy, _ptr(residual), _stream(stream), err, ERR_CAP)
+        _check(ok, err, "m27b_qmv_f32_rmsnorm")
+    return y
 
 
 def argmax_key_index(key):
