@@ -97,6 +97,14 @@ M27B_API bool m27b_engine_enable_p2p(M27BEngine *e, char *err, size_t err_cap);
 M27B_API bool m27b_engine_load_tensor(M27BEngine *e, const char *name, uint32_t ggml_type, uint32_t row_elems,
                                       uint32_t row_count, const void *host, char *err, size_t err_cap);
 
+/* Load every entry of an opened `.m27b` blob (m27b_blob.h) whose
+ * source_model equals `source` (M27B_SOURCE_TARGET for this engine) through
+ * m27b_engine_load_tensor, by its GGUF name.  An entry the engine does not
+ * know, or whose payload is shorter than its shape, is an error. */
+struct M27BBlob;
+M27B_API bool m27b_engine_load_blob(M27BEngine *e, const struct M27BBlob *blob, uint32_t source, char *err,
+                                    size_t err_cap);
+
 /* Fill every weight with seeded synthetic GGUF blocks generated on the GPU
  * in global coordinates (identical tensors for every tp_size); norms = 1.
  * The q4_K / q6_K values have standard deviation ~ sigma. */

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "m27b_device.cuh"
+#include "m27b_blob.h"
 #include "m27b_engine.h"
 #include "m27b_launch.cuh"
 #include "qmv_kernels.cuh"
@@ -668,6 +669,31 @@ bool m27b_engine_load_tensor(M27BEngine *e, const char *name, uint32_t type, uin
         return load_slice(e, Ly.wd, hb, row_elems / be, 0, c.hidden, e->f_lo / (int)be, 0, err, err_cap);
     }
     return efail(err, err_cap, "unknown tensor %s", name);
+}
+
+bool m27b_engine_load_blob(M27BEngine *e, const M27BBlob *blob, uint32_t source, char *err, size_t err_cap) {
+    if (!e || !blob) return efail(err, err_cap, "m27b_engine_load_blob: null argument");
+    const size_t n = m27b_blob_count(blob);
+    size_t loaded = 0;
+    for (size_t i = 0; i < n; ++i) {
+        M27BWeightEntry en;
+        const void *data = nullptr;
+        if (!m27b_blob_entry(blob, i, &en, &data, err, err_cap)) return false;
+        if (en.source_model != source) continue;
+        // the payload of an entry must hold the tensor its shape describes
+        const uint32_t base = en.ggml_type;
+        const uint64_t need = base == M27B_TYPE_F32 ? (uint64_t)en.row_elems * en.row_count * 4
+                                                    : (uint64_t)en.row_count * (en.row_elems / block_elems(base)) *
+                                                          block_bytes(base);
+        if (need == 0 || en.data_bytes < need)
+            return efail(err, err_cap, "m27b_engine_load_blob: entry %s: %llu bytes for a %ux%u type-%u tensor",
+                         en.name, (unsigned long long)en.data_bytes, en.row_count, en.row_elems, en.ggml_type);
+        ECALL(m27b_engine_load_tensor(e, en.name, en.ggml_type, en.row_elems, en.row_count, data, err, err_cap));
+        ++loaded;
+    }
+    if (loaded == 0) return efail(err, err_cap, "m27b_engine_load_blob: no entry of source %u", source);
+    if (err && err_cap) err[0] = '\0';
+    return true;
 }
 
 bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char *err, size_t err_cap) {

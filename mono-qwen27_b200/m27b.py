@@ -374,6 +374,11 @@ class Engine:
         self._call("m27b_engine_load_tensor", self.h, name.encode(), ggml_type, row_elems, row_count,
                    ctypes.c_void_p(a.ctypes.data))
 
+    def load_blob(self, blob, source=1):
+        """Load a .m27b blob's entries of `source` (a Blob, or a path)."""
+        b = blob if isinstance(blob, Blob) else Blob(blob)
+        engine_load_blob(self, b, source)
+
     def random_weights(self, seed=0, sigma=0.02):
         self._call("m27b_engine_random_weights", self.h, seed, ctypes.c_float(sigma))
 
@@ -415,3 +420,140 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+# --------------------------------------------------------------------------
+# .m27b blobs (include/m27b_blob.h)
+
+SOURCE_TARGET, SOURCE_DRAFT = 1, 2
+ROLE_NONE, ROLE_TARGET_MATVEC, ROLE_DRAFT_MATVEC, ROLE_OUTPUT_HEAD = 0, 1, 2, 3
+
+
+class BlobHeader(ctypes.Structure):
+    _fields_ = [("magic", ctypes.c_uint32), ("schema_version", ctypes.c_uint32), ("section_count", ctypes.c_uint32),
+                ("reserved0", ctypes.c_uint32), ("file_bytes", ctypes.c_uint64), ("tensor_table_offset", ctypes.c_uint64),
+                ("section_table_offset", ctypes.c_uint64), ("tokenizer_offset", ctypes.c_uint64),
+                ("tokenizer_bytes", ctypes.c_uint64), ("max_ctx_hint", ctypes.c_uint32),
+                ("target_layers", ctypes.c_uint32), ("draft_layers", ctypes.c_uint32), ("target_arch", ctypes.c_char * 16),
+                ("draft_arch", ctypes.c_char * 16), ("target_quant", ctypes.c_char * 16),
+                ("draft_quant", ctypes.c_char * 16)]
+
+
+class WeightEntry(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 64), ("ggml_type", ctypes.c_uint32), ("source_model", ctypes.c_uint32),
+                ("role", ctypes.c_uint32), ("row_elems", ctypes.c_uint32), ("row_count", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32), ("data_offset", ctypes.c_uint64), ("data_bytes", ctypes.c_uint64)]
+
+
+class PackTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("ggml_type", ctypes.c_uint32), ("source", ctypes.c_uint32),
+                ("role", ctypes.c_uint32), ("row_elems", ctypes.c_uint32), ("row_count", ctypes.c_uint32),
+                ("data", ctypes.c_void_p), ("bytes", ctypes.c_uint64)]
+
+
+class PackInfo(ctypes.Structure):
+    _fields_ = [("max_ctx_hint", ctypes.c_uint32), ("target_layers", ctypes.c_uint32), ("draft_layers", ctypes.c_uint32),
+                ("target_arch", ctypes.c_char_p), ("draft_arch", ctypes.c_char_p), ("target_quant", ctypes.c_char_p),
+                ("draft_quant", ctypes.c_char_p), ("vocab_size", ctypes.c_uint32), ("bos_id", ctypes.c_uint32),
+                ("eos_id", ctypes.c_uint32), ("im_start_id", ctypes.c_uint32), ("im_end_id", ctypes.c_uint32)]
+
+
+def _blob_lib():
+    L = lib()
+    if getattr(L, "_blob_sigs", False):
+        return L
+    vp, cp, sz, b = ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_bool
+    L.m27b_blob_pack.restype = b
+    L.m27b_blob_pack.argtypes = [cp, ctypes.POINTER(PackInfo), ctypes.POINTER(PackTensor), sz, cp, sz]
+    L.m27b_blob_open.restype = b
+    L.m27b_blob_open.argtypes = [cp, ctypes.POINTER(vp), cp, sz]
+    L.m27b_blob_header.restype = ctypes.POINTER(BlobHeader)
+    L.m27b_blob_header.argtypes = [vp]
+    L.m27b_blob_count.restype = sz
+    L.m27b_blob_count.argtypes = [vp]
+    L.m27b_blob_entry.restype = b
+    L.m27b_blob_entry.argtypes = [vp, sz, ctypes.POINTER(WeightEntry), ctypes.POINTER(vp), cp, sz]
+    L.m27b_blob_close.restype = None
+    L.m27b_blob_close.argtypes = [vp]
+    L.m27b_engine_load_blob.restype = b
+    L.m27b_engine_load_blob.argtypes = [vp, vp, ctypes.c_uint32, cp, sz]
+    L._blob_sigs = True
+    return L
+
+
+def blob_pack(path, tensors, max_ctx_hint=8192, target_layers=0, draft_layers=0, target_arch="qwen35",
+              draft_arch="dflash-draft", target_quant="q4_k_m", draft_quant="q8_0", vocab_size=1, bos_id=0, eos_id=0,
+              im_start_id=0, im_end_id=0):
+    """Write a .m27b blob.  tensors: iterable of dicts with name, ggml_type,
+    data (numpy bytes in GGUF layout or fp32), row_elems, row_count and
+    optionally source (default target) and role (default: output head for
+    output.weight, target/draft matvec for quantized 2-D tensors, 0 otherwise)."""
+    import numpy as np
+    keep, arr = [], []
+    for t in tensors:
+        d = np.ascontiguousarray(t["data"])
+        keep.append(d)
+        src = t.get("source", SOURCE_TARGET)
+        role = t.get("role")
+        if role is None:
+            if t["name"] == "output.weight":
+                role = ROLE_OUTPUT_HEAD
+            elif t["ggml_type"] != F32 and t["row_count"] > 1:
+                role = ROLE_TARGET_MATVEC if src == SOURCE_TARGET else ROLE_DRAFT_MATVEC
+            else:
+                role = ROLE_NONE
+        arr.append(PackTensor(t["name"].encode(), t["ggml_type"], src, role, t["row_elems"], t["row_count"],
+                              ctypes.c_void_p(d.ctypes.data), d.nbytes))
+    tarr = (PackTensor * len(arr))(*arr)
+    info = PackInfo(max_ctx_hint, target_layers, draft_layers, target_arch.encode(), draft_arch.encode(),
+                    target_quant.encode(), draft_quant.encode(), vocab_size, bos_id, eos_id, im_start_id, im_end_id)
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(_blob_lib().m27b_blob_pack(str(path).encode(), ctypes.byref(info), tarr, len(arr), err, ERR_CAP), err,
+           "m27b_blob_pack")
+
+
+class Blob:
+    """A mapped, validated .m27b blob."""
+
+    def __init__(self, path):
+        self.L = _blob_lib()
+        self.h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(ERR_CAP)
+        _check(self.L.m27b_blob_open(str(path).encode(), ctypes.byref(self.h), err, ERR_CAP), err, "m27b_blob_open")
+
+    @property
+    def header(self):
+        return self.L.m27b_blob_header(self.h).contents
+
+    def __len__(self):
+        return self.L.m27b_blob_count(self.h)
+
+    def entry(self, i):
+        """(WeightEntry, payload as a read-only numpy uint8 view of the mapping)."""
+        import numpy as np
+        e = WeightEntry()
+        p = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(ERR_CAP)
+        _check(self.L.m27b_blob_entry(self.h, i, ctypes.byref(e), ctypes.byref(p), err, ERR_CAP), err,
+               "m27b_blob_entry")
+        buf = (ctypes.c_uint8 * e.data_bytes).from_address(p.value)
+        return e, np.frombuffer(buf, dtype=np.uint8)
+
+    def entries(self):
+        return [self.entry(i) for i in range(len(self))]
+
+    def close(self):
+        if self.h:
+            self.L.m27b_blob_close(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def engine_load_blob(engine, blob, source=SOURCE_TARGET):
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(_blob_lib().m27b_engine_load_blob(engine.h, blob.h, source, err, ERR_CAP), err, "m27b_engine_load_blob")

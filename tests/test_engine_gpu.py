@@ -105,6 +105,30 @@ def test_engine_generate_matches_steps(orc, m27b):
         e.close()
 
 
+def test_engine_load_blob_equals_tensors(orc, m27b, tmp_path):
+    # a model packed into a .m27b blob and loaded from it decodes bit for bit
+    # like the same tensors loaded one by one
+    c = dict(R.TINY, n_layers=2)
+    model = R.make_model(orc, c, seed=8)
+    path = tmp_path / "m.m27b"
+    m27b.blob_pack(path, [dict(name=n, ggml_type=t, row_elems=re, row_count=rc, data=d)
+                          for n, (t, re, rc, d) in model.items()], target_layers=c["n_layers"], vocab_size=c["vocab"])
+    outs = []
+    for via_blob in (False, True):
+        e = _engine(m27b, c)
+        try:
+            if via_blob:
+                e.load_blob(path)
+            else:
+                _load(e, model)
+            steps = [e.decode_step(t, pos, logits=True) for pos, t in enumerate([4, 40, 400])]
+            outs.append([(tok, lg.copy()) for tok, lg in steps])
+        finally:
+            e.close()
+    for (t0, l0), (t1, l1) in zip(*outs):
+        assert t0 == t1 and np.array_equal(l0, l1)
+
+
 def test_engine_errors(m27b):
     e = _engine(m27b, R.TINY)
     try:
