@@ -387,6 +387,15 @@ def decode_bench(args, world, rank, dev, dist, uuid):
             return out
 
         ms_e2e, gen_e2e, _ = timed(host_loop)
+        # speculative verification: one pass over n drafted tokens (tensor cores for the q4_K matrices)
+        verify = {}
+        if world == 1 or args.comm == "nccl":
+            vt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.vocab, 16)]
+            for n in (8, 16):
+                e.verify(vt[:n], p0)  # capture
+                reps = 5
+                vms, _, _ = timed(lambda: [e.verify(vt[:n], p0) for _ in range(reps)])
+                verify[str(n)] = {"ms_per_pass": round(vms / reps, 4), "tokens_per_s": round(n * reps / (vms / 1e3), 1)}
         wb = e.weight_bytes_per_token()
         kv_bytes = 2 * args.layers * (p0 + 1 + args.gen / 2) * e_kv_heads(cfg) * cfg.head_dim * 4
         tps = args.gen / (ms / 1e3)
@@ -399,6 +408,7 @@ def decode_bench(args, world, rank, dev, dist, uuid):
             "weight_gbs_per_rank": round(per_rank_gbs, 1), "weight_gbs_total": round(per_rank_gbs * world, 1),
             "roofline_frac": round(per_rank_gbs / peak, 4), "peak_gbs": peak, "peak_kind": peak_kind,
             "tokens_match": list(map(int, gen)) == list(map(int, gen_e2e)),
+            "verify": verify,
             "layers": args.layers, "prompt": args.prompt, "gen": args.gen, "weights_init_s": round(t_load, 1),
             "allreduce": "none" if world == 1 else ("fused NVLink push (P2P stores + release flags)" if args.comm == "p2p"
                                                    else "NCCL all-reduce"),

@@ -52,6 +52,9 @@ typedef struct M27BModelConfig {
     int max_ctx;      /* KV cache positions */
     int tp_rank;      /* this process's tensor-parallel rank */
     int tp_size;      /* 1, 2, 4 or 8 */
+    uint32_t weight_type; /* m27b_engine_random_weights: 0 = the q4_k_m mix
+                             (q4_K, q6_K for ffn_down and output), 8 = q8_0
+                             everywhere (a draft model) */
 } M27BModelConfig;
 
 typedef struct M27BEngine M27BEngine;
@@ -123,6 +126,21 @@ M27B_API bool m27b_engine_reset(M27BEngine *e, char *err, size_t err_cap);
  * graph that later steps replay; synchronises before returning. */
 M27B_API bool m27b_engine_decode_step(M27BEngine *e, int token, int pos, int *next, float *logits, char *err,
                                       size_t err_cap);
+
+/* Most tokens m27b_engine_verify takes in one pass. */
+#define M27B_VERIFY_MAX 16
+
+/* Speculative verification: run the n (1..M27B_VERIFY_MAX) tokens tokens[0..n)
+ * at positions pos .. pos+n-1 in one pass — their K/V appended, token i
+ * attending to the cache up to position pos+i — and write the greedy next
+ * token after each to next[i] (the target's choice at every drafted
+ * position; tokens a caller rejects leave K/V behind that later steps simply
+ * overwrite).  q4_K matrices run 5+ tokens on the tensor cores.  logits
+ * (tp_size 1 only, may be NULL) receive n rows of vocab floats.  The pass is
+ * captured into a CUDA graph per n on first use; not with the fused NVLink
+ * all-reduce (NCCL or tp_size 1).  Synchronises before returning. */
+M27B_API bool m27b_engine_verify(M27BEngine *e, const int *tokens, int n, int pos, int *next, float *logits, char *err,
+                                 size_t err_cap);
 
 /* Greedy generation of n tokens on the device: step i (position pos + i)
  * consumes the token step i-1 produced (`token` for i = 0), with no host

@@ -10,7 +10,7 @@
 namespace m27b {
 cudaError_t attn_prepare();
 cudaError_t attn_launch(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
-                        int nq, int nkv, int hd, int S, float scale, cudaStream_t st);
+                        int nq, int nkv, int hd, int S, float scale, cudaStream_t st, int n_tok = 1);
 }  // namespace m27b
 
 namespace {

@@ -26,7 +26,7 @@
 namespace m27b {
 __global__ void k_qk_norm_rope_cache(const float *qkv, const float *q_norm, const float *k_norm, float *q, float *gate,
                                      float *kc, float *vc, const int *pos_p, int nq, int nkv, int hd, int n_rot,
-                                     float theta, float eps);
+                                     float theta, float eps, int qkv_stride, int qg_stride);
 cudaError_t attn_prepare();
 bool attn_fused_supported(int hd);
 cudaError_t attn_fused_launch(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
@@ -34,7 +34,7 @@ cudaError_t attn_fused_launch(const float *qkv, const float *q_norm, const float
                               const float2 *rope, int n_rot, float eps, cudaStream_t st);
 cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float theta, cudaStream_t st);
 cudaError_t attn_launch(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
-                        int nq, int nkv, int hd, int S, float scale, cudaStream_t st);
+                        int nq, int nkv, int hd, int S, float scale, cudaStream_t st, int n_tok = 1);
 __global__ void k_fill_blocks(uint8_t *out, int type, int rows, int nblk, long row0, int blk0, uint64_t seed, int tid,
                               float sigma);
 __global__ void k_fill_f32(float *out, long n, float v);
@@ -84,6 +84,11 @@ size_t block_bytes(uint32_t t) { return t == M27B_TYPE_Q4_K ? 144 : t == M27B_TY
 int block_elems(uint32_t t) { return t == M27B_TYPE_Q8_0 ? 32 : 256; }
 
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// q8_0 matrices take q8_0 activations, the k-quants q8_K (ggml's pairing).
+uint32_t act_type_of(uint32_t weight_type) {
+    return weight_type == M27B_TYPE_Q8_0 ? M27B_TYPE_Q8_0 : M27B_TYPE_Q8_K;
+}
 
 // Receive window of the fused all-reduce (same layout on every rank), in
 // epoch-tagged 8-byte words {value bits, epoch}:
@@ -140,6 +145,10 @@ struct M27BEngine {
     float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *q = nullptr, *gate = nullptr, *o = nullptr, *a = nullptr;
     float *part = nullptr, *logits = nullptr;
     float2 *rope = nullptr;  // (cos, sin) of the step's position, n_rot/2 pairs
+    int *vtok = nullptr;                 // device: the tokens of a verify pass
+    int *h_vtok = nullptr;               // pinned copy
+    unsigned long long *h_vbest = nullptr;  // pinned: the verify pass's argmax keys
+    cudaGraphExec_t vgraph[M27B_VERIFY_MAX + 1] = {};  // verify pass, per token count
     uint8_t *xq = nullptr;
     unsigned long long *best = nullptr;
     int *ctl = nullptr;                      // device [token, pos, generated count, pad]
@@ -307,6 +316,13 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
     const int hd = c.head_dim;
     const bool r0 = c.tp_rank == 0;
     const bool p2p = e->p2p;
+    if (p2p) {
+        // the fused all-reduce's consumer hands its successors q8_K activations
+        bool k_quants = e->lmh.type != M27B_TYPE_Q8_0;
+        for (const Layer &Ly : e->L)
+            k_quants = k_quants && Ly.wqkv.type != M27B_TYPE_Q8_0 && Ly.wg.type != M27B_TYPE_Q8_0;
+        if (!k_quants) return efail(err, err_cap, "the fused NVLink all-reduce needs k-quant (not q8_0) matrices");
+    }
     const int *pos = e->ctl + 1;
     ECALL(m27b_dequant_rows(&e->embd.v, e->ctl, 1, e->h, c.hidden, e->st, err, err_cap));
     ECUDA(rope_table_launch(e->rope, pos, c.n_rot, c.rope_theta, e->st));  // this step's rotary table
@@ -323,18 +339,18 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         else
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wqkv.v, nullptr, e->h, c.hidden, Ly.attn_norm, c.rms_eps, 1, e->xq, e->qkv,
                                        Ly.wqkv.rows, nullptr, e->st, err, err_cap));
-        if (attn_fused_supported(hd)) {
+        if (attn_fused_supported(hd) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
             // q/k norm + RoPE + KV append + attention, then reduce + gate + q8_K for o_proj
             ECUDA(attn_fused_launch(e->qkv, Ly.q_norm, Ly.k_norm, Ly.kc, Ly.vc, e->part, e->xq, pos, e->H, e->KV, hd,
                                     e->S, 1.0f / sqrtf((float)hd), e->rope, c.n_rot, c.rms_eps, e->st));
         } else {
             ECUDA(launch_pdl(k_qk_norm_rope_cache, dim3(e->H + e->KV), dim3(hd), (size_t)(hd + 32) * 4, e->st,
                              (const float *)e->qkv, (const float *)Ly.q_norm, (const float *)Ly.k_norm, e->q, e->gate,
-                             Ly.kc, Ly.vc, pos, e->H, e->KV, hd, c.n_rot, c.rope_theta, c.rms_eps));
+                             Ly.kc, Ly.vc, pos, e->H, e->KV, hd, c.n_rot, c.rope_theta, c.rms_eps, 0, 0));
             ECUDA(attn_launch(e->q, Ly.kc, Ly.vc, e->part, e->o, pos, e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd),
                               e->st));
-            ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, 1, e->H * hd, M27B_TYPE_Q8_K, e->xq, e->st, err,
-                                       err_cap));
+            ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, 1, e->H * hd, act_type_of(Ly.wo.type), e->xq, e->st,
+                                       err, err_cap));
         }
         // o_proj partial (+ residual on rank 0), summed over ranks -> h2, then post-attention RMSNorm -> xq
         if (p2p) {
@@ -347,7 +363,7 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
                                        nullptr, e->st, err, err_cap));
         }
-        ECALL(m27b_act_quant(e->a, e->F, 1, e->F, M27B_TYPE_Q8_K, e->xq, e->st, err, err_cap));
+        ECALL(m27b_act_quant(e->a, e->F, 1, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
         // down partial (+ residual on rank 0), summed over ranks -> h, then the
         // next layer's input RMSNorm (the output norm after the last layer) -> xq
         const float *next_norm = l + 1 < c.n_layers ? e->L[l + 1].attn_norm : e->out_norm;
@@ -360,8 +376,8 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         }
     }
     if (!p2p)
-        ECALL(m27b_act_quant_rmsnorm(e->h, e->out_norm, c.rms_eps, c.hidden, 1, c.hidden, M27B_TYPE_Q8_K, e->xq, e->st,
-                                     err, err_cap));
+        ECALL(m27b_act_quant_rmsnorm(e->h, e->out_norm, c.rms_eps, c.hidden, 1, c.hidden, act_type_of(e->lmh.type),
+                                     e->xq, e->st, err, err_cap));
     ECALL(m27b_qmv_argmax(&e->lmh.v, e->xq, 1, e->logits, e->V, e->best, (uint32_t)e->v_lo, e->st, err, err_cap));
     // next token and position for the following step (greedy generation on the device)
     if (p2p) {
@@ -379,6 +395,42 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         k_advance<<<1, 32, 0, e->st>>>(e->best, e->ctl, e->hist, c.max_ctx);
     }
     ECUDA(cudaGetLastError());
+    return true;
+}
+
+// Enqueue a verify pass over n tokens (device e->vtok, positions ctl[1] ..
+// ctl[1]+n-1): the same layer arithmetic as enqueue_step on n rows, with the
+// unfused attention (each token at its own position) and the NCCL all-reduce.
+bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
+    const M27BModelConfig &c = e->c;
+    const int hd = c.head_dim, D = c.hidden;
+    const bool r0 = c.tp_rank == 0;
+    const int *pos = e->ctl + 1;
+    const int qkv_rows = e->H * 2 * hd + 2 * e->KV * hd;
+    ECALL(m27b_dequant_rows(&e->embd.v, e->vtok, n, e->h, D, e->st, err, err_cap));
+    for (int l = 0; l < c.n_layers; ++l) {
+        Layer &Ly = e->L[l];
+        ECALL(m27b_qmv_f32_rmsnorm(&Ly.wqkv.v, nullptr, e->h, D, Ly.attn_norm, c.rms_eps, n, e->xq, e->qkv, qkv_rows,
+                                   nullptr, e->st, err, err_cap));
+        ECUDA(launch_pdl(k_qk_norm_rope_cache, dim3(e->H + e->KV, n), dim3(hd), (size_t)(hd + 32) * 4, e->st,
+                         (const float *)e->qkv, (const float *)Ly.q_norm, (const float *)Ly.k_norm, e->q, e->gate, Ly.kc,
+                         Ly.vc, pos, e->H, e->KV, hd, c.n_rot, c.rope_theta, c.rms_eps, qkv_rows, e->H * hd));
+        ECUDA(attn_launch(e->q, Ly.kc, Ly.vc, e->part, e->o, pos, e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd), e->st,
+                          n));
+        ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, n, e->H * hd, act_type_of(Ly.wo.type), e->xq, e->st, err,
+                                   err_cap));
+        ECALL(m27b_qmv(&Ly.wo.v, e->xq, n, e->h2, D, r0 ? e->h : nullptr, e->st, err, err_cap));
+        if (c.tp_size > 1) ENCCL(ncclAllReduce(e->h2, e->h2, (size_t)n * D, ncclFloat32, ncclSum, e->comm, e->st));
+        ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, D, Ly.post_norm, c.rms_eps, n, e->xq, e->a, e->F, nullptr,
+                                   e->st, err, err_cap));
+        ECALL(m27b_act_quant(e->a, e->F, n, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
+        ECALL(m27b_qmv(&Ly.wd.v, e->xq, n, e->h, D, r0 ? e->h2 : nullptr, e->st, err, err_cap));
+        if (c.tp_size > 1) ENCCL(ncclAllReduce(e->h, e->h, (size_t)n * D, ncclFloat32, ncclSum, e->comm, e->st));
+    }
+    ECALL(m27b_act_quant_rmsnorm(e->h, e->out_norm, c.rms_eps, D, n, D, act_type_of(e->lmh.type), e->xq, e->st, err,
+                                 err_cap));
+    ECALL(m27b_qmv_argmax(&e->lmh.v, e->xq, n, e->logits, e->V, e->best, (uint32_t)e->v_lo, e->st, err, err_cap));
+    if (c.tp_size > 1) ENCCL(ncclAllReduce(e->best, e->best, (size_t)n, ncclUint64, ncclMax, e->comm, e->st));
     return true;
 }
 
@@ -521,13 +573,14 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
     char e2[512];
     auto A = [&](void **p, size_t n) { return dalloc(e, p, n, e2, sizeof(e2)); };
     const int xmax = std::max(std::max(c.hidden, e->F), e->H * hd);
-    bool ok = A((void **)&e->h, (size_t)c.hidden * 4) && A((void **)&e->h2, (size_t)c.hidden * 4) &&
-              A((void **)&e->qkv, (size_t)(e->H * 2 + e->KV * 2) * hd * 4) && A((void **)&e->q, (size_t)e->H * hd * 4) &&
-              A((void **)&e->gate, (size_t)e->H * hd * 4) && A((void **)&e->o, (size_t)e->H * hd * 4) &&
-              A((void **)&e->a, (size_t)e->F * 4) && A((void **)&e->part, (size_t)e->S * e->H * (hd + 4) * 4) &&
-              A((void **)&e->logits, (size_t)e->V * 4) && A((void **)&e->xq, m27b_act_bytes(M27B_TYPE_Q8_K, xmax)) &&
-              A((void **)&e->best, 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4) &&
-              A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2));
+    const size_t VM = M27B_VERIFY_MAX;  // activation buffers hold a whole verify pass
+    bool ok = A((void **)&e->h, VM * c.hidden * 4) && A((void **)&e->h2, VM * c.hidden * 4) &&
+              A((void **)&e->qkv, VM * (e->H * 2 + e->KV * 2) * hd * 4) && A((void **)&e->q, VM * e->H * hd * 4) &&
+              A((void **)&e->gate, VM * e->H * hd * 4) && A((void **)&e->o, VM * e->H * hd * 4) &&
+              A((void **)&e->a, VM * e->F * 4) && A((void **)&e->part, VM * e->S * e->H * (hd + 4) * 4) &&
+              A((void **)&e->logits, VM * e->V * 4) && A((void **)&e->xq, VM * m27b_act_bytes(M27B_TYPE_Q8_K, xmax)) &&
+              A((void **)&e->best, VM * 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4) &&
+              A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2)) && A((void **)&e->vtok, VM * 4);
     for (int l = 0; ok && l < c.n_layers; ++l) {
         const size_t kvb = (size_t)c.max_ctx * e->KV * hd * 4;
         ok = A((void **)&e->L[l].kc, kvb) && A((void **)&e->L[l].vc, kvb) &&
@@ -536,7 +589,9 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
     ok = ok && cudaMemset(e->ctl, 0, 16) == cudaSuccess;
     if (!ok) return bail(efail(err, err_cap, "%s", e2));
     if (cudaMallocHost((void **)&e->h_ctl, 16) != cudaSuccess || cudaMallocHost((void **)&e->h_best, 8) != cudaSuccess ||
-        cudaMallocHost((void **)&e->h_hist, (size_t)c.max_ctx * 4) != cudaSuccess)
+        cudaMallocHost((void **)&e->h_hist, (size_t)c.max_ctx * 4) != cudaSuccess ||
+        cudaMallocHost((void **)&e->h_vtok, M27B_VERIFY_MAX * 4) != cudaSuccess ||
+        cudaMallocHost((void **)&e->h_vbest, M27B_VERIFY_MAX * 8) != cudaSuccess)
         return bail(efail(err, err_cap, "pinned allocation failed"));
     if (attn_prepare() != cudaSuccess)
         return bail(efail(err, err_cap, "attention shared-memory opt-in failed"));
@@ -700,7 +755,10 @@ bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char 
     if (!e) return efail(err, err_cap, "null engine");
     const M27BModelConfig &c = e->c;
     const int hd = c.head_dim;
-    const uint32_t Q4 = M27B_TYPE_Q4_K, Q6 = M27B_TYPE_Q6_K;
+    if (c.weight_type != 0 && c.weight_type != M27B_TYPE_Q8_0)
+        return efail(err, err_cap, "weight_type must be 0 (q4_k_m mix) or 8 (q8_0)");
+    const bool q80 = c.weight_type == M27B_TYPE_Q8_0;
+    const uint32_t Q4 = q80 ? M27B_TYPE_Q8_0 : M27B_TYPE_Q4_K, Q6 = q80 ? M27B_TYPE_Q8_0 : M27B_TYPE_Q6_K;
     auto ones = [&](float **p, size_t n) -> bool {
         if (!*p) ECALL(dalloc(e, (void **)p, n * 4, err, err_cap));
         k_fill_f32<<<64, 256, 0, e->st>>>(*p, (long)n, 1.0f);
@@ -729,13 +787,13 @@ bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char 
         ECALL(fill_slice(e, Ly.wqkv, tid + 3, seed, sigma, (long)e->kv_lo * hd, e->KV * hd, 0,
                          e->H * 2 * hd + e->KV * hd, err, err_cap));
         ECALL(ensure_mat(e, Ly.wo, Q4, c.hidden, e->H * hd, err, err_cap));
-        ECALL(fill_slice(e, Ly.wo, tid + 4, seed, sigma, 0, c.hidden, e->q_lo * hd / 256, 0, err, err_cap));
+        ECALL(fill_slice(e, Ly.wo, tid + 4, seed, sigma, 0, c.hidden, e->q_lo * hd / block_elems(Q4), 0, err, err_cap));
         ECALL(ensure_mat(e, Ly.wg, Q4, e->F, c.hidden, err, err_cap));
         ECALL(fill_slice(e, Ly.wg, tid + 5, seed, sigma, e->f_lo, e->F, 0, 0, err, err_cap));
         ECALL(ensure_mat(e, Ly.wu, Q4, e->F, c.hidden, err, err_cap));
         ECALL(fill_slice(e, Ly.wu, tid + 6, seed, sigma, e->f_lo, e->F, 0, 0, err, err_cap));
         ECALL(ensure_mat(e, Ly.wd, Q6, c.hidden, e->F, err, err_cap));
-        ECALL(fill_slice(e, Ly.wd, tid + 7, seed, sigma, 0, c.hidden, e->f_lo / 256, 0, err, err_cap));
+        ECALL(fill_slice(e, Ly.wd, tid + 7, seed, sigma, 0, c.hidden, e->f_lo / block_elems(Q6), 0, err, err_cap));
         ECALL(ones(&Ly.attn_norm, c.hidden));
         ECALL(ones(&Ly.post_norm, c.hidden));
         ECALL(ones(&Ly.q_norm, hd));
@@ -797,6 +855,47 @@ bool m27b_engine_generate(M27BEngine *e, int token, int pos, int n, int *tokens,
     return true;
 }
 
+bool m27b_engine_verify(M27BEngine *e, const int *tokens, int n, int pos, int *next, float *logits, char *err,
+                        size_t err_cap) {
+    if (!e || !tokens || !next) return efail(err, err_cap, "m27b_engine_verify: null argument");
+    if (n < 1 || n > M27B_VERIFY_MAX) return efail(err, err_cap, "m27b_engine_verify: n must be in [1, %d]", M27B_VERIFY_MAX);
+    if (e->p2p) return efail(err, err_cap, "m27b_engine_verify: not with the fused NVLink all-reduce");
+    if (logits && e->c.tp_size != 1) return efail(err, err_cap, "logits are only returned with tp_size 1");
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= e->c.vocab)
+            return efail(err, err_cap, "token %d outside the vocabulary", tokens[i]);
+    ECALL(check_ready(e, pos, n, err, err_cap));
+    std::memcpy(e->h_vtok, tokens, (size_t)n * 4);
+    ECUDA(cudaMemcpyAsync(e->vtok, e->h_vtok, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
+    ECALL(set_ctl(e, tokens[0], pos, err, err_cap));
+    if (!e->vgraph[n]) {
+        // eager once (module loading, first-use set-up), then capture; the
+        // replay rewrites the same KV-cache entries
+        ECALL(enqueue_verify(e, n, err, err_cap));
+        ECUDA(cudaStreamSynchronize(e->st));
+        ECUDA(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+        const bool ok = enqueue_verify(e, n, err, err_cap);
+        cudaGraph_t g = nullptr;
+        const cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+        if (!ok) {
+            if (g) cudaGraphDestroy(g);
+            return false;
+        }
+        ECUDA(ce);
+        const cudaError_t ie = cudaGraphInstantiate(&e->vgraph[n], g, 0);
+        cudaGraphDestroy(g);
+        ECUDA(ie);
+    }
+    ECUDA(cudaGraphLaunch(e->vgraph[n], e->st));
+    ECUDA(cudaMemcpyAsync(e->h_vbest, e->best, (size_t)n * 8, cudaMemcpyDeviceToHost, e->st));
+    if (logits) ECUDA(cudaMemcpyAsync(logits, e->logits, (size_t)n * e->V * 4, cudaMemcpyDeviceToHost, e->st));
+    ECUDA(cudaStreamSynchronize(e->st));
+    for (int i = 0; i < n; ++i) next[i] = (int)m27b_argmax_key_index(e->h_vbest[i]);
+    ECALL(check_status(err, err_cap));
+    if (err && err_cap) err[0] = '\0';
+    return true;
+}
+
 bool m27b_engine_hidden(M27BEngine *e, float *host, char *err, size_t err_cap) {
     if (!e || !host) return efail(err, err_cap, "null argument");
     ECUDA(cudaMemcpyAsync(host, e->h, (size_t)e->c.hidden * 4, cudaMemcpyDeviceToHost, e->st));
@@ -810,13 +909,18 @@ void *m27b_engine_stream(M27BEngine *e) { return e ? (void *)e->st : nullptr; }
 void m27b_engine_destroy(M27BEngine *e) {
     if (!e) return;
     if (e->st) cudaStreamSynchronize(e->st);
-    if (e->gexec) cudaGraphExecDestroy(e->gexec);  // before the communicator it holds
+    // graphs before the communicator they hold
+    if (e->gexec) cudaGraphExecDestroy(e->gexec);
+    for (cudaGraphExec_t g : e->vgraph)
+        if (g) cudaGraphExecDestroy(g);
     for (int q = 0; q < 8; ++q)
         if (e->peer_win[q] && e->peer_win[q] != e->win) cudaIpcCloseMemHandle(e->peer_win[q]);
     if (e->win) cudaFree(e->win);
     if (e->comm) ncclCommDestroy(e->comm);
     for (void *p : e->allocs) cudaFree(p);
     if (e->scratch) cudaFree(e->scratch);
+    if (e->h_vtok) cudaFreeHost(e->h_vtok);
+    if (e->h_vbest) cudaFreeHost(e->h_vbest);
     if (e->h_ctl) cudaFreeHost(e->h_ctl);
     if (e->h_hist) cudaFreeHost(e->h_hist);
     if (e->h_best) cudaFreeHost(e->h_best);

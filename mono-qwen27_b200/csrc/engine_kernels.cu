@@ -17,18 +17,22 @@ namespace m27b {
 
 // ---------------------------------------------------------------------------
 // q/k RMSNorm + RoPE + KV-cache append.
-// qkv (one matvec output) = [local q/gate heads interleaved, 2*hd each |
-// local k heads, hd each | local v heads, hd each].  CTA h < nq handles q head
-// h (writes q[h] and gate[h]); CTA nq + j handles kv head j (writes K/V cache
-// at position *pos).  blockDim.x = hd.
+// qkv (one matvec output row per token) = [local q/gate heads interleaved,
+// 2*hd each | local k heads, hd each | local v heads, hd each].  Grid
+// (nq + nkv, tokens): CTA (h < nq, t) handles q head h of token t (writes
+// q[t][h] and gate[t][h]); CTA (nq + j, t) handles kv head j (writes the K/V
+// cache at position *pos + t).  blockDim.x = hd.
 __global__ void k_qk_norm_rope_cache(const float *qkv, const float *q_norm, const float *k_norm, float *q, float *gate,
                                      float *kc, float *vc, const int *pos_p, int nq, int nkv, int hd, int n_rot,
-                                     float theta, float eps) {
+                                     float theta, float eps, int qkv_stride, int qg_stride) {
     pdl_wait();
     pdl_trigger();
     extern __shared__ float sh[];  // hd values + 32 partials
-    const int h = blockIdx.x, d = threadIdx.x;
-    const int pos = *pos_p;
+    const int h = blockIdx.x, d = threadIdx.x, t = blockIdx.y;
+    const int pos = *pos_p + t;
+    qkv += (size_t)t * qkv_stride;
+    q += (size_t)t * qg_stride;
+    gate += (size_t)t * qg_stride;
     const bool is_q = h < nq;
     const float *src = is_q ? qkv + (size_t)h * 2 * hd : qkv + (size_t)nq * 2 * hd + (size_t)(h - nq) * hd;
     const float v = src[d];
@@ -106,13 +110,17 @@ M27B_DI void ld_dims(const float *p, float (&v)[DPL]) {
 
 template <int DPL>
 __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const float *kc, const float *vc, float *part,
-                                                      const int *pos_p, int nq, int nkv, float scale) {
+                                                      const int *pos_p, int nq, int nkv, float scale, int q_stride,
+                                                      int part_stride) {
     pdl_wait();
     pdl_trigger();
     constexpr int hd = DPL * 32, rec = hd + 4;
     const int j = blockIdx.x, s = blockIdx.y;
     const int G = nq / nkv;
-    const int L = *pos_p + 1;
+    // token z of a batch sees the cache up to its own position *pos + z
+    q += (size_t)blockIdx.z * q_stride;
+    part += (size_t)blockIdx.z * part_stride;
+    const int L = *pos_p + 1 + (int)blockIdx.z;
     const int S = att_splits(L, gridDim.y);
     if (s >= S) return;
     const int p0 = (int)(((long)L * s) / S), p1 = (int)(((long)L * (s + 1)) / S);
@@ -188,14 +196,17 @@ __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const floa
 }
 
 template <int DPL>
-__global__ void __launch_bounds__(256) k_attn_reduce(const float *part, float *out, const int *pos_p, int nq, int smax) {
+__global__ void __launch_bounds__(256) k_attn_reduce(const float *part, float *out, const int *pos_p, int nq, int smax,
+                                                     int part_stride, int out_stride) {
     pdl_wait();
     pdl_trigger();
     constexpr int hd = DPL * 32, rec = hd + 4;
     __shared__ __align__(16) float red[8][rec];
     __shared__ float wmax[8];
     const int h = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int S = att_splits(*pos_p + 1, smax);
+    part += (size_t)blockIdx.y * part_stride;
+    out += (size_t)blockIdx.y * out_stride;
+    const int S = att_splits(*pos_p + 1 + (int)blockIdx.y, smax);
     float M = -INFINITY;
     for (int s = warp; s < S; s += 8) M = fmaxf(M, part[((size_t)s * nq + h) * rec + hd]);
     if (lane == 0) wmax[warp] = M;
@@ -454,11 +465,15 @@ size_t attn_smem_bytes(int G, int hd) { return (size_t)(G * hd + 8 * G * (hd + 4
 
 template <int DPL>
 static cudaError_t attn_run(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
-                            int nq, int nkv, int S, float scale, cudaStream_t st) {
-    const size_t smem = attn_smem_bytes(nq / nkv, DPL * 32);
-    cudaError_t e = launch_pdl(k_attn_partial<DPL>, dim3(nkv, S), dim3(256), smem, st, q, kc, vc, part, pos, nq, nkv, scale);
+                            int nq, int nkv, int S, float scale, int n_tok, cudaStream_t st) {
+    constexpr int hd = DPL * 32;
+    const size_t smem = attn_smem_bytes(nq / nkv, hd);
+    const int q_stride = nq * hd, part_stride = S * nq * (hd + 4);
+    cudaError_t e = launch_pdl(k_attn_partial<DPL>, dim3(nkv, S, n_tok), dim3(256), smem, st, q, kc, vc, part, pos, nq,
+                               nkv, scale, q_stride, part_stride);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_attn_reduce<DPL>, dim3(nq), dim3(256), 0, st, (const float *)part, out, pos, nq, S);
+    return launch_pdl(k_attn_reduce<DPL>, dim3(nq, n_tok), dim3(256), 0, st, (const float *)part, out, pos, nq, S,
+                      part_stride, q_stride);
 }
 
 template <int DPL>
@@ -512,19 +527,21 @@ cudaError_t attn_prepare() {
     return e;
 }
 
-// Enqueue decode attention: out[h][:] for the nq local query heads.  part
-// holds S * nq * (hd + 4) floats; hd is a multiple of 32, at most 256.
+// Enqueue decode attention for n_tok consecutive tokens (token t at position
+// *pos + t, attending to the cache up to its own position): out[t][h][:] for
+// the nq local query heads of each token.  q holds n_tok rows of nq * hd,
+// part n_tok * S * nq * (hd + 4) floats; hd is a multiple of 32, at most 256.
 cudaError_t attn_launch(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
-                        int nq, int nkv, int hd, int S, float scale, cudaStream_t st) {
+                        int nq, int nkv, int hd, int S, float scale, cudaStream_t st, int n_tok) {
     switch (hd / 32) {
-        case 1: return attn_run<1>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
-        case 2: return attn_run<2>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
-        case 3: return attn_run<3>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
-        case 4: return attn_run<4>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
-        case 5: return attn_run<5>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
-        case 6: return attn_run<6>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
-        case 7: return attn_run<7>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
-        case 8: return attn_run<8>(q, kc, vc, part, out, pos, nq, nkv, S, scale, st);
+        case 1: return attn_run<1>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
+        case 2: return attn_run<2>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
+        case 3: return attn_run<3>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
+        case 4: return attn_run<4>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
+        case 5: return attn_run<5>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
+        case 6: return attn_run<6>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
+        case 7: return attn_run<7>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
+        case 8: return attn_run<8>(q, kc, vc, part, out, pos, nq, nkv, S, scale, n_tok, st);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -50,6 +50,12 @@ constexpr int MMA_TMEM_COLS = 512;               // D: 2 blocks x 8 sub-blocks x
 constexpr int MMA_ACOL = 256;                    // first TMEM column of the A buffers
 constexpr int MMA_NA = 2;                        // A buffers (half-blocks the unpacking may run ahead)
 constexpr size_t MMA_SMEM_LIMIT = 227 * 1024;
+// Every CTA asks for more than half of an SM's shared memory, so no two CTAs
+// of this kernel (of one launch, or of two launches that programmatic
+// dependent launch overlaps) are ever resident on one SM: each allocates all
+// 512 TMEM columns, and tcgen05.alloc has no bounded form — a second
+// allocator on the SM would wait for the first CTA to exit, unbounded.
+constexpr size_t MMA_SMEM_MIN = 116 * 1024;
 
 struct MmaLayout {
     size_t b, dx, bs, raw, bar, flag, total;
@@ -163,6 +169,12 @@ M27B_DI bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort, 
             return false;
         }
     }
+}
+
+// The same wait for a whole worker warp: every lane leaves with one answer,
+// so a warp never runs its .sync.aligned TMEM accesses with lanes missing.
+M27B_DI bool warp_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort, int *status) {
+    return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort, status)) != 0;
 }
 
 template <int NB>
@@ -368,16 +380,22 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
         bool ok = true;
         for (int j = 0; j < J; ++j) {
             const int bi = j >> 1, q = j & 1, ab = j % MMA_NA;
-            if (q == 0 && !wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) {
+            if (q == 0 && !warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) {
                 ok = false;
                 break;
             }
-            // A buffer ab is free once the MMAs of half-block j - MMA_NA are done
+            // A buffer ab is free once the MMAs of half-block j - MMA_NA are done.
+            // This is also the only wait on those MMAs before the epilogue of
+            // block bi - 1 (at q == 1 it covers that block's last half-block):
+            // waiting again after this warp's a_full arrival below could find
+            // half-block j's MMAs already complete, one phase past the awaited
+            // one, and the parity test would then wait for the phase after.
             if (j >= MMA_NA &&
-                !wait_or_abort(&mma_done[ab], (uint32_t)(((j - MMA_NA) / MMA_NA) & 1), abort, a.status)) {
+                !warp_wait_or_abort(&mma_done[ab], (uint32_t)(((j - MMA_NA) / MMA_NA) & 1), abort, a.status)) {
                 ok = false;
                 break;
             }
+            tc_fence_after();
             const uint8_t *rw = raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144;
             if (q == 0) {
                 const uint4 hd = *(const uint4 *)rw;
@@ -409,12 +427,8 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
                 if (q == 1) mbar_arrive(&empty[bi % stages]);  // this warp is done with the raw stage
             }
             if (q == 1 && bi >= 1) {
-                // block bi - 1: its last half-block's MMAs (half-block j - 2)
-                if (!wait_or_abort(&mma_done[(j - 2) % MMA_NA], (uint32_t)(((j - 2) / MMA_NA) & 1), abort, a.status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+                // block bi - 1: both half-blocks' MMAs were awaited above (j - 3 at
+                // q == 0, j - 2 at this q == 1), before this warp's arrival
                 epilogue(bi - 1);
                 tc_fence_before();
                 __syncwarp();
@@ -424,8 +438,8 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
         if (ok && nblk > 0) {
             // the last block: its two half-blocks' MMAs, then its epilogue
             const bool done =
-                wait_or_abort(&mma_done[(J - 2) % MMA_NA], (uint32_t)(((J - 2) / MMA_NA) & 1), abort, a.status) &&
-                wait_or_abort(&mma_done[(J - 1) % MMA_NA], (uint32_t)(((J - 1) / MMA_NA) & 1), abort, a.status);
+                warp_wait_or_abort(&mma_done[(J - 2) % MMA_NA], (uint32_t)(((J - 2) / MMA_NA) & 1), abort, a.status) &&
+                warp_wait_or_abort(&mma_done[(J - 1) % MMA_NA], (uint32_t)(((J - 1) / MMA_NA) & 1), abort, a.status);
             if (done) {
                 shift_scales();
                 tc_fence_after();
@@ -461,8 +475,9 @@ static cudaError_t run_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream
     if (!encode_rows_u32(&tm, a.w0, a.row_stride, a.rows, 36, MMA_ROWS)) return cudaErrorInvalidValue;
     const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS;
     const int grid = ntiles < sm_count ? ntiles : sm_count;
+    const size_t smem = L.total > MMA_SMEM_MIN ? L.total : MMA_SMEM_MIN;
     *launched = true;
-    return launch_pdl(k_qmv_q4k_mma<NB>, dim3(grid), dim3(MMA_THREADS), L.total, st, a, tm, n_tok, stages);
+    return launch_pdl(k_qmv_q4k_mma<NB>, dim3(grid), dim3(MMA_THREADS), smem, st, a, tm, n_tok, stages);
 }
 
 bool q4k_mma_supported(int rb, int n_tok) {

@@ -284,7 +284,7 @@ class ModelConfig(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("ffn", ctypes.c_int), ("n_head", ctypes.c_int),
                 ("n_kv_head", ctypes.c_int), ("head_dim", ctypes.c_int), ("vocab", ctypes.c_int), ("n_rot", ctypes.c_int),
                 ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("max_ctx", ctypes.c_int),
-                ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int)]
+                ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int), ("weight_type", ctypes.c_uint32)]
 
 
 class Partition(ctypes.Structure):
@@ -320,6 +320,7 @@ def _engine_lib():
         "m27b_engine_reset": (b, [vp, cp, sz]),
         "m27b_engine_decode_step": (b, [vp, i32, i32, ctypes.POINTER(ctypes.c_int), vp, cp, sz]),
         "m27b_engine_generate": (b, [vp, i32, i32, i32, vp, cp, sz]),
+        "m27b_engine_verify": (b, [vp, vp, i32, i32, vp, vp, cp, sz]),
         "m27b_engine_hidden": (b, [vp, vp, cp, sz]),
         "m27b_engine_stream": (vp, [vp]),
         "m27b_engine_destroy": (None, [vp]),
@@ -399,6 +400,16 @@ class Engine:
         out = np.empty(n, dtype=np.int32)
         self._call("m27b_engine_generate", self.h, int(token), int(pos), int(n), ctypes.c_void_p(out.ctypes.data))
         return out
+
+    def verify(self, tokens, pos, logits=False):
+        """Greedy next token after each of `tokens` (at positions pos, pos+1, ...), one pass."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = np.empty(len(t), dtype=np.int32)
+        lg = np.empty((len(t), self.cfg.vocab), dtype=np.float32) if logits else None
+        self._call("m27b_engine_verify", self.h, ctypes.c_void_p(t.ctypes.data), len(t), int(pos),
+                   ctypes.c_void_p(nxt.ctypes.data), ctypes.c_void_p(lg.ctypes.data) if logits else None)
+        return (nxt, lg) if logits else nxt
 
     def stream(self):
         """The engine's cudaStream_t as an integer handle."""
@@ -557,3 +568,37 @@ class Blob:
 def engine_load_blob(engine, blob, source=SOURCE_TARGET):
     err = ctypes.create_string_buffer(ERR_CAP)
     _check(_blob_lib().m27b_engine_load_blob(engine.h, blob.h, source, err, ERR_CAP), err, "m27b_engine_load_blob")
+
+
+# --------------------------------------------------------------------------
+# speculative decoding (draft engine + target engine, greedy)
+
+
+def speculative_generate(target, draft, prompt, n_new, k=7):
+    """Greedy speculative decoding: the draft proposes k tokens (device-side
+    greedy generation), the target checks them in one verify pass of k + 1
+    tokens and keeps the longest agreeing prefix plus its own next token.
+    Lossless: the result equals the target's own greedy decoding of `prompt`.
+    Both engines must start empty; returns (tokens, stats)."""
+    assert 1 <= k < M27B_VERIFY_MAX and len(prompt) >= 1
+    for pos, t in enumerate(prompt[:-1]):
+        target.decode_step(int(t), pos)
+        draft.decode_step(int(t), pos)
+    out, last, pos = [], int(prompt[-1]), len(prompt) - 1
+    iters = accepted = 0
+    while len(out) < n_new:
+        props = [int(t) for t in draft.generate(last, pos, k)]  # draft K/V at pos .. pos+k-1
+        nxt = [int(t) for t in target.verify([last] + props, pos)]  # target K/V at pos .. pos+k
+        j = 0
+        while j < k and props[j] == nxt[j]:
+            j += 1
+        if j == k:  # every proposal kept: the draft has not yet seen the last one
+            draft.decode_step(props[k - 1], pos + k)
+        out += props[:j] + [nxt[j]]
+        iters += 1
+        accepted += j
+        last, pos = nxt[j], pos + j + 1
+    return out[:n_new], dict(iterations=iters, accepted=accepted, proposed=iters * k)
+
+
+M27B_VERIFY_MAX = 16

@@ -35,17 +35,19 @@ TINY = dict(n_layers=2, hidden=512, ffn=1024, n_head=4, n_kv_head=2, head_dim=12
             rope_theta=1e7, rms_eps=1e-6)
 
 
-def make_model(orc, c, seed=0, sigma=0.02, norm_jitter=0.1):
+def make_model(orc, c, seed=0, sigma=0.02, norm_jitter=0.1, qtype=None):
     """name -> (ggml_type, row_elems, row_count, array): GGUF-named tensors of
-    N(0, sigma^2) weights quantized by the oracle, norms 1 + N(0, jitter^2)."""
+    N(0, sigma^2) weights quantized by the oracle (the q4_k_m mix, or every
+    matrix as `qtype`, e.g. q8_0 for a draft), norms 1 + N(0, jitter^2)."""
     rng = np.random.default_rng(seed)
     hd, H, KV = c["head_dim"], c["n_head"], c["n_kv_head"]
     t = {}
     s = [seed * 1000]
 
-    def q(name, qtype, rows, k):
+    def q(name, qt, rows, k):
         s[0] += 1
-        t[name] = (qtype, k, rows, gauss_weights(orc, qtype, rows, k, s[0], sigma))
+        qt = qtype or qt
+        t[name] = (qt, k, rows, gauss_weights(orc, qt, rows, k, s[0], sigma))
 
     def norm(name, n):
         t[name] = (F32, n, 1, (1.0 + norm_jitter * rng.standard_normal(n)).astype(np.float32))
@@ -106,39 +108,42 @@ class RefDecoder:
         self.allreduce = allreduce or (lambda v: v)
         p, hd = self.p, c["head_dim"]
         self.Gg = c["n_head"] // c["n_kv_head"]
+        self.qt = {n: v[0] for n, v in model.items()}
         self.embd = model["token_embd.weight"][3]
         self.lmh = np.ascontiguousarray(model["output.weight"][3][p["v_lo"]:p["v_lo"] + p["n_v"]])
         self.out_norm = model["output_norm.weight"][3]
         self.layers = []
         for l in range(c["n_layers"]):
             g = lambda n: model[f"blk.{l}.{n}.weight"][3]
+            tq = lambda n: model[f"blk.{l}.{n}.weight"][0]
             self.layers.append(dict(
+                tqkv=tq("attn_q"), to=tq("attn_output"), tg=tq("ffn_gate"), td=tq("ffn_down"),
                 attn_norm=g("attn_norm"), post_norm=g("post_attention_norm"), q_norm=g("attn_q_norm"),
                 k_norm=g("attn_k_norm"),
                 wq=np.ascontiguousarray(g("attn_q")[p["q_lo"] * 2 * hd:(p["q_lo"] + p["n_q"]) * 2 * hd]),
                 wk=np.ascontiguousarray(g("attn_k")[p["kv_lo"] * hd:(p["kv_lo"] + p["n_kv"]) * hd]),
                 wv=np.ascontiguousarray(g("attn_v")[p["kv_lo"] * hd:(p["kv_lo"] + p["n_kv"]) * hd]),
-                wo=col_slice(Q4_K, g("attn_output"), p["q_lo"] * hd, p["n_q"] * hd),
+                wo=col_slice(tq("attn_output"), g("attn_output"), p["q_lo"] * hd, p["n_q"] * hd),
                 wg=np.ascontiguousarray(g("ffn_gate")[p["f_lo"]:p["f_lo"] + p["n_f"]]),
                 wu=np.ascontiguousarray(g("ffn_up")[p["f_lo"]:p["f_lo"] + p["n_f"]]),
-                wd=col_slice(Q6_K, g("ffn_down"), p["f_lo"], p["n_f"]),
+                wd=col_slice(tq("ffn_down"), g("ffn_down"), p["f_lo"], p["n_f"]),
                 kc=np.zeros((max_ctx, p["n_kv"], hd), np.float32), vc=np.zeros((max_ctx, p["n_kv"], hd), np.float32)))
         self.hidden = None
 
     def _mv(self, qtype, w, k, x):
-        return self.orc.matvec(qtype, w, k, self.orc.quantize_q8_K(x[None]))[0]
+        return self.orc.matvec(qtype, w, k, self.orc.quantize_act(qtype, x[None]))[0]
 
     def step(self, token, pos):
         """Returns (local logits, hidden state before the output norm)."""
         orc, c, p = self.orc, self.c, self.p
         hd, D, eps = c["head_dim"], c["hidden"], c["rms_eps"]
         r0 = self.rank == 0
-        h = orc.dequantize(Q4_K, self.embd[token:token + 1], D)[0]
+        h = orc.dequantize(self.qt["token_embd.weight"], self.embd[token:token + 1], D)[0]
         for Ly in self.layers:
             x = rms_scaled(h, Ly["attn_norm"], eps)
-            qg = self._mv(Q4_K, Ly["wq"], D, x)
-            kk = self._mv(Q4_K, Ly["wk"], D, x)
-            vv = self._mv(Q4_K, Ly["wv"], D, x)
+            qg = self._mv(Ly["tqkv"], Ly["wq"], D, x)
+            kk = self._mv(Ly["tqkv"], Ly["wk"], D, x)
+            vv = self._mv(Ly["tqkv"], Ly["wv"], D, x)
             for j in range(p["n_kv"]):
                 kh = rms_scaled(kk[j * hd:(j + 1) * hd], Ly["k_norm"], eps)
                 Ly["kc"][pos, j] = rope(kh, pos, c["n_rot"], c["rope_theta"])
@@ -156,18 +161,18 @@ class RefDecoder:
                 w = np.exp(sc - sc.max())
                 o[hh * hd:(hh + 1) * hd] = (w @ V / w.sum()).astype(np.float32)
             og = (o * (np.float32(1.0) / (np.float32(1.0) + np.exp(-gate)))).astype(np.float32)
-            h2 = self._mv(Q4_K, Ly["wo"], p["n_q"] * hd, og)
+            h2 = self._mv(Ly["to"], Ly["wo"], p["n_q"] * hd, og)
             if r0:
                 h2 = h2 + h
             h2 = self.allreduce(h2)
             x2 = rms_scaled(h2, Ly["post_norm"], eps)
-            g = self._mv(Q4_K, Ly["wg"], D, x2)
-            u = self._mv(Q4_K, Ly["wu"], D, x2)
+            g = self._mv(Ly["tg"], Ly["wg"], D, x2)
+            u = self._mv(Ly["tg"], Ly["wu"], D, x2)
             a = orc.silu_mul(g, u)
-            h = self._mv(Q6_K, Ly["wd"], p["n_f"], a)
+            h = self._mv(Ly["td"], Ly["wd"], p["n_f"], a)
             if r0:
                 h = h + h2
             h = self.allreduce(h)
         self.hidden = h
-        logits = self._mv(Q6_K, self.lmh, D, rms_scaled(h, self.out_norm, eps))
+        logits = self._mv(self.qt["output.weight"], self.lmh, D, rms_scaled(h, self.out_norm, eps))
         return logits, h

@@ -7,7 +7,11 @@ sum_s sc_s * dot_s); only the fp32 accumulation order differs, so the tight
 tolerance of the dp4a kernels applies.  Shapes cover a partial last 128-row
 tile, a tile smaller than 128 rows, more tiles than SMs (the persistent tile
 loop), K of 1..24 super-blocks, every token count 5..16 (MMA N = 8 and 16,
-padded token columns), the residual epilogue and rows read in place."""
+padded token columns), the residual epilogue and rows read in place.  Every
+run also checks the device status word: a pipeline hand-off that stalls shows
+up there (a bounded wait that ran out) even when the sums come out right.  A
+long chain of back-to-back launches at the decode engine's shapes exercises
+the hand-offs under every warp timing the scheduler produces."""
 import numpy as np
 import pytest
 
@@ -33,7 +37,9 @@ def _run(torch, orc, m27b, rows, k, n, seed, residual=False):
         want = want + r
         res = torch.from_numpy(r).cuda()
     m27b.qmv(W, xq, n, y, residual=res)
-    return orc.rel_l2(y.cpu().numpy(), want)
+    got = y.cpu().numpy()
+    assert m27b.device_status() == 0  # no bounded wait of the pipeline ran out
+    return orc.rel_l2(got, want)
 
 
 @pytest.mark.parametrize("n", list(range(5, 17)))
@@ -66,3 +72,25 @@ def test_mma_matches_single_token_kernel(torch, orc, m27b):
     for t in range(n):
         m27b.qmv(W, xq[t * nb:(t + 1) * nb], 1, y1[t:t + 1])
     assert orc.rel_l2(y16.cpu().numpy(), y1.cpu().numpy()) <= 1e-6
+
+
+@pytest.mark.parametrize("n", [8, 16])
+def test_mma_chain_of_launches(torch, orc, m27b, n):
+    # 400 launches back to back (each overlapping its neighbours through
+    # programmatic dependent launch) at o_proj's shape: same result every
+    # time, no stalled hand-off
+    rows, k = 5120, 6144
+    w = D.gauss_weights(orc, Q4_K, rows, k, 21)
+    x = D.gauss_act(n, k, 22)
+    want = orc.matvec(Q4_K, w, k, orc.quantize_q8_K(x))
+    W = m27b.QWeight(w, Q4_K, k, rows)
+    xq = m27b.act_quant(torch.from_numpy(x).cuda(), Q8_K)
+    ys = [torch.empty((n, rows), device="cuda") for _ in range(2)]
+    m27b.qmv(W, xq, n, ys[0])
+    first = ys[0].clone()
+    for i in range(400):
+        m27b.qmv(W, xq, n, ys[i & 1])
+    torch.cuda.synchronize()
+    assert m27b.device_status() == 0
+    assert torch.equal(ys[0], first) and torch.equal(ys[1], first)
+    assert orc.rel_l2(first.cpu().numpy(), want) <= TIGHT
