@@ -10,7 +10,10 @@
  *   m27b_act_quant_gated<- k_quant_q8_1_fused_gate              src/mono27b_executor.cu:109-138, :2460
  *   m27b_qmv            <- l_mv_q8_on / l_mv_quant_residual     src/mono27b_executor.cu:2054-2102
  *                          (k_q4k_mv_q8_dp4a :320-364, k_q6k_mv_q8_dp4a :630-645,
- *                          k_q80_mv_q8_dp4a :533-580)
+ *                          k_q80_mv_q8_dp4a :533-580, k_q5k_mv_q8 :499-531,
+ *                          k_iq4xs_mv_q8_dp4a :674-686)
+ *   m27b_qmv_f32        <- l_mv_quant / l_mv_fallback           src/mono27b_executor.cu:2033-2050, :2127-2137
+ *                          (f16 / f32 weights: k_f16_mv :900-916, k_f32_mv :1101-1114)
  *   m27b_qmv_swiglu     <- l_ffn_gate_up_swiglu                 src/mono27b_executor.cu:2239-2261
  *                          (k_q4k_q4k_swiglu_dp4a :369-417)
  *   m27b_qmv_argmax     <- lm_head block + k_argmax             src/mono27b_executor.cu:2577-2593, :209-239
@@ -29,10 +32,13 @@
  * Weight rows: a WeightView {ptr, ggml_type, row_blocks, row_count} as the
  * reference loader fills it (include/mono27b_config.h:63-68, filled at
  * src/mono27b_executor.cu:1695-1716): row_count rows of row_blocks blocks.
- * q4_K rows are read in their GGUF layout.  q6_K and q8_0 rows must first be
- * repacked with m27b_repack; the repacked view carries
- * ggml_type | M27B_LAYOUT_PLANAR.  ptr must be 16-byte aligned (cudaMalloc
- * gives 256).
+ * q4_K, q5_K and IQ4_XS rows are read in their GGUF layout (IQ4_XS rows need
+ * an even block count, so that rows stay 16-byte aligned).  q6_K and q8_0
+ * rows must first be repacked with m27b_repack; the repacked view carries
+ * ggml_type | M27B_LAYOUT_PLANAR.  f16 / f32 rows (row_blocks = values per
+ * row, as the reference loader sets it; a multiple of 8 / 4) take fp32
+ * activations through m27b_qmv_f32 only.  ptr must be 16-byte aligned
+ * (cudaMalloc gives 256).
  *
  * Activations: m27b_act_quant writes n_tok rows of m27b_act_bytes(type, k)
  * bytes, ggml block_q8_K (for q4_K / q6_K weights) or block_q8_0 (for q8_0
@@ -90,7 +96,8 @@ M27B_API bool m27b_device_status(int *status, int clear, char *err, size_t err_c
 M27B_API size_t m27b_act_bytes(uint32_t act_type, int k);
 
 /* Activation type a weight type is multiplied against (q8_0 for q8_0 weights,
- * q8_K for k-quants); 0 for an unsupported weight type. */
+ * q8_K for q4_K / q5_K / q6_K / IQ4_XS); 0 for f16 / f32 weights (fp32
+ * activations, m27b_qmv_f32) and unsupported types. */
 M27B_API uint32_t m27b_act_type_for(uint32_t ggml_type);
 
 /* Quantize n_tok rows of k fp32 values (row stride ldx floats) into
@@ -145,19 +152,22 @@ M27B_API bool m27b_qmv_argmax(const struct WeightView *w, const void *xq, int n_
 /* fp32 activations in, like the reference's l_mv_quant(W, x, y)
  * (src/mono27b_executor.cu:2033-2050, its quantizer k_quant_q8_1 :84-107):
  * x rows (n_tok of them, stride ldx floats) are quantized to q8_K / q8_0 and
- * multiplied, y = W.x (+ residual).  For a q4_K matrix and up to 4 tokens
- * (x 16-byte aligned, ldx a multiple of 4) the matvec kernel quantizes the
- * rows in its own prologue (one launch, same codes as m27b_act_quant);
- * otherwise the rows are first quantized into xq_scratch
+ * multiplied, y = W.x (+ residual).  For a q4_K, q5_K or IQ4_XS matrix and
+ * up to 4 tokens (x 16-byte aligned, ldx a multiple of 4) the matvec kernel
+ * quantizes the rows in its own prologue (one launch, same codes as
+ * m27b_act_quant); otherwise the rows are first quantized into xq_scratch
  * (n_tok * m27b_act_bytes(m27b_act_type_for(type), k) bytes; may be NULL on
- * the one-launch path). */
+ * the one-launch path).  f16 / f32 matrices multiply the fp32 rows directly
+ * (x 16-byte aligned, ldx a multiple of 4; the f16 path rounds x to fp16
+ * first, as ggml does; xq_scratch unused). */
 M27B_API bool m27b_qmv_f32(const struct WeightView *w, const float *x, int ldx, int n_tok, void *xq_scratch, float *y,
                            int ldy, const float *residual, cudaStream_t stream, char *err, size_t err_cap);
 
 /* The same with RMSNorm(x) * norm_w (eps; norm_w may be NULL: 1.0) before
  * the quantization, the reference's l_rms + MV pair (:2139-2141).  With
  * w_up non-NULL the epilogue is SwiGLU, y = silu(W.x) * (W_up.x) (no
- * residual) — the FFN's gate/up after the post-attention norm. */
+ * residual) — the FFN's gate/up after the post-attention norm.  Quantized
+ * weight types only. */
 M27B_API bool m27b_qmv_f32_rmsnorm(const struct WeightView *w, const struct WeightView *w_up, const float *x, int ldx,
                                    const float *norm_w, float eps, int n_tok, void *xq_scratch, float *y, int ldy,
                                    const float *residual, cudaStream_t stream, char *err, size_t err_cap);

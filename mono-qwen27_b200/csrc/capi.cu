@@ -66,24 +66,32 @@ int sm_count_current() {
     return n;
 }
 
+// Values per block; 1 for f16 / f32, whose WeightView.row_blocks counts
+// values (the reference loader's convention, src/mono27b_executor.cu:1704).
 int block_elems(uint32_t base_type) {
     switch (base_type) {
     case M27B_TYPE_Q4_K:
+    case M27B_TYPE_Q5_K:
     case M27B_TYPE_Q6_K:
+    case M27B_TYPE_IQ4_XS:
     case M27B_TYPE_Q8_K: return 256;
     case M27B_TYPE_Q8_0: return 32;
+    case M27B_TYPE_F16:
+    case M27B_TYPE_F32: return 1;
     default: return 0;
     }
 }
 
 // Validated description of a weight view for the matvec kernels.
 struct WDesc {
-    int kind;       // W_Q4K / W_Q6KP / W_Q80P
+    int kind;       // W_Q4K / W_Q6KP / W_Q80P / W_Q5K / W_IQ4XS / W_F16 / W_F32
     int base;       // base ggml type
     int k;
     int passes;
     size_t row_stride;
 };
+
+bool is_float_kind(int kind) { return kind == W_F16 || kind == W_F32; }
 
 bool describe(const WeightView *w, WDesc &d, const char *what, char *err, size_t cap) {
     if (!w) return fail(err, cap, "%s: null WeightView", what);
@@ -110,11 +118,32 @@ bool describe(const WeightView *w, WDesc &d, const char *what, char *err, size_t
         d.kind = W_Q80P;
         d.row_stride = planar_row_bytes(M27B_TYPE_Q8_0, (int)w->row_blocks);
         d.passes = (int)((w->row_blocks + 31) / 32);
+    } else if (base == M27B_TYPE_Q5_K && !planar) {
+        d.kind = W_Q5K;
+        d.row_stride = (size_t)w->row_blocks * 176;
+        d.passes = (int)((w->row_blocks + 3) / 4);
+    } else if (base == M27B_TYPE_IQ4_XS && !planar) {
+        // 136-byte blocks: rows are 16-byte aligned (tensor-map rows) when the block count is even
+        if (w->row_blocks & 1u)
+            return fail(err, cap, "%s: IQ4_XS rows need an even number of blocks (got %u)", what, w->row_blocks);
+        d.kind = W_IQ4XS;
+        d.row_stride = (size_t)w->row_blocks * 136;
+        d.passes = (int)((w->row_blocks + 3) / 4);
+    } else if ((base == M27B_TYPE_F16 || base == M27B_TYPE_F32) && !planar) {
+        const uint32_t per16 = base == M27B_TYPE_F16 ? 8u : 4u;
+        if (w->row_blocks % per16)
+            return fail(err, cap, "%s: %s rows need a multiple of %u values (got %u)", what,
+                        base == M27B_TYPE_F16 ? "f16" : "f32", per16, w->row_blocks);
+        d.kind = base == M27B_TYPE_F16 ? W_F16 : W_F32;
+        d.row_stride = (size_t)w->row_blocks * (base == M27B_TYPE_F16 ? 2 : 4);
+        d.passes = 0;
     } else if ((base == M27B_TYPE_Q6_K || base == M27B_TYPE_Q8_0) && !planar) {
         return fail(err, cap, "%s: ggml type %u must be repacked with m27b_repack before the matvec", what, base);
     } else {
-        return fail(err, cap, "%s: unsupported weight type 0x%x (q4_K, planar q6_K and planar q8_0 are supported)", what,
-                    w->ggml_type);
+        return fail(err, cap,
+                    "%s: unsupported weight type 0x%x (q4_K, q5_K, IQ4_XS, f16, f32, planar q6_K and planar q8_0 are "
+                    "supported)",
+                    what, w->ggml_type);
     }
     d.k = (int)w->row_blocks * block_elems(base);
     return true;
@@ -160,10 +189,42 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
             return fail(err, cap, "%s: gate and up must have the same type and shape", what);
     }
     if (!xq && !xa) return fail(err, cap, "%s: null activation pointer", what);
-    if (xa && (d0.kind != W_Q4K || n_tok > 4 || !xa->xf || ((uintptr_t)xa->xf & 15) || (xa->ldxf & 3)))
-        return fail(err, cap, "%s: in-kernel quantization needs q4_K weights, <= 4 tokens, 16-byte aligned rows", what);
     if (n_tok < 1 || n_tok > M27B_MAX_TOKENS)
         return fail(err, cap, "%s: n_tok must be in [1, %d] (got %d)", what, M27B_MAX_TOKENS, n_tok);
+    if (is_float_kind(d0.kind)) {
+        // f16 / f32 weights take fp32 activations: the plain store epilogue only
+        if (!xa) return fail(err, cap, "%s: f16 / f32 weights take fp32 activations (use m27b_qmv_f32)", what);
+        if (epi != EPI_STORE || xa->norm_on)
+            return fail(err, cap, "%s: f16 / f32 weights support the plain matvec (+ residual) only", what);
+        if (!xa->xf || ((uintptr_t)xa->xf & 15) || (xa->ldxf & 3) || !y)
+            return fail(err, cap, "%s: f16 / f32 matvec needs 16-byte aligned x rows (ldx a multiple of 4) and y",
+                        what);
+        if (ldy < (int)w0->row_count && n_tok > 1)
+            return fail(err, cap, "%s: ldy (%d) < row_count (%u)", what, ldy, w0->row_count);
+        const int sms = sm_count_current();
+        if (sms <= 0) return fail(err, cap, "%s: no CUDA device", what);
+        for (int t0 = 0; t0 < n_tok; t0 += 4) {
+            const int nt = n_tok - t0 < 4 ? n_tok - t0 : 4;
+            QmvArgs a{};
+            a.w0 = (const uint8_t *)w0->ptr;
+            a.xf = xa->xf + (size_t)t0 * xa->ldxf;
+            a.ldxf = xa->ldxf;
+            a.y = y + (size_t)t0 * ldy;
+            a.residual = residual ? residual + (size_t)t0 * ldy : nullptr;
+            a.row_stride = d0.row_stride;
+            a.ldy = ldy;
+            a.rows = (int)w0->row_count;
+            a.k = d0.k;
+            cudaError_t e = launch_qmv_float(d0.kind, a, nt, sms, stream);
+            if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
+        }
+        return ok(err, cap);
+    }
+    const bool kblk = d0.kind == W_Q4K || d0.kind == W_Q5K || d0.kind == W_IQ4XS;
+    if (xa && (!kblk || n_tok > 4 || !xa->xf || ((uintptr_t)xa->xf & 15) || (xa->ldxf & 3)))
+        return fail(err, cap,
+                    "%s: in-kernel quantization needs q4_K / q5_K / IQ4_XS weights, <= 4 tokens, 16-byte aligned rows",
+                    what);
     if (epi == EPI_PUSH) {
         if (!push || push->npeers < 1 || push->npeers > M27B_MAX_PEERS || !push->epoch_base)
             return fail(err, cap, "%s: bad push descriptor", what);
@@ -259,7 +320,8 @@ size_t m27b_act_bytes(uint32_t act_type, int k) { return act_bytes(act_type, k);
 uint32_t m27b_act_type_for(uint32_t ggml_type) {
     const uint32_t b = ggml_type & M27B_TYPE_MASK;
     if (b == M27B_TYPE_Q8_0) return M27B_TYPE_Q8_0;
-    if (b == M27B_TYPE_Q4_K || b == M27B_TYPE_Q6_K) return M27B_TYPE_Q8_K;
+    if (b == M27B_TYPE_Q4_K || b == M27B_TYPE_Q5_K || b == M27B_TYPE_Q6_K || b == M27B_TYPE_IQ4_XS)
+        return M27B_TYPE_Q8_K;
     return 0;
 }
 
@@ -325,10 +387,18 @@ static bool qmv_f32_common(const WeightView *w, const WeightView *w_up, const fl
     if (w_up && residual) return fail(err, cap, "%s: the SwiGLU epilogue takes no residual", what);
     const int epi = w_up ? EPI_SWIGLU : EPI_STORE;
     const uint32_t base = w->ggml_type & M27B_TYPE_MASK;
-    const int k = (int)w->row_blocks * (base == M27B_TYPE_Q8_0 ? 32 : 256);
+    const int k = (int)w->row_blocks * block_elems(base);
+    if (k <= 0) return fail(err, cap, "%s: unsupported weight type 0x%x", what, w->ggml_type);
     if (ldx < k) return fail(err, cap, "%s: ldx (%d) < k (%d)", what, ldx, k);
-    if (base == M27B_TYPE_Q4_K && w->ggml_type == M27B_TYPE_Q4_K && n_tok >= 1 && n_tok <= 4 &&
-        ((uintptr_t)x & 15) == 0 && (ldx & 3) == 0) {
+    if (base == M27B_TYPE_F16 || base == M27B_TYPE_F32) {
+        // fp32 activations go straight into the f16 / f32 kernel
+        XArgs xa{x, ldx, norm_on, norm_w, eps};
+        return qmv_common(epi, w, w_up, nullptr, n_tok, y, ldy, residual, nullptr, 0, stream, err, cap, what, nullptr,
+                          &xa);
+    }
+    const bool kblk = w->ggml_type == M27B_TYPE_Q4_K || w->ggml_type == M27B_TYPE_Q5_K ||
+                      w->ggml_type == M27B_TYPE_IQ4_XS;
+    if (kblk && n_tok >= 1 && n_tok <= 4 && ((uintptr_t)x & 15) == 0 && (ldx & 3) == 0) {
         XArgs xa{x, ldx, norm_on, norm_w, eps};
         return qmv_common(epi, w, w_up, nullptr, n_tok, y, ldy, residual, nullptr, 0, stream, err, cap, what, nullptr,
                           &xa);
@@ -361,8 +431,9 @@ bool m27b_dequant_rows(const WeightView *w, const int32_t *rows, int n, float *o
     const uint32_t base = w->ggml_type & M27B_TYPE_MASK;
     const bool planar = (w->ggml_type & M27B_LAYOUT_PLANAR) != 0;
     const int be = block_elems(base);
-    if (be == 0 || base == M27B_TYPE_Q8_K || (planar && base == M27B_TYPE_Q4_K))
-        return fail(err, err_cap, "m27b_dequant_rows: unsupported weight type 0x%x", w->ggml_type);
+    if ((base != M27B_TYPE_Q4_K && base != M27B_TYPE_Q6_K && base != M27B_TYPE_Q8_0) ||
+        (planar && base == M27B_TYPE_Q4_K))
+        return fail(err, err_cap, "m27b_dequant_rows: unsupported weight type 0x%x (q4_K, q6_K, q8_0)", w->ggml_type);
     if (w->row_blocks == 0 || w->row_blocks > 0x7fffffffu / 256u) return fail(err, err_cap, "m27b_dequant_rows: bad row_blocks");
     const int k = (int)w->row_blocks * be;
     if (ldo < k) return fail(err, err_cap, "m27b_dequant_rows: ldo (%d) < k (%d)", ldo, k);

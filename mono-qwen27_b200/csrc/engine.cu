@@ -80,8 +80,19 @@ bool efail(char *err, size_t cap, const char *fmt, ...) {
         if (!(call)) return false;  \
     } while (0)
 
-size_t block_bytes(uint32_t t) { return t == M27B_TYPE_Q4_K ? 144 : t == M27B_TYPE_Q6_K ? 210 : t == M27B_TYPE_Q8_0 ? 34 : 0; }
+size_t block_bytes(uint32_t t) {
+    switch (t) {
+    case M27B_TYPE_Q4_K: return 144;
+    case M27B_TYPE_Q5_K: return 176;
+    case M27B_TYPE_Q6_K: return 210;
+    case M27B_TYPE_IQ4_XS: return 136;
+    case M27B_TYPE_Q8_0: return 34;
+    default: return 0;
+    }
+}
 int block_elems(uint32_t t) { return t == M27B_TYPE_Q8_0 ? 32 : 256; }
+// q4_K, q5_K and IQ4_XS rows are read in their GGUF layout; q6_K and q8_0 are repacked.
+bool raw_layout(uint32_t t) { return t == M27B_TYPE_Q4_K || t == M27B_TYPE_Q5_K || t == M27B_TYPE_IQ4_XS; }
 
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
@@ -184,19 +195,21 @@ bool ensure_mat(M27BEngine *e, QMat &m, uint32_t type, int rows, int k, char *er
                          k, m.type, m.rows, m.k);
         return true;
     }
-    if (type != M27B_TYPE_Q4_K && type != M27B_TYPE_Q6_K && type != M27B_TYPE_Q8_0)
-        return efail(err, err_cap, "unsupported matrix type %u", type);
+    if (block_bytes(type) == 0)
+        return efail(err, err_cap, "unsupported matrix type %u (q4_K, q5_K, q6_K, IQ4_XS, q8_0)", type);
     if (k % block_elems(type)) return efail(err, err_cap, "k=%d not a multiple of the block size", k);
     const uint32_t rb = (uint32_t)(k / block_elems(type));
+    if (type == M27B_TYPE_IQ4_XS && (rb & 1u))
+        return efail(err, err_cap, "IQ4_XS matrices need an even number of blocks per (rank's) row, got %u", rb);
     const size_t raw = (size_t)rows * rb * block_bytes(type);
-    const size_t n = type == M27B_TYPE_Q4_K ? raw : m27b_repacked_bytes(type, rb, (uint32_t)rows);
+    const size_t n = raw_layout(type) ? raw : m27b_repacked_bytes(type, rb, (uint32_t)rows);
     ECALL(dalloc(e, &m.d, n, err, err_cap));
     m.type = type;
     m.rows = rows;
     m.k = k;
     m.gguf_bytes = raw;
     m.v.ptr = m.d;
-    m.v.ggml_type = type == M27B_TYPE_Q4_K ? type : (type | M27B_LAYOUT_PLANAR);
+    m.v.ggml_type = raw_layout(type) ? type : (type | M27B_LAYOUT_PLANAR);
     m.v.row_blocks = rb;
     m.v.row_count = (uint32_t)rows;
     return true;
@@ -214,7 +227,7 @@ bool ensure_scratch(M27BEngine *e, size_t n, char *err, size_t err_cap) {
 // Place raw GGUF rows (device, `rows` x row_blocks blocks) at row `row_at` of m.
 bool place_rows(M27BEngine *e, QMat &m, const uint8_t *raw_dev, int rows, int row_at, char *err, size_t err_cap) {
     const size_t rowb = (size_t)m.v.row_blocks * block_bytes(m.type);
-    if (m.type == M27B_TYPE_Q4_K) {
+    if (raw_layout(m.type)) {
         ECUDA(cudaMemcpyAsync((uint8_t *)m.d + (size_t)row_at * rowb, raw_dev, rowb * rows, cudaMemcpyDeviceToDevice, e->st));
         return true;
     }
@@ -319,9 +332,15 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
     if (p2p) {
         // the fused all-reduce's consumer hands its successors q8_K activations
         bool k_quants = e->lmh.type != M27B_TYPE_Q8_0;
-        for (const Layer &Ly : e->L)
+        bool push_types = true;  // o_proj / down store into the windows: q4_K or q6_K kernels
+        for (const Layer &Ly : e->L) {
             k_quants = k_quants && Ly.wqkv.type != M27B_TYPE_Q8_0 && Ly.wg.type != M27B_TYPE_Q8_0;
+            push_types = push_types && (Ly.wo.type == M27B_TYPE_Q4_K || Ly.wo.type == M27B_TYPE_Q6_K) &&
+                         (Ly.wd.type == M27B_TYPE_Q4_K || Ly.wd.type == M27B_TYPE_Q6_K);
+        }
         if (!k_quants) return efail(err, err_cap, "the fused NVLink all-reduce needs k-quant (not q8_0) matrices");
+        if (!push_types)
+            return efail(err, err_cap, "the fused NVLink all-reduce needs q4_K or q6_K attn_output / ffn_down matrices");
     }
     const int *pos = e->ctl + 1;
     ECALL(m27b_dequant_rows(&e->embd.v, e->ctl, 1, e->h, c.hidden, e->st, err, err_cap));
@@ -670,6 +689,8 @@ bool m27b_engine_load_tensor(M27BEngine *e, const char *name, uint32_t type, uin
     const std::string nm = name;
     if (nm == "token_embd.weight") {
         if (row_count != (uint32_t)c.vocab || row_elems != (uint32_t)c.hidden) return efail(err, err_cap, "token_embd shape");
+        if (type != M27B_TYPE_Q4_K && type != M27B_TYPE_Q6_K && type != M27B_TYPE_Q8_0)
+            return efail(err, err_cap, "token_embd must be q4_K, q6_K or q8_0 (got type %u)", type);
         ECALL(ensure_mat(e, e->embd, type, c.vocab, c.hidden, err, err_cap));
         return load_slice(e, e->embd, hb, e->embd.v.row_blocks, 0, c.vocab, 0, 0, err, err_cap);
     }

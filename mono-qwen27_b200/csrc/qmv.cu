@@ -67,6 +67,8 @@ bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows,
 size_t qmv_smem_bytes(int wtype, int k, int ntok) {
     if (wtype == M27B_TYPE_Q8_0) return (size_t)ntok * k + (size_t)ntok * (k / 32) * 4;
     if (wtype == M27B_TYPE_Q4_K) return blk_warps(k, ntok) > 0 ? blk_smem_bytes(k, ntok) : 0;  // qmv_blk.cuh
+    if (wtype == M27B_TYPE_Q5_K) return blk_warps(k, ntok, 176) > 0 ? blk_smem_bytes(k, ntok, 176) : 0;
+    if (wtype == M27B_TYPE_IQ4_XS) return blk_warps(k, ntok, 136) > 0 ? blk_smem_bytes(k, ntok, 136) : 0;
     if (wtype == M27B_TYPE_Q6_K) return q6t_warps(k, ntok) > 0 ? q6t_smem_bytes(k, ntok) : 0;   // qmv_q6k_tile.cuh
     return (size_t)ntok * k + (size_t)ntok * (k / 256) * 32 + (size_t)ntok * (k / 256) * 4;
 }
@@ -76,6 +78,8 @@ cudaError_t launch_qmv(int wt, int epi, QmvArgs a, int nt, int sm_count, cudaStr
     case W_Q4K: return run_qmv_format<W_Q4K>(epi, nt, a, sm_count, st);
     case W_Q6KP: return run_qmv_format<W_Q6KP>(epi, nt, a, sm_count, st);
     case W_Q80P: return run_qmv_format<W_Q80P>(epi, nt, a, sm_count, st);
+    case W_Q5K: return run_qmv_format<W_Q5K>(epi, nt, a, sm_count, st);
+    case W_IQ4XS: return run_qmv_format<W_IQ4XS>(epi, nt, a, sm_count, st);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -1,5 +1,10 @@
-// qmv_blk.cuh — q4_K matvec with one super-block per lane, weights streamed
-// through shared memory with coalesced asynchronous copies.
+// qmv_blk.cuh — k-quant matvec with one super-block per lane, weights
+// streamed through shared memory with coalesced asynchronous copies: q4_K
+// (the target's matrices), q5_K and IQ4_XS (the reference's other 256-value
+// types, k_q5k_mv_q8 src/mono27b_executor.cu:499-531 and k_iq4xs_mv_q8_dp4a
+// :647-686).  The block type enters only through a traits struct (bytes per
+// block, how a lane loads it, its dot product); the description below uses
+// q4_K's 144 bytes.
 //
 // Mapping: a warp owns groups of 8 consecutive rows; lane L works on row slot
 // L/4 of the group and, in pass p, on super-block 4p + L%4 of that row.  A
@@ -38,30 +43,35 @@
 namespace m27b {
 
 constexpr int BLK_XREC = 272;                 // bytes per staged (token, block) activation record
-constexpr int BLK_ITEM = 8 * 4 * 144;         // 4608 bytes: one item (8 rows x 4 blocks)
 constexpr int BLK_STAGES = 2;                 // stages per warp
 constexpr int BLK_WARPS = 8;                  // most warps per CTA (two CTAs per SM)
 constexpr int BLK_THREADS = BLK_WARPS * 32;
 constexpr size_t BLK_SMEM_MAX = 112 * 1024;   // two CTAs per SM within the 228 KB of shared memory
 
+// One item: 8 rows x 4 consecutive blocks of `bytes` bytes (q4_K: 4608).
+constexpr int blk_item(int bytes) { return 8 * 4 * bytes; }
+// stages + barriers of one warp
+constexpr size_t blk_warp_bytes(int bytes) { return (size_t)BLK_STAGES * blk_item(bytes) + (size_t)BLK_STAGES * 8; }
+
 inline size_t blk_x_bytes(int k, int nt) { return (size_t)nt * ((size_t)k / 256) * (BLK_XREC + 4); }
-constexpr size_t BLK_WARP_BYTES = (size_t)BLK_STAGES * BLK_ITEM + (size_t)BLK_STAGES * 8;  // stages + barriers
 
 // Warps per CTA: as many as the shared memory left after the staged
 // activations holds stages for (at most BLK_WARPS); 0 if not even one fits.
 inline size_t blk_part_bytes(int nt) { return (size_t)BLK_WARPS * 8 * 2 * nt * 4; }
 
-inline int blk_warps(int k, int nt) {
+inline int blk_warps(int k, int nt, int bytes = 144) {
     const size_t x = blk_x_bytes(k, nt) + blk_part_bytes(nt);
     if (x + 16 >= BLK_SMEM_MAX) return 0;
-    const size_t w = (BLK_SMEM_MAX - x - 16) / BLK_WARP_BYTES;
+    const size_t w = (BLK_SMEM_MAX - x - 16) / blk_warp_bytes(bytes);
     return (int)(w < (size_t)BLK_WARPS ? w : (size_t)BLK_WARPS);
 }
 
-inline size_t blk_smem_for(int nwarps, int k, int nt) {
-    return (size_t)nwarps * BLK_WARP_BYTES + blk_x_bytes(k, nt) + blk_part_bytes(nt) + 16;
+inline size_t blk_smem_for(int nwarps, int k, int nt, int bytes = 144) {
+    return (size_t)nwarps * blk_warp_bytes(bytes) + blk_x_bytes(k, nt) + blk_part_bytes(nt) + 16;
 }
-inline size_t blk_smem_bytes(int k, int nt) { return blk_smem_for(blk_warps(k, nt), k, nt); }
+inline size_t blk_smem_bytes(int k, int nt, int bytes = 144) {
+    return blk_smem_for(blk_warps(k, nt, bytes), k, nt, bytes);
+}
 
 // ---- mbarrier + bulk-copy helpers (sm_90+ PTX; no cluster multicast) ----
 M27B_DI uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -346,13 +356,200 @@ M27B_DI void q4k_block_mac(const uint4 (&v)[9], const uint8_t *xrec0, const floa
     }
 }
 
+// One q5_K block (176 bytes: d, dmin, scales[12] | qh[32] | qs[128]) times
+// NT staged activation blocks.  The nibbles and the 6-bit scales/mins are
+// q4_K's; bit s of qh[l] is bit 4 of element l of sub-block s, merged into
+// the byte lanes before the dp4a (codes 0..31), as k_q5k_mv_q8 and ggml's
+// vec_dot_q5_K_q8_K define the value (src/mono27b_executor.cu:955-969).
+template <int NT>
+M27B_DI void q5k_block_mac(const uint4 (&v)[11], const uint8_t *xrec0, const float *xd0, int nb, float (&acc)[NT]) {
+    const uint4 hd = v[0];
+    const uint32_t sc03 = hd.y & 0x3f3f3f3fu;
+    const uint32_t mn03 = hd.z & 0x3f3f3f3fu;
+    const uint32_t sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
+    const uint32_t mn47 = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
+    const float dw = h2f(hd.x), dmw = h2f(hd.x >> 16);
+    const uint32_t qh[8] = {v[1].x, v[1].y, v[1].z, v[1].w, v[2].x, v[2].y, v[2].z, v[2].w};
+    int isum[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) isum[t] = 0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const uint4 qa = v[3 + 2 * g], qb = v[4 + 2 * g];  // qs bytes 32g .. 32g+31
+        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        uint32_t lo[8], hi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            lo[i] = (w[i] & 0x0f0f0f0fu) | (((qh[i] >> (2 * g)) & 0x01010101u) << 4);
+            hi[i] = ((w[i] >> 4) & 0x0f0f0f0fu) | (((qh[i] >> (2 * g + 1)) & 0x01010101u) << 4);
+        }
+        const uint32_t scw = g < 2 ? sc03 : sc47;
+        const int sh = 16 * (g & 1);
+        const int s_lo = (int)((scw >> sh) & 0xffu), s_hi = (int)((scw >> (sh + 8)) & 0xffu);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const uint8_t *xr = xrec0 + (size_t)t * nb * BLK_XREC + 64 * g;
+            const int4 x0 = *(const int4 *)(xr);
+            const int4 x1 = *(const int4 *)(xr + 16);
+            const int4 x2 = *(const int4 *)(xr + 32);
+            const int4 x3 = *(const int4 *)(xr + 48);
+            int dl = dp4a_us(lo[0], x0.x, 0);
+            dl = dp4a_us(lo[1], x0.y, dl);
+            dl = dp4a_us(lo[2], x0.z, dl);
+            dl = dp4a_us(lo[3], x0.w, dl);
+            dl = dp4a_us(lo[4], x1.x, dl);
+            dl = dp4a_us(lo[5], x1.y, dl);
+            dl = dp4a_us(lo[6], x1.z, dl);
+            dl = dp4a_us(lo[7], x1.w, dl);
+            int dh = dp4a_us(hi[0], x2.x, 0);
+            dh = dp4a_us(hi[1], x2.y, dh);
+            dh = dp4a_us(hi[2], x2.z, dh);
+            dh = dp4a_us(hi[3], x2.w, dh);
+            dh = dp4a_us(hi[4], x3.x, dh);
+            dh = dp4a_us(hi[5], x3.y, dh);
+            dh = dp4a_us(hi[6], x3.z, dh);
+            dh = dp4a_us(hi[7], x3.w, dh);
+            isum[t] += s_lo * dl + s_hi * dh;
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        const uint8_t *xr = xrec0 + (size_t)t * nb * BLK_XREC;
+        const int4 bs = *(const int4 *)(xr + 256);
+        int msum = __dp2a_lo(bs.x, (int)mn03, 0);
+        msum = __dp2a_hi(bs.y, (int)mn03, msum);
+        msum = __dp2a_lo(bs.z, (int)mn47, msum);
+        msum = __dp2a_hi(bs.w, (int)mn47, msum);
+        const float dx = xd0[t * nb];
+        acc[t] = fmaf(dw * dx, (float)isum[t], acc[t]);
+        acc[t] = fmaf(-(dmw * dx), (float)msum, acc[t]);
+    }
+}
+
+M27B_DI uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// The IQ4_NL / IQ4_XS codebook (reference src/mono27b_executor.cu:51-55) as
+// four words of signed bytes: entries 0-3, 4-7, 8-11, 12-15.
+constexpr uint32_t iq4_word(int a, int b, int c, int d) {
+    return (uint32_t)(uint8_t)a | ((uint32_t)(uint8_t)b << 8) | ((uint32_t)(uint8_t)c << 16) |
+           ((uint32_t)(uint8_t)d << 24);
+}
+constexpr uint32_t IQ4_T0 = iq4_word(-127, -104, -83, -65), IQ4_T1 = iq4_word(-49, -35, -22, -10);
+constexpr uint32_t IQ4_T2 = iq4_word(1, 13, 25, 38), IQ4_T3 = iq4_word(53, 69, 89, 113);
+
+// The 8 codes of one qs word (4 bytes, low nibble = element j of the
+// sub-block's first half, high nibble = element j of its second half) as
+// codebook bytes: lo4 = the four low-nibble values, hi4 = the four high.
+// prmt looks a nibble's low 3 bits up in entries 0-7 and in 8-15; a second
+// prmt in sign-replicate mode turns each nibble's bit 3 into a byte mask that
+// picks one of the two (selector nibble 0x9 replicates the sign of byte 1 =
+// 0x80 -> 0xff, 0x0 takes byte 0 = 0x00); the lookups come out interleaved
+// (l0 h0 l1 h1 | l2 h2 l3 h3) and two more prmt split them.
+M27B_DI void iq4_lookup(uint32_t q, uint32_t &lo4, uint32_t &hi4) {
+    const uint32_t s = q & 0x77777777u;
+    const uint32_t m8 = q & 0x88888888u;
+    const uint32_t sm = m8 | (m8 >> 3);
+    const uint32_t a0 = prmt(IQ4_T0, IQ4_T1, s), b0 = prmt(IQ4_T2, IQ4_T3, s);
+    const uint32_t a1 = prmt(IQ4_T0, IQ4_T1, s >> 16), b1 = prmt(IQ4_T2, IQ4_T3, s >> 16);
+    const uint32_t k0 = prmt(0x8000u, 0u, sm), k1 = prmt(0x8000u, 0u, sm >> 16);
+    const uint32_t v0 = (a0 & ~k0) | (b0 & k0), v1 = (a1 & ~k1) | (b1 & k1);
+    lo4 = prmt(v0, v1, 0x6420u);
+    hi4 = prmt(v0, v1, 0x7531u);
+}
+
+// One IQ4_XS block (136 bytes: d, scales_h | scales_l[4] | qs[128], read as
+// 17 x 8 bytes) times NT staged activation blocks: per 32-value sub-block ib
+// the signed dot of its codebook values with the q8_K codes, times the
+// stored 6-bit scale minus 32, summed in integers over the block, then times
+// d * d_x (ggml's vec_dot_iq4_xs_q8_K in integer form).
+template <int NT>
+M27B_DI void iq4xs_block_mac(const uint2 (&v)[17], const uint8_t *xrec0, const float *xd0, int nb, float (&acc)[NT]) {
+    const float dw = h2f(v[0].x);
+    const uint32_t sh = v[0].x >> 16, sl = v[0].y;
+    int isum[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) isum[t] = 0;
+#pragma unroll
+    for (int ib = 0; ib < 8; ++ib) {
+        const int ls = (int)(((sl >> (4 * ib)) & 0xfu) | (((sh >> (2 * ib)) & 3u) << 4)) - 32;
+        const uint32_t q[4] = {v[1 + 2 * ib].x, v[1 + 2 * ib].y, v[2 + 2 * ib].x, v[2 + 2 * ib].y};
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) iq4_lookup(q[i], lo[i], hi[i]);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            const uint8_t *xr = xrec0 + (size_t)t * nb * BLK_XREC + 32 * ib;
+            const int4 xl = *(const int4 *)(xr);       // values 0..15 of the sub-block
+            const int4 xh = *(const int4 *)(xr + 16);  // values 16..31
+            int dot = __dp4a((int)lo[0], xl.x, 0);
+            dot = __dp4a((int)lo[1], xl.y, dot);
+            dot = __dp4a((int)lo[2], xl.z, dot);
+            dot = __dp4a((int)lo[3], xl.w, dot);
+            dot = __dp4a((int)hi[0], xh.x, dot);
+            dot = __dp4a((int)hi[1], xh.y, dot);
+            dot = __dp4a((int)hi[2], xh.z, dot);
+            dot = __dp4a((int)hi[3], xh.w, dot);
+            isum[t] += ls * dot;
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = fmaf(dw * xd0[t * nb], (float)isum[t], acc[t]);
+}
+
+// Block traits: bytes per block, the lane's register copy of its block (read
+// from the stage), and the block's dot product with the staged activations.
+struct BlkQ4K {
+    static constexpr int BYTES = 144;
+    struct Reg { uint4 v[9]; };
+    static M27B_DI void load(const uint8_t *p, Reg &r) {
+#pragma unroll
+        for (int j = 0; j < 9; ++j) r.v[j] = *(const uint4 *)(p + 16 * j);
+    }
+    template <int NT>
+    static M27B_DI void mac(const Reg &r, const uint8_t *xrec0, const float *xd0, int nb, float (&acc)[NT]) {
+        q4k_block_mac<NT>(r.v, xrec0, xd0, nb, acc);
+    }
+};
+
+struct BlkQ5K {
+    static constexpr int BYTES = 176;
+    struct Reg { uint4 v[11]; };
+    static M27B_DI void load(const uint8_t *p, Reg &r) {
+#pragma unroll
+        for (int j = 0; j < 11; ++j) r.v[j] = *(const uint4 *)(p + 16 * j);
+    }
+    template <int NT>
+    static M27B_DI void mac(const Reg &r, const uint8_t *xrec0, const float *xd0, int nb, float (&acc)[NT]) {
+        q5k_block_mac<NT>(r.v, xrec0, xd0, nb, acc);
+    }
+};
+
+// 136-byte blocks sit at 8-byte offsets in the stage: 8-byte reads (the 16
+// lanes of a 64-bit shared-memory phase land on distinct banks: 544-byte slot
+// and 136-byte block strides).
+struct BlkIQ4XS {
+    static constexpr int BYTES = 136;
+    struct Reg { uint2 v[17]; };
+    static M27B_DI void load(const uint8_t *p, Reg &r) {
+#pragma unroll
+        for (int j = 0; j < 17; ++j) r.v[j] = *(const uint2 *)(p + 8 * j);
+    }
+    template <int NT>
+    static M27B_DI void mac(const Reg &r, const uint8_t *xrec0, const float *xd0, int nb, float (&acc)[NT]) {
+        iq4xs_block_mac<NT>(r.v, xrec0, xd0, nb, acc);
+    }
+};
+
 // Work of a warp: items (group, pass, matrix) in that order, matrix fastest
 // (SWIGLU streams the gate blocks, then the up blocks, of the same pass).
-template <int NT, int EPI>
-__global__ void __launch_bounds__(BLK_THREADS, 2)
-    k_qmv_q4k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
-                  int split) {
+template <class BT, int NT, int EPI>
+M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUtensorMap *tm1, int split) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
+    constexpr int ITEM = blk_item(BT::BYTES);
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int slot = lane >> 2, qd = lane & 3;
@@ -372,8 +569,8 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
     const int my_passes = (split == 1 ? P : ((warp + 1) * P) / split) - p_lo;
 
     // [stages of all warps | activation records | block scales | partials | barriers]
-    uint8_t *stage0 = smem + (size_t)warp * BLK_STAGES * BLK_ITEM;
-    uint8_t *xrec = smem + (size_t)nwarps * BLK_STAGES * BLK_ITEM;
+    uint8_t *stage0 = smem + (size_t)warp * BLK_STAGES * ITEM;
+    uint8_t *xrec = smem + (size_t)nwarps * BLK_STAGES * ITEM;
     float *xd = (float *)(xrec + (size_t)NT * nb * BLK_XREC);
     float *part = (float *)(((uintptr_t)(xd + NT * nb) + 15) & ~(uintptr_t)15);  // [BLK_WARPS][8][2][NT]
     uint64_t *bar = (uint64_t *)(part + (size_t)BLK_WARPS * 8 * 2 * NT) + (size_t)warp * BLK_STAGES;
@@ -390,8 +587,8 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
             if (lane == 0) {
                 uint64_t *b = &bar[ls];
                 fence_proxy_async();  // the stage's previous reads precede the async writes
-                mbar_arrive_expect_tx(b, BLK_ITEM);
-                tma_load_2d(stage0 + ls * BLK_ITEM, (NM == 2 && lm == 1) ? &tm1 : &tm0, (p_lo + lp) * 144,
+                mbar_arrive_expect_tx(b, ITEM);
+                tma_load_2d(stage0 + ls * ITEM, (NM == 2 && lm == 1) ? tm1 : tm0, (p_lo + lp) * BT::BYTES,
                             (wg + lg * W) * 8, b);
             }
             ++li;
@@ -439,15 +636,13 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
                 if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
                 // take this lane's block into registers, then hand the stage back
                 // to the copy engine: a later item streams in during the math
-                uint4 v[9];
-                const uint8_t *blk = stage0 + cs * BLK_ITEM + slot * 576 + qd * 144;
-#pragma unroll
-                for (int j = 0; j < 9; ++j) v[j] = *(const uint4 *)(blk + 16 * j);
+                typename BT::Reg v;
+                BT::load(stage0 + cs * ITEM + slot * (4 * BT::BYTES) + qd * BT::BYTES, v);
                 __syncwarp();
                 issue_item();
                 ++ci;
                 if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
-                if (row < a.rows && b < nb) q4k_block_mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[m]);
+                if (row < a.rows && b < nb) BT::template mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[m]);
             }
             if (!ok) break;
         }
@@ -529,6 +724,27 @@ __global__ void __launch_bounds__(BLK_THREADS, 2)
                 if (best[t] != 0ull) atomicMax(a.best + t, best[t]);
         }
     }
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(BLK_THREADS, 2)
+    k_qmv_q4k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
+                  int split) {
+    qmv_kblk_body<BlkQ4K, NT, EPI>(a, &tm0, &tm1, split);
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(BLK_THREADS, 2)
+    k_qmv_q5k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
+                  int split) {
+    qmv_kblk_body<BlkQ5K, NT, EPI>(a, &tm0, &tm1, split);
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(BLK_THREADS, 2)
+    k_qmv_iq4xs_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
+                    int split) {
+    qmv_kblk_body<BlkIQ4XS, NT, EPI>(a, &tm0, &tm1, split);
 }
 
 }  // namespace m27b

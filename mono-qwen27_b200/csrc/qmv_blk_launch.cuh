@@ -1,0 +1,80 @@
+// qmv_blk_launch.cuh — launch the block-per-lane k-quant matvec (qmv_blk.cuh)
+// for one block type: grid shape, shared memory, tensor maps.
+#pragma once
+
+#include "qmv_blk.cuh"
+#include "m27b_launch.cuh"
+#include "qmv_launch.cuh"
+
+namespace m27b {
+
+template <class BT, int NT, int EPI>
+inline auto blk_kernel() {
+    if constexpr (BT::BYTES == BlkQ4K::BYTES) return k_qmv_q4k_blk<NT, EPI>;
+    else if constexpr (BT::BYTES == BlkQ5K::BYTES) return k_qmv_q5k_blk<NT, EPI>;
+    else return k_qmv_iq4xs_blk<NT, EPI>;
+}
+
+template <class BT, int NT, int EPI>
+cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
+    auto kern = blk_kernel<BT, NT, EPI>();
+    const int nw = blk_warps(a.k, NT, BT::BYTES);
+    if (nw < 1) return cudaErrorInvalidValue;
+    const size_t smem = blk_smem_bytes(a.k, NT, BT::BYTES);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static size_t opted[64] = {0};
+    if (smem > 48 * 1024 && (dev >= 64 || smem > opted[dev])) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) opted[dev] = smem;
+    }
+    // two resident CTAs per SM by construction (shared memory <= 112 KB each)
+    const long groups = (a.rows + 7) / 8;
+    const int P = (a.rb + 3) / 4;
+    const long slots = (long)sm_count * 2;
+    int split, nthreads;
+    long grid;
+    size_t smem_launch;
+    if (2 * groups >= slots * nw || P < 2) {
+        // every warp streams whole row groups: the fewest groups per warp
+        // that the resident warps allow, then just enough warps
+        split = 1;
+        const long max_warps = slots * nw;
+        const long gpw = (groups + max_warps - 1) / max_warps;
+        const long warps = (groups + gpw - 1) / gpw;
+        grid = (warps + nw - 1) / nw;
+        nthreads = nw * 32;
+        smem_launch = smem;
+    } else {
+        // few row groups: the warps of a CTA split each group's passes
+        split = P < nw ? P : nw;
+        const long gpc = (groups + slots - 1) / slots;
+        grid = (groups + gpc - 1) / gpc;
+        nthreads = split * 32;
+        smem_launch = blk_smem_for(split, a.k, NT, BT::BYTES);
+    }
+    // box: 8 rows x 4 blocks (BT::BYTES uint32 words)
+    CUtensorMap tm0, tm1;
+    if (!encode_rows_u32(&tm0, a.w0, a.row_stride, a.rows, BT::BYTES)) return cudaErrorInvalidValue;
+    if (EPI == EPI_SWIGLU) {
+        if (!encode_rows_u32(&tm1, a.w1, a.row_stride, a.rows, BT::BYTES)) return cudaErrorInvalidValue;
+    } else {
+        tm1 = tm0;
+    }
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(nthreads), smem_launch, st, a, tm0, tm1, split);
+}
+
+template <class BT, int EPI>
+cudaError_t run_blk_nt(int nt, const QmvArgs &a, int sm_count, cudaStream_t st) {
+    switch (nt) {
+    case 1: return run_blk<BT, 1, EPI>(a, sm_count, st);
+    case 2: return run_blk<BT, 2, EPI>(a, sm_count, st);
+    case 3: return run_blk<BT, 3, EPI>(a, sm_count, st);
+    case 4: return run_blk<BT, 4, EPI>(a, sm_count, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace m27b

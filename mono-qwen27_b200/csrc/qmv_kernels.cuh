@@ -9,7 +9,7 @@ namespace m27b {
 constexpr int QMV_WARPS = 8;
 constexpr int QMV_THREADS = QMV_WARPS * 32;
 
-enum WeightKind { W_Q4K = 0, W_Q6KP = 1, W_Q80P = 2 };
+enum WeightKind { W_Q4K = 0, W_Q6KP = 1, W_Q80P = 2, W_Q5K = 3, W_IQ4XS = 4, W_F16 = 5, W_F32 = 6 };
 enum Epilogue { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ARGMAX = 2, EPI_PUSH = 3 };
 
 // EPI_PUSH: the matvec half of a fused matvec + all-reduce over NVLink.  Row
@@ -416,6 +416,8 @@ inline int pick_ps(int P, int cap) {
 
 size_t qmv_smem_bytes(int wtype, int k, int ntok);
 cudaError_t launch_qmv(int wt, int epi, QmvArgs a, int nt, int sm_count, cudaStream_t st);
+// f16 / f32 weights x fp32 activations (a.xf, a.ldxf), store epilogue (qmv_float.cu).
+cudaError_t launch_qmv_float(int wt, const QmvArgs &a, int nt, int sm_count, cudaStream_t st);
 // q4_K x 5..16 tokens on the tensor cores (qmv_q4k_mma.cu), store epilogue.
 bool q4k_mma_supported(int rb, int n_tok);
 cudaError_t launch_q4k_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st);

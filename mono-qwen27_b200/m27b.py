@@ -12,11 +12,12 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libm27b.so")
 
-# ggml type codes (reference include/mono27b_gguf.h:28-44)
-Q8_0, Q4_K, Q6_K, Q8_K = 8, 12, 14, 15
+# ggml type codes (reference include/mono27b_gguf.h:28-44; IQ4_XS = 23)
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, IQ4_XS = 0, 1, 8, 12, 13, 14, 15, 23
 LAYOUT_PLANAR = 0x100
 MAX_TOKENS = 16
-BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292)}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
+         Q8_K: (256, 292), IQ4_XS: (256, 136)}
 
 ERR_CAP = 512
 
@@ -89,7 +90,9 @@ def row_bytes(qtype, k):
 
 
 def act_type_for(qtype):
-    return Q8_0 if (qtype & 0xff) == Q8_0 else Q8_K
+    """q8_0 for q8_0 weights, q8_K for the 256-value types, 0 (fp32 rows) for f16 / f32."""
+    b = qtype & 0xff
+    return Q8_0 if b == Q8_0 else (0 if b in (F16, F32) else Q8_K)
 
 
 def act_bytes(act_type, k):
@@ -112,10 +115,11 @@ def _check(ok, err, what):
 
 
 class QWeight:
-    """A quantized weight matrix resident on the device.
+    """A quantized (or f16 / f32) weight matrix resident on the device.
 
     Holds the device bytes (a torch uint8 tensor) and the WeightView the C ABI
-    consumes.  q6_K and q8_0 are repacked to the planar layout on upload.
+    consumes.  q6_K and q8_0 are repacked to the planar layout on upload; for
+    f16 / f32 row_blocks counts values, as in the reference loader.
     """
 
     def __init__(self, raw_u8, qtype, k, rows, device="cuda", stream=None, keep_raw=False):
@@ -124,6 +128,8 @@ class QWeight:
         be = BLOCK[qtype][0]
         self.row_blocks = k // be
         raw = torch.as_tensor(raw_u8).reshape(-1)
+        if raw.dtype != torch.uint8:
+            raw = raw.view(torch.uint8)
         assert raw.numel() == rows * row_bytes(qtype, k), (raw.numel(), rows, row_bytes(qtype, k))
         raw_dev = raw.to(device) if raw.device.type != "cuda" else raw
         if qtype in (Q6_K, Q8_0):
@@ -294,7 +300,6 @@ class Partition(ctypes.Structure):
 
 QWEN27 = dict(n_layers=64, hidden=5120, ffn=17408, n_head=24, n_kv_head=4, head_dim=256, vocab=248320, n_rot=64,
               rope_theta=1e7, rms_eps=1e-6)
-F32 = 0
 
 
 def model_config(max_ctx=1024, tp_rank=0, tp_size=1, **kw):

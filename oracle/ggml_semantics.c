@@ -9,27 +9,37 @@
  * ----------------
  * The named oracle is ggml's CPU path (llama.cpp, ggml/src/ggml-quants.c and
  * ggml/src/ggml-cpu/quants.c): quantize_row_q8_K_ref, quantize_row_q8_0_ref,
- * quantize_row_q4_K_ref (make_qkx2_quants), quantize_row_q6_K_ref
- * (make_qx_quants), dequantize_row_q4_K / q6_K / q8_0 and the generic
- * ggml_vec_dot_q4_K_q8_K / q6_K_q8_K / q8_0_q8_0.  llama.cpp is vendored by the
+ * quantize_row_q4_K_ref / q5_K_ref (make_qkx2_quants), quantize_row_q6_K_ref
+ * (make_qx_quants), dequantize_row_q4_K / q5_K / q6_K / q8_0 / iq4_xs and
+ * the generic ggml_vec_dot_q4_K_q8_K / q5_K_q8_K / q6_K_q8_K / iq4_xs_q8_K /
+ * q8_0_q8_0 / f16 / f32.  llama.cpp is vendored by the
  * reference as an EMPTY, git-ignored directory (reference .gitignore:3,
  * ref/llama.cpp/) with no pinned commit, so the algorithms below are written
  * from ggml's published block formats and quantization rules, not from a
  * copy of its source.
  *
  * Block layouts follow the reference's structs:
- *   BlockQ4K  src/mono27b_executor.cu:18-23   (144 B)
- *   BlockQ8   src/mono27b_executor.cu:25-28   (q8_0, 34 B)
- *   BlockQ8K  src/mono27b_executor.cu:38-42   (292 B)
- *   BlockQ6K  src/mono27b_executor.cu:57-62   (210 B)
- * Dequant formulas follow debug/official_dequant.c:47-65 (q4_K) and
- * src/mono27b_executor.cu:1026-1048 (q6k_val), and get_scale_min_k4 at
- * src/mono27b_executor.cu:690-693.
+ *   BlockQ4K    src/mono27b_executor.cu:18-23   (144 B)
+ *   BlockQ8     src/mono27b_executor.cu:25-28   (q8_0, 34 B)
+ *   BlockQ5K    src/mono27b_executor.cu:30-36   (176 B)
+ *   BlockQ8K    src/mono27b_executor.cu:38-42   (292 B)
+ *   BlockIQ4XS  src/mono27b_executor.cu:44-49   (136 B; codebook :51-55)
+ *   BlockQ6K    src/mono27b_executor.cu:57-62   (210 B)
+ * Dequant formulas follow debug/official_dequant.c:47-65 (q4_K),
+ * src/mono27b_executor.cu:955-969 (q5k_val), :1004-1011 (IQ4_XS) and
+ * :1026-1048 (q6k_val), and get_scale_min_k4 at src/mono27b_executor.cu:690-693.
+ * f16 / f32 weights (the reference's k_f16_mv / k_f32_mv, :900-916,
+ * :1101-1114) take fp32 activations; ggml converts them to the weight's
+ * vec_dot type first (fp16 for f16 weights, round to nearest even) and sums
+ * the products in double.
  *
  * Pinning: dequant and the q8_0 quantizer are checked bit for bit against the
  * gguf 0.19.0 Python package (llama.cpp's gguf-py) through committed golden
  * fixtures, and the q4_K dequant against the 16 known outputs of
- * debug/official_dequant.c / debug/mono_give_current.debug.tsv:2.
+ * debug/official_dequant.c / debug/mono_give_current.debug.tsv:2.  The
+ * IQ4_XS weight quantizer here is this oracle's own simple nearest-codebook
+ * fit (ggml's search is not restated): it only generates test weights, and
+ * the GPU and the CPU consume the same bytes.
  *
  * Build with -ffp-contract=off: every dequantized value is
  * fl(fl(d*sc)*q) - fl(dmin*m) with no fused multiply-add, which is the
@@ -49,11 +59,19 @@ typedef struct { uint16_t d, dmin; uint8_t scales[12]; uint8_t qs[128]; } orc_q4
 typedef struct { uint8_t ql[128]; uint8_t qh[64]; int8_t scales[16]; uint16_t d; } orc_q6K;
 typedef struct { uint16_t d; int8_t qs[32]; } orc_q80;
 typedef struct { float d; int8_t qs[256]; int16_t bsums[16]; } orc_q8K;
+typedef struct { uint16_t d, dmin; uint8_t scales[12]; uint8_t qh[32]; uint8_t qs[128]; } orc_q5K;
+typedef struct { uint16_t d; uint16_t scales_h; uint8_t scales_l[4]; uint8_t qs[128]; } orc_iq4xs;
+
+/* The IQ4_NL / IQ4_XS codebook: the 16 signed values a 4-bit code stands for
+ * (a format constant; reference src/mono27b_executor.cu:51-55). */
+static const int8_t IQ4_VALUES[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
 
 _Static_assert(sizeof(orc_q4K) == 144, "q4_K block is 144 bytes");
 _Static_assert(sizeof(orc_q6K) == 210, "q6_K block is 210 bytes");
 _Static_assert(sizeof(orc_q80) == 34, "q8_0 block is 34 bytes");
 _Static_assert(sizeof(orc_q8K) == 292, "q8_K block is 292 bytes");
+_Static_assert(sizeof(orc_q5K) == 176, "q5_K block is 176 bytes");
+_Static_assert(sizeof(orc_iq4xs) == 136, "IQ4_XS block is 136 bytes");
 
 /* ---- fp16 <-> fp32 ------------------------------------------------------ */
 
@@ -149,6 +167,57 @@ void orc_dequantize_row_q6_K(const void *vx, float *y, int64_t k) {
     }
 }
 
+/* q5_K: sub-block s = 2g + h takes the low (h = 0) or high (h = 1) nibbles of
+ * qs[32g .. 32g+31] plus 16 x bit s of qh[l]; value d*sc*q - dmin*m. */
+void orc_dequantize_row_q5_K(const void *vx, float *y, int64_t k) {
+    const orc_q5K *x = (const orc_q5K *)vx;
+    for (int64_t b = 0; b < k / QK; ++b) {
+        const float d = orc_fp16_to_fp32(x[b].d), dmin = orc_fp16_to_fp32(x[b].dmin);
+        for (int g = 0; g < 4; ++g) {
+            int sc0, m0, sc1, m1;
+            q4K_scale_min(2 * g, x[b].scales, &sc0, &m0);
+            q4K_scale_min(2 * g + 1, x[b].scales, &sc1, &m1);
+            const float d0 = d * (float)sc0, n0 = dmin * (float)m0;
+            const float d1 = d * (float)sc1, n1 = dmin * (float)m1;
+            const uint8_t *q = x[b].qs + 32 * g;
+            float *o = y + b * QK + 64 * g;
+            for (int l = 0; l < 32; ++l)
+                o[l] = d0 * (float)((q[l] & 15) + ((x[b].qh[l] >> (2 * g)) & 1 ? 16 : 0)) - n0;
+            for (int l = 0; l < 32; ++l)
+                o[32 + l] = d1 * (float)((q[l] >> 4) + ((x[b].qh[l] >> (2 * g + 1)) & 1 ? 16 : 0)) - n1;
+        }
+    }
+}
+
+/* The 6-bit scale of sub-block ib of an IQ4_XS block, as stored (0..63;
+ * the multiplier is ls - 32). */
+static int iq4xs_ls(const orc_iq4xs *b, int ib) {
+    return ((b->scales_l[ib / 2] >> (4 * (ib % 2))) & 15) | (((b->scales_h >> (2 * ib)) & 3) << 4);
+}
+
+/* IQ4_XS: sub-block ib holds qs[16ib .. 16ib+15]; low nibbles are its
+ * elements 0..15, high nibbles 16..31; value (d*(ls-32)) * codebook[q]. */
+void orc_dequantize_row_iq4_xs(const void *vx, float *y, int64_t k) {
+    const orc_iq4xs *x = (const orc_iq4xs *)vx;
+    for (int64_t b = 0; b < k / QK; ++b) {
+        const float d = orc_fp16_to_fp32(x[b].d);
+        for (int ib = 0; ib < 8; ++ib) {
+            const float dl = d * (float)(iq4xs_ls(&x[b], ib) - 32);
+            const uint8_t *q = x[b].qs + 16 * ib;
+            float *o = y + b * QK + 32 * ib;
+            for (int j = 0; j < 16; ++j) {
+                o[j] = dl * (float)IQ4_VALUES[q[j] & 15];
+                o[16 + j] = dl * (float)IQ4_VALUES[q[j] >> 4];
+            }
+        }
+    }
+}
+
+void orc_dequantize_row_f16(const void *vx, float *y, int64_t k) {
+    const uint16_t *x = (const uint16_t *)vx;
+    for (int64_t i = 0; i < k; ++i) y[i] = orc_fp16_to_fp32(x[i]);
+}
+
 void orc_dequantize_row_q8_0(const void *vx, float *y, int64_t k) {
     const orc_q80 *x = (const orc_q80 *)vx;
     for (int64_t b = 0; b < k / 32; ++b) {
@@ -207,10 +276,11 @@ void orc_quantize_row_q8_0(const float *x, void *vy, int64_t k) {
  * grids iscale = (nmax + rmin + rdelta*is)/(max-min), each refined by the
  * weighted least-squares scale/offset for its codes; the trial with the
  * smallest weighted squared error wins.  Returns the scale and stores -offset
- * in *neg_off.  (ggml's make_qkx2_quants, called with rmin=-1, rdelta=0.1,
- * nstep=20, squared error.) */
+ * in *neg_off.  (ggml's make_qkx2_quants with squared error; q4_K calls it
+ * with rmin=-1, rdelta=0.1, nstep=20, q5_K with rmin=-0.5, rdelta=0.1,
+ * nstep=15.) */
 static float fit_asym(int n, int nmax, const float *x, const float *w, uint8_t *L,
-                      float *neg_off, uint8_t *trial) {
+                      float *neg_off, uint8_t *trial, float rmin, float rdelta, int nstep) {
     float lo = x[0], hi = x[0], sw = w[0], swx = w[0] * x[0];
     for (int i = 1; i < n; ++i) {
         if (x[i] < lo) lo = x[i];
@@ -234,8 +304,8 @@ static float fit_asym(int n, int nmax, const float *x, const float *w, uint8_t *
         const float r = scale * (float)l + lo - x[i];
         err_best += w[i] * (r * r);
     }
-    for (int is = 0; is <= 20; ++is) {
-        inv = (-1.0f + 0.1f * (float)is + (float)nmax) / (hi - lo);
+    for (int is = 0; is <= nstep; ++is) {
+        inv = (rmin + rdelta * (float)is + (float)nmax) / (hi - lo);
         float sl = 0, sl2 = 0, sxl = 0;
         for (int i = 0; i < n; ++i) {
             int l = rne_int(inv * (x[i] - lo));
@@ -267,54 +337,130 @@ static float fit_asym(int n, int nmax, const float *x, const float *w, uint8_t *
     return scale;
 }
 
+/* The shared part of the q4_K / q5_K weight quantizers for one super-block
+ * of 256 values: fit each 32-value sub-block (weights rms + |x|) to codes
+ * 0..nmax, quantize the 8 scales and 8 mins to 6 bits against the largest of
+ * each (packed as get_scale_min_k4 reads them), then re-derive every code
+ * from the stored scales: L[e] = clamp(rne((x + dmin*m)/(d*sc)), 0, nmax). */
+static void quantize_kblock(const float *x, int nmax, float rmin, float rdelta, int nstep, uint8_t scales[12],
+                            uint16_t *d16, uint16_t *dmin16, uint8_t L[QK]) {
+    uint8_t trial[32];
+    float w[32], sc[8], mn[8];
+    float sc_max = 0, mn_max = 0;
+    for (int j = 0; j < 8; ++j) {
+        float s2 = 0;
+        for (int l = 0; l < 32; ++l) s2 += x[32 * j + l] * x[32 * j + l];
+        const float rms = sqrtf(s2 / 32.0f);
+        for (int l = 0; l < 32; ++l) w[l] = rms + fabsf(x[32 * j + l]);
+        sc[j] = fit_asym(32, nmax, x + 32 * j, w, L + 32 * j, &mn[j], trial, rmin, rdelta, nstep);
+        if (sc[j] > sc_max) sc_max = sc[j];
+        if (mn[j] > mn_max) mn_max = mn[j];
+    }
+    const float isc = sc_max > 0 ? 63.0f / sc_max : 0.0f;
+    const float imn = mn_max > 0 ? 63.0f / mn_max : 0.0f;
+    memset(scales, 0, 12);
+    for (int j = 0; j < 8; ++j) {
+        int ls = rne_int(isc * sc[j]), lm = rne_int(imn * mn[j]);
+        ls = ls > 63 ? 63 : ls;
+        lm = lm > 63 ? 63 : lm;
+        if (j < 4) {
+            scales[j] = (uint8_t)ls;
+            scales[j + 4] = (uint8_t)lm;
+        } else {
+            scales[j + 4] = (uint8_t)((ls & 15) | ((lm & 15) << 4));
+            scales[j - 4] |= (uint8_t)((ls >> 4) << 6);
+            scales[j] |= (uint8_t)((lm >> 4) << 6);
+        }
+    }
+    *d16 = orc_fp32_to_fp16(sc_max / 63.0f);
+    *dmin16 = orc_fp32_to_fp16(mn_max / 63.0f);
+    for (int j = 0; j < 8; ++j) {
+        int s6, m6;
+        q4K_scale_min(j, scales, &s6, &m6);
+        const float d = orc_fp16_to_fp32(*d16) * (float)s6;
+        if (d == 0.0f) continue;
+        const float dm = orc_fp16_to_fp32(*dmin16) * (float)m6;
+        for (int l = 0; l < 32; ++l) {
+            int q = rne_int((x[32 * j + l] + dm) / d);
+            L[32 * j + l] = (uint8_t)(q < 0 ? 0 : (q > nmax ? nmax : q));
+        }
+    }
+}
+
 void orc_quantize_row_q4_K(const float *x, void *vy, int64_t k) {
     orc_q4K *y = (orc_q4K *)vy;
-    uint8_t L[QK], trial[32];
-    float w[32], sc[8], mn[8];
+    uint8_t L[QK];
     for (int64_t b = 0; b < k / QK; ++b, x += QK) {
-        float sc_max = 0, mn_max = 0;
-        for (int j = 0; j < 8; ++j) {
-            float s2 = 0;
-            for (int l = 0; l < 32; ++l) s2 += x[32 * j + l] * x[32 * j + l];
-            const float rms = sqrtf(s2 / 32.0f);
-            for (int l = 0; l < 32; ++l) w[l] = rms + fabsf(x[32 * j + l]);
-            sc[j] = fit_asym(32, 15, x + 32 * j, w, L + 32 * j, &mn[j], trial);
-            if (sc[j] > sc_max) sc_max = sc[j];
-            if (mn[j] > mn_max) mn_max = mn[j];
-        }
-        const float isc = sc_max > 0 ? 63.0f / sc_max : 0.0f;
-        const float imn = mn_max > 0 ? 63.0f / mn_max : 0.0f;
-        memset(y[b].scales, 0, 12);
-        for (int j = 0; j < 8; ++j) {
-            int ls = rne_int(isc * sc[j]), lm = rne_int(imn * mn[j]);
-            ls = ls > 63 ? 63 : ls;
-            lm = lm > 63 ? 63 : lm;
-            if (j < 4) {
-                y[b].scales[j] = (uint8_t)ls;
-                y[b].scales[j + 4] = (uint8_t)lm;
-            } else {
-                y[b].scales[j + 4] = (uint8_t)((ls & 15) | ((lm & 15) << 4));
-                y[b].scales[j - 4] |= (uint8_t)((ls >> 4) << 6);
-                y[b].scales[j] |= (uint8_t)((lm >> 4) << 6);
-            }
-        }
-        y[b].d = orc_fp32_to_fp16(sc_max / 63.0f);
-        y[b].dmin = orc_fp32_to_fp16(mn_max / 63.0f);
-        for (int j = 0; j < 8; ++j) {
-            int s6, m6;
-            q4K_scale_min(j, y[b].scales, &s6, &m6);
-            const float d = orc_fp16_to_fp32(y[b].d) * (float)s6;
-            if (d == 0.0f) continue;
-            const float dm = orc_fp16_to_fp32(y[b].dmin) * (float)m6;
-            for (int l = 0; l < 32; ++l) {
-                int q = rne_int((x[32 * j + l] + dm) / d);
-                L[32 * j + l] = (uint8_t)(q < 0 ? 0 : (q > 15 ? 15 : q));
-            }
-        }
+        quantize_kblock(x, 15, -1.0f, 0.1f, 20, y[b].scales, &y[b].d, &y[b].dmin, L);
         for (int g = 0; g < 4; ++g)
             for (int l = 0; l < 32; ++l)
                 y[b].qs[32 * g + l] = (uint8_t)(L[64 * g + l] | (L[64 * g + 32 + l] << 4));
     }
+}
+
+/* q5_K: the q4_K procedure with codes 0..31 (ggml's quantize_row_q5_K_ref);
+ * the low 4 bits go to the nibbles as in q4_K, bit 4 of sub-block s's code
+ * for element l to bit s of qh[l]. */
+void orc_quantize_row_q5_K(const float *x, void *vy, int64_t k) {
+    orc_q5K *y = (orc_q5K *)vy;
+    uint8_t L[QK];
+    for (int64_t b = 0; b < k / QK; ++b, x += QK) {
+        quantize_kblock(x, 31, -0.5f, 0.1f, 15, y[b].scales, &y[b].d, &y[b].dmin, L);
+        memset(y[b].qh, 0, 32);
+        for (int g = 0; g < 4; ++g)
+            for (int l = 0; l < 32; ++l) {
+                const int a = L[64 * g + l], c = L[64 * g + 32 + l];
+                y[b].qs[32 * g + l] = (uint8_t)((a & 15) | ((c & 15) << 4));
+                y[b].qh[l] |= (uint8_t)(((a >> 4) << (2 * g)) | ((c >> 4) << (2 * g + 1)));
+            }
+    }
+}
+
+/* IQ4_XS test-weight quantizer (this oracle's own fit, not ggml's search):
+ * per sub-block the scale s = max|x| / 113 (so both signs stay inside the
+ * codebook's range -127..113), the block scale d = max s / 31 in fp16, the
+ * stored ls = clamp(rne(s/d) + 32, 0, 63), and each value takes the codebook
+ * entry nearest to x / (d*(ls-32)) (first index on ties). */
+void orc_quantize_row_iq4_xs(const float *x, void *vy, int64_t k) {
+    orc_iq4xs *y = (orc_iq4xs *)vy;
+    for (int64_t b = 0; b < k / QK; ++b, x += QK) {
+        float s[8], smax = 0.0f;
+        for (int ib = 0; ib < 8; ++ib) {
+            float amax = 0.0f;
+            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(x[32 * ib + j]));
+            s[ib] = amax / 113.0f;
+            smax = fmaxf(smax, s[ib]);
+        }
+        memset(&y[b], 0, sizeof(orc_iq4xs));
+        y[b].d = orc_fp32_to_fp16(smax / 31.0f);
+        const float d = orc_fp16_to_fp32(y[b].d);
+        for (int ib = 0; ib < 8; ++ib) {
+            int ls = d > 0.0f ? rne_int(s[ib] / d) + 32 : 32;
+            ls = ls < 0 ? 0 : (ls > 63 ? 63 : ls);
+            y[b].scales_l[ib / 2] |= (uint8_t)((ls & 15) << (4 * (ib % 2)));
+            y[b].scales_h |= (uint16_t)((ls >> 4) << (2 * ib));
+            const float dl = d * (float)(ls - 32);
+            for (int j = 0; j < 32; ++j) {
+                int best = 0;
+                if (dl != 0.0f) {
+                    const float t = x[32 * ib + j] / dl;
+                    float err = fabsf(t - (float)IQ4_VALUES[0]);
+                    for (int c = 1; c < 16; ++c) {
+                        const float e2 = fabsf(t - (float)IQ4_VALUES[c]);
+                        if (e2 < err) { err = e2; best = c; }
+                    }
+                }
+                uint8_t *q = y[b].qs + 16 * ib + (j & 15);
+                *q |= (uint8_t)(j < 16 ? best : best << 4);
+            }
+        }
+    }
+}
+
+/* f16 weights: round to nearest even. */
+void orc_quantize_row_f16(const float *x, void *vy, int64_t k) {
+    uint16_t *y = (uint16_t *)vy;
+    for (int64_t i = 0; i < k; ++i) y[i] = orc_fp32_to_fp16(x[i]);
 }
 
 /* Symmetric fit of n values to signed codes -nmax..nmax-1 with weights x^2:
@@ -409,9 +555,13 @@ void orc_quantize_row_q6_K(const float *x, void *vy, int64_t k) {
 
 /* ---- dot products ------------------------------------------------------- */
 /* Each super-block contributes exact integer sums combined in fp32:
- *   q4_K:  (d_w*d_x) * sum_s sc_s*<q4,q8>_s  -  (dmin_w*d_x) * sum_s m_s*bsum_s
- *   q6_K:  (d_w*d_x) * sum_g sc_g*<q6-32,q8>_g
- *   q8_0:  sum_b <qw,qx>_b * (d_w*d_x)
+ *   q4_K:   (d_w*d_x) * sum_s sc_s*<q4,q8>_s  -  (dmin_w*d_x) * sum_s m_s*bsum_s
+ *   q5_K:   the same with 5-bit codes
+ *   q6_K:   (d_w*d_x) * sum_g sc_g*<q6-32,q8>_g
+ *   IQ4_XS: (d_w*d_x) * sum_ib (ls_ib-32)*<codebook[q],q8>_ib
+ *   q8_0:   sum_b <qw,qx>_b * (d_w*d_x)
+ * (ggml's generic code adds the per-sub-block terms in float; the integer
+ * form is exact and differs from it only in fp32 rounding order.)
  */
 
 float orc_vec_dot_q4_K_q8_K(int64_t n, const void *vx, const void *vy) {
@@ -435,6 +585,67 @@ float orc_vec_dot_q4_K_q8_K(int64_t n, const void *vx, const void *vy) {
         acc -= orc_fp16_to_fp32(x[b].dmin) * dx * (float)msum;
     }
     return acc;
+}
+
+float orc_vec_dot_q5_K_q8_K(int64_t n, const void *vx, const void *vy) {
+    const orc_q5K *x = (const orc_q5K *)vx;
+    const orc_q8K *y = (const orc_q8K *)vy;
+    float acc = 0.0f;
+    for (int64_t b = 0; b < n / QK; ++b) {
+        int32_t isum = 0, msum = 0;
+        for (int s = 0; s < 8; ++s) {
+            int sc, mn;
+            q4K_scale_min(s, x[b].scales, &sc, &mn);
+            const uint8_t *q = x[b].qs + 32 * (s / 2);
+            const int8_t *a = y[b].qs + 32 * s;
+            int32_t dot = 0;
+            for (int l = 0; l < 32; ++l) {
+                const int v = ((s & 1) ? (q[l] >> 4) : (q[l] & 15)) + (((x[b].qh[l] >> s) & 1) << 4);
+                dot += v * a[l];
+            }
+            isum += sc * dot;
+            msum += mn * (y[b].bsums[2 * s] + y[b].bsums[2 * s + 1]);
+        }
+        const float dx = y[b].d;
+        acc += orc_fp16_to_fp32(x[b].d) * dx * (float)isum;
+        acc -= orc_fp16_to_fp32(x[b].dmin) * dx * (float)msum;
+    }
+    return acc;
+}
+
+float orc_vec_dot_iq4_xs_q8_K(int64_t n, const void *vx, const void *vy) {
+    const orc_iq4xs *x = (const orc_iq4xs *)vx;
+    const orc_q8K *y = (const orc_q8K *)vy;
+    float acc = 0.0f;
+    for (int64_t b = 0; b < n / QK; ++b) {
+        int32_t isum = 0;
+        for (int ib = 0; ib < 8; ++ib) {
+            const uint8_t *q = x[b].qs + 16 * ib;
+            const int8_t *a = y[b].qs + 32 * ib;
+            int32_t dot = 0;
+            for (int j = 0; j < 16; ++j) dot += IQ4_VALUES[q[j] & 15] * a[j] + IQ4_VALUES[q[j] >> 4] * a[16 + j];
+            isum += (iq4xs_ls(&x[b], ib) - 32) * dot;
+        }
+        acc += orc_fp16_to_fp32(x[b].d) * y[b].d * (float)isum;
+    }
+    return acc;
+}
+
+/* f16 weights . fp32 activations: x rounded to fp16 (ggml's vec_dot type for
+ * f16), each product exact in fp32, summed in double. */
+float orc_vec_dot_f16_f32(int64_t n, const void *vx, const float *x) {
+    const uint16_t *w = (const uint16_t *)vx;
+    double acc = 0.0;
+    for (int64_t i = 0; i < n; ++i)
+        acc += (double)(orc_fp16_to_fp32(w[i]) * orc_fp16_to_fp32(orc_fp32_to_fp16(x[i])));
+    return (float)acc;
+}
+
+/* f32 weights . fp32 activations: fp32 products summed in double. */
+float orc_vec_dot_f32_f32(int64_t n, const float *w, const float *x) {
+    double acc = 0.0;
+    for (int64_t i = 0; i < n; ++i) acc += (double)(w[i] * x[i]);
+    return (float)acc;
 }
 
 float orc_vec_dot_q6_K_q8_K(int64_t n, const void *vx, const void *vy) {
@@ -466,12 +677,16 @@ float orc_vec_dot_q8_0_q8_0(int64_t n, const void *vx, const void *vy) {
 
 /* ---- whole-matrix drivers (OpenMP over rows) ---------------------------- */
 
-enum { ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14 };
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q5_K = 13, ORC_Q6_K = 14, ORC_IQ4_XS = 23 };
 
 static size_t row_bytes(int type, int64_t k) {
     switch (type) {
+    case ORC_F32: return (size_t)k * 4;
+    case ORC_F16: return (size_t)k * 2;
     case ORC_Q4_K: return (size_t)(k / QK) * sizeof(orc_q4K);
+    case ORC_Q5_K: return (size_t)(k / QK) * sizeof(orc_q5K);
     case ORC_Q6_K: return (size_t)(k / QK) * sizeof(orc_q6K);
+    case ORC_IQ4_XS: return (size_t)(k / QK) * sizeof(orc_iq4xs);
     case ORC_Q8_0: return (size_t)(k / 32) * sizeof(orc_q80);
     default: return 0;
     }
@@ -494,13 +709,16 @@ int orc_max_threads(void) {
 }
 
 /* y[t*rows + r] = W[r] . x[t] for t < ntok: W has `rows` rows of k values in
- * ggml type `type`, x holds ntok activation rows quantized to q8_K (k-quants)
- * or q8_0 (q8_0 weights).  Returns 0 on success, -1 on a bad type. */
+ * ggml type `type`, x holds ntok activation rows quantized to q8_K (k-quants,
+ * IQ4_XS) or q8_0 (q8_0 weights), or plain fp32 rows (f16 / f32 weights).
+ * Returns 0 on success, -1 on a bad type. */
 int orc_matvec(int type, const void *W, int64_t rows, int64_t k, const void *xq, int ntok,
                float *y, int nthreads) {
     const size_t rb = row_bytes(type, k);
     if (!rb) return -1;
-    const size_t xb = type == ORC_Q8_0 ? (size_t)(k / 32) * sizeof(orc_q80) : (size_t)(k / QK) * sizeof(orc_q8K);
+    const size_t xb = type == ORC_Q8_0 ? (size_t)(k / 32) * sizeof(orc_q80)
+                    : (type == ORC_F16 || type == ORC_F32) ? (size_t)k * 4
+                                                            : (size_t)(k / QK) * sizeof(orc_q8K);
     set_threads(nthreads);
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
@@ -508,9 +726,15 @@ int orc_matvec(int type, const void *W, int64_t rows, int64_t k, const void *xq,
         for (int t = 0; t < ntok; ++t) {
             const uint8_t *a = (const uint8_t *)xq + (size_t)t * xb;
             float v = 0.0f;
-            if (type == ORC_Q4_K) v = orc_vec_dot_q4_K_q8_K(k, w, a);
-            else if (type == ORC_Q6_K) v = orc_vec_dot_q6_K_q8_K(k, w, a);
-            else v = orc_vec_dot_q8_0_q8_0(k, w, a);
+            switch (type) {
+            case ORC_Q4_K: v = orc_vec_dot_q4_K_q8_K(k, w, a); break;
+            case ORC_Q5_K: v = orc_vec_dot_q5_K_q8_K(k, w, a); break;
+            case ORC_Q6_K: v = orc_vec_dot_q6_K_q8_K(k, w, a); break;
+            case ORC_IQ4_XS: v = orc_vec_dot_iq4_xs_q8_K(k, w, a); break;
+            case ORC_F16: v = orc_vec_dot_f16_f32(k, w, (const float *)a); break;
+            case ORC_F32: v = orc_vec_dot_f32_f32(k, (const float *)w, (const float *)a); break;
+            default: v = orc_vec_dot_q8_0_q8_0(k, w, a); break;
+            }
             y[(size_t)t * rows + r] = v;
         }
     }
@@ -526,9 +750,15 @@ int orc_quantize_rows(int type, const float *x, int64_t rows, int64_t k, void *o
     for (int64_t r = 0; r < rows; ++r) {
         const float *xr = x + (size_t)r * k;
         void *o = (uint8_t *)out + (size_t)r * rb;
-        if (type == ORC_Q4_K) orc_quantize_row_q4_K(xr, o, k);
-        else if (type == ORC_Q6_K) orc_quantize_row_q6_K(xr, o, k);
-        else orc_quantize_row_q8_0(xr, o, k);
+        switch (type) {
+        case ORC_Q4_K: orc_quantize_row_q4_K(xr, o, k); break;
+        case ORC_Q5_K: orc_quantize_row_q5_K(xr, o, k); break;
+        case ORC_Q6_K: orc_quantize_row_q6_K(xr, o, k); break;
+        case ORC_IQ4_XS: orc_quantize_row_iq4_xs(xr, o, k); break;
+        case ORC_F16: orc_quantize_row_f16(xr, o, k); break;
+        case ORC_F32: memcpy(o, xr, (size_t)k * 4); break;
+        default: orc_quantize_row_q8_0(xr, o, k); break;
+        }
     }
     return 0;
 }
@@ -539,9 +769,16 @@ int orc_dequantize_rows(int type, const void *W, int64_t rows, int64_t k, float 
     if (!rb) return -1;
     for (int64_t r = 0; r < rows; ++r) {
         const void *w = (const uint8_t *)W + (size_t)r * rb;
-        if (type == ORC_Q4_K) orc_dequantize_row_q4_K(w, y + (size_t)r * k, k);
-        else if (type == ORC_Q6_K) orc_dequantize_row_q6_K(w, y + (size_t)r * k, k);
-        else orc_dequantize_row_q8_0(w, y + (size_t)r * k, k);
+        float *o = y + (size_t)r * k;
+        switch (type) {
+        case ORC_Q4_K: orc_dequantize_row_q4_K(w, o, k); break;
+        case ORC_Q5_K: orc_dequantize_row_q5_K(w, o, k); break;
+        case ORC_Q6_K: orc_dequantize_row_q6_K(w, o, k); break;
+        case ORC_IQ4_XS: orc_dequantize_row_iq4_xs(w, o, k); break;
+        case ORC_F16: orc_dequantize_row_f16(w, o, k); break;
+        case ORC_F32: memcpy(o, w, (size_t)k * 4); break;
+        default: orc_dequantize_row_q8_0(w, o, k); break;
+        }
     }
     return 0;
 }

@@ -12,9 +12,11 @@ import numpy as np
 
 from . import build as _build
 
-Q8_0, Q4_K, Q6_K, Q8_K = 8, 12, 14, 15
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, IQ4_XS = 0, 1, 8, 12, 13, 14, 15, 23
 QK = 256
-BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292)}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210),
+         Q8_K: (256, 292), IQ4_XS: (256, 136)}
+FLOAT_TYPES = (F32, F16)
 
 _lib = None
 
@@ -27,12 +29,16 @@ def lib():
             _build.build_oracle()
         L = ctypes.CDLL(path)
         vp, i64, fp = ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p
-        for name in ("orc_dequantize_row_q4_K", "orc_dequantize_row_q6_K", "orc_dequantize_row_q8_0",
+        for name in ("orc_dequantize_row_q4_K", "orc_dequantize_row_q5_K", "orc_dequantize_row_q6_K",
+                     "orc_dequantize_row_q8_0", "orc_dequantize_row_iq4_xs", "orc_dequantize_row_f16",
                      "orc_quantize_row_q8_K", "orc_quantize_row_q8_0", "orc_quantize_row_q4_K",
-                     "orc_quantize_row_q6_K"):
+                     "orc_quantize_row_q5_K", "orc_quantize_row_q6_K", "orc_quantize_row_iq4_xs",
+                     "orc_quantize_row_f16"):
             getattr(L, name).argtypes = [vp, vp, i64]
             getattr(L, name).restype = None
-        for name in ("orc_vec_dot_q4_K_q8_K", "orc_vec_dot_q6_K_q8_K", "orc_vec_dot_q8_0_q8_0"):
+        for name in ("orc_vec_dot_q4_K_q8_K", "orc_vec_dot_q5_K_q8_K", "orc_vec_dot_q6_K_q8_K",
+                     "orc_vec_dot_iq4_xs_q8_K", "orc_vec_dot_q8_0_q8_0", "orc_vec_dot_f16_f32",
+                     "orc_vec_dot_f32_f32"):
             getattr(L, name).argtypes = [i64, vp, vp]
             getattr(L, name).restype = ctypes.c_float
         L.orc_matvec.argtypes = [ctypes.c_int, vp, i64, i64, vp, ctypes.c_int, fp, ctypes.c_int]
@@ -104,18 +110,24 @@ def quantize_q8_0(x):
 
 
 def act_type_for(qtype):
-    return Q8_0 if qtype == Q8_0 else Q8_K
+    """Activation format a weight type's dot product takes: q8_0 for q8_0,
+    fp32 rows for f16 / f32 (converted inside the dot), q8_K otherwise."""
+    return Q8_0 if qtype == Q8_0 else (F32 if qtype in FLOAT_TYPES else Q8_K)
 
 
 def quantize_act(qtype, x):
+    if qtype in FLOAT_TYPES:
+        return np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32).view(np.uint8)
     return quantize_q8_0(x) if qtype == Q8_0 else quantize_q8_K(x)
 
 
 def matvec(qtype, w, k, xq, nthreads=0):
     """y[t, r] = W[r] . x[t] with ggml dot-product semantics; xq from quantize_act."""
-    w = np.ascontiguousarray(w, dtype=np.uint8)
+    w = np.ascontiguousarray(w).view(np.uint8)
     rows = w.size // row_bytes(qtype, k)
-    xq = np.ascontiguousarray(np.atleast_2d(xq), dtype=np.uint8)
+    xq = np.ascontiguousarray(np.atleast_2d(xq))
+    if xq.dtype != np.uint8:
+        xq = xq.view(np.uint8)
     ntok = xq.shape[0]
     y = np.empty((ntok, rows), dtype=np.float32)
     assert lib().orc_matvec(qtype, _p(w), rows, k, _p(xq), ntok, _p(y), nthreads) == 0

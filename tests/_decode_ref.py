@@ -29,24 +29,27 @@ import numpy as np
 from _data import Q4_K, Q6_K, gauss_weights
 
 F32 = 0
-BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), 8: (32, 34)}
+BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), 8: (32, 34), 13: (256, 176), 23: (256, 136)}
 
 TINY = dict(n_layers=2, hidden=512, ffn=1024, n_head=4, n_kv_head=2, head_dim=128, vocab=1000, n_rot=64,
             rope_theta=1e7, rms_eps=1e-6)
 
 
-def make_model(orc, c, seed=0, sigma=0.02, norm_jitter=0.1, qtype=None):
+def make_model(orc, c, seed=0, sigma=0.02, norm_jitter=0.1, qtype=None, types=None):
     """name -> (ggml_type, row_elems, row_count, array): GGUF-named tensors of
     N(0, sigma^2) weights quantized by the oracle (the q4_k_m mix, or every
-    matrix as `qtype`, e.g. q8_0 for a draft), norms 1 + N(0, jitter^2)."""
+    matrix as `qtype`, e.g. q8_0 for a draft; `types` maps a layer tensor's
+    short name, e.g. "ffn_down", to its type), norms 1 + N(0, jitter^2)."""
     rng = np.random.default_rng(seed)
     hd, H, KV = c["head_dim"], c["n_head"], c["n_kv_head"]
     t = {}
     s = [seed * 1000]
+    types = types or {}
 
     def q(name, qt, rows, k):
         s[0] += 1
-        qt = qtype or qt
+        short = name.split(".")[-2] if name.startswith("blk.") else None
+        qt = types.get(short, qtype or qt)
         t[name] = (qt, k, rows, gauss_weights(orc, qt, rows, k, s[0], sigma))
 
     def norm(name, n):

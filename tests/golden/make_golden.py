@@ -10,6 +10,8 @@ Contents
   fields forced to finite, moderate values) and their dequantization by
   ``gguf.quants.dequantize`` — llama.cpp's own numpy restatement of
   dequantize_row_q4_K / q6_K / q8_0.
+* ``{q5K,iq4xs,f16}_raw`` / ``..._deq``: the same for q5_K, IQ4_XS and f16
+  (a second seeded generator, so the first fixtures keep their bytes).
 * ``q80_x`` / ``q80_q``: fp32 rows and their q8_0 quantization by
   ``gguf.quants.quantize`` (which gguf-py documents as matching ggml's
   quantize_row_q8_0 bit for bit).
@@ -44,6 +46,15 @@ def random_blocks(rng, qtype, nblocks):
     elif qtype == T.Q6_K:
         b = rng.integers(0, 256, (nblocks, 210), dtype=np.uint8)
         b[:, 208:210] = fp16_bits(rng, nblocks, 1e-5, 1e-3).view(np.uint8).reshape(-1, 2)
+    elif qtype == T.Q5_K:
+        b = rng.integers(0, 256, (nblocks, 176), dtype=np.uint8)
+        b[:, 0:2] = np.abs(fp16_bits(rng, nblocks, 1e-4, 2e-2).view(np.float16)).view(np.uint16).view(np.uint8).reshape(-1, 2)
+        b[:, 2:4] = np.abs(fp16_bits(rng, nblocks, 1e-4, 2e-2).view(np.float16)).view(np.uint16).view(np.uint8).reshape(-1, 2)
+    elif qtype == T.IQ4_XS:
+        b = rng.integers(0, 256, (nblocks, 136), dtype=np.uint8)
+        b[:, 0:2] = fp16_bits(rng, nblocks, 1e-5, 1e-3).view(np.uint8).reshape(-1, 2)
+    elif qtype == T.F16:
+        b = fp16_bits(rng, nblocks, 0.0, 4.0).view(np.uint8).reshape(nblocks, 2)
     else:
         b = rng.integers(0, 256, (nblocks, 34), dtype=np.uint8)
         b[:, 0:2] = fp16_bits(rng, nblocks, 1e-4, 1e-1).view(np.uint8).reshape(-1, 2)
@@ -73,6 +84,14 @@ def main():
         be = 256 if qt != T.Q8_0 else 32
         rows = 6
         raw = random_blocks(rng, qt, rows * k // be).reshape(rows, -1)
+        deq = gguf.quants.dequantize(raw, qt).reshape(rows, k).astype(np.float32)
+        out[name + "_raw"] = raw
+        out[name + "_deq"] = deq
+        out[name + "_k"] = np.int64(k)
+    rng2 = np.random.default_rng(20251202)
+    for name, qt, k, be in (("q5K", T.Q5_K, 512, 256), ("iq4xs", T.IQ4_XS, 512, 256), ("f16", T.F16, 96, 1)):
+        rows = 6
+        raw = random_blocks(rng2, qt, rows * k // be).reshape(rows, -1)
         deq = gguf.quants.dequantize(raw, qt).reshape(rows, k).astype(np.float32)
         out[name + "_raw"] = raw
         out[name + "_deq"] = deq

@@ -70,6 +70,9 @@ def _view(m27b, ptr, t, rb, rc):
     ("raw_q6K", "must be repacked"),
     ("bad_type", "unsupported weight type"),
     ("bad_flags", "unknown layout flags"),
+    ("iq4xs_odd_blocks", "even number of blocks"),
+    ("f16_ragged_row", "multiple of 8"),
+    ("f16_with_q8_acts", "fp32 activations"),
 ])
 def test_qmv_rejects_bad_views(m27b, case, needle):
     v = {
@@ -78,8 +81,11 @@ def test_qmv_rejects_bad_views(m27b, case, needle):
         "unaligned": _view(m27b, 0x1008, m27b.Q4_K, 20, 8),
         "empty": _view(m27b, 0x1000, m27b.Q4_K, 0, 8),
         "raw_q6K": _view(m27b, 0x1000, m27b.Q6_K, 20, 8),
-        "bad_type": _view(m27b, 0x1000, 1, 20, 8),
+        "bad_type": _view(m27b, 0x1000, 2, 20, 8),  # q4_0: not on this path
         "bad_flags": _view(m27b, 0x1000, m27b.Q4_K | 0x200, 20, 8),
+        "iq4xs_odd_blocks": _view(m27b, 0x1000, m27b.IQ4_XS, 3, 8),
+        "f16_ragged_row": _view(m27b, 0x1000, m27b.F16, 20, 8),
+        "f16_with_q8_acts": _view(m27b, 0x1000, m27b.F16, 64, 8),
     }[case]
     ok, msg = m27b.call_raw("m27b_qmv", v, ctypes.c_void_p(0x2000), 1, ctypes.c_void_p(0x3000), 8, None, None)
     assert not ok and needle in msg, msg

@@ -1,9 +1,10 @@
 """The CPU oracle pinned against golden vectors (CPU only).
 
-The oracle restates ggml's q4_K / q6_K / q8_0 / q8_K semantics; these tests
-pin it against gguf 0.19.0's dequantizers and q8_0 quantizer (committed
-fixtures), against the reference's own q4_K known-answer values, and check its
-integer dot-product formulation against the pinned dequantization.
+The oracle restates ggml's q4_K / q5_K / q6_K / IQ4_XS / q8_0 / q8_K / f16
+semantics; these tests pin it against gguf 0.19.0's dequantizers and q8_0
+quantizer (committed fixtures), against the reference's own q4_K known-answer
+values, and check its integer dot-product formulation against the pinned
+dequantization.
 """
 import os
 import subprocess
@@ -11,10 +12,11 @@ import subprocess
 import numpy as np
 import pytest
 
-Q8_0, Q4_K, Q6_K, Q8_K = 8, 12, 14, 15
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, IQ4_XS = 0, 1, 8, 12, 13, 14, 15, 23
 
 
-@pytest.mark.parametrize("name,qt", [("q4K", Q4_K), ("q6K", Q6_K), ("q80", Q8_0)])
+@pytest.mark.parametrize("name,qt", [("q4K", Q4_K), ("q6K", Q6_K), ("q80", Q8_0), ("q5K", Q5_K),
+                                     ("iq4xs", IQ4_XS), ("f16", F16)])
 def test_dequant_matches_gguf_bit_exact(orc, golden, name, qt):
     k = int(golden[name + "_k"])
     got = orc.dequantize(qt, golden[name + "_raw"], k)
@@ -93,16 +95,20 @@ def test_q8_K_quantizer_rules(orc):
     assert d[0] > 0 and qs[0][10] == -127 and qs[0][20] == 127  # first maximum (-5) sets the sign
 
 
-@pytest.mark.parametrize("qt,k", [(Q4_K, 1024), (Q6_K, 1024), (Q8_0, 512)])
+@pytest.mark.parametrize("qt,k", [(Q4_K, 1024), (Q6_K, 1024), (Q8_0, 512), (Q5_K, 1024), (IQ4_XS, 1024),
+                                  (F16, 200), (F32, 200)])
 def test_vec_dot_equals_dequantized_dot(orc, qt, k):
-    """The integer vec_dot equals sum(dequant(W) * dequant(x)) up to fp32 rounding."""
+    """The integer vec_dot equals sum(dequant(W) * dequant(x)) up to fp32 rounding
+    (f16: x rounded to fp16 first, as ggml converts it to the weight's type)."""
     rng = np.random.default_rng(7)
     w = orc.quantize_weights(qt, (rng.standard_normal((16, k)) * 0.02).astype(np.float32))
     x = rng.standard_normal((2, k)).astype(np.float32)
     xq = orc.quantize_act(qt, x)
     y = orc.matvec(qt, w, k, xq)
     wd = orc.dequantize(qt, w, k).astype(np.float64)
-    if qt == Q8_0:
+    if qt in (F16, F32):
+        xd = (x.astype(np.float16) if qt == F16 else x).astype(np.float64)
+    elif qt == Q8_0:
         xb = xq.reshape(2, -1, 34)
         xd = (xb[:, :, 2:].view(np.int8).astype(np.float64) *
               xb[:, :, 0:2].copy().view(np.float16).astype(np.float64)).reshape(2, k)
@@ -119,7 +125,7 @@ def test_vec_dot_equals_dequantized_dot(orc, qt, k):
 def test_weight_quantizers_are_accurate(orc):
     rng = np.random.default_rng(3)
     x = (rng.standard_normal((32, 512)) * 0.02).astype(np.float32)
-    for qt, tol in ((Q4_K, 0.09), (Q6_K, 0.025), (Q8_0, 0.008)):
+    for qt, tol in ((Q4_K, 0.09), (Q5_K, 0.045), (Q6_K, 0.025), (IQ4_XS, 0.11), (Q8_0, 0.008), (F16, 5e-4)):
         w = orc.quantize_weights(qt, x)
         assert orc.rel_l2(orc.dequantize(qt, w, 512), x) < tol
 
@@ -131,3 +137,19 @@ def test_matvec_threads_do_not_change_results(orc):
     a = orc.matvec(Q4_K, w, 512, xq, nthreads=1)
     b = orc.matvec(Q4_K, w, 512, xq, nthreads=4)
     assert np.array_equal(a, b)
+
+
+def test_iq4_xs_codebook_and_scale_fields(orc):
+    """IQ4_XS field layout: ls = 4 bits of scales_l | 2 bits of scales_h, the
+    multiplier ls - 32, low nibbles the first 16 values of a sub-block."""
+    blk = np.zeros(136, np.uint8)
+    blk[0:2] = np.array([1.0], np.float16).view(np.uint8)
+    # sub-block 0: ls = 0x21 (33 -> multiplier 1); sub-block 1: ls = 0x1e (30 -> -2)
+    blk[4] = 0x1 | (0xe << 4)
+    blk[2:4] = np.array([0x2 | (0x1 << 2)], np.uint16).view(np.uint8)
+    blk[8] = 0x0 | (0xf << 4)    # sub-block 0, element 0: code 0; element 16: code 15
+    blk[8 + 16] = 0x8            # sub-block 1, element 0: code 8
+    v = orc.dequantize(IQ4_XS, blk[None], 256)[0]
+    assert v[0] == -127 and v[16] == 113 and v[1] == -127
+    assert v[32] == -2 * 1 and v[33] == -2 * -127
+    assert np.all(v[64:] == -32 * -127)  # stored ls 0: multiplier -32, code 0: codebook -127
