@@ -72,6 +72,8 @@ def parse_args():
     p.add_argument("--prompt", type=int, default=512, help="decode: prompt tokens before generation")
     p.add_argument("--gen", type=int, default=256, help="decode: generated tokens (timed)")
     p.add_argument("--layers", type=int, default=64, help="decode: layers (64 = the Qwen-27B shape)")
+    p.add_argument("--hybrid", action="store_true",
+                   help="decode: the hybrid layout (every 4th layer attention, the rest Gated DeltaNet; 1 GPU)")
     p.add_argument("--comm", choices=["p2p", "nccl"], default="p2p",
                    help="decode, N>1: fused NVLink all-reduce (p2p) or NCCL all-reduce")
     a = p.parse_args()
@@ -335,7 +337,11 @@ def decode_bench(args, world, rank, dev, dist, uuid):
     import numpy as np
     import torch
     import m27b
-    cfg = m27b.model_config(max_ctx=args.prompt + args.gen + 8, tp_rank=rank, tp_size=world, n_layers=args.layers)
+    hybrid = bool(getattr(args, "hybrid", False))
+    if hybrid and world > 1:
+        raise SystemExit("--hybrid runs on one GPU")
+    cfg = m27b.model_config(max_ctx=args.prompt + args.gen + 8, tp_rank=rank, tp_size=world, n_layers=args.layers,
+                            **(m27b.HYBRID if hybrid else {}))
     e = m27b.Engine(cfg)
     try:
         if world > 1:
@@ -350,12 +356,22 @@ def decode_bench(args, world, rank, dev, dist, uuid):
         e.random_weights(seed=0, sigma=0.02)
         t_load = time.perf_counter() - t0
         prompt = np.random.default_rng(4).integers(0, cfg.vocab, args.prompt)
-        for pos in range(args.prompt - 1):
-            e.decode_step(int(prompt[pos]), pos)
+
+        def feed():
+            # the prompt, token by token (untimed); a hybrid model's DeltaNet
+            # state starts over, attention positions are simply rewritten
+            if hybrid:
+                e.reset()
+            for pos in range(args.prompt - 1):
+                e.decode_step(int(prompt[pos]), pos)
+
+        feed()
         start, p0 = int(prompt[-1]), args.prompt - 1
         st = torch.cuda.ExternalStream(e.stream(), device=dev)
         warm = max(3, min(args.warmup, 16))
         e.generate(start, p0, warm)  # warm-up (rewritten by the timed runs)
+        if hybrid:
+            feed()
 
         def timed(fn, sampler=None):
             torch.cuda.synchronize()
@@ -378,6 +394,8 @@ def decode_bench(args, world, rank, dev, dist, uuid):
             return ms, out, clk
 
         ms, gen, clocks = timed(lambda: e.generate(start, p0, args.gen), ClockSampler(uuid))
+        if hybrid:
+            feed()
 
         def host_loop():
             tok, out = start, []
@@ -389,7 +407,7 @@ def decode_bench(args, world, rank, dev, dist, uuid):
         ms_e2e, gen_e2e, _ = timed(host_loop)
         # speculative verification: one pass over n drafted tokens (tensor cores for the q4_K matrices)
         verify = {}
-        if world == 1 or args.comm == "nccl":
+        if (world == 1 or args.comm == "nccl") and not hybrid:
             vt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.vocab, 16)]
             for n in (8, 16):
                 e.verify(vt[:n], p0)  # capture
@@ -397,7 +415,8 @@ def decode_bench(args, world, rank, dev, dist, uuid):
                 vms, _, _ = timed(lambda: [e.verify(vt[:n], p0) for _ in range(reps)])
                 verify[str(n)] = {"ms_per_pass": round(vms / reps, 4), "tokens_per_s": round(n * reps / (vms / 1e3), 1)}
         wb = e.weight_bytes_per_token()
-        kv_bytes = 2 * args.layers * (p0 + 1 + args.gen / 2) * e_kv_heads(cfg) * cfg.head_dim * 4
+        n_attn = sum((l + 1) % 4 == 0 for l in range(args.layers)) if hybrid else args.layers
+        kv_bytes = 2 * n_attn * (p0 + 1 + args.gen / 2) * e_kv_heads(cfg) * cfg.head_dim * 4
         tps = args.gen / (ms / 1e3)
         peak, peak_kind = measured_peak()
         per_rank_gbs = wb * tps / 1e9
@@ -409,6 +428,8 @@ def decode_bench(args, world, rank, dev, dist, uuid):
             "roofline_frac": round(per_rank_gbs / peak, 4), "peak_gbs": peak, "peak_kind": peak_kind,
             "tokens_match": list(map(int, gen)) == list(map(int, gen_e2e)),
             "verify": verify,
+            "hybrid": (dict(m27b.HYBRID, deltanet_layers=sum((l + 1) % 4 != 0 for l in range(args.layers)))
+                       if hybrid else None),
             "layers": args.layers, "prompt": args.prompt, "gen": args.gen, "weights_init_s": round(t_load, 1),
             "allreduce": "none" if world == 1 else ("fused NVLink push (P2P stores + release flags)" if args.comm == "p2p"
                                                    else "NCCL all-reduce"),

@@ -14,6 +14,22 @@
  * attn_q_norm, attn_k_norm, post_attention_norm, ffn_gate, ffn_up,
  * ffn_down}.weight.
  *
+ * Hybrid models (attn_interval > 0, the reference's Qwen3.5/3.6 layout:
+ * layer il is attention iff (il + 1) % attn_interval == 0) run the other
+ * layers as the reference's Gated DeltaNet block (:2484-2548): RMSNorm ->
+ * qkv (conv channels) and z projections -> beta / alpha projections ->
+ * causal conv + SiLU with a per-layer conv state -> L2-normalised q / k ->
+ * gated delta rule with a per-layer 128 x 128 state per value head ->
+ * RMSNorm * ssm_norm * silu(z) -> ssm_out + residual -> the FFN.  Their
+ * tensors: blk.N.{attn_qkv | attn_q | ssm_in}.weight (qkv),
+ * blk.N.{attn_gate | attn_k | ssm_in_gate}.weight (z), ssm_beta.weight,
+ * ssm_alpha.weight (f16 / f32 or quantized, same type), ssm_conv1d.weight
+ * (f32 / f16, conv_kern values per channel), ssm_dt.bias | ssm_dt_bias,
+ * ssm_a | ssm_a_log (f32, the negative decay rates), ssm_norm.weight (f32,
+ * 128), ssm_out.weight, plus attn_norm, post_attention_norm and the FFN.
+ * Hybrid models run on one GPU (tp_size 1) and without the verify pass
+ * (rolling the recurrent state back after a rejected draft is not built).
+ *
  * Tensor parallelism over tp_size GPUs (one process per GPU): q/gate by
  * heads, k/v by the kv heads the local q heads use (replicated when
  * tp_size > n_kv_head), gate/up by 256-value blocks of the FFN dimension,
@@ -55,6 +71,14 @@ typedef struct M27BModelConfig {
     uint32_t weight_type; /* m27b_engine_random_weights: 0 = the q4_k_m mix
                              (q4_K, q6_K for ffn_down and output), 8 = q8_0
                              everywhere (a draft model) */
+    int attn_interval;    /* 0: every layer is attention; k > 0: layer il is
+                             attention iff (il + 1) % k == 0, the others
+                             Gated DeltaNet (4 in the reference model) */
+    int ssm_d_inner;      /* value channels, ssm_dt_rank x 128 (6144) */
+    int ssm_d_state;      /* key head width, 128 */
+    int ssm_dt_rank;      /* value heads, even (48) */
+    int ssm_n_group;      /* q / k groups; value head j uses group j % n (16) */
+    int ssm_conv_kern;    /* causal conv width, 2..8 (4) */
 } M27BModelConfig;
 
 typedef struct M27BEngine M27BEngine;

@@ -48,6 +48,14 @@ struct BestExchange {
 __global__ void k_advance_p2p(unsigned long long *best, int *ctl, int *hist, int cap, BestExchange b);
 bool qmv_push(const WeightView *w, const void *xq, const float *residual, const PushArgs &push, cudaStream_t stream,
               char *err, size_t cap);
+// Gated DeltaNet block (ssm.cu)
+cudaError_t ssm_rmsnorm_launch(const float *x, const float *w, float eps, int n, float *y, cudaStream_t st);
+cudaError_t ssm_conv_launch(const float *x, const float *w, float *cstate, float *out, const float *ba,
+                            const float *dt_bias, const float *ssm_a, float *bg, int conv_ch, int K, int ng, int dr,
+                            float eps, cudaStream_t st);
+cudaError_t ssm_delta_launch(const float *xc, const float *bg, const float *z, const float *ssm_norm, float *S,
+                             void *xq, int ng, int dr, float eps, cudaStream_t st);
+__global__ void k_fill_f32_rand(float *out, long n, uint64_t seed, float scale, float offset);
 }  // namespace m27b
 
 using namespace m27b;
@@ -80,8 +88,25 @@ bool efail(char *err, size_t cap, const char *fmt, ...) {
         if (!(call)) return false;  \
     } while (0)
 
+// IEEE binary16 bits -> float (host; exact).
+float half_bits_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, ex = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+    uint32_t bits;
+    if (ex == 0x1f) bits = sign | 0x7f800000u | (man << 13);
+    else if (ex != 0) bits = sign | ((ex + 112u) << 23) | (man << 13);
+    else {
+        const float v = (float)man * 5.9604644775390625e-08f;  // subnormal: man * 2^-24
+        return sign ? -v : v;
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
 size_t block_bytes(uint32_t t) {
     switch (t) {
+    case M27B_TYPE_F32: return 4;
+    case M27B_TYPE_F16: return 2;
     case M27B_TYPE_Q4_K: return 144;
     case M27B_TYPE_Q5_K: return 176;
     case M27B_TYPE_Q6_K: return 210;
@@ -90,9 +115,18 @@ size_t block_bytes(uint32_t t) {
     default: return 0;
     }
 }
-int block_elems(uint32_t t) { return t == M27B_TYPE_Q8_0 ? 32 : 256; }
-// q4_K, q5_K and IQ4_XS rows are read in their GGUF layout; q6_K and q8_0 are repacked.
-bool raw_layout(uint32_t t) { return t == M27B_TYPE_Q4_K || t == M27B_TYPE_Q5_K || t == M27B_TYPE_IQ4_XS; }
+int block_elems(uint32_t t) {
+    return t == M27B_TYPE_Q8_0 ? 32 : (t == M27B_TYPE_F16 || t == M27B_TYPE_F32) ? 1 : 256;
+}
+// q4_K, q5_K, IQ4_XS, f16 and f32 rows are read in their GGUF layout; q6_K and q8_0 are repacked.
+bool raw_layout(uint32_t t) {
+    return t == M27B_TYPE_Q4_K || t == M27B_TYPE_Q5_K || t == M27B_TYPE_IQ4_XS || t == M27B_TYPE_F16 ||
+           t == M27B_TYPE_F32;
+}
+// layer il of a hybrid model is attention iff (il + 1) % attn_interval == 0 (reference :2372)
+bool is_attention_layer(const M27BModelConfig &c, int il) {
+    return c.attn_interval <= 0 || (il + 1) % c.attn_interval == 0;
+}
 
 size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
@@ -134,9 +168,15 @@ struct QMat {
 };
 
 struct Layer {
+    bool ssm = false;  // a Gated DeltaNet layer of a hybrid model
     QMat wqkv, wo, wg, wu, wd;
     float *attn_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
     float *kc = nullptr, *vc = nullptr;
+    // DeltaNet: projections, conv weights [conv_ch][K] (fp32), per-head
+    // parameters, conv state [conv_ch][K - 1] and delta-rule state [dr][128][128]
+    QMat wqs, wz, wba, wso;
+    float *conv_w = nullptr, *dt_bias = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;
+    float *cstate = nullptr, *S = nullptr;
 };
 
 }  // namespace
@@ -155,6 +195,9 @@ struct M27BEngine {
     float *out_norm = nullptr;
     float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *q = nullptr, *gate = nullptr, *o = nullptr, *a = nullptr;
     float *part = nullptr, *logits = nullptr;
+    // DeltaNet buffers: normed input, projections, conv output, beta|g
+    float *hn = nullptr, *sx = nullptr, *sxc = nullptr, *sz = nullptr, *sba = nullptr, *sbg = nullptr;
+    int conv_ch = 0, n_ssm = 0;
     float2 *rope = nullptr;  // (cos, sin) of the step's position, n_rot/2 pairs
     int *vtok = nullptr;                 // device: the tokens of a verify pass
     int *h_vtok = nullptr;               // pinned copy
@@ -353,6 +396,24 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
                                      e->st, err, err_cap));
     for (int l = 0; l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
+        if (Ly.ssm) {
+            // Gated DeltaNet block (single GPU): norm, four projections, conv + q/k norm,
+            // delta rule + gated norm + q8_K, ssm_out + residual, then the FFN
+            const int dr = c.ssm_dt_rank;
+            ECUDA(ssm_rmsnorm_launch(e->h, Ly.attn_norm, c.rms_eps, c.hidden, e->hn, e->st));
+            ECALL(m27b_qmv_f32(&Ly.wqs.v, e->hn, c.hidden, 1, e->xq, e->sx, e->conv_ch, nullptr, e->st, err, err_cap));
+            ECALL(m27b_qmv_f32(&Ly.wz.v, e->hn, c.hidden, 1, e->xq, e->sz, c.ssm_d_inner, nullptr, e->st, err, err_cap));
+            ECALL(m27b_qmv_f32(&Ly.wba.v, e->hn, c.hidden, 1, e->xq, e->sba, 2 * dr, nullptr, e->st, err, err_cap));
+            ECUDA(ssm_conv_launch(e->sx, Ly.conv_w, Ly.cstate, e->sxc, e->sba, Ly.dt_bias, Ly.ssm_a, e->sbg, e->conv_ch,
+                                  c.ssm_conv_kern, c.ssm_n_group, dr, c.rms_eps, e->st));
+            ECUDA(ssm_delta_launch(e->sxc, e->sbg, e->sz, Ly.ssm_norm, Ly.S, e->xq, c.ssm_n_group, dr, c.rms_eps, e->st));
+            ECALL(mv(e, Ly.wso, e->xq, e->h2, e->h, err, err_cap));
+            ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
+                                       nullptr, e->st, err, err_cap));
+            ECALL(m27b_act_quant(e->a, e->F, 1, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
+            ECALL(mv(e, Ly.wd, e->xq, e->h, e->h2, err, err_cap));
+            continue;
+        }
         if (p2p)
             ECALL(mv(e, Ly.wqkv, e->xq, e->qkv, nullptr, err, err_cap));
         else
@@ -466,10 +527,53 @@ bool set_ctl(M27BEngine *e, int token, int pos, char *err, size_t err_cap) {
 // once before the capture (module loading and first-use set-up then happen
 // outside it); the caller sets the control words again afterwards.  Re-running
 // a step at one position rewrites the same KV-cache entries.
+// Bytes of every DeltaNet layer's conv and delta-rule state.
+size_t ssm_state_bytes(const M27BEngine *e, size_t *conv_b, size_t *delta_b) {
+    const M27BModelConfig &c = e->c;
+    *conv_b = (size_t)e->conv_ch * (c.ssm_conv_kern - 1) * 4;
+    *delta_b = (size_t)c.ssm_dt_rank * 128 * 128 * 4;
+    return (size_t)e->n_ssm * (*conv_b + *delta_b);
+}
+
+// Copy the DeltaNet states into buf (restore = false) or back from it.
+bool ssm_state_copy(M27BEngine *e, uint8_t *buf, bool restore, char *err, size_t err_cap) {
+    size_t cb, db, off = 0;
+    ssm_state_bytes(e, &cb, &db);
+    for (Layer &Ly : e->L) {
+        if (!Ly.ssm) continue;
+        ECUDA(cudaMemcpyAsync(restore ? (void *)Ly.cstate : buf + off, restore ? buf + off : (void *)Ly.cstate, cb,
+                              cudaMemcpyDeviceToDevice, e->st));
+        off += cb;
+        ECUDA(cudaMemcpyAsync(restore ? (void *)Ly.S : buf + off, restore ? buf + off : (void *)Ly.S, db,
+                              cudaMemcpyDeviceToDevice, e->st));
+        off += db;
+    }
+    return true;
+}
+
 bool ensure_graph(M27BEngine *e, char *err, size_t err_cap) {
     if (e->gexec) return true;
-    ECALL(enqueue_step(e, err, err_cap));
-    ECUDA(cudaStreamSynchronize(e->st));
+    // the eager run advances the DeltaNet states (attention only rewrites one
+    // KV-cache entry): keep a copy and put it back before the capture
+    uint8_t *bk = nullptr;
+    size_t cb, db;
+    if (e->n_ssm) {
+        ECUDA(cudaMalloc(&bk, ssm_state_bytes(e, &cb, &db)));
+        if (!ssm_state_copy(e, bk, false, err, err_cap)) {
+            cudaFree(bk);
+            return false;
+        }
+    }
+    const bool eager = enqueue_step(e, err, err_cap);
+    const cudaError_t se = cudaStreamSynchronize(e->st);
+    if (bk) {
+        const bool back = eager && se == cudaSuccess && ssm_state_copy(e, bk, true, err, err_cap) &&
+                          cudaStreamSynchronize(e->st) == cudaSuccess;
+        cudaFree(bk);
+        if (eager && se == cudaSuccess && !back) return efail(err, err_cap, "restoring the DeltaNet states failed");
+    }
+    if (!eager) return false;
+    ECUDA(se);
     ECUDA(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
     const bool ok = enqueue_step(e, err, err_cap);
     cudaGraph_t g = nullptr;
@@ -490,10 +594,14 @@ bool check_ready(M27BEngine *e, int pos, int n, char *err, size_t err_cap) {
     if (pos < 0 || n < 1 || pos + n > c.max_ctx)
         return efail(err, err_cap, "positions %d..%d outside the cache (max_ctx %d)", pos, pos + n - 1, c.max_ctx);
     if (c.tp_size > 1 && !e->comm) return efail(err, err_cap, "m27b_engine_set_nccl was not called");
-    for (const Layer &Ly : e->L)
-        if (!Ly.wqkv.d || !Ly.wo.d || !Ly.wg.d || !Ly.wu.d || !Ly.wd.d || !Ly.attn_norm || !Ly.post_norm || !Ly.q_norm ||
-            !Ly.k_norm)
+    for (const Layer &Ly : e->L) {
+        if (!Ly.wg.d || !Ly.wu.d || !Ly.wd.d || !Ly.attn_norm || !Ly.post_norm)
             return efail(err, err_cap, "weights are not loaded");
+        if (Ly.ssm ? (!Ly.wqs.d || !Ly.wz.d || !Ly.wba.d || !Ly.wso.d || !Ly.conv_w || !Ly.dt_bias || !Ly.ssm_a ||
+                      !Ly.ssm_norm)
+                   : (!Ly.wqkv.d || !Ly.wo.d || !Ly.q_norm || !Ly.k_norm))
+            return efail(err, err_cap, "weights are not loaded");
+    }
     if (!e->embd.d || !e->lmh.d || !e->out_norm) return efail(err, err_cap, "weights are not loaded");
     return true;
 }
@@ -540,6 +648,15 @@ bool m27b_engine_partition(const M27BModelConfig *cfg, M27BPartition *out, char 
     if (((c.n_head / t) * c.head_dim) % 256) return efail(err, err_cap, "local heads x head_dim must be a multiple of 256");
     if (c.n_rot < 2 || c.n_rot > c.head_dim || c.n_rot % 2) return efail(err, err_cap, "bad n_rot");
     if (c.ffn / 256 < t || c.vocab < t || c.max_ctx < 1) return efail(err, err_cap, "shape too small for tp_size");
+    if (c.attn_interval < 0) return efail(err, err_cap, "attn_interval must be >= 0");
+    if (c.attn_interval > 0) {
+        if (t != 1) return efail(err, err_cap, "hybrid (Gated DeltaNet) models run with tp_size 1");
+        if (c.ssm_d_state != 128 || c.ssm_dt_rank < 2 || c.ssm_dt_rank % 2 || c.ssm_d_inner != c.ssm_dt_rank * 128)
+            return efail(err, err_cap,
+                         "DeltaNet shape: ssm_d_state must be 128, ssm_dt_rank even, ssm_d_inner = ssm_dt_rank x 128");
+        if (c.ssm_n_group < 1 || c.ssm_n_group > c.ssm_dt_rank || c.ssm_conv_kern < 2 || c.ssm_conv_kern > 8)
+            return efail(err, err_cap, "DeltaNet shape: 1 <= ssm_n_group <= ssm_dt_rank, 2 <= ssm_conv_kern <= 8");
+    }
     const int G = c.n_head / c.n_kv_head;
     M27BPartition p;
     p.n_q = c.n_head / t;
@@ -591,7 +708,12 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
     e->L.resize(c.n_layers);
     char e2[512];
     auto A = [&](void **p, size_t n) { return dalloc(e, p, n, e2, sizeof(e2)); };
-    const int xmax = std::max(std::max(c.hidden, e->F), e->H * hd);
+    int xmax = std::max(std::max(c.hidden, e->F), e->H * hd);
+    for (int l = 0; l < c.n_layers; ++l) e->L[l].ssm = !is_attention_layer(c, l);
+    e->n_ssm = 0;
+    for (const Layer &Ly : e->L) e->n_ssm += Ly.ssm ? 1 : 0;
+    e->conv_ch = c.attn_interval > 0 ? c.ssm_d_inner + 2 * c.ssm_n_group * c.ssm_d_state : 0;
+    if (e->n_ssm) xmax = std::max(xmax, c.ssm_d_inner);
     const size_t VM = M27B_VERIFY_MAX;  // activation buffers hold a whole verify pass
     bool ok = A((void **)&e->h, VM * c.hidden * 4) && A((void **)&e->h2, VM * c.hidden * 4) &&
               A((void **)&e->qkv, VM * (e->H * 2 + e->KV * 2) * hd * 4) && A((void **)&e->q, VM * e->H * hd * 4) &&
@@ -601,10 +723,21 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
               A((void **)&e->best, VM * 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4) &&
               A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2)) && A((void **)&e->vtok, VM * 4);
     for (int l = 0; ok && l < c.n_layers; ++l) {
+        Layer &Ly = e->L[l];
+        if (Ly.ssm) {
+            const size_t cs = (size_t)e->conv_ch * (c.ssm_conv_kern - 1) * 4, ss = (size_t)c.ssm_dt_rank * 128 * 128 * 4;
+            ok = A((void **)&Ly.cstate, cs) && A((void **)&Ly.S, ss) && cudaMemset(Ly.cstate, 0, cs) == cudaSuccess &&
+                 cudaMemset(Ly.S, 0, ss) == cudaSuccess;
+            continue;
+        }
         const size_t kvb = (size_t)c.max_ctx * e->KV * hd * 4;
-        ok = A((void **)&e->L[l].kc, kvb) && A((void **)&e->L[l].vc, kvb) &&
-             cudaMemset(e->L[l].kc, 0, kvb) == cudaSuccess && cudaMemset(e->L[l].vc, 0, kvb) == cudaSuccess;
+        ok = A((void **)&Ly.kc, kvb) && A((void **)&Ly.vc, kvb) && cudaMemset(Ly.kc, 0, kvb) == cudaSuccess &&
+             cudaMemset(Ly.vc, 0, kvb) == cudaSuccess;
     }
+    if (ok && e->n_ssm)
+        ok = A((void **)&e->hn, (size_t)c.hidden * 4) && A((void **)&e->sx, (size_t)e->conv_ch * 4) &&
+             A((void **)&e->sxc, (size_t)e->conv_ch * 4) && A((void **)&e->sz, (size_t)c.ssm_d_inner * 4) &&
+             A((void **)&e->sba, (size_t)2 * c.ssm_dt_rank * 4) && A((void **)&e->sbg, (size_t)2 * c.ssm_dt_rank * 4);
     ok = ok && cudaMemset(e->ctl, 0, 16) == cudaSuccess;
     if (!ok) return bail(efail(err, err_cap, "%s", e2));
     if (cudaMallocHost((void **)&e->h_ctl, 16) != cudaSuccess || cudaMallocHost((void **)&e->h_best, 8) != cudaSuccess ||
@@ -712,6 +845,51 @@ bool m27b_engine_load_tensor(M27BEngine *e, const char *name, uint32_t type, uin
         if (!is_f32(c.hidden)) return efail(err, err_cap, "%s must be f32[%d]", name, c.hidden);
         return load_f32(e, what[0] == 'a' ? &Ly.attn_norm : &Ly.post_norm, host, c.hidden, err, err_cap);
     }
+    if (Ly.ssm && what.compare(0, 4, "ffn_") != 0) {
+        // Gated DeltaNet tensors, under the reference loader's names (:1775-1825)
+        const int dr = c.ssm_dt_rank, K = c.ssm_conv_kern;
+        auto mat = [&](QMat &m, int rows, int k, int row_at) -> bool {
+            ECALL(ensure_mat(e, m, type, rows, k, err, err_cap));
+            return load_slice(e, m, hb, row_elems / be, 0, (int)row_count, 0, row_at, err, err_cap);
+        };
+        if (what == "attn_qkv.weight" || what == "attn_q.weight" || what == "ssm_in.weight") {
+            if (row_count != (uint32_t)e->conv_ch || row_elems != (uint32_t)c.hidden) return efail(err, err_cap, "%s shape", name);
+            return mat(Ly.wqs, e->conv_ch, c.hidden, 0);
+        }
+        if (what == "attn_gate.weight" || what == "attn_k.weight" || what == "ssm_in_gate.weight") {
+            if (row_count != (uint32_t)c.ssm_d_inner || row_elems != (uint32_t)c.hidden) return efail(err, err_cap, "%s shape", name);
+            return mat(Ly.wz, c.ssm_d_inner, c.hidden, 0);
+        }
+        if (what == "ssm_beta.weight" || what == "ssm_alpha.weight") {
+            if (row_count != (uint32_t)dr || row_elems != (uint32_t)c.hidden) return efail(err, err_cap, "%s shape", name);
+            ECALL(ensure_mat(e, Ly.wba, type, 2 * dr, c.hidden, err, err_cap));  // rows: beta | alpha
+            return load_slice(e, Ly.wba, hb, row_elems / be, 0, dr, 0, what[4] == 'b' ? 0 : dr, err, err_cap);
+        }
+        if (what == "ssm_out.weight") {
+            if (row_count != (uint32_t)c.hidden || row_elems != (uint32_t)c.ssm_d_inner) return efail(err, err_cap, "%s shape", name);
+            if (act_type_of(type) != M27B_TYPE_Q8_K || type == M27B_TYPE_F16 || type == M27B_TYPE_F32)
+                return efail(err, err_cap, "%s must be a 256-value k-quant (q4_K, q5_K, q6_K, IQ4_XS)", name);
+            return mat(Ly.wso, c.hidden, c.ssm_d_inner, 0);
+        }
+        if (what == "ssm_conv1d.weight") {
+            if (row_elems != (uint32_t)K || row_count != (uint32_t)e->conv_ch ||
+                (type != M27B_TYPE_F32 && type != M27B_TYPE_F16))
+                return efail(err, err_cap, "%s must be f32 / f16 [%d x %d]", name, e->conv_ch, K);
+            std::vector<float> w((size_t)K * e->conv_ch);
+            for (size_t i = 0; i < w.size(); ++i)
+                w[i] = type == M27B_TYPE_F32 ? ((const float *)host)[i] : half_bits_to_float(((const uint16_t *)host)[i]);
+            return load_f32(e, &Ly.conv_w, w.data(), w.size(), err, err_cap);
+        }
+        if (what == "ssm_dt.bias" || what == "ssm_dt_bias" || what == "ssm_a" || what == "ssm_a_log") {
+            if (!is_f32(dr)) return efail(err, err_cap, "%s must be f32[%d]", name, dr);
+            return load_f32(e, what.compare(0, 6, "ssm_dt") == 0 ? &Ly.dt_bias : &Ly.ssm_a, host, dr, err, err_cap);
+        }
+        if (what == "ssm_norm.weight") {
+            if (!is_f32(128)) return efail(err, err_cap, "%s must be f32[128]", name);
+            return load_f32(e, &Ly.ssm_norm, host, 128, err, err_cap);
+        }
+        return efail(err, err_cap, "unknown tensor %s for a DeltaNet layer", name);
+    }
     if (what == "attn_q_norm.weight" || what == "attn_k_norm.weight") {
         if (!is_f32(hd)) return efail(err, err_cap, "%s must be f32[%d]", name, hd);
         return load_f32(e, what[5] == 'q' ? &Ly.q_norm : &Ly.k_norm, host, hd, err, err_cap);
@@ -802,13 +980,45 @@ bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char 
     for (int l = 0; l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
         const int tid = 16 * l;
-        ECALL(ensure_mat(e, Ly.wqkv, Q4, qkv_rows, c.hidden, err, err_cap));
-        ECALL(fill_slice(e, Ly.wqkv, tid + 1, seed, sigma, (long)e->q_lo * 2 * hd, e->H * 2 * hd, 0, 0, err, err_cap));
-        ECALL(fill_slice(e, Ly.wqkv, tid + 2, seed, sigma, (long)e->kv_lo * hd, e->KV * hd, 0, e->H * 2 * hd, err, err_cap));
-        ECALL(fill_slice(e, Ly.wqkv, tid + 3, seed, sigma, (long)e->kv_lo * hd, e->KV * hd, 0,
-                         e->H * 2 * hd + e->KV * hd, err, err_cap));
-        ECALL(ensure_mat(e, Ly.wo, Q4, c.hidden, e->H * hd, err, err_cap));
-        ECALL(fill_slice(e, Ly.wo, tid + 4, seed, sigma, 0, c.hidden, e->q_lo * hd / block_elems(Q4), 0, err, err_cap));
+        if (Ly.ssm) {
+            // DeltaNet: projections in the matrix mix (beta / alpha as one q4_K matrix), random conv
+            // taps, dt_bias 0, ssm_a -1 (decay e^-softplus(a)), unit norms
+            const int dr = c.ssm_dt_rank;
+            ECALL(ensure_mat(e, Ly.wqs, Q4, e->conv_ch, c.hidden, err, err_cap));
+            ECALL(fill_slice(e, Ly.wqs, tid + 8, seed, sigma, 0, e->conv_ch, 0, 0, err, err_cap));
+            ECALL(ensure_mat(e, Ly.wz, Q4, c.ssm_d_inner, c.hidden, err, err_cap));
+            ECALL(fill_slice(e, Ly.wz, tid + 9, seed, sigma, 0, c.ssm_d_inner, 0, 0, err, err_cap));
+            ECALL(ensure_mat(e, Ly.wba, Q4, 2 * dr, c.hidden, err, err_cap));
+            ECALL(fill_slice(e, Ly.wba, tid + 10, seed, sigma, 0, 2 * dr, 0, 0, err, err_cap));
+            ECALL(ensure_mat(e, Ly.wso, Q4, c.hidden, c.ssm_d_inner, err, err_cap));
+            ECALL(fill_slice(e, Ly.wso, tid + 11, seed, sigma, 0, c.hidden, 0, 0, err, err_cap));
+            const size_t ncw = (size_t)e->conv_ch * c.ssm_conv_kern;
+            if (!Ly.conv_w) ECALL(dalloc(e, (void **)&Ly.conv_w, ncw * 4, err, err_cap));
+            k_fill_f32_rand<<<64, 256, 0, e->st>>>(Ly.conv_w, (long)ncw, seed * 131 + (uint64_t)tid, 0.5f, 0.0f);
+            ECUDA(cudaGetLastError());
+            auto fill = [&](float **p, size_t n, float v) -> bool {
+                if (!*p) ECALL(dalloc(e, (void **)p, n * 4, err, err_cap));
+                k_fill_f32<<<64, 256, 0, e->st>>>(*p, (long)n, v);
+                ECUDA(cudaGetLastError());
+                return true;
+            };
+            ECALL(fill(&Ly.dt_bias, dr, 0.0f));
+            ECALL(fill(&Ly.ssm_a, dr, -1.0f));
+            ECALL(fill(&Ly.ssm_norm, 128, 1.0f));
+        } else {
+            ECALL(ensure_mat(e, Ly.wqkv, Q4, qkv_rows, c.hidden, err, err_cap));
+            ECALL(fill_slice(e, Ly.wqkv, tid + 1, seed, sigma, (long)e->q_lo * 2 * hd, e->H * 2 * hd, 0, 0, err,
+                             err_cap));
+            ECALL(fill_slice(e, Ly.wqkv, tid + 2, seed, sigma, (long)e->kv_lo * hd, e->KV * hd, 0, e->H * 2 * hd, err,
+                             err_cap));
+            ECALL(fill_slice(e, Ly.wqkv, tid + 3, seed, sigma, (long)e->kv_lo * hd, e->KV * hd, 0,
+                             e->H * 2 * hd + e->KV * hd, err, err_cap));
+            ECALL(ensure_mat(e, Ly.wo, Q4, c.hidden, e->H * hd, err, err_cap));
+            ECALL(fill_slice(e, Ly.wo, tid + 4, seed, sigma, 0, c.hidden, e->q_lo * hd / block_elems(Q4), 0, err,
+                             err_cap));
+            ECALL(ones(&Ly.q_norm, hd));
+            ECALL(ones(&Ly.k_norm, hd));
+        }
         ECALL(ensure_mat(e, Ly.wg, Q4, e->F, c.hidden, err, err_cap));
         ECALL(fill_slice(e, Ly.wg, tid + 5, seed, sigma, e->f_lo, e->F, 0, 0, err, err_cap));
         ECALL(ensure_mat(e, Ly.wu, Q4, e->F, c.hidden, err, err_cap));
@@ -817,8 +1027,6 @@ bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char 
         ECALL(fill_slice(e, Ly.wd, tid + 7, seed, sigma, 0, c.hidden, e->f_lo / block_elems(Q6), 0, err, err_cap));
         ECALL(ones(&Ly.attn_norm, c.hidden));
         ECALL(ones(&Ly.post_norm, c.hidden));
-        ECALL(ones(&Ly.q_norm, hd));
-        ECALL(ones(&Ly.k_norm, hd));
     }
     ECUDA(cudaStreamSynchronize(e->st));
     if (err && err_cap) err[0] = '\0';
@@ -828,14 +1036,26 @@ bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char 
 size_t m27b_engine_weight_bytes_per_token(const M27BEngine *e) {
     if (!e) return 0;
     size_t n = e->lmh.gguf_bytes + (e->embd.rows ? e->embd.gguf_bytes / e->embd.rows : 0);
-    for (const Layer &Ly : e->L) n += Ly.wqkv.gguf_bytes + Ly.wo.gguf_bytes + Ly.wg.gguf_bytes + Ly.wu.gguf_bytes + Ly.wd.gguf_bytes;
+    for (const Layer &Ly : e->L)
+        n += Ly.wqkv.gguf_bytes + Ly.wo.gguf_bytes + Ly.wg.gguf_bytes + Ly.wu.gguf_bytes + Ly.wd.gguf_bytes +
+             Ly.wqs.gguf_bytes + Ly.wz.gguf_bytes + Ly.wba.gguf_bytes + Ly.wso.gguf_bytes;
     return n;
 }
 
 bool m27b_engine_reset(M27BEngine *e, char *err, size_t err_cap) {
     if (!e) return efail(err, err_cap, "null engine");
+    // attention: positions index the cache, a new sequence simply starts at pos 0;
+    // DeltaNet: the recurrent states start from zero
+    size_t cb, db;
+    ssm_state_bytes(e, &cb, &db);
+    for (Layer &Ly : e->L) {
+        if (!Ly.ssm) continue;
+        ECUDA(cudaMemsetAsync(Ly.cstate, 0, cb, e->st));
+        ECUDA(cudaMemsetAsync(Ly.S, 0, db, e->st));
+    }
+    ECUDA(cudaStreamSynchronize(e->st));
     if (err && err_cap) err[0] = '\0';
-    return true;  // positions index the cache; a new sequence simply starts at pos 0
+    return true;
 }
 
 bool m27b_engine_decode_step(M27BEngine *e, int token, int pos, int *next, float *logits, char *err, size_t err_cap) {
@@ -881,6 +1101,10 @@ bool m27b_engine_verify(M27BEngine *e, const int *tokens, int n, int pos, int *n
     if (!e || !tokens || !next) return efail(err, err_cap, "m27b_engine_verify: null argument");
     if (n < 1 || n > M27B_VERIFY_MAX) return efail(err, err_cap, "m27b_engine_verify: n must be in [1, %d]", M27B_VERIFY_MAX);
     if (e->p2p) return efail(err, err_cap, "m27b_engine_verify: not with the fused NVLink all-reduce");
+    if (e->n_ssm)
+        return efail(err, err_cap,
+                     "m27b_engine_verify: not for hybrid models (the DeltaNet state cannot be rolled back after a "
+                     "rejected draft)");
     if (logits && e->c.tp_size != 1) return efail(err, err_cap, "logits are only returned with tp_size 1");
     for (int i = 0; i < n; ++i)
         if (tokens[i] < 0 || tokens[i] >= e->c.vocab)

@@ -550,7 +550,8 @@ template <class BT, int NT, int EPI>
 M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUtensorMap *tm1, int split) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
     constexpr int ITEM = blk_item(BT::BYTES);
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t kblk_smem[];
+    uint8_t *smem = kblk_smem;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int slot = lane >> 2, qd = lane & 3;
     const int nwarps = blockDim.x >> 5;

@@ -22,15 +22,21 @@
 //
 // Pipeline per CTA (one 128-row tile at a time, persistent over tiles, one
 // CTA per SM), warp-specialized and synchronised only by mbarriers:
-//   * warp 8 issues: TMA copies of one raw 128-row x 144-byte block column per
-//     stage (2-D tensor map, no multicast), and, per half-block (4
-//     sub-blocks), the 4 MMAs plus a commit;
-//   * warps 0-7 unpack a half-block into one of two TMEM A buffers, and run
-//     the epilogue of the previous block (tcgen05.ld of its 8 accumulators,
-//     one row per thread, eight tokens per thread);
+//   * warp 13 streams the weights: one TMA copy of a raw 128-row x 144-byte
+//     block column per stage (2-D tensor map, no multicast), refilling a
+//     stage once every reader has handed it back;
+//   * warp 12 issues, per half-block (4 sub-blocks), the 4 MMAs plus a
+//     commit (and one more commit per block) — nothing else, since one
+//     thread's issue rate bounds the whole pipeline;
+//   * warps 0-3 unpack: thread r (TMEM lane r) writes row r's half-block
+//     into one of two TMEM A buffers;
+//   * warps 4-11 run the epilogue, concurrently with the unpacking of the
+//     next block: two warps per TMEM lane quarter, each for half of the
+//     tokens (tcgen05.ld of the block's 8 accumulators, one row per thread);
 //   * hand-offs: stage full (TMA) -> stage empty (the unpacking warps have
-//     read it), A buffer full -> MMAs done (the buffer is free again and the
-//     block's accumulators are final), accumulators free (epilogue read).
+//     read the nibbles and the epilogue warps the block header), A buffer
+//     full -> half-block MMAs done (the buffer is free again), block MMAs
+//     done (its accumulators are final) -> accumulators free (epilogue read).
 // The activations (all K, all tokens) are staged once per CTA in the
 // canonical K-major no-swizzle UMMA layout, with their scales and bsum
 // pairs.  Every wait is bounded (2 s); a timeout records status 5 and raises
@@ -43,8 +49,11 @@
 namespace m27b {
 
 constexpr int MMA_ROWS = 128;
-constexpr int MMA_WORKERS = 256;                 // warps 0-7: unpack + epilogue
-constexpr int MMA_THREADS = MMA_WORKERS + 32;    // warp 8: TMA + MMA issue
+constexpr int MMA_UNPACK_WARPS = 4;              // warps 0-3: A unpack, one row per thread
+constexpr int MMA_EPI_WARPS = 8;                 // warps 4-11: epilogue, two per lane quarter
+constexpr int MMA_ISSUER = MMA_UNPACK_WARPS + MMA_EPI_WARPS;  // warp 12: MMA issue
+constexpr int MMA_PRODUCER = MMA_ISSUER + 1;                    // warp 13: TMA weight copies
+constexpr int MMA_THREADS = (MMA_PRODUCER + 1) * 32;
 constexpr int MMA_RAW_BYTES = MMA_ROWS * 144;    // one TMA box: 128 rows x one q4_K block
 constexpr int MMA_TMEM_COLS = 512;               // D: 2 blocks x 8 sub-blocks x 16; A: 2 x 32
 constexpr int MMA_ACOL = 256;                    // first TMEM column of the A buffers
@@ -75,8 +84,8 @@ __host__ __device__ inline MmaLayout mma_layout(int rb, int nb_tok, int stages) 
     off = (off + 127) & ~(size_t)127;
     L.raw = off;
     off += (size_t)stages * MMA_RAW_BYTES;
-    L.bar = off;  // full[stages], empty[stages], a_full[NA], mma_done[NA], d_free[2], drain
-    off += (size_t)(2 * stages + 2 * MMA_NA + 3) * 8;
+    L.bar = off;  // full[stages], empty[stages], a_full[NA], mma_done[NA], blk_done[2], d_free[2], drain
+    off += (size_t)(2 * stages + 2 * MMA_NA + 5) * 8;
     L.flag = off;  // abort flag, TMEM address slot
     off += 16;
     L.total = off;
@@ -121,6 +130,13 @@ M27B_DI void umma_commit(uint64_t *bar) {
 M27B_DI void tmem_ld8(uint32_t taddr, int (&v)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+// Four consecutive 32-bit TMEM columns of this thread's lane.
+M27B_DI void tmem_ld4(uint32_t taddr, int (&v)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                  : "r"(taddr)
                  : "memory");
 }
@@ -180,11 +196,9 @@ M27B_DI bool warp_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *ab
 template <int NB>
 __global__ void __launch_bounds__(MMA_THREADS, 1)
     k_qmv_q4k_mma(const QmvArgs a, const __grid_constant__ CUtensorMap tm, int n_tok, int stages) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t mma_smem[];
+    uint8_t *smem = mma_smem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool issuer_warp = warp == 8;
-    const int r = tid & (MMA_ROWS - 1);  // workers: row of the tile (TMEM lane)
-    const int h = (tid >> 7) & 1;        // workers: which half of the row's work
     const int rb = a.rb;
     const MmaLayout L = mma_layout(rb, NB, stages);
     uint8_t *bsm = smem + L.b;
@@ -194,8 +208,9 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     uint64_t *full = (uint64_t *)(smem + L.bar);
     uint64_t *empty = full + stages;
     uint64_t *a_full = empty + stages;      // [MMA_NA]
-    uint64_t *mma_done = a_full + MMA_NA;   // [MMA_NA]
-    uint64_t *d_free = mma_done + MMA_NA;   // [2]
+    uint64_t *mma_done = a_full + MMA_NA;   // [MMA_NA]: one half-block's MMAs
+    uint64_t *blk_done = mma_done + MMA_NA; // [2]: all MMAs of a block (accumulator buffer bi & 1)
+    uint64_t *d_free = blk_done + 2;        // [2]
     uint64_t *drain = d_free + 2;
     volatile int *abort = (volatile int *)(smem + L.flag);
     uint32_t *tslot = (uint32_t *)(smem + L.flag + 8);
@@ -208,14 +223,16 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     if (tid == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 8);
+            mbar_init(&empty[s], MMA_UNPACK_WARPS + MMA_EPI_WARPS);
         }
         for (int b = 0; b < MMA_NA; ++b) {
-            mbar_init(&a_full[b], 8);
+            mbar_init(&a_full[b], MMA_UNPACK_WARPS);
             mbar_init(&mma_done[b], 1);
         }
-        mbar_init(&d_free[0], 8);
-        mbar_init(&d_free[1], 8);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&blk_done[b], 1);
+            mbar_init(&d_free[b], MMA_EPI_WARPS);
+        }
         mbar_init(drain, 1);
         *abort = 0;
         fence_mbar_init();
@@ -228,17 +245,18 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
+    // the readers' generic loads of a stage are ordered before its refill by
+    // the empty barrier (arrive-release, wait-acquire) that the producer waits on
     auto issue_block = [&](int bi) {
         const int tl = bi / rb, k = bi - tl * rb;
         const int row0 = ((int)blockIdx.x + tl * (int)gridDim.x) * MMA_ROWS;
         uint64_t *b = &full[bi % stages];
-        fence_proxy_async();
         mbar_arrive_expect_tx(b, MMA_RAW_BYTES);
         tma_load_2d(raw + (size_t)(bi % stages) * MMA_RAW_BYTES, &tm, k * 36, row0, b);
     };
     // the first raw block columns go out at once: weights do not depend on the previous kernel
     int issued = 0;
-    if (issuer_warp && lane == 0)
+    if (warp == MMA_PRODUCER && lane == 0)
         for (; issued < stages && issued < nblk; ++issued) issue_block(issued);
 
     // activations: codes into the UMMA layout (tokens >= n_tok are zero),
@@ -281,7 +299,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     fence_proxy_async();  // the codes are read by the tensor cores (async proxy)
     __syncthreads();
 
-    if (issuer_warp) {
+    if (warp == MMA_ISSUER) {
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_i8<NB>();
             const uint32_t b_base = smem_u32(bsm);
@@ -300,63 +318,122 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
                                tmem + (uint32_t)(MMA_ACOL + ab * 32 + s * 8), bd, idesc, 0u);
                 }
                 umma_commit(&mma_done[ab]);
-                // the block's raw stage, once every worker warp has read it, takes block bi + stages
-                if (q == 1 && issued < nblk) {
-                    if (!wait_or_abort(&empty[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) break;
-                    issue_block(issued++);
-                }
+                if (q == 1) umma_commit(&blk_done[db]);  // the block's 8 accumulators are final
             }
-            // drain: every MMA issued above, and every copy still in flight (bounded, even after an abort)
+            // drain: every MMA issued above (bounded, even after an abort)
             umma_commit(drain);
             mbar_wait_bounded(drain, 0u, a.status, 5);
+        }
+        __syncwarp();
+    } else if (warp == MMA_PRODUCER) {
+        if (lane == 0) {
+            // block bi goes into the stage block bi - stages used, once every
+            // unpacking and epilogue warp has handed that one back
+            for (; issued < nblk; ++issued) {
+                const int bi = issued;
+                if (!wait_or_abort(&empty[bi % stages], (uint32_t)((bi / stages - 1) & 1), abort, a.status)) break;
+                issue_block(bi);
+            }
+            // every copy still in flight lands before the CTA's shared memory is released (bounded)
             for (int bi = issued - stages < 0 ? 0 : issued - stages; bi < issued; ++bi)
                 mbar_wait_bounded(&full[bi % stages], (uint32_t)((bi / stages) & 1), a.status, 5);
         }
         __syncwarp();
+    } else if (warp < MMA_UNPACK_WARPS) {
+        // A operand: thread r = TMEM lane r = row r of the tile
+        const int r = tid;
+        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+        for (int j = 0; j < J; ++j) {
+            const int bi = j >> 1, q = j & 1, ab = j % MMA_NA;
+            if (q == 0 && !warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status))
+                break;
+            // A buffer ab is free once the MMAs of half-block j - MMA_NA are done
+            if (j >= MMA_NA &&
+                !warp_wait_or_abort(&mma_done[ab], (uint32_t)(((j - MMA_NA) / MMA_NA) & 1), abort, a.status))
+                break;
+            tc_fence_after();
+            const uint8_t *rw = raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144;
+            const uint32_t acol = tmem + lane_base + (uint32_t)(MMA_ACOL + ab * 32);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                // qs group g = 2q + h: low nibbles are sub-block 2g, high 2g+1,
+                // i.e. sub-blocks 2h and 2h + 1 of the half-block
+                const int g = 2 * q + h;
+                const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
+                tmem_st8(acol + 16 * h, qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu,
+                         qa.w & 0x0f0f0f0fu, qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu,
+                         qb.w & 0x0f0f0f0fu);
+                tmem_st8(acol + 16 * h + 8, (qa.x >> 4) & 0x0f0f0f0fu, (qa.y >> 4) & 0x0f0f0f0fu,
+                         (qa.z >> 4) & 0x0f0f0f0fu, (qa.w >> 4) & 0x0f0f0f0fu, (qb.x >> 4) & 0x0f0f0f0fu,
+                         (qb.y >> 4) & 0x0f0f0f0fu, (qb.z >> 4) & 0x0f0f0f0fu, (qb.w >> 4) & 0x0f0f0f0fu);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&a_full[ab]);
+                if (q == 1) mbar_arrive(&empty[bi % stages]);  // this warp is done with the raw stage
+            }
+        }
     } else {
-        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-        const bool epi_thread = NB == 16 || h == 0;
-        const int toff = NB == 16 ? 8 * h : 0;
-        float acc[8];
+        // epilogue: warp 4 + 4 * th + quarter; thread lane of that quarter = row r;
+        // tokens [th * NB / 2, (th + 1) * NB / 2)
+        constexpr int TPT = NB / 2;  // tokens per thread
+        const int e = warp - MMA_UNPACK_WARPS, quarter = e & 3, th = e >> 2;
+        const int r = 32 * quarter + lane;
+        const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+        const int toff = th * TPT;
+        float acc[TPT];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-        // scales of the block being unpacked and of the previous one (its epilogue)
-        float cur_d = 0.0f, cur_dm = 0.0f, prev_d = 0.0f, prev_dm = 0.0f;
-        uint32_t sc03 = 0, sc47 = 0, cur_m03 = 0, cur_m47 = 0;
-        uint32_t psc03 = 0, psc47 = 0, prev_m03 = 0, prev_m47 = 0;
-
-        auto epilogue = [&](int bi) {
+        for (int i = 0; i < TPT; ++i) acc[i] = 0.0f;
+        for (int bi = 0; bi < nblk; ++bi) {
             const int tl = bi / rb, k = bi - tl * rb;
-            if (epi_thread) {
-                int v[8][8];
-                const uint32_t dcol = tmem + lane_base + (uint32_t)((bi & 1) * 128 + toff);
+            // the block header of row r (scales, mins), read before the stage is handed back
+            if (!warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) break;
+            const uint4 hd = *(const uint4 *)(raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[bi % stages]);
+            const float dw = h2f(hd.x), dmw = h2f(hd.x >> 16);
+            const uint32_t sc03 = hd.y & 0x3f3f3f3fu, mn03 = hd.z & 0x3f3f3f3fu;
+            const uint32_t sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
+            const uint32_t mn47 = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
+            // the block's MMAs (both half-blocks)
+            if (!warp_wait_or_abort(&blk_done[bi & 1], (uint32_t)((bi >> 1) & 1), abort, a.status)) break;
+            tc_fence_after();
+            int v[8][TPT];
+            const uint32_t dcol = tmem + lane_base + (uint32_t)((bi & 1) * 128 + toff);
 #pragma unroll
-                for (int s = 0; s < 8; ++s) tmem_ld8(dcol + (uint32_t)(s * 16), v[s]);
-                tmem_wait_ld();
+            for (int s = 0; s < 8; ++s) {
+                if constexpr (TPT == 8) tmem_ld8(dcol + (uint32_t)(s * 16), v[s]);
+                else tmem_ld4(dcol + (uint32_t)(s * 16), v[s]);
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d_free[bi & 1]);  // the accumulators are in registers
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    int isum = 0;
+            for (int i = 0; i < TPT; ++i) {
+                int isum = 0;
 #pragma unroll
-                    for (int s = 0; s < 8; ++s) {
-                        const int sc = (int)(((s < 4 ? psc03 : psc47) >> (8 * (s & 3))) & 0xffu);
-                        isum += sc * v[s][i];
-                    }
-                    const int t = toff + i;
-                    const int4 bs = bss[t * rb + k];
-                    int msum = __dp2a_lo(bs.x, (int)prev_m03, 0);
-                    msum = __dp2a_hi(bs.y, (int)prev_m03, msum);
-                    msum = __dp2a_lo(bs.z, (int)prev_m47, msum);
-                    msum = __dp2a_hi(bs.w, (int)prev_m47, msum);
-                    const float dx = dxs[t * rb + k];
-                    acc[i] = fmaf(prev_d * dx, (float)isum, acc[i]);
-                    acc[i] = fmaf(-(prev_dm * dx), (float)msum, acc[i]);
+                for (int s = 0; s < 8; ++s) {
+                    const int sc = (int)(((s < 4 ? sc03 : sc47) >> (8 * (s & 3))) & 0xffu);
+                    isum += sc * v[s][i];
                 }
+                const int t = toff + i;
+                const int4 bs = bss[t * rb + k];
+                int msum = __dp2a_lo(bs.x, (int)mn03, 0);
+                msum = __dp2a_hi(bs.y, (int)mn03, msum);
+                msum = __dp2a_lo(bs.z, (int)mn47, msum);
+                msum = __dp2a_hi(bs.w, (int)mn47, msum);
+                const float dx = dxs[t * rb + k];
+                acc[i] = fmaf(dw * dx, (float)isum, acc[i]);
+                acc[i] = fmaf(-(dmw * dx), (float)msum, acc[i]);
             }
             if (k == rb - 1) {  // the tile's last block: write its rows
                 const int row = ((int)blockIdx.x + tl * (int)gridDim.x) * MMA_ROWS + r;
-                if (epi_thread && row < a.rows) {
+                if (row < a.rows) {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < TPT; ++i) {
                         const int t = toff + i;
                         if (t < n_tok) {
                             const size_t o = (size_t)t * a.ldy + row;
@@ -365,85 +442,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
                     }
                 }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-            }
-        };
-        auto shift_scales = [&]() {
-            prev_d = cur_d;
-            prev_dm = cur_dm;
-            prev_m03 = cur_m03;
-            prev_m47 = cur_m47;
-            psc03 = sc03;
-            psc47 = sc47;
-        };
-
-        bool ok = true;
-        for (int j = 0; j < J; ++j) {
-            const int bi = j >> 1, q = j & 1, ab = j % MMA_NA;
-            if (q == 0 && !warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) {
-                ok = false;
-                break;
-            }
-            // A buffer ab is free once the MMAs of half-block j - MMA_NA are done.
-            // This is also the only wait on those MMAs before the epilogue of
-            // block bi - 1 (at q == 1 it covers that block's last half-block):
-            // waiting again after this warp's a_full arrival below could find
-            // half-block j's MMAs already complete, one phase past the awaited
-            // one, and the parity test would then wait for the phase after.
-            if (j >= MMA_NA &&
-                !warp_wait_or_abort(&mma_done[ab], (uint32_t)(((j - MMA_NA) / MMA_NA) & 1), abort, a.status)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint8_t *rw = raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144;
-            if (q == 0) {
-                const uint4 hd = *(const uint4 *)rw;
-                shift_scales();
-                cur_d = h2f(hd.x);
-                cur_dm = h2f(hd.x >> 16);
-                sc03 = hd.y & 0x3f3f3f3fu;
-                cur_m03 = hd.z & 0x3f3f3f3fu;
-                sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
-                cur_m47 = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
-            }
-            {
-                // qs group g = 2q + h of row r: low nibbles are sub-block 2g, high 2g+1,
-                // i.e. sub-blocks 2h and 2h + 1 of the half-block
-                const int g = 2 * q + h;
-                const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
-                const uint32_t acol = tmem + lane_base + (uint32_t)(MMA_ACOL + ab * 32 + 2 * h * 8);
-                tmem_st8(acol, qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu, qa.w & 0x0f0f0f0fu,
-                         qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu, qb.w & 0x0f0f0f0fu);
-                tmem_st8(acol + 8, (qa.x >> 4) & 0x0f0f0f0fu, (qa.y >> 4) & 0x0f0f0f0fu, (qa.z >> 4) & 0x0f0f0f0fu,
-                         (qa.w >> 4) & 0x0f0f0f0fu, (qb.x >> 4) & 0x0f0f0f0fu, (qb.y >> 4) & 0x0f0f0f0fu,
-                         (qb.z >> 4) & 0x0f0f0f0fu, (qb.w >> 4) & 0x0f0f0f0fu);
-                tmem_wait_st();
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&a_full[ab]);
-                if (q == 1) mbar_arrive(&empty[bi % stages]);  // this warp is done with the raw stage
-            }
-            if (q == 1 && bi >= 1) {
-                // block bi - 1: both half-blocks' MMAs were awaited above (j - 3 at
-                // q == 0, j - 2 at this q == 1), before this warp's arrival
-                epilogue(bi - 1);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&d_free[(bi - 1) & 1]);
-            }
-        }
-        if (ok && nblk > 0) {
-            // the last block: its two half-blocks' MMAs, then its epilogue
-            const bool done =
-                warp_wait_or_abort(&mma_done[(J - 2) % MMA_NA], (uint32_t)(((J - 2) / MMA_NA) & 1), abort, a.status) &&
-                warp_wait_or_abort(&mma_done[(J - 1) % MMA_NA], (uint32_t)(((J - 1) / MMA_NA) & 1), abort, a.status);
-            if (done) {
-                shift_scales();
-                tc_fence_after();
-                epilogue(nblk - 1);
+                for (int i = 0; i < TPT; ++i) acc[i] = 0.0f;
             }
         }
     }

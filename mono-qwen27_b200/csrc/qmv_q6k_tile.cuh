@@ -87,7 +87,8 @@ __global__ void __launch_bounds__(Q6T_WARPS * 32, 2)
     k_qmv_q6k_tile(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
                    int split) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t q6t_smem[];
+    uint8_t *smem = q6t_smem;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int qd = lane >> 3, c = lane & 7;
     const int half = c >> 2, rr = (c >> 1) & 1, lsub = c & 1;

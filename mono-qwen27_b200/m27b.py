@@ -290,7 +290,9 @@ class ModelConfig(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("ffn", ctypes.c_int), ("n_head", ctypes.c_int),
                 ("n_kv_head", ctypes.c_int), ("head_dim", ctypes.c_int), ("vocab", ctypes.c_int), ("n_rot", ctypes.c_int),
                 ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float), ("max_ctx", ctypes.c_int),
-                ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int), ("weight_type", ctypes.c_uint32)]
+                ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int), ("weight_type", ctypes.c_uint32),
+                ("attn_interval", ctypes.c_int), ("ssm_d_inner", ctypes.c_int), ("ssm_d_state", ctypes.c_int),
+                ("ssm_dt_rank", ctypes.c_int), ("ssm_n_group", ctypes.c_int), ("ssm_conv_kern", ctypes.c_int)]
 
 
 class Partition(ctypes.Structure):
@@ -300,6 +302,8 @@ class Partition(ctypes.Structure):
 
 QWEN27 = dict(n_layers=64, hidden=5120, ffn=17408, n_head=24, n_kv_head=4, head_dim=256, vocab=248320, n_rot=64,
               rope_theta=1e7, rms_eps=1e-6)
+# the reference's hybrid layout (include/mono27b_config.h:43-50; every 4th layer attention)
+HYBRID = dict(attn_interval=4, ssm_d_inner=6144, ssm_d_state=128, ssm_dt_rank=48, ssm_n_group=16, ssm_conv_kern=4)
 
 
 def model_config(max_ctx=1024, tp_rank=0, tp_size=1, **kw):
@@ -398,6 +402,10 @@ class Engine:
         self._call("m27b_engine_decode_step", self.h, int(token), int(pos), ctypes.byref(nxt),
                    ctypes.c_void_p(lg.ctypes.data) if logits else None)
         return (nxt.value, lg) if logits else nxt.value
+
+    def reset(self):
+        """Start a new sequence: the DeltaNet states return to zero (attention needs nothing)."""
+        self._call("m27b_engine_reset", self.h)
 
     def generate(self, token, pos, n):
         """Greedy tokens of steps pos..pos+n-1 (step i consumes step i-1's token), all on the device."""

@@ -18,6 +18,22 @@ the FFN, :2577-2593 for the head):
           x2 = q8_K(RMSNorm(h2) * post_attention_norm)
   logits = output . q8_K(RMSNorm(h) * output_norm); next = first argmax
 
+Hybrid models (attn_interval > 0: layer il is attention iff (il + 1) %
+attn_interval == 0, reference src/mono27b_executor.cu:2372) run every other
+layer as the Gated DeltaNet block of :2484-2548 (single GPU):
+
+  x    = RMSNorm(h) * attn_norm
+  c    = attn_qkv . x  (conv channels: q [ng][dk] | k [ng][dk] | v [dr][dv])
+  z    = attn_gate . x ;  b, a = ssm_beta . x, ssm_alpha . x   (f16 weights: fp32 x)
+  beta = sigmoid(b) ;  g = softplus(a + dt_bias) * ssm_a          (:816-826)
+  c    = silu(causal conv over the last conv_kern inputs)         (:1488-1501)
+  q, k = L2-normalised per group (sum of squares in fp64)         (:1118-1133)
+  per value head j (group j % ng), state S_j [dv][dk]:            (:1526-1603)
+    kv = S_j k ;  d = (v_j - e^g kv) * beta ;  S_j = e^g S_j + d k^T
+    o_j = (S_j q) / sqrt(dk)
+  y    = RMSNorm_j(o_j) * ssm_norm * silu(z_j)                   (:735-765)
+  h2   = ssm_out . q8_K(y) + h, then the FFN as above
+
 `RefDecoder(model, cfg, part)` computes the slice one tensor-parallel rank
 holds: its query heads and the kv heads they use, its FFN rows, and its
 vocabulary rows; o_proj / down then give partial sums that an `allreduce`
@@ -33,6 +49,20 @@ BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), 8: (32, 34), 13: (256, 176), 23: (2
 
 TINY = dict(n_layers=2, hidden=512, ffn=1024, n_head=4, n_kv_head=2, head_dim=128, vocab=1000, n_rot=64,
             rope_theta=1e7, rms_eps=1e-6)
+
+
+F16 = 1
+
+
+def is_attention(c, il):
+    k = c.get("attn_interval", 0)
+    return k == 0 or (il + 1) % k == 0
+
+
+def ssm_dims(c):
+    ng, dk, dr = c["ssm_n_group"], c["ssm_d_state"], c["ssm_dt_rank"]
+    dv = c["ssm_d_inner"] // dr
+    return ng, dk, dr, dv, c["ssm_d_inner"] + 2 * ng * dk, c["ssm_conv_kern"]
 
 
 def make_model(orc, c, seed=0, sigma=0.02, norm_jitter=0.1, qtype=None, types=None):
@@ -62,15 +92,31 @@ def make_model(orc, c, seed=0, sigma=0.02, norm_jitter=0.1, qtype=None, types=No
         p = f"blk.{l}."
         norm(p + "attn_norm.weight", c["hidden"])
         norm(p + "post_attention_norm.weight", c["hidden"])
+        q(p + "ffn_gate.weight", Q4_K, c["ffn"], c["hidden"])
+        q(p + "ffn_up.weight", Q4_K, c["ffn"], c["hidden"])
+        q(p + "ffn_down.weight", Q6_K, c["hidden"], c["ffn"])
+        if not is_attention(c, l):
+            ng, dk, dr, dv, cc, K = ssm_dims(c)
+            q(p + "attn_qkv.weight", Q4_K, cc, c["hidden"])
+            q(p + "attn_gate.weight", Q4_K, c["ssm_d_inner"], c["hidden"])
+            q(p + "ssm_beta.weight", F16, dr, c["hidden"])
+            q(p + "ssm_alpha.weight", F16, dr, c["hidden"])
+            cw = (0.3 * rng.standard_normal((cc, K))).astype(np.float32)
+            if types.get("ssm_conv1d") == F16:
+                t[p + "ssm_conv1d.weight"] = (F16, K, cc, cw.astype(np.float16))
+            else:
+                t[p + "ssm_conv1d.weight"] = (F32, K, cc, cw)
+            t[p + "ssm_dt.bias"] = (F32, dr, 1, (0.5 * rng.standard_normal(dr)).astype(np.float32))
+            t[p + "ssm_a"] = (F32, dr, 1, (-np.exp(0.5 * rng.standard_normal(dr))).astype(np.float32))
+            norm(p + "ssm_norm.weight", dv)
+            q(p + "ssm_out.weight", Q4_K, c["hidden"], c["ssm_d_inner"])
+            continue
         norm(p + "attn_q_norm.weight", hd)
         norm(p + "attn_k_norm.weight", hd)
         q(p + "attn_q.weight", Q4_K, H * 2 * hd, c["hidden"])
         q(p + "attn_k.weight", Q4_K, KV * hd, c["hidden"])
         q(p + "attn_v.weight", Q4_K, KV * hd, c["hidden"])
         q(p + "attn_output.weight", Q4_K, c["hidden"], H * hd)
-        q(p + "ffn_gate.weight", Q4_K, c["ffn"], c["hidden"])
-        q(p + "ffn_up.weight", Q4_K, c["ffn"], c["hidden"])
-        q(p + "ffn_down.weight", Q6_K, c["hidden"], c["ffn"])
     return t
 
 
@@ -119,7 +165,19 @@ class RefDecoder:
         for l in range(c["n_layers"]):
             g = lambda n: model[f"blk.{l}.{n}.weight"][3]
             tq = lambda n: model[f"blk.{l}.{n}.weight"][0]
-            self.layers.append(dict(
+            if not is_attention(c, l):
+                assert self.rank == 0 and p == full_partition(c), "hybrid layers: single GPU"
+                ng, dk, dr, dv, cc, K = ssm_dims(c)
+                self.layers.append(dict(
+                    ssm=True, attn_norm=g("attn_norm"), post_norm=g("post_attention_norm"),
+                    t_qkv=tq("attn_qkv"), w_qkv=g("attn_qkv"), t_gate=tq("attn_gate"), w_gate=g("attn_gate"),
+                    t_beta=tq("ssm_beta"), w_beta=g("ssm_beta"), t_alpha=tq("ssm_alpha"), w_alpha=g("ssm_alpha"),
+                    conv_w=g("ssm_conv1d").astype(np.float32), dt_bias=model[f"blk.{l}.ssm_dt.bias"][3],
+                    ssm_a=model[f"blk.{l}.ssm_a"][3], ssm_norm=g("ssm_norm"), t_out=tq("ssm_out"), w_out=g("ssm_out"),
+                    tg=tq("ffn_gate"), td=tq("ffn_down"), wg=g("ffn_gate"), wu=g("ffn_up"), wd=g("ffn_down"),
+                    conv=np.zeros((cc, K - 1), np.float32), S=np.zeros((dr, dv, dk), np.float32)))
+                continue
+            self.layers.append(dict(ssm=False, 
                 tqkv=tq("attn_q"), to=tq("attn_output"), tg=tq("ffn_gate"), td=tq("ffn_down"),
                 attn_norm=g("attn_norm"), post_norm=g("post_attention_norm"), q_norm=g("attn_q_norm"),
                 k_norm=g("attn_k_norm"),
@@ -136,6 +194,61 @@ class RefDecoder:
     def _mv(self, qtype, w, k, x):
         return self.orc.matvec(qtype, w, k, self.orc.quantize_act(qtype, x[None]))[0]
 
+    def _ffn(self, Ly, h2, p, r0):
+        """RMSNorm -> gate/up SwiGLU -> down (+ residual on rank 0), summed over ranks."""
+        D, eps = self.c["hidden"], self.c["rms_eps"]
+        x2 = rms_scaled(h2, Ly["post_norm"], eps)
+        g = self._mv(Ly["tg"], Ly["wg"], D, x2)
+        u = self._mv(Ly["tg"], Ly["wu"], D, x2)
+        a = self.orc.silu_mul(g, u)
+        h = self._mv(Ly["td"], Ly["wd"], p["n_f"], a)
+        if r0:
+            h = h + h2
+        return self.allreduce(h)
+
+    def _ssm(self, Ly, h):
+        """The Gated DeltaNet block (reference src/mono27b_executor.cu:2484-2548): h -> h2."""
+        c = self.c
+        D, eps = c["hidden"], c["rms_eps"]
+        ng, dk, dr, dv, cc, K = ssm_dims(c)
+        f32 = np.float32
+        silu = lambda v: (v / (f32(1) + np.exp(-v))).astype(f32)
+        x = rms_scaled(h, Ly["attn_norm"], eps)
+        qkv = self._mv(Ly["t_qkv"], Ly["w_qkv"], D, x)
+        z = self._mv(Ly["t_gate"], Ly["w_gate"], D, x)
+        braw = self._mv(Ly["t_beta"], Ly["w_beta"], D, x)
+        araw = self._mv(Ly["t_alpha"], Ly["w_alpha"], D, x)
+        beta = (f32(1) / (f32(1) + np.exp(-braw))).astype(f32)
+        zz = (araw + Ly["dt_bias"]).astype(f32)
+        sp = np.where(zz > 20, zz, np.log(f32(1) + np.exp(np.minimum(zz, 20)))).astype(f32)
+        g = (sp * Ly["ssm_a"]).astype(f32)
+        # causal conv, state oldest first (:1488-1501)
+        st, w = Ly["conv"], Ly["conv_w"]
+        s = ((st * w[:, :K - 1]).sum(1) + qkv * w[:, K - 1]).astype(f32)
+        st[:, :-1] = st[:, 1:]
+        st[:, -1] = qkv
+        cv = silu(s)
+
+        def l2(a):
+            ss = (a.astype(np.float64) ** 2).sum(1).astype(f32)
+            return (a * (f32(1) / np.sqrt(np.maximum(ss, f32(eps) * f32(eps))))[:, None]).astype(f32)
+
+        q = l2(cv[:ng * dk].reshape(ng, dk))
+        k = l2(cv[ng * dk:2 * ng * dk].reshape(ng, dk))
+        v = cv[2 * ng * dk:].reshape(dr, dv)
+        o = np.empty((dr, dv), f32)
+        for j in range(dr):
+            gi = j % ng
+            S = Ly["S"][j]
+            gv = np.exp(g[j]).astype(f32)
+            kv = (S.astype(np.float64) @ k[gi].astype(np.float64)).astype(f32)
+            d = ((v[j] - gv * kv) * beta[j]).astype(f32)
+            S[:] = (gv * S + d[:, None] * k[gi][None, :]).astype(f32)
+            o[j] = (S.astype(np.float64) @ q[gi].astype(np.float64) / np.sqrt(dk)).astype(f32)
+        zs = silu(z)
+        y = np.concatenate([rms_scaled(o[j], Ly["ssm_norm"], eps) * zs[j * dv:(j + 1) * dv] for j in range(dr)])
+        return self._mv(Ly["t_out"], Ly["w_out"], c["ssm_d_inner"], y.astype(f32)) + h
+
     def step(self, token, pos):
         """Returns (local logits, hidden state before the output norm)."""
         orc, c, p = self.orc, self.c, self.p
@@ -143,6 +256,10 @@ class RefDecoder:
         r0 = self.rank == 0
         h = orc.dequantize(self.qt["token_embd.weight"], self.embd[token:token + 1], D)[0]
         for Ly in self.layers:
+            if Ly["ssm"]:
+                h2 = self._ssm(Ly, h)
+                h = self._ffn(Ly, h2, p, r0)
+                continue
             x = rms_scaled(h, Ly["attn_norm"], eps)
             qg = self._mv(Ly["tqkv"], Ly["wq"], D, x)
             kk = self._mv(Ly["tqkv"], Ly["wk"], D, x)
@@ -168,14 +285,7 @@ class RefDecoder:
             if r0:
                 h2 = h2 + h
             h2 = self.allreduce(h2)
-            x2 = rms_scaled(h2, Ly["post_norm"], eps)
-            g = self._mv(Ly["tg"], Ly["wg"], D, x2)
-            u = self._mv(Ly["tg"], Ly["wu"], D, x2)
-            a = orc.silu_mul(g, u)
-            h = self._mv(Ly["td"], Ly["wd"], p["n_f"], a)
-            if r0:
-                h = h + h2
-            h = self.allreduce(h)
+            h = self._ffn(Ly, h2, p, r0)
         self.hidden = h
         logits = self._mv(self.qt["output.weight"], self.lmh, D, rms_scaled(h, self.out_norm, eps))
         return logits, h

@@ -42,14 +42,31 @@ def test_partition_qwen_shapes(m27b):
     assert sorted({p.n_f // 256 for p in p8}) == [8, 9]
 
 
+HYB_OK = dict(attn_interval=4, ssm_d_inner=6144, ssm_d_state=128, ssm_dt_rank=48, ssm_n_group=16, ssm_conv_kern=4)
+
+
+def _hyb(**kw):
+    d = dict(HYB_OK)
+    d.update(kw)
+    return d
+
+
 @pytest.mark.parametrize("bad", [dict(tp_size=5), dict(tp_rank=2, tp_size=2), dict(hidden=5000), dict(head_dim=288),
                                  dict(n_head=24, n_kv_head=5), dict(n_head=36, n_kv_head=4), dict(n_rot=3),
-                                 dict(ffn=256, tp_size=2)])
+                                 dict(ffn=256, tp_size=2), dict(attn_interval=-1),
+                                 _hyb(tp_size=2), _hyb(ssm_d_state=64), _hyb(ssm_dt_rank=47, ssm_d_inner=47 * 128),
+                                 _hyb(ssm_d_inner=6000), _hyb(ssm_n_group=0), _hyb(ssm_conv_kern=1),
+                                 _hyb(ssm_conv_kern=9)])
 def test_partition_rejects(m27b, bad):
     kw = dict(tp_rank=0, tp_size=1)
     kw.update(bad)
     with pytest.raises(m27b.M27BError):
         m27b.partition(_cfg(m27b, **kw))
+
+
+def test_partition_accepts_the_hybrid_layout(m27b):
+    p = m27b.partition(_cfg(m27b, tp_rank=0, tp_size=1, **HYB_OK))
+    assert p.n_q == 24 and p.n_f == 17408 and p.n_v == 248320
 
 
 # Shape that exercises shared kv heads (4 q heads per kv head) and an uneven
