@@ -25,9 +25,9 @@
 //   * warp 13 streams the weights: one TMA copy of a raw 128-row x 144-byte
 //     block column per stage (2-D tensor map, no multicast), refilling a
 //     stage once every reader has handed it back;
-//   * warp 12 issues, per half-block (4 sub-blocks), the 4 MMAs plus a
-//     commit (and one more commit per block) — nothing else, since one
-//     thread's issue rate bounds the whole pipeline;
+//   * warps 12 and 14 issue the MMAs, one per half-block of every block
+//     (4 sub-blocks: 4 MMAs plus two commits) — nothing else, since the
+//     issuing threads' instruction rate bounds the whole pipeline;
 //   * warps 0-3 unpack: thread r (TMEM lane r) writes row r's half-block
 //     into one of two TMEM A buffers;
 //   * warps 4-11 run the epilogue, concurrently with the unpacking of the
@@ -51,13 +51,14 @@ namespace m27b {
 constexpr int MMA_ROWS = 128;
 constexpr int MMA_UNPACK_WARPS = 4;              // warps 0-3: A unpack, one row per thread
 constexpr int MMA_EPI_WARPS = 8;                 // warps 4-11: epilogue, two per lane quarter
-constexpr int MMA_ISSUER = MMA_UNPACK_WARPS + MMA_EPI_WARPS;  // warp 12: MMA issue
+constexpr int MMA_ISSUER = MMA_UNPACK_WARPS + MMA_EPI_WARPS;  // warp 12: MMAs of first half-blocks
 constexpr int MMA_PRODUCER = MMA_ISSUER + 1;                    // warp 13: TMA weight copies
-constexpr int MMA_THREADS = (MMA_PRODUCER + 1) * 32;
+constexpr int MMA_ISSUER2 = MMA_PRODUCER + 1;                   // warp 14: MMAs of second half-blocks
+constexpr int MMA_THREADS = (MMA_ISSUER2 + 1) * 32;
 constexpr int MMA_RAW_BYTES = MMA_ROWS * 144;    // one TMA box: 128 rows x one q4_K block
 constexpr int MMA_TMEM_COLS = 512;               // D: 2 blocks x 8 sub-blocks x 16; A: 2 x 32
 constexpr int MMA_ACOL = 256;                    // first TMEM column of the A buffers
-constexpr int MMA_NA = 2;                        // A buffers (half-blocks the unpacking may run ahead)
+constexpr int MMA_NA = 2;                        // A buffers: one per half-block position (= issuing warp)
 constexpr size_t MMA_SMEM_LIMIT = 227 * 1024;
 // Every CTA asks for more than half of an SM's shared memory, so no two CTAs
 // of this kernel (of one launch, or of two launches that programmatic
@@ -230,10 +231,10 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
             mbar_init(&mma_done[b], 1);
         }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&blk_done[b], 1);
+            mbar_init(&blk_done[b], 2);  // both issuing warps commit
             mbar_init(&d_free[b], MMA_EPI_WARPS);
         }
-        mbar_init(drain, 1);
+        mbar_init(drain, 2);
         *abort = 0;
         fence_mbar_init();
     }
@@ -299,26 +300,27 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     fence_proxy_async();  // the codes are read by the tensor cores (async proxy)
     __syncthreads();
 
-    if (warp == MMA_ISSUER) {
+    if (warp == MMA_ISSUER || warp == MMA_ISSUER2) {
         if (lane == 0) {
+            // half-block q of every block: A buffer q, sub-blocks 4q .. 4q+3
+            const int q = warp == MMA_ISSUER ? 0 : 1;
             constexpr uint32_t idesc = umma_idesc_i8<NB>();
             const uint32_t b_base = smem_u32(bsm);
-            for (int j = 0; j < J; ++j) {
-                const int bi = j >> 1, q = j & 1, ab = j % MMA_NA, db = bi & 1;
-                // a block's first MMAs overwrite accumulators whose epilogue (block bi - 2) is done
-                if (q == 0 && bi >= 2 && !wait_or_abort(&d_free[db], (uint32_t)(((bi - 2) >> 1) & 1), abort, a.status))
-                    break;
-                if (!wait_or_abort(&a_full[ab], (uint32_t)((j / MMA_NA) & 1), abort, a.status)) break;
+            for (int bi = 0; bi < nblk; ++bi) {
+                const int db = bi & 1;
+                // the block's MMAs overwrite accumulators whose epilogue (block bi - 2) is done
+                if (bi >= 2 && !wait_or_abort(&d_free[db], (uint32_t)(((bi - 2) >> 1) & 1), abort, a.status)) break;
+                if (!wait_or_abort(&a_full[q], (uint32_t)(bi & 1), abort, a.status)) break;
                 tc_fence_after();
                 const int k = bi % rb;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
                     const uint64_t bd = umma_desc(b_base + (uint32_t)((k * 8 + 4 * q + s) * NB * 32));
                     umma_i8_ts(tmem + (uint32_t)(db * 128 + (4 * q + s) * 16),
-                               tmem + (uint32_t)(MMA_ACOL + ab * 32 + s * 8), bd, idesc, 0u);
+                               tmem + (uint32_t)(MMA_ACOL + q * 32 + s * 8), bd, idesc, 0u);
                 }
-                umma_commit(&mma_done[ab]);
-                if (q == 1) umma_commit(&blk_done[db]);  // the block's 8 accumulators are final
+                umma_commit(&mma_done[q]);
+                umma_commit(&blk_done[db]);  // with the other warp's commit: the block's accumulators are final
             }
             // drain: every MMA issued above (bounded, even after an abort)
             umma_commit(drain);
