@@ -65,6 +65,18 @@ def ssm_dims(c):
     return ng, dk, dr, dv, c["ssm_d_inner"] + 2 * ng * dk, c["ssm_conv_kern"]
 
 
+def delta_rule(S, q, k, v, beta, g):
+    """One gated delta-rule step on a value head's state S [dv][dk] (fp32,
+    updated in place), reference src/mono27b_executor.cu:1559-1589:
+    kv = S k; d = (v - e^g kv) * beta; S = e^g S + d k^T; returns (S q) / sqrt(dk)."""
+    f32 = np.float32
+    gv = np.exp(f32(g)).astype(f32)
+    kv = (S.astype(np.float64) @ k.astype(np.float64)).astype(f32)
+    d = ((v - gv * kv) * f32(beta)).astype(f32)
+    S[:] = (gv * S + d[:, None] * k[None, :]).astype(f32)
+    return (S.astype(np.float64) @ q.astype(np.float64) / np.sqrt(S.shape[1])).astype(f32)
+
+
 def make_model(orc, c, seed=0, sigma=0.02, norm_jitter=0.1, qtype=None, types=None):
     """name -> (ggml_type, row_elems, row_count, array): GGUF-named tensors of
     N(0, sigma^2) weights quantized by the oracle (the q4_k_m mix, or every
@@ -238,13 +250,8 @@ class RefDecoder:
         v = cv[2 * ng * dk:].reshape(dr, dv)
         o = np.empty((dr, dv), f32)
         for j in range(dr):
-            gi = j % ng
-            S = Ly["S"][j]
-            gv = np.exp(g[j]).astype(f32)
-            kv = (S.astype(np.float64) @ k[gi].astype(np.float64)).astype(f32)
-            d = ((v[j] - gv * kv) * beta[j]).astype(f32)
-            S[:] = (gv * S + d[:, None] * k[gi][None, :]).astype(f32)
-            o[j] = (S.astype(np.float64) @ q[gi].astype(np.float64) / np.sqrt(dk)).astype(f32)
+            gi = j % ng  # value head j reads q/k group j % ng
+            o[j] = delta_rule(Ly["S"][j], q[gi], k[gi], v[j], beta[j], g[j])
         zs = silu(z)
         y = np.concatenate([rms_scaled(o[j], Ly["ssm_norm"], eps) * zs[j * dv:(j + 1) * dv] for j in range(dr)])
         return self._mv(Ly["t_out"], Ly["w_out"], c["ssm_d_inner"], y.astype(f32)) + h

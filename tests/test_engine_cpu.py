@@ -140,3 +140,29 @@ def test_tp_sharded_decode_gloo(orc, world, tmp_path):
         assert orc.rel_l2(got["hidden"][pos], h) <= 1e-5, pos
         assert got["best"][pos] == orc.argmax(lg)
         tok = TOKENS[pos + 1] if pos + 1 < len(TOKENS) else int(got["best"][pos])
+
+
+def test_delta_rule_reference_properties():
+    """The decode reference's gated delta rule (the DeltaNet recurrence the
+    GPU kernel is checked against) does what the rule defines: with beta = 1
+    and no decay, writing value v at unit key k makes S k = v and leaves
+    S unchanged on keys orthogonal to k; a decay e^g scales the old state."""
+    import numpy as np
+    import _decode_ref as R
+    rng = np.random.default_rng(0)
+    dk = dv = 8
+    S = rng.standard_normal((dv, dk)).astype(np.float32)
+    k = np.zeros(dk, np.float32)
+    k[3] = 1.0
+    other = np.zeros(dk, np.float32)
+    other[5] = 1.0
+    v = rng.standard_normal(dv).astype(np.float32)
+    before_other = S @ other
+    R.delta_rule(S, k, k, v, 1.0, 0.0)
+    assert np.allclose(S @ k, v, atol=1e-6)
+    assert np.allclose(S @ other, before_other, atol=1e-6)
+    # beta = 0: only the decay acts
+    S2 = rng.standard_normal((dv, dk)).astype(np.float32)
+    want = np.float32(np.exp(-0.5)) * S2
+    R.delta_rule(S2, k, k, v, 0.0, -0.5)
+    assert np.allclose(S2, want, atol=1e-6)
