@@ -8,6 +8,8 @@
  *                          (activations are quantized to ggml's q8_K / q8_0, not q8_1,
  *                          so that results follow ggml's CPU vec_dot semantics)
  *   m27b_act_quant_gated<- k_quant_q8_1_fused_gate              src/mono27b_executor.cu:109-138, :2460
+ *   m27b_act_quant_swiglu<- k_elem_swiglu + l_quant_q8_n         src/mono27b_executor.cu:833-838, :2022-2030
+ *                          (gate and up computed as separate matvecs, e.g. a verify batch)
  *   m27b_qmv            <- l_mv_q8_on / l_mv_quant_residual     src/mono27b_executor.cu:2054-2102
  *                          (k_q4k_mv_q8_dp4a :320-364, k_q6k_mv_q8_dp4a :630-645,
  *                          k_q80_mv_q8_dp4a :533-580, k_q5k_mv_q8 :499-531,
@@ -109,6 +111,12 @@ M27B_API bool m27b_act_quant(const float *x, int k, int n_tok, int ldx, uint32_t
  * that feeds o_proj. */
 M27B_API bool m27b_act_quant_gated(const float *x, const float *gate, int k, int n_tok, int ldx,
                           uint32_t act_type, void *xq, cudaStream_t stream, char *err, size_t err_cap);
+
+/* Quantize silu(gate[i]) * up[i] (the FFN activation that feeds ffn_down),
+ * n_tok rows of k values with row stride ldx in both inputs; the same fp32
+ * expression as the SwiGLU epilogue of m27b_qmv_swiglu. */
+M27B_API bool m27b_act_quant_swiglu(const float *gate, const float *up, int k, int n_tok, int ldx, uint32_t act_type,
+                                   void *xq, cudaStream_t stream, char *err, size_t err_cap);
 
 /* As m27b_act_quant, of RMSNorm(x) * w (w may be NULL for weight 1.0) with
  * the given eps; the norm is taken over each row of k values. */

@@ -14,7 +14,9 @@
 //
 // Modes: plain x; x * sigmoid(gate) (the gated attention output feeding
 // o_proj, reference :2452-2473); RMSNorm(x) * w (the norm that precedes every
-// projection, reference l_rms :2139-2141).  IEEE division and expf are used
+// projection, reference l_rms :2139-2141); silu(gate) * x (the FFN activation
+// feeding ffn_down when gate and up were computed as separate matvecs; the
+// same fp32 expression as the matvec SwiGLU epilogue).  IEEE division and expf are used
 // (no fast-math) so plain-mode output is bit-exact.
 #include "m27b_device.cuh"
 #include "m27b_launch.cuh"
@@ -45,6 +47,9 @@ M27B_DI float act_value(const ActArgs &a, const float *xr, const float *gr, int 
     if (MODE == ACT_GATED) {
         const float g = gr[i];
         v = v * (1.0f / (1.0f + expf(-g)));
+    } else if (MODE == ACT_SWIGLU) {
+        const float g = gr[i];
+        v = g / (1.0f + expf(-g)) * v;
     } else if (MODE == ACT_RMSNORM) {
         v = v * nscale;
         if (a.w) v = v * a.w[i];
@@ -235,6 +240,7 @@ cudaError_t launch_act_quant(int act_type, int mode, const ActArgs &a, int n_tok
     if (act_type == M27B_TYPE_Q8_K) {
         if (mode == ACT_PLAIN) return launch_pdl(k_act_quant_q8K<ACT_PLAIN>, grid, dim3(256), 0, st, a);
         if (mode == ACT_GATED) return launch_pdl(k_act_quant_q8K<ACT_GATED>, grid, dim3(256), 0, st, a);
+        if (mode == ACT_SWIGLU) return launch_pdl(k_act_quant_q8K<ACT_SWIGLU>, grid, dim3(256), 0, st, a);
         if (mode == ACT_RMSNORM_SUM) {
             if (n_tok != 1 || a.nsrc < 1 || a.nsrc > M27B_MAX_SRC || !a.words || !a.ss_words || !a.epoch_base ||
                 !a.x_out || nb > 256)
@@ -247,6 +253,7 @@ cudaError_t launch_act_quant(int act_type, int mode, const ActArgs &a, int n_tok
     if (mode == ACT_RMSNORM_SUM) return cudaErrorInvalidValue;
     if (mode == ACT_PLAIN) return launch_pdl(k_act_quant_q80<ACT_PLAIN>, grid, dim3(256), 0, st, a);
     if (mode == ACT_GATED) return launch_pdl(k_act_quant_q80<ACT_GATED>, grid, dim3(256), 0, st, a);
+    if (mode == ACT_SWIGLU) return launch_pdl(k_act_quant_q80<ACT_SWIGLU>, grid, dim3(256), 0, st, a);
     return launch_pdl(k_act_quant_q80<ACT_RMSNORM>, grid, dim3(256), 0, st, a);
 }
 

@@ -159,7 +159,7 @@ size_t act_bytes(uint32_t act_type, int k) {
 bool act_quant_common(int mode, const float *x, const float *gate, const float *w, float eps, int k, int n_tok, int ldx,
                       uint32_t act_type, void *xq, cudaStream_t stream, char *err, size_t cap, const char *what) {
     if (!x || !xq) return fail(err, cap, "%s: null pointer", what);
-    if (mode == ACT_GATED && !gate) return fail(err, cap, "%s: null gate", what);
+    if ((mode == ACT_GATED || mode == ACT_SWIGLU) && !gate) return fail(err, cap, "%s: null gate", what);
     if (n_tok < 1) return fail(err, cap, "%s: n_tok must be >= 1 (got %d)", what, n_tok);
     if (ldx < k) return fail(err, cap, "%s: ldx (%d) < k (%d)", what, ldx, k);
     if (act_bytes(act_type, k) == 0) return fail(err, cap, "%s: k=%d is not a multiple of the block size of type %u", what, k, act_type);
@@ -329,6 +329,13 @@ bool m27b_act_quant(const float *x, int k, int n_tok, int ldx, uint32_t act_type
                     size_t err_cap) {
     return act_quant_common(ACT_PLAIN, x, nullptr, nullptr, 0.0f, k, n_tok, ldx, act_type, xq, stream, err, err_cap,
                             "m27b_act_quant");
+}
+
+bool m27b_act_quant_swiglu(const float *gate, const float *up, int k, int n_tok, int ldx, uint32_t act_type, void *xq,
+                           cudaStream_t stream, char *err, size_t err_cap) {
+    if (!gate) return fail(err, err_cap, "m27b_act_quant_swiglu: null gate");
+    return act_quant_common(ACT_SWIGLU, up, gate, nullptr, 0.0f, k, n_tok, ldx, act_type, xq, stream, err, err_cap,
+                            "m27b_act_quant_swiglu");
 }
 
 bool m27b_act_quant_gated(const float *x, const float *gate, int k, int n_tok, int ldx, uint32_t act_type, void *xq,

@@ -194,6 +194,7 @@ struct M27BEngine {
     QMat embd, lmh;
     float *out_norm = nullptr;
     float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *q = nullptr, *gate = nullptr, *o = nullptr, *a = nullptr;
+    float *a2 = nullptr;  // verify pass: the up projection next to the gate one in `a`
     float *part = nullptr, *logits = nullptr;
     // DeltaNet buffers: normed input, projections, conv output, beta|g
     float *hn = nullptr, *sx = nullptr, *sxc = nullptr, *sz = nullptr, *sba = nullptr, *sbg = nullptr;
@@ -501,9 +502,19 @@ bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
                                    err_cap));
         ECALL(m27b_qmv(&Ly.wo.v, e->xq, n, e->h2, D, r0 ? e->h : nullptr, e->st, err, err_cap));
         if (c.tp_size > 1) ENCCL(ncclAllReduce(e->h2, e->h2, (size_t)n * D, ncclFloat32, ncclSum, e->comm, e->st));
-        ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, D, Ly.post_norm, c.rms_eps, n, e->xq, e->a, e->F, nullptr,
-                                   e->st, err, err_cap));
-        ECALL(m27b_act_quant(e->a, e->F, n, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
+        if (n >= 5 && Ly.wg.type == M27B_TYPE_Q4_K) {
+            // 5+ tokens: gate and up on the tensor cores, then silu(gate) * up -> q8 for down
+            ECALL(m27b_act_quant_rmsnorm(e->h2, Ly.post_norm, c.rms_eps, D, n, D, M27B_TYPE_Q8_K, e->xq, e->st, err,
+                                         err_cap));
+            ECALL(m27b_qmv(&Ly.wg.v, e->xq, n, e->a, e->F, nullptr, e->st, err, err_cap));
+            ECALL(m27b_qmv(&Ly.wu.v, e->xq, n, e->a2, e->F, nullptr, e->st, err, err_cap));
+            ECALL(m27b_act_quant_swiglu(e->a, e->a2, e->F, n, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err,
+                                        err_cap));
+        } else {
+            ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, D, Ly.post_norm, c.rms_eps, n, e->xq, e->a, e->F,
+                                       nullptr, e->st, err, err_cap));
+            ECALL(m27b_act_quant(e->a, e->F, n, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
+        }
         ECALL(m27b_qmv(&Ly.wd.v, e->xq, n, e->h, D, r0 ? e->h2 : nullptr, e->st, err, err_cap));
         if (c.tp_size > 1) ENCCL(ncclAllReduce(e->h, e->h, (size_t)n * D, ncclFloat32, ncclSum, e->comm, e->st));
     }
@@ -718,7 +729,8 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
     bool ok = A((void **)&e->h, VM * c.hidden * 4) && A((void **)&e->h2, VM * c.hidden * 4) &&
               A((void **)&e->qkv, VM * (e->H * 2 + e->KV * 2) * hd * 4) && A((void **)&e->q, VM * e->H * hd * 4) &&
               A((void **)&e->gate, VM * e->H * hd * 4) && A((void **)&e->o, VM * e->H * hd * 4) &&
-              A((void **)&e->a, VM * e->F * 4) && A((void **)&e->part, VM * e->S * e->H * (hd + 4) * 4) &&
+              A((void **)&e->a, VM * e->F * 4) && A((void **)&e->a2, VM * e->F * 4) &&
+              A((void **)&e->part, VM * e->S * e->H * (hd + 4) * 4) &&
               A((void **)&e->logits, VM * e->V * 4) && A((void **)&e->xq, VM * m27b_act_bytes(M27B_TYPE_Q8_K, xmax)) &&
               A((void **)&e->best, VM * 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4) &&
               A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2)) && A((void **)&e->vtok, VM * 4);

@@ -24,11 +24,11 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-enum ActMode { ACT_PLAIN = 0, ACT_GATED = 1, ACT_RMSNORM = 2, ACT_RMSNORM_SUM = 3 };
+enum ActMode { ACT_PLAIN = 0, ACT_GATED = 1, ACT_RMSNORM = 2, ACT_RMSNORM_SUM = 3, ACT_SWIGLU = 4 };
 
 struct ActArgs {
     const float *x;
-    const float *gate;  // ACT_GATED
+    const float *gate;  // ACT_GATED, ACT_SWIGLU (the gate projection)
     const float *w;     // ACT_RMSNORM / ACT_RMSNORM_SUM (may be null: weight 1.0)
     float eps;
     int k;

@@ -50,8 +50,10 @@ cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     } else {
         // few row groups: the warps of a CTA split each group's passes
         split = P < nw ? P : nw;
-        const long gpc = (groups + slots - 1) / slots;
-        grid = (groups + gpc - 1) / gpc;
+        // one CTA per resident slot; CTA c takes groups c, c + grid, ...: the
+        // two CTAs an SM holds then carry (nearly) the same number of groups,
+        // and the SMs differ by at most one group
+        grid = groups < slots ? groups : slots;
         nthreads = split * 32;
         smem_launch = blk_smem_for(split, a.k, NT, BT::BYTES);
     }

@@ -53,6 +53,7 @@ def lib():
         "m27b_act_type_for": (u32, [u32]),
         "m27b_act_quant": (b, [vp, i32, i32, i32, u32, vp, vp, cp, sz]),
         "m27b_act_quant_gated": (b, [vp, vp, i32, i32, i32, u32, vp, vp, cp, sz]),
+        "m27b_act_quant_swiglu": (b, [vp, vp, i32, i32, i32, u32, vp, vp, cp, sz]),
         "m27b_act_quant_rmsnorm": (b, [vp, vp, fp, i32, i32, i32, u32, vp, vp, cp, sz]),
         "m27b_repacked_bytes": (sz, [u32, u32, u32]),
         "m27b_repack": (b, [vp, u32, u32, u32, vp, vp, cp, sz]),
@@ -172,6 +173,19 @@ def act_quant(x, act_type, out=None, stream=None, gate=None, norm_w=None, eps=No
     else:
         ok = L.m27b_act_quant(_ptr(x), k, n, x.stride(0), act_type, _ptr(out), _stream(stream), err, ERR_CAP)
     _check(ok, err, "m27b_act_quant")
+    return out
+
+
+def act_quant_swiglu(gate, up, act_type, out=None, stream=None):
+    """Quantize silu(gate) * up (device rows [n, k]) to q8_K / q8_0 blocks."""
+    import torch
+    n, k = up.shape
+    nb = act_bytes(act_type, k)
+    if out is None:
+        out = torch.empty(n * nb, dtype=torch.uint8, device=up.device)
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(lib().m27b_act_quant_swiglu(_ptr(gate), _ptr(up), k, n, up.stride(0), act_type, _ptr(out), _stream(stream),
+                                       err, ERR_CAP), err, "m27b_act_quant_swiglu")
     return out
 
 

@@ -69,3 +69,24 @@ def test_qmv_f32_two_launch_path(torch, orc, m27b, qtype, n):
     assert orc.rel_l2(got.cpu().numpy(), want) <= TOL
     with pytest.raises(m27b.M27BError, match="xq_scratch"):
         m27b.qmv_f32(W, torch.from_numpy(x).cuda(), n, got)
+
+
+@pytest.mark.parametrize("n", [1, 4])
+def test_act_quant_swiglu_equals_swiglu_epilogue(torch, orc, m27b, n):
+    # gate and up as two matvecs, then silu(gate) * up quantized, gives the
+    # same q8_K bytes as the fused SwiGLU epilogue followed by a quantizer
+    rows, k = 2048, 5120
+    (_, G), (_, U) = _w(orc, m27b, Q4_K, rows, k, 91), _w(orc, m27b, Q4_K, rows, k, 92)
+    xq = m27b.act_quant(torch.from_numpy(D.gauss_act(n, k, 93)).cuda(), Q8_K)
+    a = torch.empty((n, rows), device="cuda")
+    m27b.qmv_swiglu(G, U, xq, n, a)
+    fused = m27b.act_quant(a, Q8_K)
+    g, u = torch.empty((n, rows), device="cuda"), torch.empty((n, rows), device="cuda")
+    m27b.qmv(G, xq, n, g)
+    m27b.qmv(U, xq, n, u)
+    sep = m27b.act_quant_swiglu(g, u, Q8_K)
+    want = orc.quantize_q8_K(orc.silu_mul(g.cpu().numpy(), u.cpu().numpy()))
+    assert torch.equal(sep, fused)
+    # against the oracle's silu * up (fp64 exp): at most a rare last-code flip
+    got = sep.cpu().numpy().reshape(n, -1)
+    assert (got != want).mean() < 1e-3
