@@ -536,6 +536,9 @@ def run_reference(args, world, rank):
 
 def main():
     args = parse_args()
+    # stdout carries exactly one JSON line: NCCL's own log lines (e.g. its
+    # version banner under NCCL_DEBUG=VERSION) go to stderr unless a log file is set
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
