@@ -46,9 +46,13 @@ M27B_API bool m27b_attn_decode(const float *q, const float *k_cache, const float
                                cudaStream_t stream, char *err, size_t err_cap);
 
 /* Capacity of the static scratch m27b_attn_decode_noalloc uses (1 MiB): enough
- * for 24 query heads of 256 values over 37 splits (921,600 bytes, the
- * single-GPU Qwen-27B shape). */
+ * for 24 query heads of 256 values over 37 splits (37 * 24 * (256 + 4) * 4 =
+ * 923,520 bytes by m27b_attn_part_bytes, the single-GPU Qwen-27B shape). */
 #define M27B_ATTN_NOALLOC_SCRATCH_BYTES (1u << 20)
+
+/* M27B_ATTN_NOALLOC_SCRATCH_BYTES as compiled into the library, for bindings
+ * that do not read this header. */
+M27B_API size_t m27b_attn_noalloc_scratch_bytes(void);
 
 /* m27b_attn_decode without the `part` argument: the split partials live in a
  * file-scope __device__ array of M27B_ATTN_NOALLOC_SCRATCH_BYTES inside the

@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(256) k_allreduce_norm_quant_q8K(ActArgs a) {
 #pragma unroll
     for (int s = 0; s < M27B_MAX_SRC; ++s)
         if (s < a.nsrc) {
-            w[s] = wait_word(a.words + (size_t)s * a.src_stride + i, w[s], ep, a.status, 3);
+            w[s] = wait_word(a.words + (size_t)s * a.src_stride + i, w[s], ep, a.status, 3, a.wait_ns);
             v = s == 0 ? __uint_as_float(w[s].x) : v + __uint_as_float(w[s].x);
         }
     a.x_out[i] = v;
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(256) k_allreduce_norm_quant_q8K(ActArgs a) {
     }
     if ((int)threadIdx.x < nb) {
         const uint2 *q = a.ss_words + threadIdx.x;
-        css[threadIdx.x] = __uint_as_float(wait_word(q, ld_word(q), ep, a.status, 3).x);
+        css[threadIdx.x] = __uint_as_float(wait_word(q, ld_word(q), ep, a.status, 3, a.wait_ns).x);
     }
     __syncthreads();
     if (warp != 0) return;

@@ -97,6 +97,8 @@ bool m27b_attn_decode(const float *q, const float *k_cache, const float *v_cache
     return true;
 }
 
+size_t m27b_attn_noalloc_scratch_bytes(void) { return M27B_ATTN_NOALLOC_SCRATCH_BYTES; }
+
 bool m27b_attn_decode_noalloc(const float *q, const float *k_cache, const float *v_cache, const int *pos, int n_q,
                               int n_kv, int head_dim, int splits, float scale, float *out, cudaStream_t stream, char *err,
                               size_t err_cap) {

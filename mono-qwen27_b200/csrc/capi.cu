@@ -8,6 +8,7 @@
 
 #include "m27b_device.cuh"
 #include "m27b_qmv.h"
+#include "m27b_allreduce.h"
 #include "qmv_kernels.cuh"
 
 #include "m27b_launch.cuh"
@@ -450,6 +451,38 @@ bool m27b_dequant_rows(const WeightView *w, const int32_t *rows, int n, float *o
     return cuda_ok(launch_dequant_rows((int)base, planar, w->ptr, stride, (int)w->row_blocks, (int)w->row_count, k, rows, n,
                                        out, ldo, stream),
                    "m27b_dequant_rows", err, err_cap);
+}
+
+bool m27b_allreduce_norm_quant(const void *words, int nsrc, int src_stride, void *ss_words, const unsigned *epoch,
+                               const float *norm_w, float eps, int k, float *x_out, void *xq, unsigned long long wait_ns,
+                               cudaStream_t stream, char *err, size_t err_cap) {
+    const char *what = "m27b_allreduce_norm_quant";
+    if (!words || !ss_words || !epoch || !x_out || !xq) return fail(err, err_cap, "%s: null pointer", what);
+    if (nsrc < 1 || nsrc > M27B_ALLREDUCE_MAX_SRC)
+        return fail(err, err_cap, "%s: nsrc must be in [1, %d] (got %d)", what, M27B_ALLREDUCE_MAX_SRC, nsrc);
+    if (k < 256 || k % 256 || k > 65536) return fail(err, err_cap, "%s: k must be a multiple of 256 in [256, 65536]", what);
+    if (src_stride < k) return fail(err, err_cap, "%s: src_stride (%d) < k (%d)", what, src_stride, k);
+    if (((uintptr_t)words & 7u) || ((uintptr_t)ss_words & 7u))
+        return fail(err, err_cap, "%s: words must be 8-byte aligned", what);
+    if (((uintptr_t)xq & 3u) != 0) return fail(err, err_cap, "%s: output must be 4-byte aligned", what);
+    ActArgs a{};
+    a.w = norm_w;
+    a.eps = eps;
+    a.k = k;
+    a.ldx = k;
+    a.out = xq;
+    a.words = (const uint2 *)words;
+    a.nsrc = nsrc;
+    a.src_stride = src_stride;
+    a.ss_words = (uint2 *)ss_words;
+    a.epoch_base = epoch;
+    a.epoch_mul = 1u;
+    a.epoch_add = 0u;
+    a.x_out = x_out;
+    a.status = status_ptr_current();
+    a.wait_ns = wait_ns;
+    if (!a.status) return fail(err, err_cap, "%s: cannot resolve the device status word", what);
+    return cuda_ok(launch_act_quant(M27B_TYPE_Q8_K, ACT_RMSNORM_SUM, a, 1, stream), what, err, err_cap);
 }
 
 }  // extern "C"

@@ -82,63 +82,41 @@ M27B_DI unsigned long long global_ns() {
     return t;
 }
 
-M27B_DI unsigned ld_acquire_sys(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-M27B_DI void st_release_sys(unsigned *p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-M27B_DI void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
 // ---- epoch-tagged words ----
-// A value travels with its epoch in one aligned 8-byte word {bits, epoch},
-// written by a single 8-byte store and read by a single 8-byte load, so a
-// reader sees either the old word or the new one, never a mix: a word whose
-// epoch matches is complete, and no fence or separate flag is needed.  Reads
-// bypass L1 (the word is rewritten by another SM or another GPU).
+// A value travels with its epoch in one aligned 8-byte word {bits, epoch}
+// (bits in the low half), written by one relaxed system-scope 64-bit store
+// and read by one relaxed system-scope 64-bit load.  Under the PTX memory
+// model an aligned scalar b64 access at .sys scope is single-copy atomic and
+// does not race with the writer, so a reader sees either the whole old word
+// or the whole new one: a word whose epoch matches carries that epoch's
+// value, with no fence or separate flag.  (A v2.b32 vector access would be two
+// scalar accesses in unspecified order, and a weak one a data race.)  The
+// relaxed .sys load is not served from L1, so a re-read sees a store made
+// by another SM or another GPU.
 M27B_DI void st_word(uint2 *p, uint32_t bits, uint32_t ep) {
-    asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(bits), "r"(ep) : "memory");
+    const unsigned long long w = (unsigned long long)bits | ((unsigned long long)ep << 32);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 M27B_DI uint2 ld_word(const uint2 *p) {
-    uint2 w;
-    asm volatile("ld.global.cv.v2.b32 {%0, %1}, [%2];" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
-    return w;
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return make_uint2((uint32_t)w, (uint32_t)(w >> 32));
 }
-// Re-read *p until its epoch is `ep`, for at most M27B_WAIT_NS (or until an
-// earlier wait has failed: *status non-zero); on failure record `code` and
-// return the last word read.
-M27B_DI uint2 wait_word(const uint2 *p, uint2 w, uint32_t ep, int *status, int code) {
+// Re-read *p until its epoch is `ep`, for at most `limit_ns` nanoseconds
+// (0: M27B_WAIT_NS) or until an earlier wait has failed (*status non-zero);
+// on failure record `code` in *status and return the last word read.
+M27B_DI uint2 wait_word(const uint2 *p, uint2 w, uint32_t ep, int *status, int code,
+                        unsigned long long limit_ns = 0) {
     if (w.y == ep) return w;
+    const unsigned long long lim = limit_ns ? limit_ns : M27B_WAIT_NS;
     const unsigned long long t0 = global_ns();
     for (unsigned it = 0;; ++it) {
         w = ld_word(p);
         if (w.y == ep) return w;
-        if ((it & 31u) == 31u &&
-            (global_ns() - t0 > M27B_WAIT_NS || (status && *(volatile int *)status != 0))) {
+        if ((it & 31u) == 31u && (global_ns() - t0 > lim || (status && *(volatile int *)status != 0))) {
             if (status) atomicCAS(status, 0, code);
             return w;
         }
-    }
-}
-
-// Wait (acquire, system scope) until the monotonic counter *f reaches epoch
-// `ep` (wrap-safe compare), for at most M27B_WAIT_NS.  On timeout, or when
-// *status is already non-zero (an earlier wait gave up), record `code` and
-// return false instead of waiting.
-M27B_DI bool wait_epoch_sys(const unsigned *f, unsigned ep, int *status, int code) {
-    if ((int)(ld_acquire_sys(f) - ep) >= 0) return true;
-    const unsigned long long t0 = global_ns();
-    for (unsigned it = 0;; ++it) {
-        if ((int)(ld_acquire_sys(f) - ep) >= 0) return true;
-        if ((it & 63u) == 63u) {
-            if (global_ns() - t0 > M27B_WAIT_NS || (status && *(volatile int *)status != 0)) {
-                if (status) atomicCAS(status, 0, code);
-                return false;
-            }
-        }
-        __nanosleep(64);
     }
 }
 

@@ -47,6 +47,7 @@ struct ActArgs {
     unsigned epoch_mul, epoch_add;
     float *x_out;
     int *status;
+    unsigned long long wait_ns;  // bound on each word wait (0: M27B_WAIT_NS)
 };
 
 cudaError_t launch_act_quant(int act_type, int mode, const ActArgs &a, int n_tok, cudaStream_t st);

@@ -63,6 +63,7 @@ def lib():
         "m27b_qmv_f32": (b, [wvp, vp, i32, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_qmv_f32_rmsnorm": (b, [wvp, wvp, vp, i32, vp, fp, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
+        "m27b_allreduce_norm_quant": (b, [vp, i32, i32, vp, vp, vp, fp, i32, vp, vp, ctypes.c_ulonglong, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -176,6 +177,19 @@ def act_quant(x, act_type, out=None, stream=None, gate=None, norm_w=None, eps=No
     return out
 
 
+def allreduce_norm_quant(words, nsrc, src_stride, ss_words, epoch, k, x_out, xq, norm_w=None, eps=1e-6, wait_ns=0,
+                         stream=None):
+    """The fused all-reduce's consumer (include/m27b_allreduce.h): sum the nsrc
+    ranks' epoch-tagged words (device int64 tensors, value bits low, epoch
+    high) once they carry *epoch (device uint32), then RMSNorm + q8_K into xq."""
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ok = lib().m27b_allreduce_norm_quant(_ptr(words), nsrc, src_stride, _ptr(ss_words), _ptr(epoch), _ptr(norm_w),
+                                         ctypes.c_float(eps), k, _ptr(x_out), _ptr(xq), ctypes.c_ulonglong(wait_ns),
+                                         _stream(stream), err, ERR_CAP)
+    _check(ok, err, "m27b_allreduce_norm_quant")
+    return xq
+
+
 def act_quant_swiglu(gate, up, act_type, out=None, stream=None):
     """Quantize silu(gate) * up (device rows [n, k]) to q8_K / q8_0 blocks."""
     import torch
@@ -267,6 +281,8 @@ def _attn_lib():
     L.m27b_attn_decode.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, fp, vp, vp, vp, cp, sz]
     L.m27b_attn_decode_noalloc.restype = b
     L.m27b_attn_decode_noalloc.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, fp, vp, vp, cp, sz]
+    L.m27b_attn_noalloc_scratch_bytes.restype = sz
+    L.m27b_attn_noalloc_scratch_bytes.argtypes = []
     L._attn_sigs = True
     return L
 
@@ -284,7 +300,9 @@ def attn_decode(q, k_cache, v_cache, pos, n_q, n_kv, head_dim, splits, scale, pa
     return out
 
 
-ATTN_NOALLOC_SCRATCH_BYTES = 1 << 20
+def attn_noalloc_scratch_bytes():
+    """Capacity of m27b_attn_decode_noalloc's static scratch, as compiled into the library."""
+    return _attn_lib().m27b_attn_noalloc_scratch_bytes()
 
 
 def attn_decode_noalloc(q, k_cache, v_cache, pos, n_q, n_kv, head_dim, splits, scale, out, stream=None):

@@ -16,7 +16,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_KAT = os.path.join(REF_DIR, "official_dequant")
-REFERENCE_ROOT = os.environ.get("M27B_REFERENCE_ROOT", "/root/reference")
+# The reference checkout: M27B_REFERENCE_ROOT, else a directory named
+# "reference" beside this repository's own directory (absent on a GPU box,
+# where the programs built from it travel prebuilt).
+REFERENCE_ROOT = os.environ.get("M27B_REFERENCE_ROOT") or os.path.join(
+    os.path.dirname(os.path.dirname(HERE)), "reference")
 
 
 def _stale(out, srcs):

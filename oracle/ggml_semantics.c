@@ -790,3 +790,141 @@ int64_t orc_argmax(const float *v, int64_t n) {
         if (v[i] > v[best]) best = i;
     return n > 0 ? best : -1;
 }
+
+/* ---- vectorised q4_K . q8_K (the timed CPU baseline) -------------------- *
+ * ggml's x86 builds replace the generic vec_dot_q4_K_q8_K with SIMD code:
+ * the AVX2 form multiplies the unsigned 4-bit codes by the signed q8 codes
+ * with vpmaddubsw (pairs of u8*s8 summed to s16; at most 2*15*128 = 3840, no
+ * saturation), widens with vpmaddwd against the sub-block's 6-bit scale, and
+ * sums in int32; with AVX-512 VNNI, vpdpbusd does the u8*s8 products and the
+ * sum of four in one instruction.  The restatements below follow that
+ * instruction mapping, compute the same exact int32 sums (sum_s sc*dot and
+ * sum_s m*bsum) as orc_vec_dot_q4_K_q8_K, and combine them into the fp32
+ * accumulator in the same order, so their results equal the scalar oracle's
+ * bit for bit (the CPU tests check this).  They are only the CPU baseline;
+ * the scalar function stays the checker. */
+#if defined(__x86_64__)
+#include <immintrin.h>
+
+/* All eight 6-bit scales and mins at once, one byte each (the same values
+ * q4K_scale_min gives, from three little-endian words of the packed bytes). */
+static void q4K_unpack8(const uint8_t *s, int sc[8], int mn[8]) {
+    uint32_t w0, w1, w2;
+    memcpy(&w0, s, 4);
+    memcpy(&w1, s + 4, 4);
+    memcpy(&w2, s + 8, 4);
+    const uint32_t sc03 = w0 & 0x3f3f3f3fu, mn03 = w1 & 0x3f3f3f3fu;
+    const uint32_t sc47 = (w2 & 0x0f0f0f0fu) | ((w0 >> 2) & 0x30303030u);
+    const uint32_t mn47 = ((w2 >> 4) & 0x0f0f0f0fu) | ((w1 >> 2) & 0x30303030u);
+    for (int j = 0; j < 4; ++j) {
+        sc[j] = (int)((sc03 >> (8 * j)) & 0xff);
+        mn[j] = (int)((mn03 >> (8 * j)) & 0xff);
+        sc[j + 4] = (int)((sc47 >> (8 * j)) & 0xff);
+        mn[j + 4] = (int)((mn47 >> (8 * j)) & 0xff);
+    }
+}
+
+/* fp16 -> fp32 with the F16C instruction (exact, as orc_fp16_to_fp32). */
+__attribute__((target("f16c")))
+static inline float h2f_f16c(uint16_t h) { return _cvtsh_ss(h); }
+
+__attribute__((target("avx2,fma,f16c")))
+static float dot_q4K_avx2(int64_t n, const orc_q4K *x, const orc_q8K *y) {
+    const __m256i m4 = _mm256_set1_epi8(0x0f);
+    float acc = 0.0f;
+    for (int64_t b = 0; b < n / QK; ++b) {
+        int sc[8], mn[8];
+        q4K_unpack8(x[b].scales, sc, mn);
+        __m256i vs = _mm256_setzero_si256();
+        for (int g = 0; g < 4; ++g) {
+            const __m256i q = _mm256_loadu_si256((const __m256i *)(x[b].qs + 32 * g));
+            const __m256i lo = _mm256_and_si256(q, m4);
+            const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(q, 4), m4);
+            const __m256i a0 = _mm256_loadu_si256((const __m256i *)(y[b].qs + 64 * g));
+            const __m256i a1 = _mm256_loadu_si256((const __m256i *)(y[b].qs + 64 * g + 32));
+            const __m256i p0 = _mm256_madd_epi16(_mm256_maddubs_epi16(lo, a0), _mm256_set1_epi16((short)sc[2 * g]));
+            const __m256i p1 = _mm256_madd_epi16(_mm256_maddubs_epi16(hi, a1), _mm256_set1_epi16((short)sc[2 * g + 1]));
+            vs = _mm256_add_epi32(vs, _mm256_add_epi32(p0, p1));
+        }
+        __m128i h = _mm_add_epi32(_mm256_castsi256_si128(vs), _mm256_extracti128_si256(vs, 1));
+        h = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0x4e));
+        h = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0xb1));
+        const int32_t isum = _mm_cvtsi128_si32(h);
+        int32_t msum = 0;
+        for (int s = 0; s < 8; ++s) msum += mn[s] * (y[b].bsums[2 * s] + y[b].bsums[2 * s + 1]);
+        const float dx = y[b].d;
+        acc += h2f_f16c(x[b].d) * dx * (float)isum;
+        acc -= h2f_f16c(x[b].dmin) * dx * (float)msum;
+    }
+    return acc;
+}
+
+__attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c")))
+static float dot_q4K_vnni(int64_t n, const orc_q4K *x, const orc_q8K *y) {
+    const __m256i m4 = _mm256_set1_epi8(0x0f);
+    float acc = 0.0f;
+    for (int64_t b = 0; b < n / QK; ++b) {
+        int sc[8], mn[8];
+        q4K_unpack8(x[b].scales, sc, mn);
+        __m512i vs = _mm512_setzero_si512();
+        for (int g = 0; g < 4; ++g) {
+            /* sub-blocks 2g (low nibbles) and 2g+1 (high nibbles) against the
+             * 64 contiguous q8 codes of those two sub-blocks */
+            const __m256i q = _mm256_loadu_si256((const __m256i *)(x[b].qs + 32 * g));
+            const __m512i codes = _mm512_inserti64x4(_mm512_castsi256_si512(_mm256_and_si256(q, m4)),
+                                                     _mm256_and_si256(_mm256_srli_epi16(q, 4), m4), 1);
+            const __m512i a = _mm512_loadu_si512((const void *)(y[b].qs + 64 * g));
+            const __m512i dot = _mm512_dpbusd_epi32(_mm512_setzero_si512(), codes, a);
+            const __m512i scv = _mm512_inserti64x4(_mm512_set1_epi32(sc[2 * g]), _mm256_set1_epi32(sc[2 * g + 1]), 1);
+            vs = _mm512_add_epi32(vs, _mm512_mullo_epi32(dot, scv));
+        }
+        const int32_t isum = _mm512_reduce_add_epi32(vs);
+        int32_t msum = 0;
+        for (int s = 0; s < 8; ++s) msum += mn[s] * (y[b].bsums[2 * s] + y[b].bsums[2 * s + 1]);
+        const float dx = y[b].d;
+        acc += h2f_f16c(x[b].d) * dx * (float)isum;
+        acc -= h2f_f16c(x[b].dmin) * dx * (float)msum;
+    }
+    return acc;
+}
+#endif
+
+/* The instruction set orc_matvec_q4K_simd uses on this CPU: 2 = AVX-512
+ * VNNI, 1 = AVX2, 0 = none (it then calls the scalar function). */
+int orc_simd_level(void) {
+#if defined(__x86_64__)
+    __builtin_cpu_init();
+    if (__builtin_cpu_supports("avx512vnni") && __builtin_cpu_supports("avx512bw") &&
+        __builtin_cpu_supports("avx512vl"))
+        return 2;
+    if (__builtin_cpu_supports("avx2")) return 1;
+#endif
+    return 0;
+}
+
+/* orc_matvec for q4_K weights with the vectorised dot product (level from
+ * orc_simd_level(), or a lower one if `level` is smaller).  Returns the level
+ * used. */
+int orc_matvec_q4K_simd(const void *W, int64_t rows, int64_t k, const void *xq, int ntok, float *y, int nthreads,
+                        int level) {
+    int lv = orc_simd_level();
+    if (level >= 0 && level < lv) lv = level;
+    const size_t rb = row_bytes(ORC_Q4_K, k), xb = (size_t)(k / QK) * sizeof(orc_q8K);
+    set_threads(nthreads);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const orc_q4K *w = (const orc_q4K *)((const uint8_t *)W + (size_t)r * rb);
+        for (int t = 0; t < ntok; ++t) {
+            const orc_q8K *a = (const orc_q8K *)((const uint8_t *)xq + (size_t)t * xb);
+            float v;
+#if defined(__x86_64__)
+            if (lv == 2) v = dot_q4K_vnni(k, w, a);
+            else if (lv == 1) v = dot_q4K_avx2(k, w, a);
+            else
+#endif
+                v = orc_vec_dot_q4_K_q8_K(k, w, a);
+            y[(size_t)t * rows + r] = v;
+        }
+    }
+    return lv;
+}

@@ -54,6 +54,10 @@ def lib():
         L.orc_max_threads.restype = ctypes.c_int
         L.orc_argmax.argtypes = [fp, i64]
         L.orc_argmax.restype = ctypes.c_int64
+        L.orc_simd_level.restype = ctypes.c_int
+        L.orc_simd_level.argtypes = []
+        L.orc_matvec_q4K_simd.argtypes = [vp, i64, i64, vp, ctypes.c_int, fp, ctypes.c_int, ctypes.c_int]
+        L.orc_matvec_q4K_simd.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -132,6 +136,28 @@ def matvec(qtype, w, k, xq, nthreads=0):
     y = np.empty((ntok, rows), dtype=np.float32)
     assert lib().orc_matvec(qtype, _p(w), rows, k, _p(xq), ntok, _p(y), nthreads) == 0
     return y
+
+
+SIMD_NAMES = {0: "scalar", 1: "AVX2 (vpmaddubsw + vpmaddwd)", 2: "AVX-512 VNNI (vpdpbusd)"}
+
+
+def simd_level():
+    """Instruction set of the vectorised q4_K matvec on this CPU (see SIMD_NAMES)."""
+    return int(lib().orc_simd_level())
+
+
+def matvec_q4K_simd(w, k, xq, nthreads=0, level=-1):
+    """q4_K matvec with the vectorised dot product (the timed CPU baseline);
+    equal bit for bit to matvec(Q4_K, ...).  Returns (y, level used)."""
+    w = np.ascontiguousarray(w).view(np.uint8)
+    rows = w.size // row_bytes(Q4_K, k)
+    xq = np.ascontiguousarray(np.atleast_2d(xq))
+    if xq.dtype != np.uint8:
+        xq = xq.view(np.uint8)
+    ntok = xq.shape[0]
+    y = np.empty((ntok, rows), dtype=np.float32)
+    lv = lib().orc_matvec_q4K_simd(_p(w), rows, k, _p(xq), ntok, _p(y), nthreads, level)
+    return y, lv
 
 
 def argmax(v):

@@ -28,7 +28,9 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("M27B_REFERENCE_ROOT", "/root/reference")
+# the reference checkout: M27B_REFERENCE_ROOT, else "reference" beside this repository
+REF = os.environ.get("M27B_REFERENCE_ROOT") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))), "reference")
 
 
 def fp16_bits(rng, n, lo, hi):

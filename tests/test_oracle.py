@@ -12,6 +12,8 @@ import subprocess
 import numpy as np
 import pytest
 
+import _data as D
+
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, IQ4_XS = 0, 1, 8, 12, 13, 14, 15, 23
 
 
@@ -153,3 +155,23 @@ def test_iq4_xs_codebook_and_scale_fields(orc):
     assert v[0] == -127 and v[16] == 113 and v[1] == -127
     assert v[32] == -2 * 1 and v[33] == -2 * -127
     assert np.all(v[64:] == -32 * -127)  # stored ls 0: multiplier -32, code 0: codebook -127
+
+
+def test_simd_q4K_matvec_equals_scalar_oracle(orc):
+    """The vectorised q4_K . q8_K (the timed CPU baseline) gives the scalar
+    oracle's results bit for bit, at every instruction-set level this CPU has
+    (extreme codes and scales included)."""
+    rng = np.random.default_rng(21)
+    for rows, k, ntok in ((37, 256, 1), (300, 5120, 3), (64, 17408, 2)):
+        w = D.random_valid_blocks(orc.Q4_K, rows, k, 5 + rows)
+        wb = w.reshape(rows, -1, 144)
+        wb[0, :, 4:16] = 0xff          # every 6-bit scale and min at 63
+        wb[1, :, 16:] = 0xff           # every code at 15
+        x = (rng.standard_normal((ntok, k)) * 3).astype(np.float32)
+        x[0, :256] = 127.0             # saturating activation codes
+        xq = orc.quantize_q8_K(x)
+        want = orc.matvec(orc.Q4_K, w, k, xq)
+        for level in range(orc.simd_level() + 1):
+            got, used = orc.matvec_q4K_simd(w, k, xq, level=level)
+            assert used == level
+            assert np.array_equal(got, want), (rows, k, level)
