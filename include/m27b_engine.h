@@ -106,6 +106,15 @@ M27B_API bool m27b_nccl_unique_id(void *id, char *err, size_t err_cap);
  * allocates this rank's weight shards, the KV cache and the workspace. */
 M27B_API bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err, size_t err_cap);
 
+/* Create a second engine (tp_size 1) on the current device that shares src's
+ * weights and has its own KV cache of max_ctx positions, DeltaNet states,
+ * workspace and CUDA graphs: several independent sequences over one copy of
+ * the weights (the reference keeps weights and state apart the same way,
+ * include/mono27b_config.h:155-166).  src must outlive it and must not load
+ * further tensors meanwhile; this engine never frees the weights. */
+M27B_API bool m27b_engine_create_sharing(const M27BEngine *src, int max_ctx, M27BEngine **out, char *err,
+                                         size_t err_cap);
+
 /* Join the tensor-parallel group (tp_size > 1): id from m27b_nccl_unique_id. */
 M27B_API bool m27b_engine_set_nccl(M27BEngine *e, const void *id, char *err, size_t err_cap);
 

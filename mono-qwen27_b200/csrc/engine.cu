@@ -22,6 +22,7 @@
 #include "m27b_engine.h"
 #include "m27b_launch.cuh"
 #include "qmv_kernels.cuh"
+#include "engine_state.h"
 
 namespace m27b {
 __global__ void k_qk_norm_rope_cache(const float *qkv, const float *q_norm, const float *k_norm, float *q, float *gate,
@@ -158,70 +159,8 @@ WinLayout win_layout(int N, int hidden) {
     return w;
 }
 
-// A quantized matrix resident on the device (repacked when its type needs it).
-struct QMat {
-    void *d = nullptr;
-    WeightView v{};
-    uint32_t type = 0;
-    int rows = 0, k = 0;
-    size_t gguf_bytes = 0;  // algorithmic bytes (GGUF layout)
-};
-
-struct Layer {
-    bool ssm = false;  // a Gated DeltaNet layer of a hybrid model
-    QMat wqkv, wo, wg, wu, wd;
-    float *attn_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
-    float *kc = nullptr, *vc = nullptr;
-    // DeltaNet: projections, conv weights [conv_ch][K] (fp32), per-head
-    // parameters, conv state [conv_ch][K - 1] and delta-rule state [dr][128][128]
-    QMat wqs, wz, wba, wso;
-    float *conv_w = nullptr, *dt_bias = nullptr, *ssm_a = nullptr, *ssm_norm = nullptr;
-    float *cstate = nullptr, *S = nullptr;
-};
-
 }  // namespace
 
-struct M27BEngine {
-    M27BModelConfig c{};
-    int dev = 0;
-    int H = 0, q_lo = 0;     // local q heads
-    int KV = 0, kv_lo = 0;   // local kv heads
-    int G = 0;               // q heads per kv head
-    int F = 0, f_lo = 0;     // local FFN slice (values)
-    int V = 0, v_lo = 0;     // local vocabulary rows
-    int S = 1;               // attention splits
-    std::vector<Layer> L;
-    QMat embd, lmh;
-    float *out_norm = nullptr;
-    float *h = nullptr, *h2 = nullptr, *qkv = nullptr, *q = nullptr, *gate = nullptr, *o = nullptr, *a = nullptr;
-    float *a2 = nullptr;  // verify pass: the up projection next to the gate one in `a`
-    float *part = nullptr, *logits = nullptr;
-    // DeltaNet buffers: normed input, projections, conv output, beta|g
-    float *hn = nullptr, *sx = nullptr, *sxc = nullptr, *sz = nullptr, *sba = nullptr, *sbg = nullptr;
-    int conv_ch = 0, n_ssm = 0;
-    float2 *rope = nullptr;  // (cos, sin) of the step's position, n_rot/2 pairs
-    int *vtok = nullptr;                 // device: the tokens of a verify pass
-    int *h_vtok = nullptr;               // pinned copy
-    unsigned long long *h_vbest = nullptr;  // pinned: the verify pass's argmax keys
-    cudaGraphExec_t vgraph[M27B_VERIFY_MAX + 1] = {};  // verify pass, per token count
-    uint8_t *xq = nullptr;
-    unsigned long long *best = nullptr;
-    int *ctl = nullptr;                      // device [token, pos, generated count, pad]
-    int *hist = nullptr;                     // device: tokens generated by m27b_engine_generate
-    int *h_ctl = nullptr;                    // pinned [token, pos, 0, 0]
-    int *h_hist = nullptr;                   // pinned copy of hist
-    unsigned long long *h_best = nullptr;    // pinned
-    uint8_t *scratch = nullptr;              // load-time staging (raw GGUF bytes before repack)
-    size_t scratch_bytes = 0;
-    cudaStream_t st = nullptr;
-    cudaGraphExec_t gexec = nullptr;
-    ncclComm_t comm = nullptr;
-    // fused all-reduce over NVLink (m27b_engine_enable_p2p)
-    bool p2p = false;
-    uint8_t *win = nullptr;         // this rank's receive window (exported by CUDA IPC)
-    uint8_t *peer_win[8] = {};      // every rank's window as mapped here (own: win)
-    std::vector<void *> allocs;
-};
 
 namespace {
 
@@ -764,6 +703,36 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
     return true;
 }
 
+bool m27b_engine_create_sharing(const M27BEngine *src, int max_ctx, M27BEngine **out, char *err, size_t err_cap) {
+    if (!src || !out) return efail(err, err_cap, "m27b_engine_create_sharing: null argument");
+    *out = nullptr;
+    if (src->c.tp_size != 1) return efail(err, err_cap, "m27b_engine_create_sharing: tp_size must be 1");
+    M27BModelConfig c = src->c;
+    c.max_ctx = max_ctx;
+    M27BEngine *e = nullptr;
+    if (!m27b_engine_create(&c, &e, err, err_cap)) return false;
+    if (e->dev != src->dev) {
+        m27b_engine_destroy(e);
+        return efail(err, err_cap, "m27b_engine_create_sharing: the source engine lives on device %d, current is %d",
+                     src->dev, e->dev);
+    }
+    // the weights are borrowed: they are not in e->allocs, so this engine never frees them
+    for (size_t l = 0; l < e->L.size(); ++l) {
+        Layer &d = e->L[l];
+        const Layer &s = src->L[l];
+        d.wqkv = s.wqkv, d.wo = s.wo, d.wg = s.wg, d.wu = s.wu, d.wd = s.wd;
+        d.attn_norm = s.attn_norm, d.post_norm = s.post_norm, d.q_norm = s.q_norm, d.k_norm = s.k_norm;
+        d.wqs = s.wqs, d.wz = s.wz, d.wba = s.wba, d.wso = s.wso;
+        d.conv_w = s.conv_w, d.dt_bias = s.dt_bias, d.ssm_a = s.ssm_a, d.ssm_norm = s.ssm_norm;
+    }
+    e->embd = src->embd;
+    e->lmh = src->lmh;
+    e->out_norm = src->out_norm;
+    *out = e;
+    if (err && err_cap) err[0] = '\0';
+    return true;
+}
+
 bool m27b_engine_set_nccl(M27BEngine *e, const void *id, char *err, size_t err_cap) {
     if (!e || !id) return efail(err, err_cap, "m27b_engine_set_nccl: null argument");
     if (e->c.tp_size == 1) return efail(err, err_cap, "tp_size is 1");
@@ -1186,3 +1155,11 @@ void m27b_engine_destroy(M27BEngine *e) {
 }
 
 }  // extern "C"
+
+namespace m27b {
+size_t stored_row_bytes(const QMat &m) {
+    if (!m.d || m.rows <= 0) return 0;
+    const uint32_t rb = m.v.row_blocks;
+    return raw_layout(m.type) ? (size_t)rb * block_bytes(m.type) : m27b_repacked_bytes(m.type, rb, 1);
+}
+}  // namespace m27b
