@@ -64,7 +64,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=None)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "decode"], default="cfg0")
+    p.add_argument("--workload", choices=["cfg0", "cfg1", "cfg2", "cfg3", "decode", "spec"], default="cfg0")
     p.add_argument("--rows", type=int, default=None, help="override the row count (smaller profiling cases)")
     p.add_argument("--ntok", type=int, default=None, help="tokens per matvec (cfg2: 16, cfg3: 1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -74,11 +74,12 @@ def parse_args():
     p.add_argument("--layers", type=int, default=64, help="decode: layers (64 = the Qwen-27B shape)")
     p.add_argument("--hybrid", action="store_true",
                    help="decode: the hybrid layout (every 4th layer attention, the rest Gated DeltaNet; 1 GPU)")
+    p.add_argument("--k", type=int, default=7, help="spec: tokens the draft proposes per round")
     p.add_argument("--comm", choices=["p2p", "nccl"], default="p2p",
                    help="decode, N>1: fused NVLink all-reduce (p2p) or NCCL all-reduce")
     a = p.parse_args()
     if a.steps is None:
-        a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg2": 20000, "cfg3": 8000, "decode": a.gen}[a.workload]
+        a.steps = {"cfg0": 40000, "cfg1": 2000, "cfg2": 20000, "cfg3": 8000, "decode": a.gen, "spec": a.gen}[a.workload]
     if a.ntok is None:
         a.ntok = 16 if a.workload == "cfg2" else 1
     return a
@@ -552,6 +553,104 @@ def tp_parity_check(world, rank, dev, dist):
     return out
 
 
+# --------------------------------------------------------------------------
+# speculative decoding (cfg4 target + q8_0 draft), one GPU
+
+
+def spec_main(args, dev, uuid):
+    """--workload spec: the 64-layer target and the BASELINE cfg4 q8_0 draft
+    (28 layers, hidden 1024, FFN 3072), seeded random weights, 512-token
+    prompt.  Measured with CUDA events on the engines' streams: the target's
+    plain greedy decode, the draft's generation per token, the target's verify
+    pass of k + 1 tokens, and the whole speculative loop
+    (m27b_engine_speculative_generate, C++) with this draft.  Random weights
+    give two unrelated models, so the measured acceptance is ~0; the line also
+    gives the tokens/s the measured costs imply at acceptance rates a trained
+    draft reaches (expected tokens per round (1 - a^(k+1)) / (1 - a), one
+    round = k draft tokens + one verify pass)."""
+    import numpy as np
+    import torch
+    import m27b
+    k = args.k
+    ctx = args.prompt + args.gen + 2 * k + 8
+    tc = m27b.model_config(max_ctx=ctx, n_layers=args.layers)
+    d = dict(m27b.DRAFT)
+    dc = m27b.model_config(max_ctx=ctx, **d)
+    target, draft = m27b.Engine(tc), m27b.Engine(dc)
+    try:
+        target.random_weights(seed=0, sigma=0.02)
+        draft.random_weights(seed=1, sigma=0.02)
+        prompt = [int(t) for t in np.random.default_rng(4).integers(0, tc.vocab, args.prompt)]
+        sts = [torch.cuda.ExternalStream(e.stream(), device=dev) for e in (target, draft)]
+
+        def timed(fn):
+            torch.cuda.synchronize()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in sts]
+            for (a, _), s in zip(evs, sts):
+                a.record(s)
+            t0 = time.perf_counter()
+            out = fn()
+            host_ms = (time.perf_counter() - t0) * 1e3
+            for (_, b), s in zip(evs, sts):
+                b.record(s)
+            torch.cuda.synchronize()
+            return out, host_ms, [a.elapsed_time(b) for a, b in evs]
+
+        def feed(e, n):
+            for pos in range(n):
+                e.decode_step(prompt[pos], pos)
+
+        p0 = args.prompt - 1
+        feed(target, p0)
+        feed(draft, p0)
+        target.generate(prompt[-1], p0, 4)  # warm-up (graphs captured; rewritten below)
+        draft.generate(prompt[-1], p0, 4)
+        _, _, (t_ms, _) = timed(lambda: target.generate(prompt[-1], p0, args.gen))
+        _, _, (_, d_ms) = timed(lambda: draft.generate(prompt[-1], p0, args.gen))
+        vt = [prompt[-1]] + [int(t) for t in np.random.default_rng(5).integers(0, tc.vocab, k)]
+        target.verify(vt, p0)  # capture
+        reps = 5
+        _, _, (v_ms, _) = timed(lambda: [target.verify(vt, p0) for _ in range(reps)])
+        v_ms /= reps
+        # the whole loop from an empty cache, prompt included (the prompt's
+        # share is reported apart, from the loop's own host clocks)
+        (toks, st), host_ms, _ = timed(lambda: m27b.speculative_generate(target, draft, prompt, args.gen, k=k))
+        loop_ms = st["draft_ms"] + st["verify_ms"]
+        spec_tps = args.gen / (loop_ms / 1e3)
+        plain_tps = args.gen / (t_ms / 1e3)
+        d_tok = d_ms / args.gen
+        proj = {}
+        for a in (0.5, 0.7, 0.8, 0.9):
+            per_round = (1 - a ** (k + 1)) / (1 - a)
+            proj[str(a)] = round(per_round / ((k * d_tok + v_ms) / 1e3), 1)
+        line = {
+            "metric": "speculative decode tokens/s", "value": round(spec_tps, 2), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.gen, "warmup": 4, "ms_per_step": round(loop_ms / args.gen, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "target q4_K/q6_K, draft q8_0, * q8_K / q8_0 activations, f32 accumulate",
+            "data": "synthetic (seeded random valid blocks for both models: unrelated, acceptance ~0)",
+            "config": {"workload": f"cfg4 speculative: {args.layers}-layer target + 28-layer q8_0 draft "
+                                   f"(hidden 1024, FFN 3072), k={k}, {args.prompt}-token prompt, {args.gen} tokens",
+                       "k": k, "parallelism": "tp1"},
+            "spec": {"acceptance": round(st["accepted"] / max(1, st["proposed"]), 4), "rounds": st["iterations"],
+                     "loop_host_ms": round(loop_ms, 2), "prefill_host_ms": round(st["prefill_ms"], 1),
+                     "target_plain_tokens_per_s": round(plain_tps, 2), "target_ms_per_token": round(t_ms / args.gen, 4),
+                     "draft_ms_per_token": round(d_tok, 4), "draft_tokens_per_s": round(args.gen / (d_ms / 1e3), 1),
+                     "verify_ms_per_pass": round(v_ms, 4), "verify_tokens": k + 1,
+                     "verify_over_step": round(v_ms / (t_ms / args.gen), 3),
+                     "projected_tokens_per_s_at_acceptance": proj,
+                     "draft_weight_bytes_per_token": draft.weight_bytes_per_token()},
+            "e2e": {"value": round(args.gen / (host_ms / 1e3), 2), "unit": "tokens/s (prompt feeding included)",
+                    "h2d_bytes_per_step": 4 * (k + 1), "d2h_bytes_per_step": 4 * (2 * k + 1)},
+            "device_status": m27b.device_status(clear=True), "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+        return 0 if line["device_status"] == 0 else 1
+    finally:
+        target.close()
+        draft.close()
+
+
 def e_kv_heads(cfg):
     import m27b
     return m27b.partition(cfg).n_kv
@@ -576,6 +675,80 @@ def cpu_oracle_gbs(w_host, k, seconds, nthreads=0):
             break
     bytes_per = wbytes(Q4_K, n, k) + k * 4 + n * 4
     return bytes_per * reps / el / 1e9, reps, (nthreads or orc.max_threads()), orc.SIMD_NAMES[level]
+
+
+def reference_gpu_leg(steps=20, warmup=5):
+    """The reference executor's own q8_1 quantizer + dp4a matvec kernels,
+    compiled for sm_100a from the reference checkout (oracle/_ref/, a
+    comparison arm), timed on this GPU the way the GPU arm is timed: cfg0
+    (6 rotating 17408 x 5120 q4_K matrices, one quantize + matvec each, CUDA
+    graph, CUDA events), plus the q6_K lm_head (cfg1 shape) and ffn_down
+    shapes.  None without a GPU or without the built harness."""
+    try:
+        import torch
+        from oracle import ref_gpu
+        if not torch.cuda.is_available() or not ref_gpu.available():
+            return None
+    except Exception:
+        return None
+    from _data import random_valid_blocks
+    import numpy as np
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    out = {"kernels": "k_quant_q8_1 + k_q4k_mv_q8_dp4a / k_q6k_mv_q8_dp4a (reference src/mono27b_executor.cu, "
+                      "sm_100a, --use_fast_math)"}
+
+    def run(qtype, rows, k, copies):
+        be = 256
+        rb = k // be
+        Ws = [torch.from_numpy(random_valid_blocks(qtype, rows, k, 100 + c).reshape(-1)).to(dev) for c in range(copies)]
+        xs = [torch.from_numpy(np.random.default_rng(7 + c).standard_normal(k).astype(np.float32)).to(dev)
+              for c in range(copies)]
+        q8 = [torch.empty(ref_gpu.q8_1_bytes(k), dtype=torch.uint8, device=dev) for _ in range(copies)]
+        ys = [torch.empty(rows, dtype=torch.float32, device=dev) for _ in range(copies)]
+        s = torch.cuda.Stream()
+
+        def step(kernel_only=False):
+            h = s.cuda_stream
+            for c in range(copies):
+                if not kernel_only:
+                    ref_gpu.quant_q8_1(xs[c].data_ptr(), q8[c].data_ptr(), k, h)
+                ref_gpu.matvec(qtype, Ws[c].data_ptr(), q8[c].data_ptr(), ys[c].data_ptr(), rb, rows, h)
+
+        res = {}
+        for ko in (False, True):
+            with torch.cuda.stream(s):
+                step(ko)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    step(ko)
+            for _ in range(warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(steps):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / steps
+            mv_bytes = rows * rb * (144 if qtype == Q4_K else 210) + k * 4 + rows * 4
+            res["kernel_gbs" if ko else "gbs"] = round(copies * mv_bytes / (ms / 1e3) / 1e9, 1)
+            if ko:
+                res["matvec_us"] = round(ms * 1e3 / copies, 2)
+            del g
+        return res
+
+    peak, _ = measured_peak()
+    r = run(Q4_K, 17408, 5120, 6)
+    r["frac_of_peak"] = round(r["kernel_gbs"] / peak, 4)
+    out["cfg0_q4K_17408x5120"] = r
+    out["q6K_ffn_down_5120x17408"] = run(Q6_K, 5120, 17408, 4)
+    out["q6K_lm_head_248320x5120"] = run(Q6_K, 248320, 5120, 1)
+    torch.cuda.synchronize()
+    return out
 
 
 REF_TIMED_S = 10.0   # CPU seconds the reference arm's timed steps add up to
@@ -628,6 +801,7 @@ def run_reference(args, world, rank):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": ("CPU restatement of ggml's vec_dot_q4_K_q8_K in its x86 SIMD form (bit for bit the scalar "
                  "restatement); ggml itself is absent from the reference checkout"),
+        "reference_gpu": reference_gpu_leg(),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -663,6 +837,10 @@ def main():
     tp_parity = tp_parity_check(world, rank, dev, dist) if world > 1 else None
     if args.workload == "decode":
         return decode_main(args, world, rank, dev, dist, uuid, tp_parity)
+    if args.workload == "spec":
+        if world > 1:
+            raise SystemExit("--workload spec runs on one GPU")
+        return spec_main(args, dev, uuid)
 
     wl = Workload(args, dev, rank)
     # eager pass: validates the calls and warms per-kernel state before capture

@@ -146,6 +146,13 @@ M27B_API bool m27b_engine_load_blob(M27BEngine *e, const struct M27BBlob *blob, 
  * The q4_K / q6_K values have standard deviation ~ sigma. */
 M27B_API bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char *err, size_t err_cap);
 
+/* While a decode step's attention runs (the DRAM is otherwise idle then), its
+ * kernel prefetches into L2 up to `bytes` of the weights that follow: the
+ * layer's o_proj, then the first rows of gate and up in equal parts.
+ * Default 24 MiB; 0 turns it off.  Takes effect at the next graph capture
+ * (call before the first decode step). */
+M27B_API bool m27b_engine_set_l2_prefetch(M27BEngine *e, unsigned long long bytes, char *err, size_t err_cap);
+
 /* Bytes of weights this rank streams per token (its shards, as stored). */
 M27B_API size_t m27b_engine_weight_bytes_per_token(const M27BEngine *e);
 
@@ -174,6 +181,31 @@ M27B_API bool m27b_engine_decode_step(M27BEngine *e, int token, int pos, int *ne
  * all-reduce (NCCL or tp_size 1).  Synchronises before returning. */
 M27B_API bool m27b_engine_verify(M27BEngine *e, const int *tokens, int n, int pos, int *next, float *logits, char *err,
                                  size_t err_cap);
+
+/* Counters and host times of m27b_engine_speculative_generate. */
+typedef struct M27BSpecStats {
+    int iterations;    /* draft + verify rounds */
+    int proposed;      /* drafted tokens (iterations x k) */
+    int accepted;      /* drafted tokens the target's greedy choice agreed with */
+    double prefill_ms; /* feeding the prompt to both engines */
+    double draft_ms;   /* the draft's generation calls */
+    double verify_ms;  /* the target's verify passes */
+} M27BSpecStats;
+
+/* Greedy speculative decoding (the loop the reference lists as next,
+ * README.md:41-45): feeds prompt[0 .. n_prompt-2] to both engines at
+ * positions 0 .., then repeats: the draft proposes k tokens (1 <= k <
+ * M27B_VERIFY_MAX) by greedy generation on the device, the target verifies
+ * the last token and the k proposals in one pass, and the longest agreeing
+ * prefix plus the target's own next token are kept.  out_tokens receives
+ * exactly n_new tokens, the target's plain greedy continuation of the prompt
+ * (lossless).  Both engines must have tp_size 1 or use NCCL (the verify
+ * pass's all-reduce) and hold nothing else: positions from 0 are rewritten;
+ * both need n_prompt + n_new + k positions of cache.  Hybrid (DeltaNet)
+ * targets are refused by the verify pass.  stats may be NULL. */
+M27B_API bool m27b_engine_speculative_generate(M27BEngine *target, M27BEngine *draft, const int *prompt, int n_prompt,
+                                               int n_new, int k, int *out_tokens, M27BSpecStats *stats, char *err,
+                                               size_t err_cap);
 
 /* Greedy generation of n tokens on the device: step i (position pos + i)
  * consumes the token step i-1 produced (`token` for i = 0), with no host

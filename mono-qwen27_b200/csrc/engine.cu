@@ -34,6 +34,11 @@ cudaError_t attn_fused_launch(const float *qkv, const float *q_norm, const float
                               float *part, void *xq, const int *pos, int nq, int nkv, int hd, int S, float scale,
                               const float2 *rope, int n_rot, float eps, cudaStream_t st);
 cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float theta, cudaStream_t st);
+bool attn_step_supported(int hd, int G, int smax);
+cudaError_t attn_step_launch(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
+                             float *part, void *xq, const int *pos, unsigned *count, int nq, int nkv, int hd, int S,
+                             float scale, const float2 *rope, int n_rot, float eps, const void *const *pf,
+                             const unsigned long long *pf_bytes, cudaStream_t st);
 cudaError_t attn_launch(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
                         int nq, int nkv, int hd, int S, float scale, cudaStream_t st, int n_tok = 1);
 __global__ void k_fill_blocks(uint8_t *out, int type, int rows, int nblk, long row0, int blk0, uint64_t seed, int tid,
@@ -359,7 +364,28 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         else
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wqkv.v, nullptr, e->h, c.hidden, Ly.attn_norm, c.rms_eps, 1, e->xq, e->qkv,
                                        Ly.wqkv.rows, nullptr, e->st, err, err_cap));
-        if (attn_fused_supported(hd) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
+        if (e->attn_count && attn_step_supported(hd, e->G, e->S) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
+            // one launch: q/k norm + RoPE + KV append + attention + split reduce + gate + q8_K; the DRAM
+            // is idle meanwhile, so it prefetches o_proj's weights and the start of gate/up into L2
+            const void *pf[3] = {nullptr, nullptr, nullptr};
+            unsigned long long pfb[3] = {0, 0, 0};
+            unsigned long long budget = e->l2_prefetch;
+            const unsigned long long wob = (unsigned long long)stored_row_bytes(Ly.wo) * Ly.wo.rows;
+            if (budget && Ly.wo.d) {
+                pf[0] = Ly.wo.d;
+                pfb[0] = wob < budget ? wob : budget;
+                budget -= pfb[0];
+            }
+            const unsigned long long ffb = (unsigned long long)stored_row_bytes(Ly.wg) * Ly.wg.rows;
+            if (budget >= 32 && Ly.wg.d && Ly.wu.d) {
+                pf[1] = Ly.wg.d;
+                pf[2] = Ly.wu.d;
+                pfb[1] = pfb[2] = budget / 2 < ffb ? budget / 2 : ffb;
+            }
+            ECUDA(attn_step_launch(e->qkv, Ly.q_norm, Ly.k_norm, Ly.kc, Ly.vc, e->part, e->xq, pos, e->attn_count,
+                                   e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd), e->rope, c.n_rot, c.rms_eps, pf, pfb,
+                                   e->st));
+        } else if (attn_fused_supported(hd) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
             // q/k norm + RoPE + KV append + attention, then reduce + gate + q8_K for o_proj
             ECUDA(attn_fused_launch(e->qkv, Ly.q_norm, Ly.k_norm, Ly.kc, Ly.vc, e->part, e->xq, pos, e->H, e->KV, hd,
                                     e->S, 1.0f / sqrtf((float)hd), e->rope, c.n_rot, c.rms_eps, e->st));
@@ -672,7 +698,9 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
               A((void **)&e->part, VM * e->S * e->H * (hd + 4) * 4) &&
               A((void **)&e->logits, VM * e->V * 4) && A((void **)&e->xq, VM * m27b_act_bytes(M27B_TYPE_Q8_K, xmax)) &&
               A((void **)&e->best, VM * 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4) &&
-              A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2)) && A((void **)&e->vtok, VM * 4);
+              A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2)) && A((void **)&e->vtok, VM * 4) &&
+              A((void **)&e->attn_count, (size_t)e->KV * sizeof(unsigned)) &&
+              cudaMemset(e->attn_count, 0, (size_t)e->KV * sizeof(unsigned)) == cudaSuccess;
     for (int l = 0; ok && l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
         if (Ly.ssm) {
@@ -729,6 +757,14 @@ bool m27b_engine_create_sharing(const M27BEngine *src, int max_ctx, M27BEngine *
     e->lmh = src->lmh;
     e->out_norm = src->out_norm;
     *out = e;
+    if (err && err_cap) err[0] = '\0';
+    return true;
+}
+
+bool m27b_engine_set_l2_prefetch(M27BEngine *e, unsigned long long bytes, char *err, size_t err_cap) {
+    if (!e) return efail(err, err_cap, "m27b_engine_set_l2_prefetch: null engine");
+    if (e->gexec) return efail(err, err_cap, "m27b_engine_set_l2_prefetch: call it before the first decode step");
+    e->l2_prefetch = bytes;
     if (err && err_cap) err[0] = '\0';
     return true;
 }

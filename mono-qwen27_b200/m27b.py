@@ -334,6 +334,10 @@ class Partition(ctypes.Structure):
 
 QWEN27 = dict(n_layers=64, hidden=5120, ffn=17408, n_head=24, n_kv_head=4, head_dim=256, vocab=248320, n_rot=64,
               rope_theta=1e7, rms_eps=1e-6)
+# the BASELINE cfg4 draft: a 0.6B-shaped q8_0 model (hidden 1024, FFN 3072,
+# 28 layers; 16 query / 8 kv heads of 128, the target's vocabulary)
+DRAFT = dict(n_layers=28, hidden=1024, ffn=3072, n_head=16, n_kv_head=8, head_dim=128, vocab=248320, n_rot=64,
+             rope_theta=1e6, rms_eps=1e-6, weight_type=8)
 # the reference's hybrid layout (include/mono27b_config.h:43-50; every 4th layer attention)
 HYBRID = dict(attn_interval=4, ssm_d_inner=6144, ssm_d_state=128, ssm_dt_rank=48, ssm_n_group=16, ssm_conv_kern=4)
 
@@ -365,6 +369,9 @@ def _engine_lib():
         "m27b_engine_hidden": (b, [vp, vp, cp, sz]),
         "m27b_engine_stream": (vp, [vp]),
         "m27b_engine_destroy": (None, [vp]),
+        "m27b_engine_create_sharing": (b, [vp, i32, ctypes.POINTER(vp), cp, sz]),
+        "m27b_engine_set_l2_prefetch": (b, [vp, ctypes.c_ulonglong, cp, sz]),
+        "m27b_engine_speculative_generate": (b, [vp, vp, vp, i32, i32, i32, vp, ctypes.POINTER(SpecStats), cp, sz]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -420,6 +427,10 @@ class Engine:
         """Load a .m27b blob's entries of `source` (a Blob, or a path)."""
         b = blob if isinstance(blob, Blob) else Blob(blob)
         engine_load_blob(self, b, source)
+
+    def set_l2_prefetch(self, nbytes):
+        """Bytes of the following weights the attention kernel prefetches into L2 (before the first step)."""
+        self._call("m27b_engine_set_l2_prefetch", self.h, ctypes.c_ulonglong(int(nbytes)))
 
     def random_weights(self, seed=0, sigma=0.02):
         self._call("m27b_engine_random_weights", self.h, seed, ctypes.c_float(sigma))
@@ -619,31 +630,29 @@ def engine_load_blob(engine, blob, source=SOURCE_TARGET):
 # speculative decoding (draft engine + target engine, greedy)
 
 
+class SpecStats(ctypes.Structure):
+    """M27BSpecStats (include/m27b_engine.h)."""
+    _fields_ = [("iterations", ctypes.c_int), ("proposed", ctypes.c_int), ("accepted", ctypes.c_int),
+                ("prefill_ms", ctypes.c_double), ("draft_ms", ctypes.c_double), ("verify_ms", ctypes.c_double)]
+
+
 def speculative_generate(target, draft, prompt, n_new, k=7):
-    """Greedy speculative decoding: the draft proposes k tokens (device-side
-    greedy generation), the target checks them in one verify pass of k + 1
-    tokens and keeps the longest agreeing prefix plus its own next token.
-    Lossless: the result equals the target's own greedy decoding of `prompt`.
-    Both engines must start empty; returns (tokens, stats)."""
-    assert 1 <= k < M27B_VERIFY_MAX and len(prompt) >= 1
-    for pos, t in enumerate(prompt[:-1]):
-        target.decode_step(int(t), pos)
-        draft.decode_step(int(t), pos)
-    out, last, pos = [], int(prompt[-1]), len(prompt) - 1
-    iters = accepted = 0
-    while len(out) < n_new:
-        props = [int(t) for t in draft.generate(last, pos, k)]  # draft K/V at pos .. pos+k-1
-        nxt = [int(t) for t in target.verify([last] + props, pos)]  # target K/V at pos .. pos+k
-        j = 0
-        while j < k and props[j] == nxt[j]:
-            j += 1
-        if j == k:  # every proposal kept: the draft has not yet seen the last one
-            draft.decode_step(props[k - 1], pos + k)
-        out += props[:j] + [nxt[j]]
-        iters += 1
-        accepted += j
-        last, pos = nxt[j], pos + j + 1
-    return out[:n_new], dict(iterations=iters, accepted=accepted, proposed=iters * k)
+    """Greedy speculative decoding through m27b_engine_speculative_generate
+    (the loop runs in the library): the draft proposes k tokens, the target
+    verifies k + 1 in one pass and keeps the longest agreeing prefix plus its
+    own next token.  Lossless: equals the target's greedy decoding of
+    `prompt`.  Both engines must start empty; returns (tokens, stats)."""
+    import numpy as np
+    p = np.ascontiguousarray(prompt, dtype=np.int32)
+    out = np.empty(n_new, dtype=np.int32)
+    st = SpecStats()
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(_engine_lib().m27b_engine_speculative_generate(target.h, draft.h, ctypes.c_void_p(p.ctypes.data), len(p),
+                                                          int(n_new), int(k), ctypes.c_void_p(out.ctypes.data),
+                                                          ctypes.byref(st), err, ERR_CAP),
+           err, "m27b_engine_speculative_generate")
+    stats = {f: getattr(st, f) for f, _ in SpecStats._fields_}
+    return [int(t) for t in out], stats
 
 
 M27B_VERIFY_MAX = 16

@@ -1,0 +1,107 @@
+"""The reference executor's C API (include/mono27b_api.h) on the GPU, driven
+by a C++ program written the way the reference's chat driver uses it
+(tests/abi/api_driver.cpp; init_state before load_weights, logits read back
+from device memory, argmax, embed, free_weights before free_state).
+
+The model is a GGUF-style tensor table of a tiny model quantized by the
+oracle (tests/_decode_ref.py).  Checked: the inferred shape, every step's
+logits against the decode reference (the structure test_hybrid_gpu.py
+explains: most steps at fp32 rounding level, a lone step within 2e-2 where a
+q8_K code rounds the other way) and bit for
+bit against the engine loaded tensor by tensor (the same kernels), the argmax
+entry against the logits' first maximum, the embedding row bit for bit
+against the oracle's dequantization (a zero row for an out-of-range token),
+and that freed weights are refused."""
+import os
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import _decode_ref as R
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+DRIVER = os.path.join(ROOT, "tests", "abi", "api_driver.cpp")
+LIBDIR = os.path.join(ROOT, "mono-qwen27_b200", "lib")
+TOKENS = [7, 70, 700, 77, 707, 17, 170, 901]
+STEP_TOL, MEDIAN_TOL, RUN_TOL = 2e-2, 1e-5, 1e-4
+HYB = dict(R.TINY, n_layers=4, attn_interval=2, ssm_d_inner=512, ssm_d_state=128, ssm_dt_rank=4, ssm_n_group=2,
+           ssm_conv_kern=4)
+
+
+def _write_model(path, model):
+    """The tensor table and data in the driver's format; dims[0] = values per row."""
+    heads, blobs, off = [], [], 0
+    for name, (qtype, row_elems, row_count, data) in model.items():
+        b = np.ascontiguousarray(data).tobytes()
+        nd = 1 if row_count == 1 else 2
+        dims = (row_elems, row_count if nd == 2 else 0, 0, 0)
+        nb = name.encode()
+        heads.append(struct.pack("<I", len(nb)) + nb + struct.pack("<II4QQQ", qtype, nd, *dims, off, len(b)))
+        blobs.append(b)
+        off += len(b)
+    with open(path, "wb") as f:
+        f.write(b"M27T" + struct.pack("<I", len(heads)) + b"".join(heads) + b"".join(blobs))
+
+
+@pytest.fixture(scope="module")
+def driver(tmp_path_factory):
+    exe = str(tmp_path_factory.mktemp("abi") / "api_driver")
+    cmd = ["g++", "-std=c++17", "-O1", "-I", os.path.join(ROOT, "include"), "-I", "/usr/local/cuda/include", DRIVER,
+           "-o", exe, "-L", LIBDIR, "-lm27b", "-Wl,-rpath," + LIBDIR, "-L", "/usr/local/cuda/lib64", "-lcudart",
+           "-Wl,-rpath,/usr/local/cuda/lib64"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return exe
+
+
+def _engine_logits(m27b, cfg, model):
+    d = dict(m27b.QWEN27)
+    d.update(cfg)
+    e = m27b.Engine(m27b.model_config(max_ctx=32, **d))
+    try:
+        for name, (qtype, row_elems, row_count, data) in model.items():
+            e.load_tensor(name, qtype, row_elems, row_count, data)
+        return np.array([e.decode_step(t, pos, logits=True)[1] for pos, t in enumerate(TOKENS)])
+    finally:
+        e.close()
+
+
+@pytest.mark.parametrize("kind", ["attention", "hybrid"])
+def test_reference_api_decode(orc, m27b, driver, tmp_path, kind):
+    cfg = R.TINY if kind == "attention" else HYB
+    model = R.make_model(orc, cfg, seed=5)
+    path, out = str(tmp_path / "model.m27t"), str(tmp_path / "out.bin")
+    _write_model(path, model)
+    r = subprocess.run([driver, path, out, "32"] + [str(t) for t in TOKENS], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    V, H, n = cfg["vocab"], cfg["hidden"], len(TOKENS)
+    n_attn = sum(R.is_attention(cfg, l) for l in range(cfg["n_layers"]))
+    assert f"vocab {V} hidden {H} layers {cfg['n_layers']} attention {n_attn}" in r.stdout, r.stdout
+    assert "decode steps" in r.stderr  # print_timing
+    assert "decode_after_free 0 mono27b_engine_decode_step: weights not loaded" in r.stdout, r.stdout
+    raw = np.fromfile(out, dtype=np.uint8)
+    logits = raw[:n * V * 4].view(np.float32).reshape(n, V)
+    am = raw[n * V * 4:n * V * 4 + n * 4].view(np.int32)
+    emb = raw[n * V * 4 + n * 4:].view(np.float32).reshape(2, H)
+    # the same kernels as the engine's own API: identical logits
+    np.testing.assert_array_equal(logits, _engine_logits(m27b, cfg, model))
+    ref = R.RefDecoder(orc, model, cfg)
+    errs = [orc.rel_l2(logits[pos], ref.step(t, pos)[0]) for pos, t in enumerate(TOKENS)]
+    print(kind, "rel-L2 per step:", ["%.2e" % x for x in errs])
+    # an activation within fp32 rounding of a q8_K tie may take the other code
+    # on one side (both sides' fp32 sums run in different orders), moving one
+    # step's logits by up to ~1e-2; a wrong result would persist
+    assert max(errs) <= STEP_TOL, errs
+    assert float(np.median(errs)) <= MEDIAN_TOL, errs
+    assert not any(a > RUN_TOL and b > RUN_TOL for a, b in zip(errs, errs[1:])), errs
+    for pos in range(n):
+        assert am[pos] == int(np.argmax(logits[pos])), pos
+    qt, k, rows, w = model["token_embd.weight"]
+    want = orc.dequantize(qt, np.ascontiguousarray(w).reshape(rows, -1)[5:6], k).reshape(-1)
+    np.testing.assert_array_equal(emb[0], want)
+    assert not emb[1].any()
