@@ -911,6 +911,26 @@ def main():
     wl_config, wl_metric, wl_profile, wl_kernel = wl.config, wl.metric, wl.profile, wl.kernel
     wl_h2d, wl_d2h, wl_launches = wl.h2d, wl.d2h, wl.launches_per_step
 
+    # the read ceiling for launches of this size: a plain streaming read of
+    # the same bytes per launch, same rotation and graph structure
+    probe = None
+    if wl.name == "cfg0":
+        bufs = [torch.empty(wbytes(Q4_K, wl.rows, wl.k), dtype=torch.uint8, device=dev) for _ in range(wl.copies)]
+        sink = torch.zeros(4 * torch.cuda.get_device_properties(dev).multi_processor_count, dtype=torch.int32,
+                           device=dev)
+        best = None
+        for cps in (1, 2, 4):
+            fn = (lambda c: (lambda: [wl.m27b.hbm_read_probe(b, sink, c) for b in bufs]))(cps)
+            run_steps(fn, GRAPH_STEPS)
+            pms, _ = timed(fn, args.steps, warm)
+            us = pms * 1e3 / (args.steps * wl.copies)
+            gbs = bufs[0].numel() / (us * 1e-6) / 1e9
+            if best is None or gbs > best["gbs"]:
+                best = {"gbs": round(gbs, 1), "launch_us": round(us, 3), "ctas_per_sm": cps}
+        probe = dict(best, bytes_per_launch=bufs[0].numel(), kernel="m27b_hbm_read_probe (16-byte streaming loads)")
+        del bufs
+        graphs.clear()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and wl.name == "cfg0":
         gbs, reps, threads, isa = cpu_oracle_gbs(wl.host_w0, wl.k, 10.0)
@@ -936,7 +956,9 @@ def main():
             "config": cfg,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": ncu_traffic_per_launch(wl_profile),
-                         "kernel": wl_kernel, "mean_launch_us": round(kern_us, 3), "peak_kind": peak_kind},
+                         "kernel": wl_kernel, "mean_launch_us": round(kern_us, 3), "peak_kind": peak_kind,
+                         "read_probe": probe,
+                         "frac_of_read_probe": round(achieved / probe["gbs"], 4) if probe else None},
             "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": wl_h2d, "d2h_bytes_per_step": wl_d2h},
             "gpu_launches": wl_launches * args.steps,
             "clocks": clocks,

@@ -160,10 +160,11 @@ M27B_API bool m27b_qmv_argmax(const struct WeightView *w, const void *xq, int n_
 /* fp32 activations in, like the reference's l_mv_quant(W, x, y)
  * (src/mono27b_executor.cu:2033-2050, its quantizer k_quant_q8_1 :84-107):
  * x rows (n_tok of them, stride ldx floats) are quantized to q8_K / q8_0 and
- * multiplied, y = W.x (+ residual).  For a q4_K, q5_K or IQ4_XS matrix and
- * up to 4 tokens (x 16-byte aligned, ldx a multiple of 4) the matvec kernel
- * quantizes the rows in its own prologue (one launch, same codes as
- * m27b_act_quant); otherwise the rows are first quantized into xq_scratch
+ * multiplied, y = W.x (+ residual).  For a q4_K, q5_K, IQ4_XS or (repacked)
+ * q6_K matrix and up to 4 tokens (x 16-byte aligned, ldx a multiple of 4)
+ * the matvec kernel quantizes the rows in its own prologue (one launch, same
+ * codes as m27b_act_quant; with m27b_qmv_f32_rmsnorm not for q6_K);
+ * otherwise the rows are first quantized into xq_scratch
  * (n_tok * m27b_act_bytes(m27b_act_type_for(type), k) bytes; may be NULL on
  * the one-launch path).  f16 / f32 matrices multiply the fp32 rows directly
  * (x 16-byte aligned, ldx a multiple of 4; the f16 path rounds x to fp16
@@ -185,6 +186,14 @@ M27B_API bool m27b_qmv_f32_rmsnorm(const struct WeightView *w, const struct Weig
  * (the reference embed zeroes the hidden state for such tokens). */
 M27B_API bool m27b_dequant_rows(const struct WeightView *w, const int32_t *rows, int n, float *out, int ldo,
                        cudaStream_t stream, char *err, size_t err_cap);
+
+/* Measurement support (no counterpart in the reference): stream `bytes`
+ * (16-byte aligned, a multiple of 16) from device memory p with plain 16-byte
+ * loads on ctas_per_sm x SM-count CTAs of 512 threads, folding the data into
+ * sink[CTA] (one word per CTA, xor-accumulated).  The time of one launch is
+ * the read ceiling a weight-streaming launch of that size can reach. */
+M27B_API bool m27b_hbm_read_probe(const void *p, size_t bytes, unsigned *sink, int ctas_per_sm, cudaStream_t stream,
+                                  char *err, size_t err_cap);
 
 /* Packed argmax key helpers (host side). */
 static inline int64_t m27b_argmax_key_index(unsigned long long key) {

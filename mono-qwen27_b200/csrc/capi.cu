@@ -222,9 +222,11 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         return ok(err, cap);
     }
     const bool kblk = d0.kind == W_Q4K || d0.kind == W_Q5K || d0.kind == W_IQ4XS;
-    if (xa && (!kblk || n_tok > 4 || !xa->xf || ((uintptr_t)xa->xf & 15) || (xa->ldxf & 3)))
+    const bool q6_prologue = d0.kind == W_Q6KP && xa && !xa->norm_on;  // q6_K: plain quantization only
+    if (xa && (!(kblk || q6_prologue) || n_tok > 4 || !xa->xf || ((uintptr_t)xa->xf & 15) || (xa->ldxf & 3)))
         return fail(err, cap,
-                    "%s: in-kernel quantization needs q4_K / q5_K / IQ4_XS weights, <= 4 tokens, 16-byte aligned rows",
+                    "%s: in-kernel quantization needs q4_K / q5_K / IQ4_XS (or, without RMSNorm, q6_K) weights, "
+                    "<= 4 tokens, 16-byte aligned rows",
                     what);
     if (epi == EPI_PUSH) {
         if (!push || push->npeers < 1 || push->npeers > M27B_MAX_PEERS || !push->epoch_base)
@@ -292,7 +294,15 @@ namespace m27b {
 // Matvec whose rows go to every rank's receive window (fused all-reduce,
 // producer side); used by the tensor-parallel decode engine.
 bool qmv_push(const WeightView *w, const void *xq, const float *residual, const PushArgs &push, cudaStream_t stream,
-              char *err, size_t cap) {
+              char *err, size_t cap, const float *xf) {
+    if (xf) {
+        // fp32 activations quantized in the kernel's prologue (one row of k values)
+        const uint32_t base = w ? (w->ggml_type & M27B_TYPE_MASK) : 0;
+        const int k = w ? (int)w->row_blocks * block_elems(base) : 0;
+        XArgs xa{xf, k, 0, nullptr, 0.0f};
+        return qmv_common(EPI_PUSH, w, nullptr, nullptr, 1, nullptr, (int)(w ? w->row_count : 0), residual, nullptr, 0,
+                          stream, err, cap, "qmv_push", &push, &xa);
+    }
     return qmv_common(EPI_PUSH, w, nullptr, xq, 1, nullptr, (int)(w ? w->row_count : 0), residual, nullptr, 0, stream,
                       err, cap, "qmv_push", &push);
 }
@@ -405,7 +415,8 @@ static bool qmv_f32_common(const WeightView *w, const WeightView *w_up, const fl
                           &xa);
     }
     const bool kblk = w->ggml_type == M27B_TYPE_Q4_K || w->ggml_type == M27B_TYPE_Q5_K ||
-                      w->ggml_type == M27B_TYPE_IQ4_XS;
+                      w->ggml_type == M27B_TYPE_IQ4_XS ||
+                      (w->ggml_type == (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) && !norm_on);
     if (kblk && n_tok >= 1 && n_tok <= 4 && ((uintptr_t)x & 15) == 0 && (ldx & 3) == 0) {
         XArgs xa{x, ldx, norm_on, norm_w, eps};
         return qmv_common(epi, w, w_up, nullptr, n_tok, y, ldy, residual, nullptr, 0, stream, err, cap, what, nullptr,

@@ -53,7 +53,7 @@ struct BestExchange {
 };
 __global__ void k_advance_p2p(unsigned long long *best, int *ctl, int *hist, int cap, BestExchange b);
 bool qmv_push(const WeightView *w, const void *xq, const float *residual, const PushArgs &push, cudaStream_t stream,
-              char *err, size_t cap);
+              char *err, size_t cap, const float *xf = nullptr);
 // Gated DeltaNet block (ssm.cu)
 cudaError_t ssm_rmsnorm_launch(const float *x, const float *w, float eps, int n, float *y, cudaStream_t st);
 cudaError_t ssm_conv_launch(const float *x, const float *w, float *cstate, float *out, const float *ba,
@@ -355,8 +355,7 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
             ECALL(mv(e, Ly.wso, e->xq, e->h2, e->h, err, err_cap));
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
                                        nullptr, e->st, err, err_cap));
-            ECALL(m27b_act_quant(e->a, e->F, 1, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
-            ECALL(mv(e, Ly.wd, e->xq, e->h, e->h2, err, err_cap));
+            ECALL(m27b_qmv_f32(&Ly.wd.v, e->a, e->F, 1, e->xq, e->h, Ly.wd.rows, e->h2, e->st, err, err_cap));
             continue;
         }
         if (p2p)
@@ -409,15 +408,17 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
                                        nullptr, e->st, err, err_cap));
         }
-        ECALL(m27b_act_quant(e->a, e->F, 1, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
         // down partial (+ residual on rank 0), summed over ranks -> h, then the
-        // next layer's input RMSNorm (the output norm after the last layer) -> xq
+        // next layer's input RMSNorm (the output norm after the last layer) -> xq;
+        // the down kernel quantizes silu(gate) * up in its own prologue
         const float *next_norm = l + 1 < c.n_layers ? e->L[l + 1].attn_norm : e->out_norm;
         if (p2p) {
-            ECALL(qmv_push(&Ly.wd.v, e->xq, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), e->st, err, err_cap));
+            ECALL(qmv_push(&Ly.wd.v, nullptr, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), e->st, err, err_cap,
+                           e->a));
             ECALL(consume(e, 1, 2u * l + 1u, next_norm, e->h, err, err_cap));
         } else {
-            ECALL(mv(e, Ly.wd, e->xq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
+            ECALL(m27b_qmv_f32(&Ly.wd.v, e->a, e->F, 1, e->xq, e->h, Ly.wd.rows, r0 ? e->h2 : nullptr, e->st, err,
+                               err_cap));
             ECALL(allreduce_hidden(e, e->h, err, err_cap));
         }
     }

@@ -551,6 +551,15 @@ struct AttnStepArgs {
     unsigned long long pf_bytes[3];
 };
 
+// 16 bytes global -> shared without a register round trip (L2 only).
+M27B_DI void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+// This thread's asynchronous copies have landed.
+M27B_DI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 M27B_DI void l2_prefetch(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -634,20 +643,21 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
     for (int c0 = p0; c0 < p1; c0 += CH) {
         const int n = p1 - c0 < CH ? p1 - c0 : CH;
         __syncthreads();  // the previous chunk is consumed; q and the new row are ready
+        // every 16-byte piece of the chunk's K and V rows as an asynchronous
+        // copy (all of a thread's pieces in flight at once), the new row from
+        // shared memory
         for (int idx = t; idx < n * Q4; idx += 256) {
             const int p = idx / Q4, c4 = idx - p * Q4, pp = c0 + p;
-            float4 kv4, vv4;
             if (pp == pos) {
-                kv4 = reinterpret_cast<const float4 *>(kn)[c4];
-                vv4 = reinterpret_cast<const float4 *>(kn + hd)[c4];
+                reinterpret_cast<float4 *>(ks + p * hd)[c4] = reinterpret_cast<const float4 *>(kn)[c4];
+                reinterpret_cast<float4 *>(vs + p * hd)[c4] = reinterpret_cast<const float4 *>(kn + hd)[c4];
             } else {
-                const size_t o = ((size_t)pp * nkv + j) * hd;
-                kv4 = reinterpret_cast<const float4 *>(a.kc + o)[c4];
-                vv4 = reinterpret_cast<const float4 *>(a.vc + o)[c4];
+                const size_t o = ((size_t)pp * nkv + j) * hd + 4 * c4;
+                cp_async16(ks + p * hd + 4 * c4, a.kc + o);
+                cp_async16(vs + p * hd + 4 * c4, a.vc + o);
             }
-            reinterpret_cast<float4 *>(ks + p * hd)[c4] = kv4;
-            reinterpret_cast<float4 *>(vs + p * hd)[c4] = vv4;
         }
+        cp_async_wait_all();
         __syncthreads();
         for (int p = warp; p < n; p += 8) {
             float kv[DPL];
@@ -688,16 +698,20 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
             }
         }
         __syncthreads();
+        // P.V: the thread's outputs advance together, one position at a time
+        // (independent chains; heads past G read head 0's weights, unused)
+        int wofs[NO], vofs[NO];
 #pragma unroll
         for (int i = 0; i < NO; ++i) {
-            const int o = t + 256 * i;
-            if (o < G * hd) {
-                const int g = o / hd, d = o - g * hd;
-                float x = acc[i] * ha[g];
-                const float *w = sc + g * CH;
-                for (int p = 0; p < n; ++p) x = fmaf(w[p], vs[p * hd + d], x);
-                acc[i] = x;
-            }
+            const int o = t + 256 * i, g = o < G * hd ? o / hd : 0;
+            wofs[i] = g * CH;
+            vofs[i] = o - (o / hd) * hd;
+            acc[i] *= ha[g];
+        }
+#pragma unroll 4
+        for (int p = 0; p < n; ++p) {
+#pragma unroll
+            for (int i = 0; i < NO; ++i) acc[i] = fmaf(sc[wofs[i] + p], vs[p * hd + vofs[i]], acc[i]);
         }
     }
     // this split's partial record per head

@@ -27,12 +27,14 @@ static cudaError_t run_q6t(const QmvArgs &a, int sm_count, cudaStream_t st) {
     }
     const long groups = (a.rows + 7) / 8;
     const int P = (a.rb + 3) / 4;
-    // two resident CTAs per SM by construction (shared memory <= 112 KB each)
-    const long slots = (long)sm_count * 2;
+    // two resident CTAs per SM (shared memory <= 112 KB each), or one for
+    // shapes whose staged activations leave two CTAs too few warps
+    const long slots = (long)sm_count * q6t_ctas_per_sm(a.k, NT);
     int split, nthreads;
     long grid;
     size_t smem;
-    if (2 * groups >= slots * nw || P < 2) {
+    const bool one_per_sm = q6t_ctas_per_sm(a.k, NT) == 1;
+    if (P < 2 || (one_per_sm ? groups >= 4 * slots * nw : 2 * groups >= slots * nw)) {
         // every warp streams whole row groups
         split = 1;
         const long max_warps = slots * nw;

@@ -37,17 +37,27 @@ constexpr int Q6T_STAGES = 2;
 constexpr int Q6T_WARPS = 8;             // most warps per CTA
 constexpr int Q6T_XREC = 288;            // per (token, block): 8 lo chunks | 8 hi chunks | 8 bsum pairs
 constexpr size_t Q6T_SMEM_MAX = 112 * 1024;  // two CTAs per SM
+// With several tokens and long rows (ffn_down: 4 tokens x 17408 values of
+// staged activations = 79 KB) two CTAs per SM would leave room for too few
+// warps; such shapes run one CTA per SM with up to this much.
+constexpr size_t Q6T_SMEM_BIG = 220 * 1024;
+constexpr int Q6T_MIN_WARPS = 4;
 
 inline size_t q6t_x_bytes(int k, int nt) { return (size_t)nt * ((size_t)k / 256) * (Q6T_XREC + 4); }
 constexpr size_t Q6T_WARP_BYTES = (size_t)Q6T_STAGES * Q6T_ITEM + (size_t)Q6T_STAGES * 8;
 // partial sums for the cooperative split: [warps][8 rows][2 matrices][NT]
 inline size_t q6t_part_bytes(int nt) { return (size_t)Q6T_WARPS * 8 * 2 * nt * 4; }
 
-inline int q6t_warps(int k, int nt) {
+inline int q6t_warps_within(int k, int nt, size_t limit) {
     const size_t fixed = q6t_x_bytes(k, nt) + q6t_part_bytes(nt) + 32;
-    if (fixed >= Q6T_SMEM_MAX) return 0;
-    const size_t w = (Q6T_SMEM_MAX - fixed) / Q6T_WARP_BYTES;
+    if (fixed >= limit) return 0;
+    const size_t w = (limit - fixed) / Q6T_WARP_BYTES;
     return (int)(w < (size_t)Q6T_WARPS ? w : (size_t)Q6T_WARPS);
+}
+// CTAs per SM for a shape: 2 within Q6T_SMEM_MAX, else 1 within Q6T_SMEM_BIG.
+inline int q6t_ctas_per_sm(int k, int nt) { return q6t_warps_within(k, nt, Q6T_SMEM_MAX) >= Q6T_MIN_WARPS ? 2 : 1; }
+inline int q6t_warps(int k, int nt) {
+    return q6t_warps_within(k, nt, q6t_ctas_per_sm(k, nt) == 2 ? Q6T_SMEM_MAX : Q6T_SMEM_BIG);
 }
 inline size_t q6t_smem_bytes(int k, int nt) {
     return (size_t)q6t_warps(k, nt) * Q6T_WARP_BYTES + q6t_x_bytes(k, nt) + q6t_part_bytes(nt) + 32;
@@ -61,6 +71,7 @@ M27B_DI void stage_x_q6t(const QmvArgs &a, uint8_t *xrec, float *xd) {
     const uint8_t *src = (const uint8_t *)a.xq;  // NT*nb blocks of 292 bytes
     // codes: 64 words per block; word w of chunk c (lo/hi) comes from element
     // e_lo(c) (+64 for hi) + 4w
+#pragma unroll 8
     for (int i = threadIdx.x; i < NT * nb * 64; i += blockDim.x) {
         const int blk = i >> 6, r = i & 63;
         const int hi = r >> 5, c = (r >> 2) & 7, w = r & 3;
@@ -78,6 +89,55 @@ M27B_DI void stage_x_q6t(const QmvArgs &a, uint8_t *xrec, float *xd) {
                 (uint32_t)(uint16_t)bs[g] | ((uint32_t)(uint16_t)bs[g + 4] << 16);
         } else {
             xd[blk] = *(const float *)sb;
+        }
+    }
+}
+
+// The same records built from fp32 activations (the fused quantize + matvec
+// entries, e.g. ffn_down's input silu(gate) * up): warp w quantizes blocks
+// w, w + nwarps, ... of the NT rows with the shared q8_K warp routine (the
+// codes, group sums and scale m27b_act_quant writes), QX_REGS blocks' loads
+// in flight before any arithmetic.  Lane l holds values 8l .. 8l+7 of a
+// block: they land in chunk c (below) at word offset ((8l >> 2) & 3); the
+// 16-value group l/2 sum goes to bsum pair word j, half h.
+template <int NT>
+M27B_DI void quant_x_q6t(const QmvArgs &a, uint8_t *xrec, float *xd) {
+    const int nb = a.k / 256;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int e = 8 * lane;
+    const int c = 4 * (e >> 7) + 2 * ((e >> 5) & 1) + ((e >> 4) & 1);
+    const int word = ((e >> 6) & 1) * 32 + c * 4 + ((e >> 2) & 3);
+    const int m = lane >> 1;
+    const int bj = 4 * (m >> 3) + 2 * ((m >> 1) & 1) + (m & 1), bh = (m >> 2) & 1;
+    const int total = NT * nb;
+    for (int i0 = warp; i0 < total; i0 += nw * QX_REGS) {
+        float v[QX_REGS][8];
+#pragma unroll
+        for (int r = 0; r < QX_REGS; ++r) {
+            const int i = i0 + r * nw;
+            if (i < total) {
+                const int t = i / nb, b = i - t * nb;
+                const float4 *xr = (const float4 *)(a.xf + (size_t)t * a.ldxf + b * 256 + lane * 8);
+                const float4 p0 = xr[0], p1 = xr[1];
+                v[r][0] = p0.x; v[r][1] = p0.y; v[r][2] = p0.z; v[r][3] = p0.w;
+                v[r][4] = p1.x; v[r][5] = p1.y; v[r][6] = p1.z; v[r][7] = p1.w;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < QX_REGS; ++r) {
+            const int i = i0 + r * nw;
+            if (i < total) {
+                uint32_t packed[2];
+                int sum;
+                float d;
+                quant_q8K_lane(v[r], lane, packed, sum, d);
+                uint8_t *rec = xrec + (size_t)i * Q6T_XREC;
+                ((uint32_t *)rec)[word] = packed[0];
+                ((uint32_t *)rec)[word + 1] = packed[1];
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                if ((lane & 1) == 0) ((int16_t *)(rec + 256 + 4 * bj))[bh] = (int16_t)sum;
+                if (lane == 0) xd[i] = d;
+            }
         }
     }
 }
@@ -142,7 +202,10 @@ __global__ void __launch_bounds__(Q6T_WARPS * 32, 2)
     // the weights are not produced by the previous kernel: their copies are
     // already in flight; the activations (and every global write) wait for it
     pdl_wait();
-    stage_x_q6t<NT>(a, xrec, xd);
+    if (a.xf)
+        quant_x_q6t<NT>(a, xrec, xd);
+    else
+        stage_x_q6t<NT>(a, xrec, xd);
     pdl_trigger();
     __syncthreads();
 

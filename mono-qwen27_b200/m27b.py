@@ -63,6 +63,7 @@ def lib():
         "m27b_qmv_f32": (b, [wvp, vp, i32, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_qmv_f32_rmsnorm": (b, [wvp, wvp, vp, i32, vp, fp, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
+        "m27b_hbm_read_probe": (b, [vp, sz, vp, i32, vp, cp, sz]),
         "m27b_allreduce_norm_quant": (b, [vp, i32, i32, vp, vp, vp, fp, i32, vp, vp, ctypes.c_ulonglong, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
@@ -188,6 +189,13 @@ def allreduce_norm_quant(words, nsrc, src_stride, ss_words, epoch, k, x_out, xq,
                                          _stream(stream), err, ERR_CAP)
     _check(ok, err, "m27b_allreduce_norm_quant")
     return xq
+
+
+def hbm_read_probe(buf, sink, ctas_per_sm=2, stream=None):
+    """One streaming read of the device tensor `buf` (see m27b_hbm_read_probe)."""
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(lib().m27b_hbm_read_probe(_ptr(buf), buf.numel() * buf.element_size(), _ptr(sink), ctas_per_sm,
+                                     _stream(stream), err, ERR_CAP), err, "m27b_hbm_read_probe")
 
 
 def act_quant_swiglu(gate, up, act_type, out=None, stream=None):

@@ -1,7 +1,7 @@
 """Matvecs from fp32 activations (m27b_qmv_f32 / m27b_qmv_f32_rmsnorm): the
-q4_K kernel quantizes its rows in the prologue with the same q8_K routine as
-m27b_act_quant, so the one-launch path must equal act_quant + qmv bit for
-bit; the RMSNorm variants are compared with the oracle (RMSNorm in fp32 +
+q4_K kernel (and, without RMSNorm, the q6_K kernel) quantizes its rows in
+the prologue with the same q8_K routine as m27b_act_quant, so the one-launch
+path must equal act_quant + qmv bit for bit; the RMSNorm variants are compared with the oracle (RMSNorm in fp32 +
 ggml q8_K + vec_dot) at the matvec tolerance, and the two-launch path (other
 weight types, more tokens) with the same entry's one-launch result."""
 import numpy as np
@@ -32,6 +32,22 @@ def test_qmv_f32_equals_separate_quant(torch, orc, m27b, rows, k, n):
     assert torch.equal(got, want)
 
 
+@pytest.mark.parametrize("rows,k,n", [(5120, 17408, 1), (333, 2048, 2), (77, 256, 4), (1000, 17408, 3)])
+def test_qmv_f32_q6K_equals_separate_quant(torch, orc, m27b, rows, k, n):
+    """ffn_down's shape (5120 x 17408) among them: the q6_K kernel's own
+    quantizing prologue gives act_quant + qmv's result bit for bit."""
+    w, W = _w(orc, m27b, Q6_K, rows, k, rows + k + 7)
+    x = torch.from_numpy(D.gauss_act(n, k, 5 + n)).cuda()
+    res = torch.from_numpy(D.gauss_act(n, rows, 6)).cuda()
+    want = torch.empty((n, rows), device="cuda")
+    m27b.qmv(W, m27b.act_quant(x, Q8_K), n, want, residual=res)
+    got = torch.full((n, rows), float("nan"), device="cuda")
+    m27b.qmv_f32(W, x, n, got, residual=res)
+    assert torch.equal(got, want)
+    assert orc.rel_l2(got.cpu().numpy() - res.cpu().numpy(),
+                      orc.matvec(Q6_K, w, k, orc.quantize_q8_K(x.cpu().numpy()))) <= TOL
+
+
 @pytest.mark.parametrize("n", [1, 3])
 def test_qmv_f32_rmsnorm(torch, orc, m27b, n):
     rows, k = 700, 5120
@@ -57,7 +73,7 @@ def test_qmv_f32_rmsnorm_swiglu(torch, orc, m27b):
     assert orc.rel_l2(got.cpu().numpy(), want) <= TOL
 
 
-@pytest.mark.parametrize("qtype,n", [(Q6_K, 1), (Q8_0, 2), (Q4_K, 8)])
+@pytest.mark.parametrize("qtype,n", [(Q6_K, 5), (Q8_0, 2), (Q4_K, 8)])
 def test_qmv_f32_two_launch_path(torch, orc, m27b, qtype, n):
     rows, k = 333, 2048
     w, W = _w(orc, m27b, qtype, rows, k, 31)
