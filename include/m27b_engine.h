@@ -146,13 +146,6 @@ M27B_API bool m27b_engine_load_blob(M27BEngine *e, const struct M27BBlob *blob, 
  * The q4_K / q6_K values have standard deviation ~ sigma. */
 M27B_API bool m27b_engine_random_weights(M27BEngine *e, uint64_t seed, float sigma, char *err, size_t err_cap);
 
-/* While a decode step's attention runs (the DRAM is otherwise idle then), its
- * kernel prefetches into L2 up to `bytes` of the weights that follow: the
- * layer's o_proj, then the first rows of gate and up in equal parts.
- * Default 24 MiB; 0 turns it off.  Takes effect at the next graph capture
- * (call before the first decode step). */
-M27B_API bool m27b_engine_set_l2_prefetch(M27BEngine *e, unsigned long long bytes, char *err, size_t err_cap);
-
 /* Bytes of weights this rank streams per token (its shards, as stored). */
 M27B_API size_t m27b_engine_weight_bytes_per_token(const M27BEngine *e);
 

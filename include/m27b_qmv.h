@@ -157,6 +157,23 @@ M27B_API bool m27b_qmv_argmax(const struct WeightView *w, const void *xq, int n_
                      unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
                      size_t err_cap);
 
+/* q6_K matvec for 5..16 tokens with the K dimension split across CTAs: the
+ * speculative verify pass's ffn_down (5120 x 17408), where the one-pass
+ * kernel's staged activations (8 tokens x 17408 values) crowd out its weight
+ * stages.  Same result semantics as m27b_qmv (per-range partial sums added
+ * in range order; within fp32 rounding of the one-pass kernel).  Needs the
+ * repacked q6_K layout and rows of at least 32 blocks; the caller passes
+ * m27b_qmv_q6k_ksplit_part_bytes scratch for partial sums and
+ * m27b_qmv_q6k_ksplit_count_bytes of counters that must be zero before the
+ * first call (each call leaves them zero).  Calls overlapping on the GPU
+ * with the same scratch race.  The reference runs this product token by
+ * token (k_q6k_mv_q8_dp4a, src/mono27b_executor.cu:630-645). */
+M27B_API size_t m27b_qmv_q6k_ksplit_part_bytes(const struct WeightView *w);
+M27B_API size_t m27b_qmv_q6k_ksplit_count_bytes(const struct WeightView *w);
+M27B_API bool m27b_qmv_q6k_ksplit(const struct WeightView *w, const void *xq, int n_tok, float *y, int ldy,
+                                  const float *residual, void *part, void *count, cudaStream_t stream, char *err,
+                                  size_t err_cap);
+
 /* fp32 activations in, like the reference's l_mv_quant(W, x, y)
  * (src/mono27b_executor.cu:2033-2050, its quantizer k_quant_q8_1 :84-107):
  * x rows (n_tok of them, stride ldx floats) are quantized to q8_K / q8_0 and
@@ -188,12 +205,12 @@ M27B_API bool m27b_dequant_rows(const struct WeightView *w, const int32_t *rows,
                        cudaStream_t stream, char *err, size_t err_cap);
 
 /* Measurement support (no counterpart in the reference): stream `bytes`
- * (16-byte aligned, a multiple of 16) from device memory p with plain 16-byte
- * loads on ctas_per_sm x SM-count CTAs of 512 threads, folding the data into
- * sink[CTA] (one word per CTA, xor-accumulated).  The time of one launch is
- * the read ceiling a weight-streaming launch of that size can reach. */
-M27B_API bool m27b_hbm_read_probe(const void *p, size_t bytes, unsigned *sink, int ctas_per_sm, cudaStream_t stream,
-                                  char *err, size_t err_cap);
+ * (16-byte aligned, a multiple of 16) from device memory p into shared memory
+ * with bulk asynchronous copies on one CTA per SM (six 32 KB copies in
+ * flight each), nothing computed.  The time of one launch is the read
+ * ceiling a weight-streaming launch of that size can reach.  A wait that
+ * runs out records status 6 (m27b_device_status). */
+M27B_API bool m27b_hbm_read_probe(const void *p, size_t bytes, cudaStream_t stream, char *err, size_t err_cap);
 
 /* Packed argmax key helpers (host side). */
 static inline int64_t m27b_argmax_key_index(unsigned long long key) {

@@ -179,9 +179,16 @@ struct XArgs {
     float eps;
 };
 
+// The SwiGLU rows also written as q8_K blocks (one token; the next matvec's input).
+struct Q8Out {
+    void *q8;
+    unsigned *cnt;  // one zeroed word per 256-row block
+};
+
 bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void *xq, int n_tok, float *y, int ldy,
                 const float *residual, unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
-                size_t cap, const char *what, const PushArgs *push = nullptr, const XArgs *xa = nullptr) {
+                size_t cap, const char *what, const PushArgs *push = nullptr, const XArgs *xa = nullptr,
+                const Q8Out *qo = nullptr) {
     WDesc d0{}, d1{};
     if (!describe(w0, d0, what, err, cap)) return false;
     if (epi == EPI_SWIGLU) {
@@ -255,6 +262,10 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
     }
     // 5..16 tokens of a q4_K matrix: one pass on the tensor cores
+    if (qo && (epi != EPI_SWIGLU || n_tok != 1 || (d0.kind != W_Q4K && d0.kind != W_Q5K && d0.kind != W_IQ4XS) ||
+               (w0->row_count % 256) != 0 || !qo->q8 || !qo->cnt || ((uintptr_t)qo->q8 & 3)))
+        return fail(err, cap, "%s: the q8_K epilogue takes one token of a 256-value k-quant SwiGLU, rows a multiple "
+                              "of 256", what);
     const bool mma = !xa && d0.kind == W_Q4K && epi == EPI_STORE && q4k_mma_supported((int)w0->row_blocks, n_tok);
     for (int t0 = 0; t0 < n_tok; t0 += 4) {
         const int nt = mma ? n_tok : (n_tok - t0 < 4 ? n_tok - t0 : 4);
@@ -281,6 +292,10 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
         a.row_offset = row_offset;
         a.status = status;
         if (push) a.push = *push;
+        if (qo) {
+            a.q8out = qo->q8;
+            a.q8cnt = qo->cnt;
+        }
         cudaError_t e = mma ? launch_q4k_mma(a, nt, sms, stream) : launch_qmv(d0.kind, epi, a, nt, sms, stream);
         if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
         if (mma) break;
@@ -291,6 +306,64 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
 }  // namespace
 
 namespace m27b {
+int q6k_ksplit_ranges(int rb);
+size_t q6k_ksplit_part_floats(int rows, int ks);
+cudaError_t launch_q6k_ksplit(const QmvArgs &a_in, int n_tok, float *part, unsigned *count, int sm_count,
+                              cudaStream_t st);
+
+// q6_K x 5..16 tokens with the K dimension split across CTAs (the verify
+// pass's ffn_down): part holds q6k_ksplit_part_floats(rows, ranges) floats,
+// count one zeroed word per 8-row group; 8 tokens per launch.
+bool qmv_q6k_ksplit(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                    float *part, unsigned *count, cudaStream_t stream, char *err, size_t cap) {
+    const char *what = "qmv_q6k_ksplit";
+    WDesc d{};
+    if (!describe(w, d, what, err, cap)) return false;
+    if (d.kind != W_Q6KP) return fail(err, cap, "%s: repacked q6_K weights only", what);
+    if (!xq || !y || !part || !count) return fail(err, cap, "%s: null pointer", what);
+    if (n_tok < 1 || n_tok > M27B_MAX_TOKENS) return fail(err, cap, "%s: bad token count %d", what, n_tok);
+    if (q6k_ksplit_ranges((int)w->row_blocks) == 0) return fail(err, cap, "%s: rows too short to split", what);
+    const int sms = sm_count_current();
+    int *status = status_ptr_current();
+    if (sms <= 0 || !status) return fail(err, cap, "%s: no CUDA device", what);
+    const size_t xb = act_bytes(M27B_TYPE_Q8_K, d.k);
+    for (int t0 = 0; t0 < n_tok; t0 += 8) {
+        const int nt = n_tok - t0 < 8 ? n_tok - t0 : 8;
+        QmvArgs a{};
+        a.w0 = (const uint8_t *)w->ptr;
+        a.xq = (const uint8_t *)xq + (size_t)t0 * xb;
+        a.y = y + (size_t)t0 * ldy;
+        a.residual = residual ? residual + (size_t)t0 * ldy : nullptr;
+        a.row_stride = d.row_stride;
+        a.ldy = ldy;
+        a.rows = (int)w->row_count;
+        a.rb = (int)w->row_blocks;
+        a.k = d.k;
+        a.status = status;
+        const cudaError_t e = launch_q6k_ksplit(a, nt, part, count, sms, stream);
+        if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
+    }
+    return ok(err, cap);
+}
+
+// Gate/up SwiGLU of one token whose epilogue also writes the rows as q8_K
+// blocks into q8out (the down projection's input), from q8_K activations xq,
+// or from fp32 rows xf RMSNormed with norm_w / eps in the kernel's prologue.
+bool qmv_swiglu_q8(const WeightView *gate, const WeightView *up, const void *xq, const float *xf, const float *norm_w,
+                   float eps, float *y, void *q8out, unsigned *q8cnt, cudaStream_t stream, char *err, size_t cap) {
+    const Q8Out qo{q8out, q8cnt};
+    const int rows = gate ? (int)gate->row_count : 0;
+    if (xf) {
+        const uint32_t base = gate ? (gate->ggml_type & M27B_TYPE_MASK) : 0;
+        const int k = gate ? (int)gate->row_blocks * block_elems(base) : 0;
+        XArgs xa{xf, k, 1, norm_w, eps};
+        return qmv_common(EPI_SWIGLU, gate, up, nullptr, 1, y, rows, nullptr, nullptr, 0, stream, err, cap,
+                          "qmv_swiglu_q8", nullptr, &xa, &qo);
+    }
+    return qmv_common(EPI_SWIGLU, gate, up, xq, 1, y, rows, nullptr, nullptr, 0, stream, err, cap, "qmv_swiglu_q8",
+                      nullptr, nullptr, &qo);
+}
+
 // Matvec whose rows go to every rank's receive window (fused all-reduce,
 // producer side); used by the tensor-parallel decode engine.
 bool qmv_push(const WeightView *w, const void *xq, const float *residual, const PushArgs &push, cudaStream_t stream,
@@ -494,6 +567,26 @@ bool m27b_allreduce_norm_quant(const void *words, int nsrc, int src_stride, void
     a.wait_ns = wait_ns;
     if (!a.status) return fail(err, err_cap, "%s: cannot resolve the device status word", what);
     return cuda_ok(launch_act_quant(M27B_TYPE_Q8_K, ACT_RMSNORM_SUM, a, 1, stream), what, err, err_cap);
+}
+
+size_t m27b_qmv_q6k_ksplit_part_bytes(const WeightView *w) {
+    if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
+    const int ks = q6k_ksplit_ranges((int)w->row_blocks);
+    return ks ? q6k_ksplit_part_floats((int)w->row_count, ks) * sizeof(float) : 0;
+}
+
+size_t m27b_qmv_q6k_ksplit_count_bytes(const WeightView *w) {
+    if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
+    return q6k_ksplit_ranges((int)w->row_blocks) ? (size_t)((w->row_count + 7) / 8) * sizeof(unsigned) : 0;
+}
+
+bool m27b_qmv_q6k_ksplit(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                         void *part, void *count, cudaStream_t stream, char *err, size_t err_cap) {
+    if (((uintptr_t)part & 15) || ((uintptr_t)count & 3))
+        return fail(err, err_cap, "m27b_qmv_q6k_ksplit: misaligned scratch");
+    if (w && n_tok > 1 && ldy < (int)w->row_count)
+        return fail(err, err_cap, "m27b_qmv_q6k_ksplit: ldy (%d) < row_count (%u)", ldy, w->row_count);
+    return qmv_q6k_ksplit(w, xq, n_tok, y, ldy, residual, (float *)part, (unsigned *)count, stream, err, err_cap);
 }
 
 }  // extern "C"

@@ -34,11 +34,11 @@ cudaError_t attn_fused_launch(const float *qkv, const float *q_norm, const float
                               float *part, void *xq, const int *pos, int nq, int nkv, int hd, int S, float scale,
                               const float2 *rope, int n_rot, float eps, cudaStream_t st);
 cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float theta, cudaStream_t st);
-bool attn_step_supported(int hd, int G, int smax);
-cudaError_t attn_step_launch(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
-                             float *part, void *xq, const int *pos, unsigned *count, int nq, int nkv, int hd, int S,
-                             float scale, const float2 *rope, int n_rot, float eps, const void *const *pf,
-                             const unsigned long long *pf_bytes, cudaStream_t st);
+bool attn_batch_supported(int hd, int G, int smax);
+cudaError_t attn_batch_launch(const float *q, const float *gate, const float *kc, const float *vc, float *part,
+                              void *xq, const int *pos, unsigned *count, int nq, int nkv, int hd, int S, float scale,
+                              int n_tok, cudaStream_t st);
+
 cudaError_t attn_launch(const float *q, const float *kc, const float *vc, float *part, float *out, const int *pos,
                         int nq, int nkv, int hd, int S, float scale, cudaStream_t st, int n_tok = 1);
 __global__ void k_fill_blocks(uint8_t *out, int type, int rows, int nblk, long row0, int blk0, uint64_t seed, int tid,
@@ -54,6 +54,12 @@ struct BestExchange {
 __global__ void k_advance_p2p(unsigned long long *best, int *ctl, int *hist, int cap, BestExchange b);
 bool qmv_push(const WeightView *w, const void *xq, const float *residual, const PushArgs &push, cudaStream_t stream,
               char *err, size_t cap, const float *xf = nullptr);
+bool qmv_q6k_ksplit(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                    float *part, unsigned *count, cudaStream_t stream, char *err, size_t cap);
+bool qmv_swiglu_q8(const WeightView *gate, const WeightView *up, const void *xq, const float *xf, const float *norm_w,
+                   float eps, float *y, void *q8out, unsigned *q8cnt, cudaStream_t stream, char *err, size_t cap);
+int q6k_ksplit_ranges(int rb);
+size_t q6k_ksplit_part_floats(int rows, int ks);
 // Gated DeltaNet block (ssm.cu)
 cudaError_t ssm_rmsnorm_launch(const float *x, const float *w, float eps, int n, float *y, cudaStream_t st);
 cudaError_t ssm_conv_launch(const float *x, const float *w, float *cstate, float *out, const float *ba,
@@ -331,6 +337,14 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
             return efail(err, err_cap, "the fused NVLink all-reduce needs q4_K or q6_K attn_output / ffn_down matrices");
     }
     const int *pos = e->ctl + 1;
+    // the FFN's gate/up kernel also writes silu(gate) * up as q8_K blocks
+    // (into xq2, the down projection's input) when the types allow: no
+    // separate quantizer launch
+    auto ffn_q8 = [&](const Layer &Ly) {
+        const uint32_t g = Ly.wg.v.ggml_type;
+        return e->xq2 && e->ffn_cnt && (g == M27B_TYPE_Q4_K || g == M27B_TYPE_Q5_K || g == M27B_TYPE_IQ4_XS) &&
+               e->F % 256 == 0 && act_type_of(Ly.wd.type) == M27B_TYPE_Q8_K;
+    };
     ECALL(m27b_dequant_rows(&e->embd.v, e->ctl, 1, e->h, c.hidden, e->st, err, err_cap));
     ECUDA(rope_table_launch(e->rope, pos, c.n_rot, c.rope_theta, e->st));  // this step's rotary table
     // with the fused all-reduce the consumer kernel hands each projection its
@@ -353,9 +367,16 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
                                   c.ssm_conv_kern, c.ssm_n_group, dr, c.rms_eps, e->st));
             ECUDA(ssm_delta_launch(e->sxc, e->sbg, e->sz, Ly.ssm_norm, Ly.S, e->xq, c.ssm_n_group, dr, c.rms_eps, e->st));
             ECALL(mv(e, Ly.wso, e->xq, e->h2, e->h, err, err_cap));
+            if (ffn_q8(Ly)) {
+                ECALL(qmv_swiglu_q8(&Ly.wg.v, &Ly.wu.v, nullptr, e->h2, Ly.post_norm, c.rms_eps, e->a, e->xq2,
+                                    e->ffn_cnt, e->st, err, err_cap));
+                ECALL(mv(e, Ly.wd, e->xq2, e->h, e->h2, err, err_cap));
+                continue;
+            }
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
                                        nullptr, e->st, err, err_cap));
-            ECALL(m27b_qmv_f32(&Ly.wd.v, e->a, e->F, 1, e->xq, e->h, Ly.wd.rows, e->h2, e->st, err, err_cap));
+            ECALL(m27b_act_quant(e->a, e->F, 1, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
+            ECALL(mv(e, Ly.wd, e->xq, e->h, e->h2, err, err_cap));
             continue;
         }
         if (p2p)
@@ -363,28 +384,7 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         else
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wqkv.v, nullptr, e->h, c.hidden, Ly.attn_norm, c.rms_eps, 1, e->xq, e->qkv,
                                        Ly.wqkv.rows, nullptr, e->st, err, err_cap));
-        if (e->attn_count && attn_step_supported(hd, e->G, e->S) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
-            // one launch: q/k norm + RoPE + KV append + attention + split reduce + gate + q8_K; the DRAM
-            // is idle meanwhile, so it prefetches o_proj's weights and the start of gate/up into L2
-            const void *pf[3] = {nullptr, nullptr, nullptr};
-            unsigned long long pfb[3] = {0, 0, 0};
-            unsigned long long budget = e->l2_prefetch;
-            const unsigned long long wob = (unsigned long long)stored_row_bytes(Ly.wo) * Ly.wo.rows;
-            if (budget && Ly.wo.d) {
-                pf[0] = Ly.wo.d;
-                pfb[0] = wob < budget ? wob : budget;
-                budget -= pfb[0];
-            }
-            const unsigned long long ffb = (unsigned long long)stored_row_bytes(Ly.wg) * Ly.wg.rows;
-            if (budget >= 32 && Ly.wg.d && Ly.wu.d) {
-                pf[1] = Ly.wg.d;
-                pf[2] = Ly.wu.d;
-                pfb[1] = pfb[2] = budget / 2 < ffb ? budget / 2 : ffb;
-            }
-            ECUDA(attn_step_launch(e->qkv, Ly.q_norm, Ly.k_norm, Ly.kc, Ly.vc, e->part, e->xq, pos, e->attn_count,
-                                   e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd), e->rope, c.n_rot, c.rms_eps, pf, pfb,
-                                   e->st));
-        } else if (attn_fused_supported(hd) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
+        if (attn_fused_supported(hd) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
             // q/k norm + RoPE + KV append + attention, then reduce + gate + q8_K for o_proj
             ECUDA(attn_fused_launch(e->qkv, Ly.q_norm, Ly.k_norm, Ly.kc, Ly.vc, e->part, e->xq, pos, e->H, e->KV, hd,
                                     e->S, 1.0f / sqrtf((float)hd), e->rope, c.n_rot, c.rms_eps, e->st));
@@ -397,28 +397,40 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
             ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, 1, e->H * hd, act_type_of(Ly.wo.type), e->xq, e->st,
                                        err, err_cap));
         }
-        // o_proj partial (+ residual on rank 0), summed over ranks -> h2, then post-attention RMSNorm -> xq
+        // o_proj partial (+ residual on rank 0), summed over ranks -> h2, then
+        // post-attention RMSNorm -> gate/up SwiGLU; its epilogue writes the
+        // down projection's q8_K input (xq2), else a quantizer launch does
+        // (quantizing it in the prologue of every down CTA instead, 68 blocks
+        // each at K = 17408, measured slower)
+        const bool fq = ffn_q8(Ly);
+        uint8_t *dxq = fq ? e->xq2 : e->xq;
         if (p2p) {
             ECALL(qmv_push(&Ly.wo.v, e->xq, r0 ? e->h : nullptr, push_args(e, 0, 2u * l), e->st, err, err_cap));
             ECALL(consume(e, 0, 2u * l, Ly.post_norm, e->h2, err, err_cap));
-            ECALL(m27b_qmv_swiglu(&Ly.wg.v, &Ly.wu.v, e->xq, 1, e->a, e->F, e->st, err, err_cap));
+            if (fq)
+                ECALL(qmv_swiglu_q8(&Ly.wg.v, &Ly.wu.v, e->xq, nullptr, nullptr, 0.0f, e->a, e->xq2, e->ffn_cnt, e->st,
+                                    err, err_cap));
+            else
+                ECALL(m27b_qmv_swiglu(&Ly.wg.v, &Ly.wu.v, e->xq, 1, e->a, e->F, e->st, err, err_cap));
         } else {
             ECALL(mv(e, Ly.wo, e->xq, e->h2, r0 ? e->h : nullptr, err, err_cap));
             ECALL(allreduce_hidden(e, e->h2, err, err_cap));
-            ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
-                                       nullptr, e->st, err, err_cap));
+            if (fq)
+                ECALL(qmv_swiglu_q8(&Ly.wg.v, &Ly.wu.v, nullptr, e->h2, Ly.post_norm, c.rms_eps, e->a, e->xq2,
+                                    e->ffn_cnt, e->st, err, err_cap));
+            else
+                ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a,
+                                           e->F, nullptr, e->st, err, err_cap));
         }
+        if (!fq) ECALL(m27b_act_quant(e->a, e->F, 1, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
         // down partial (+ residual on rank 0), summed over ranks -> h, then the
-        // next layer's input RMSNorm (the output norm after the last layer) -> xq;
-        // the down kernel quantizes silu(gate) * up in its own prologue
+        // next layer's input RMSNorm (the output norm after the last layer) -> xq
         const float *next_norm = l + 1 < c.n_layers ? e->L[l + 1].attn_norm : e->out_norm;
         if (p2p) {
-            ECALL(qmv_push(&Ly.wd.v, nullptr, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), e->st, err, err_cap,
-                           e->a));
+            ECALL(qmv_push(&Ly.wd.v, dxq, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), e->st, err, err_cap));
             ECALL(consume(e, 1, 2u * l + 1u, next_norm, e->h, err, err_cap));
         } else {
-            ECALL(m27b_qmv_f32(&Ly.wd.v, e->a, e->F, 1, e->xq, e->h, Ly.wd.rows, r0 ? e->h2 : nullptr, e->st, err,
-                               err_cap));
+            ECALL(mv(e, Ly.wd, dxq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
             ECALL(allreduce_hidden(e, e->h, err, err_cap));
         }
     }
@@ -462,10 +474,16 @@ bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
         ECUDA(launch_pdl(k_qk_norm_rope_cache, dim3(e->H + e->KV, n), dim3(hd), (size_t)(hd + 32) * 4, e->st,
                          (const float *)e->qkv, (const float *)Ly.q_norm, (const float *)Ly.k_norm, e->q, e->gate, Ly.kc,
                          Ly.vc, pos, e->H, e->KV, hd, c.n_rot, c.rope_theta, c.rms_eps, qkv_rows, e->H * hd));
-        ECUDA(attn_launch(e->q, Ly.kc, Ly.vc, e->part, e->o, pos, e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd), e->st,
-                          n));
-        ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, n, e->H * hd, act_type_of(Ly.wo.type), e->xq, e->st, err,
-                                   err_cap));
+        if (attn_batch_supported(hd, e->G, e->S) && act_type_of(Ly.wo.type) == M27B_TYPE_Q8_K) {
+            // every token's split attention, reduction, gate and q8_K in one launch
+            ECUDA(attn_batch_launch(e->q, e->gate, Ly.kc, Ly.vc, e->part, e->xq, pos, e->attn_count, e->H, e->KV, hd,
+                                    e->S, 1.0f / sqrtf((float)hd), n, e->st));
+        } else {
+            ECUDA(attn_launch(e->q, Ly.kc, Ly.vc, e->part, e->o, pos, e->H, e->KV, hd, e->S, 1.0f / sqrtf((float)hd),
+                              e->st, n));
+            ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, n, e->H * hd, act_type_of(Ly.wo.type), e->xq, e->st,
+                                       err, err_cap));
+        }
         ECALL(m27b_qmv(&Ly.wo.v, e->xq, n, e->h2, D, r0 ? e->h : nullptr, e->st, err, err_cap));
         if (c.tp_size > 1) ENCCL(ncclAllReduce(e->h2, e->h2, (size_t)n * D, ncclFloat32, ncclSum, e->comm, e->st));
         if (n >= 5 && Ly.wg.type == M27B_TYPE_Q4_K) {
@@ -481,7 +499,13 @@ bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
                                        nullptr, e->st, err, err_cap));
             ECALL(m27b_act_quant(e->a, e->F, n, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
         }
-        ECALL(m27b_qmv(&Ly.wd.v, e->xq, n, e->h, D, r0 ? e->h2 : nullptr, e->st, err, err_cap));
+        if (n >= 5 && Ly.wd.v.ggml_type == (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) &&
+            q6k_ksplit_ranges((int)Ly.wd.v.row_blocks) > 0 && Ly.wd.rows == D)
+            // 5+ tokens of a q6_K down: K split across CTAs, 8 tokens per weight pass
+            ECALL(qmv_q6k_ksplit(&Ly.wd.v, e->xq, n, e->h, D, r0 ? e->h2 : nullptr, e->ksp_part, e->ksp_count, e->st,
+                                 err, err_cap));
+        else
+            ECALL(m27b_qmv(&Ly.wd.v, e->xq, n, e->h, D, r0 ? e->h2 : nullptr, e->st, err, err_cap));
         if (c.tp_size > 1) ENCCL(ncclAllReduce(e->h, e->h, (size_t)n * D, ncclFloat32, ncclSum, e->comm, e->st));
     }
     ECALL(m27b_act_quant_rmsnorm(e->h, e->out_norm, c.rms_eps, D, n, D, act_type_of(e->lmh.type), e->xq, e->st, err,
@@ -700,8 +724,14 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
               A((void **)&e->logits, VM * e->V * 4) && A((void **)&e->xq, VM * m27b_act_bytes(M27B_TYPE_Q8_K, xmax)) &&
               A((void **)&e->best, VM * 8) && A((void **)&e->ctl, 16) && A((void **)&e->hist, (size_t)c.max_ctx * 4) &&
               A((void **)&e->rope, (size_t)c.n_rot / 2 * sizeof(float2)) && A((void **)&e->vtok, VM * 4) &&
-              A((void **)&e->attn_count, (size_t)e->KV * sizeof(unsigned)) &&
-              cudaMemset(e->attn_count, 0, (size_t)e->KV * sizeof(unsigned)) == cudaSuccess;
+              A((void **)&e->attn_count, VM * e->KV * sizeof(unsigned)) &&
+              cudaMemset(e->attn_count, 0, VM * e->KV * sizeof(unsigned)) == cudaSuccess &&
+              A((void **)&e->xq2, m27b_act_bytes(M27B_TYPE_Q8_K, e->F) + 16) &&
+              A((void **)&e->ffn_cnt, (size_t)(e->F / 256 + 1) * sizeof(unsigned)) &&
+              cudaMemset(e->ffn_cnt, 0, (size_t)(e->F / 256 + 1) * sizeof(unsigned)) == cudaSuccess &&
+              A((void **)&e->ksp_part, q6k_ksplit_part_floats(c.hidden, 4) * sizeof(float)) &&
+              A((void **)&e->ksp_count, (size_t)(c.hidden / 8) * sizeof(unsigned)) &&
+              cudaMemset(e->ksp_count, 0, (size_t)(c.hidden / 8) * sizeof(unsigned)) == cudaSuccess;
     for (int l = 0; ok && l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
         if (Ly.ssm) {
@@ -758,14 +788,6 @@ bool m27b_engine_create_sharing(const M27BEngine *src, int max_ctx, M27BEngine *
     e->lmh = src->lmh;
     e->out_norm = src->out_norm;
     *out = e;
-    if (err && err_cap) err[0] = '\0';
-    return true;
-}
-
-bool m27b_engine_set_l2_prefetch(M27BEngine *e, unsigned long long bytes, char *err, size_t err_cap) {
-    if (!e) return efail(err, err_cap, "m27b_engine_set_l2_prefetch: null engine");
-    if (e->gexec) return efail(err, err_cap, "m27b_engine_set_l2_prefetch: call it before the first decode step");
-    e->l2_prefetch = bytes;
     if (err && err_cap) err[0] = '\0';
     return true;
 }

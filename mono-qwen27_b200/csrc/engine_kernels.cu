@@ -137,10 +137,23 @@ __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const floa
 #pragma unroll
         for (int i = 0; i < DPL; ++i) acc[g][i] = 0.0f;
     }
+    // software pipeline: the next position's K/V rows are in flight while
+    // the current one is scored (one memory latency per warp, not one per position)
+    float kv[DPL], vv[DPL], kn[DPL], vn[DPL];
+    if (p0 + warp < p1) {
+        ld_dims<DPL>(kc + ((size_t)(p0 + warp) * nkv + j) * hd + lane * DPL, kn);
+        ld_dims<DPL>(vc + ((size_t)(p0 + warp) * nkv + j) * hd + lane * DPL, vn);
+    }
     for (int p = p0 + warp; p < p1; p += 8) {
-        float kv[DPL], vv[DPL];
-        ld_dims<DPL>(kc + ((size_t)p * nkv + j) * hd + lane * DPL, kv);
-        ld_dims<DPL>(vc + ((size_t)p * nkv + j) * hd + lane * DPL, vv);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+            kv[i] = kn[i];
+            vv[i] = vn[i];
+        }
+        if (p + 8 < p1) {
+            ld_dims<DPL>(kc + ((size_t)(p + 8) * nkv + j) * hd + lane * DPL, kn);
+            ld_dims<DPL>(vc + ((size_t)(p + 8) * nkv + j) * hd + lane * DPL, vn);
+        }
 #pragma unroll
         for (int g = 0; g < ATT_G; ++g) {
             if (g < G) {
@@ -208,6 +221,7 @@ __global__ void __launch_bounds__(256) k_attn_reduce(const float *part, float *o
     out += (size_t)blockIdx.y * out_stride;
     const int S = att_splits(*pos_p + 1 + (int)blockIdx.y, smax);
     float M = -INFINITY;
+#pragma unroll 4
     for (int s = warp; s < S; s += 8) M = fmaxf(M, part[((size_t)s * nq + h) * rec + hd]);
     if (lane == 0) wmax[warp] = M;
     __syncthreads();
@@ -216,6 +230,7 @@ __global__ void __launch_bounds__(256) k_attn_reduce(const float *part, float *o
     float A[DPL], Ls = 0.0f;
 #pragma unroll
     for (int i = 0; i < DPL; ++i) A[i] = 0.0f;
+#pragma unroll 4
     for (int s = warp; s < S; s += 8) {
         const float *r = part + ((size_t)s * nq + h) * rec;
         const float f = expf(r[hd] - M);  // every active split holds at least one position
@@ -345,10 +360,23 @@ __global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, cons
 #pragma unroll
         for (int i = 0; i < DPL; ++i) acc[g][i] = 0.0f;
     }
+    // software pipeline: the next position's K/V rows are in flight while
+    // the current one is scored (one memory latency per warp, not one per position)
+    float kv[DPL], vv[DPL], kn[DPL], vn[DPL];
+    if (p0 + warp < p1) {
+        ld_dims<DPL>(kc + ((size_t)(p0 + warp) * nkv + j) * hd + lane * DPL, kn);
+        ld_dims<DPL>(vc + ((size_t)(p0 + warp) * nkv + j) * hd + lane * DPL, vn);
+    }
     for (int p = p0 + warp; p < p1; p += 8) {
-        float kv[DPL], vv[DPL];
-        ld_dims<DPL>(kc + ((size_t)p * nkv + j) * hd + lane * DPL, kv);
-        ld_dims<DPL>(vc + ((size_t)p * nkv + j) * hd + lane * DPL, vv);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+            kv[i] = kn[i];
+            vv[i] = vn[i];
+        }
+        if (p + 8 < p1) {
+            ld_dims<DPL>(kc + ((size_t)(p + 8) * nkv + j) * hd + lane * DPL, kn);
+            ld_dims<DPL>(vc + ((size_t)(p + 8) * nkv + j) * hd + lane * DPL, vn);
+        }
 #pragma unroll
         for (int g = 0; g < ATT_G; ++g) {
             if (g < G) {
@@ -420,6 +448,7 @@ __global__ void __launch_bounds__(256) k_attn_reduce_gate_q8K(const float *part,
     for (int hh = 0; hh < hpb; ++hh) {
         const int h = blockIdx.x * hpb + hh;
         float M = -INFINITY;
+#pragma unroll 4
         for (int s = warp; s < S; s += 8) M = fmaxf(M, part[((size_t)s * nq + h) * rec + hd]);
         if (lane == 0) wmax[warp] = M;
         __syncthreads();
@@ -428,6 +457,7 @@ __global__ void __launch_bounds__(256) k_attn_reduce_gate_q8K(const float *part,
         float A[DPL], Ls = 0.0f;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) A[i] = 0.0f;
+#pragma unroll 4
         for (int s = warp; s < S; s += 8) {
             const float *r = part + ((size_t)s * nq + h) * rec;
             const float f = expf(r[hd] - M);
@@ -514,41 +544,37 @@ cudaError_t attn_fused_launch(const float *qkv, const float *q_norm, const float
 }
 
 // ---------------------------------------------------------------------------
-// The engine's decode attention in ONE launch (replaces the pair above when
-// head_dim is 64, 128 or 256 and a kv group's G = nq/nkv heads fill whole
-// q8_K blocks): grid (nkv, smax), 256 threads; the active splits are
-// ceil(L / AST_CH) (at most smax), so a split usually holds one chunk.  CTA (j, s):
-//   * prefetches its share of up to two weight ranges into L2 (the matvecs
-//     that follow; the DRAM is otherwise idle during attention);
-//   * normalises + rotates the G query heads of kv head j (the CTA of the
-//     last active split, which holds position pos, also the new k row, and
-//     appends k and v to the caches);
-//   * walks its positions in chunks of AST_CH: the chunk's K and V rows are
-//     staged in shared memory by all threads at once (one memory latency per
-//     chunk), warps score positions against every head, warp g updates head
-//     g's running max / sum, and each thread accumulates its output values
-//     over the chunk's V rows;
+// Decode attention of a verify pass (several tokens) in ONE launch, after
+// k_qk_norm_rope_cache has normalised and rotated every token's queries
+// (q, gate rows of nq * hd) and appended its K/V: token t at position
+// *pos + t attends to the cache up to its own position.  Grid (nkv, smax,
+// tokens), 256 threads; the active splits of token t are ceil(L_t / ABT_CH)
+// (at most smax), so a split usually holds one chunk.  CTA (j, s, t):
+//   * puts its first chunk's K and V rows in flight (cp.async: every 16-byte
+//     piece of a thread at once), then scales the G query heads of kv head j
+//     into shared memory;
+//   * per chunk of ABT_CH positions: warps score positions against every
+//     head, warp g updates head g's running max / sum, each thread
+//     accumulates its output values over the chunk's V rows;
 //   * writes its partial record (acc, max, sum) and counts itself in
-//     count[j]; the CTA that arrives last reduces all splits of the kv group
-//     in split order (vector loads from L2, eight in flight per thread),
-//     applies the sigmoid gate, quantizes the G*hd values to q8_K for o_proj,
-//     and resets count[j] to zero for the next launch.
-// No CTA waits for another: the last arriver is decided by the atomic.
-constexpr int AST_CH = 64;  // positions per staged chunk
+//     count[t][j]; the CTA that arrives last reduces the kv group's splits in
+//     split order (vector loads from L2, eight in flight per thread), applies
+//     the sigmoid gate, quantizes the G*hd values to q8_K (o_proj's input
+//     row t) and resets count[t][j] to zero for the next launch.
+// No CTA waits for another: the last arriver is decided by the atomic.  (As
+// the single-token step's attention this design measured slower than the
+// split + reduce pair above, 179 vs 189 tokens/s; the pair stays there.)
+constexpr int ABT_CH = 32;  // positions per staged chunk
 
-struct AttnStepArgs {
-    const float *qkv, *q_norm, *k_norm;
-    float *kc, *vc, *part;
-    void *xq;
+struct AttnBatchArgs {
+    const float *q, *gate;  // [tokens][nq * hd]: normalised + rotated queries, gate rows
+    const float *kc, *vc;
+    float *part;            // [tokens][smax][nq][hd + 4]
+    void *xq;               // [tokens] q8_K rows of nq * hd values
     const int *pos_p;
-    unsigned *count;  // [nkv], zero between launches
+    unsigned *count;        // [tokens][nkv], zero between launches
     int nq, nkv, smax;
     float scale;
-    const float2 *rope;
-    int n_rot;
-    float eps;
-    const void *pf[3];  // L2 prefetch ranges (16-byte aligned), may be null
-    unsigned long long pf_bytes[3];
 };
 
 // 16 bytes global -> shared without a register round trip (L2 only).
@@ -560,78 +586,54 @@ M27B_DI void cp_async16(void *smem, const void *gmem) {
 // This thread's asynchronous copies have landed.
 M27B_DI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-M27B_DI void l2_prefetch(const void *p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// CTA c of n prefetches its 16-byte-aligned share of each range, one piece per lane.
-M27B_DI void l2_prefetch_share(const AttnStepArgs &a, int c, int n, int lane) {
-#pragma unroll
-    for (int r = 0; r < 3; ++r) {
-        if (!a.pf[r] || a.pf_bytes[r] < 16) continue;
-        const unsigned long long T = a.pf_bytes[r] & ~15ull;
-        const unsigned long long per_cta = ((T + (unsigned long long)n - 1) / n + 15) & ~15ull;
-        const unsigned long long per_lane = ((per_cta + 31) / 32 + 15) & ~15ull;
-        const unsigned long long c_end = (unsigned long long)(c + 1) * per_cta;
-        const unsigned long long lo = (unsigned long long)c * per_cta + (unsigned long long)lane * per_lane;
-        const unsigned long long end = c_end < T ? c_end : T;
-        if (lo < end) {
-            const unsigned long long len = end - lo < per_lane ? end - lo : per_lane;
-            l2_prefetch((const uint8_t *)a.pf[r] + lo, (uint32_t)len);
-        }
-    }
-}
-
-M27B_DI int ast_splits(int L, int smax) {
-    const int s = (L + AST_CH - 1) / AST_CH;
+M27B_DI int abt_splits(int L, int smax) {
+    const int s = (L + ABT_CH - 1) / ABT_CH;
     return s < smax ? s : smax;
 }
 
-size_t attn_step_smem_bytes(int G, int hd) {
-    return (size_t)(G * hd + 2 * AST_CH * hd + ATT_G * AST_CH + 4 * ATT_G + 2 * hd) * sizeof(float);
+size_t attn_batch_smem_bytes(int G, int hd) {
+    return (size_t)(G * hd + 2 * ABT_CH * hd + ATT_G * ABT_CH + 4 * ATT_G) * sizeof(float);
 }
 
 template <int DPL>
-__global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
+__global__ void __launch_bounds__(256) k_attn_batch(const AttnBatchArgs a) {
     pdl_wait();
     pdl_trigger();
-    constexpr int hd = DPL * 32, rec = hd + 4, CH = AST_CH, Q4 = hd / 4;
+    constexpr int hd = DPL * 32, rec = hd + 4, CH = ABT_CH, Q4 = hd / 4;
     constexpr int NO = ATT_G * hd / 256;  // output values per thread, at most
-    const int j = blockIdx.x, s = blockIdx.y;
+    const int j = blockIdx.x, s = blockIdx.y, tok = blockIdx.z;
     const int nq = a.nq, nkv = a.nkv, G = nq / nkv;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = threadIdx.x;
-    if (warp == 7) l2_prefetch_share(a, s * nkv + j, (int)gridDim.y * nkv, lane);
-    const int pos = *a.pos_p, L = pos + 1;
-    const int S = ast_splits(L, a.smax);
+    const int L = *a.pos_p + tok + 1;
+    const int S = abt_splits(L, a.smax);
     if (s >= S) return;
+    float *part = a.part + (size_t)tok * a.smax * nq * rec;
+    unsigned *count = a.count + (size_t)tok * nkv;
     const int p0 = (int)(((long)L * s) / S), p1 = (int)(((long)L * (s + 1)) / S);
     extern __shared__ __align__(16) float sh[];
-    float *qs = sh;                 // [G][hd] queries, normalised, rotated, times scale
-    float *ks = qs + G * hd;        // [CH][hd] staged K rows
-    float *vs = ks + CH * hd;       // [CH][hd] staged V rows
-    float *sc = vs + CH * hd;       // [ATT_G][CH] scores, then softmax weights
-    float *hm = sc + ATT_G * CH;    // [ATT_G] running max
-    float *hl = hm + ATT_G;         // [ATT_G] running sum
-    float *ha = hl + ATT_G;         // [ATT_G] rescale of the previous chunks
-    float *hf = ha + ATT_G;         // [ATT_G] flag: this CTA arrived last
-    float *kn = hf + ATT_G;         // [2][hd] the new k and v rows (last split)
-    const bool owner = s == S - 1;
-    if (warp < G)
-        norm_rope_warp<DPL>(a.qkv + (size_t)(j * G + warp) * 2 * hd, a.q_norm, qs + warp * hd, a.scale, a.rope,
-                            a.n_rot, a.eps, lane);
-    if (owner && warp == (G < 8 ? G : 7)) {
-        norm_rope_warp<DPL>(a.qkv + (size_t)nq * 2 * hd + (size_t)j * hd, a.k_norm, kn, 1.0f, a.rope, a.n_rot, a.eps,
-                            lane);
-        const float *vsrc = a.qkv + (size_t)nq * 2 * hd + (size_t)nkv * hd + (size_t)j * hd;
-        const size_t off = ((size_t)pos * nkv + j) * hd;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-            const int d = lane * DPL + i;
-            const float v = vsrc[d];
-            kn[hd + d] = v;
-            a.kc[off + d] = kn[d];
-            a.vc[off + d] = v;
+    float *qs = sh;               // [G][hd] queries times scale
+    float *ks = qs + G * hd;      // [CH][hd] staged K rows
+    float *vs = ks + CH * hd;     // [CH][hd] staged V rows
+    float *sc = vs + CH * hd;     // [ATT_G][CH] scores, then softmax weights
+    float *hm = sc + ATT_G * CH;  // [ATT_G] running max
+    float *hl = hm + ATT_G;       // [ATT_G] running sum
+    float *ha = hl + ATT_G;       // [ATT_G] rescale of the previous chunks
+    float *hf = ha + ATT_G;       // flag: this CTA arrived last
+    auto stage = [&](int c0, int n) {
+        for (int idx = t; idx < n * Q4; idx += 256) {
+            const int p = idx / Q4, c4 = idx - p * Q4;
+            const size_t o = ((size_t)(c0 + p) * nkv + j) * hd + 4 * c4;
+            cp_async16(ks + p * hd + 4 * c4, a.kc + o);
+            cp_async16(vs + p * hd + 4 * c4, a.vc + o);
         }
+    };
+    stage(p0, p1 - p0 < CH ? p1 - p0 : CH);
+    const float *qrow = a.q + (size_t)tok * nq * hd;
+    if (warp < G) {
+        float qv[DPL];
+        ld_dims<DPL>(qrow + (size_t)(j * G + warp) * hd + lane * DPL, qv);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) qs[warp * hd + lane * DPL + i] = qv[i] * a.scale;
     }
     if (t < ATT_G) {
         hm[t] = -INFINITY;
@@ -642,21 +644,8 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
     for (int i = 0; i < NO; ++i) acc[i] = 0.0f;
     for (int c0 = p0; c0 < p1; c0 += CH) {
         const int n = p1 - c0 < CH ? p1 - c0 : CH;
-        __syncthreads();  // the previous chunk is consumed; q and the new row are ready
-        // every 16-byte piece of the chunk's K and V rows as an asynchronous
-        // copy (all of a thread's pieces in flight at once), the new row from
-        // shared memory
-        for (int idx = t; idx < n * Q4; idx += 256) {
-            const int p = idx / Q4, c4 = idx - p * Q4, pp = c0 + p;
-            if (pp == pos) {
-                reinterpret_cast<float4 *>(ks + p * hd)[c4] = reinterpret_cast<const float4 *>(kn)[c4];
-                reinterpret_cast<float4 *>(vs + p * hd)[c4] = reinterpret_cast<const float4 *>(kn + hd)[c4];
-            } else {
-                const size_t o = ((size_t)pp * nkv + j) * hd + 4 * c4;
-                cp_async16(ks + p * hd + 4 * c4, a.kc + o);
-                cp_async16(vs + p * hd + 4 * c4, a.vc + o);
-            }
-        }
+        __syncthreads();  // the previous chunk is consumed (the first chunk's copies are already in flight)
+        if (c0 != p0) stage(c0, n);
         cp_async_wait_all();
         __syncthreads();
         for (int p = warp; p < n; p += 8) {
@@ -677,19 +666,15 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
         }
         __syncthreads();
         if (warp < G) {
-            // lane holds positions lane and lane + 32 of the chunk
-            const float v0 = lane < n ? sc[warp * CH + lane] : -INFINITY;
-            const float v1 = lane + 32 < n ? sc[warp * CH + lane + 32] : -INFINITY;
-            float cm = fmaxf(v0, v1);
+            const float v = lane < n ? sc[warp * CH + lane] : -INFINITY;
+            float cm = v;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
             const float mo = hm[warp], mn = fmaxf(mo, cm);
-            const float w0 = lane < n ? expf(v0 - mn) : 0.0f;
-            const float w1 = lane + 32 < n ? expf(v1 - mn) : 0.0f;
-            const float sum = warp_sum(w0 + w1);
+            const float w = lane < n ? expf(v - mn) : 0.0f;
+            const float sum = warp_sum(w);
             const float al = mo == -INFINITY ? 0.0f : expf(mo - mn);
-            if (lane < n) sc[warp * CH + lane] = w0;
-            if (lane + 32 < n) sc[warp * CH + lane + 32] = w1;
+            if (lane < n) sc[warp * CH + lane] = w;
             __syncwarp();
             if (lane == 0) {
                 hm[warp] = mn;
@@ -699,7 +684,7 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
         }
         __syncthreads();
         // P.V: the thread's outputs advance together, one position at a time
-        // (independent chains; heads past G read head 0's weights, unused)
+        // (independent chains; output slots past G heads use head 0's weights, unused)
         int wofs[NO], vofs[NO];
 #pragma unroll
         for (int i = 0; i < NO; ++i) {
@@ -720,29 +705,29 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
         const int o = t + 256 * i;
         if (o < G * hd) {
             const int g = o / hd, d = o - g * hd;
-            a.part[((size_t)s * nq + j * G + g) * rec + d] = acc[i];
+            part[((size_t)s * nq + j * G + g) * rec + d] = acc[i];
         }
     }
     if (t < G) {
-        float *r = a.part + ((size_t)s * nq + j * G + t) * rec;
+        float *r = part + ((size_t)s * nq + j * G + t) * rec;
         r[hd] = hm[t];
         r[hd + 1] = hl[t];
     }
     __threadfence();
     __syncthreads();
-    if (t == 0) hf[0] = atomicAdd(a.count + j, 1u) == (unsigned)(S - 1) ? 1.0f : 0.0f;
+    if (t == 0) hf[0] = atomicAdd(count + j, 1u) == (unsigned)(S - 1) ? 1.0f : 0.0f;
     __syncthreads();
     if (hf[0] == 0.0f) return;
     // the last arriver: every split's record is visible (each CTA fenced its
     // writes before counting itself); read them from L2
-    if (t == 0) a.count[j] = 0u;
+    if (t == 0) count[j] = 0u;
     __threadfence();
-    float *fm = ks;           // [S][G] split max, then split weight
-    float *fl = ks + S * G;   // [S][G] split sum
-    float *xs = vs;           // [G * hd] gated output
+    float *fm = ks;          // [S][G] split max, then split weight
+    float *fl = ks + S * G;  // [S][G] split sum
+    float *xs = vs;          // [G * hd] gated output
     for (int idx = t; idx < S * G; idx += 256) {
         const int s2 = idx / G, g = idx - s2 * G;
-        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(a.part + ((size_t)s2 * nq + j * G + g) * rec + hd));
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(part + ((size_t)s2 * nq + j * G + g) * rec + hd));
         fm[idx] = ml.x;
         fl[idx] = ml.y;
     }
@@ -762,9 +747,10 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
         if (lane == 0) hl[g] = Ls;
     }
     __syncthreads();
+    const float *grow = a.gate + (size_t)tok * nq * hd;
     for (int q = t; q < G * Q4; q += 256) {
         const int g = q / Q4, c4 = q - g * Q4;
-        const float *base = a.part + ((size_t)j * G + g) * rec + 4 * c4;
+        const float *base = part + ((size_t)j * G + g) * rec + 4 * c4;
         const size_t sstride = (size_t)nq * rec;
         float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int s2 = 0; s2 < S; s2 += 8) {
@@ -784,7 +770,7 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
                 }
             }
         }
-        const float4 gt = *reinterpret_cast<const float4 *>(a.qkv + (size_t)(j * G + g) * 2 * hd + hd + 4 * c4);
+        const float4 gt = *reinterpret_cast<const float4 *>(grow + (size_t)(j * G + g) * hd + 4 * c4);
         const float il = 1.0f / hl[g];
         float *o = xs + g * hd + 4 * c4;
         o[0] = (x.x * il) * (1.0f / (1.0f + expf(-gt.x)));
@@ -798,29 +784,33 @@ __global__ void __launch_bounds__(256) k_attn_step(const AttnStepArgs a) {
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = xs[b * 256 + lane * 8 + i];
-        quant_q8K_warp(v, lane, (m27b_block_q8_K *)a.xq + (size_t)j * nb + b);
+        quant_q8K_warp(v, lane, (m27b_block_q8_K *)a.xq + (size_t)tok * (nq * hd / 256) + (size_t)j * nb + b);
     }
 }
 
 template <int DPL>
-static cudaError_t attn_step_opt_in() {
-    return cudaFuncSetAttribute(k_attn_step<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)attn_step_smem_bytes(ATT_G, DPL * 32));
+static cudaError_t attn_batch_opt_in() {
+    return cudaFuncSetAttribute(k_attn_batch<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)attn_batch_smem_bytes(ATT_G, DPL * 32));
 }
 
-bool attn_step_supported(int hd, int G, int smax) {
+// head_dim 64 / 128 / 256, a kv group's heads filling whole q8_K blocks, and
+// the reduction's split weights fitting the staging buffer.
+bool attn_batch_supported(int hd, int G, int smax) {
     return (hd == 64 || hd == 128 || hd == 256) && G >= 1 && G <= ATT_G && (G * hd) % 256 == 0 &&
-           2 * smax * G <= AST_CH * hd;
+           2 * smax * G <= ABT_CH * hd;
 }
 
-cudaError_t attn_step_launch(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
-                             float *part, void *xq, const int *pos, unsigned *count, int nq, int nkv, int hd, int S,
-                             float scale, const float2 *rope, int n_rot, float eps, const void *const *pf,
-                             const unsigned long long *pf_bytes, cudaStream_t st) {
-    AttnStepArgs a{};
-    a.qkv = qkv;
-    a.q_norm = q_norm;
-    a.k_norm = k_norm;
+// Token t at position *pos + t attends to the cache up to its own position;
+// q and gate rows from k_qk_norm_rope_cache (stride nq * hd), K/V already
+// appended; q8_K rows of o_proj's input in xq.  count holds n_tok * nkv
+// words (zero at rest), part n_tok * S * nq * (hd + 4) floats.
+cudaError_t attn_batch_launch(const float *q, const float *gate, const float *kc, const float *vc, float *part,
+                              void *xq, const int *pos, unsigned *count, int nq, int nkv, int hd, int S, float scale,
+                              int n_tok, cudaStream_t st) {
+    AttnBatchArgs a{};
+    a.q = q;
+    a.gate = gate;
     a.kc = kc;
     a.vc = vc;
     a.part = part;
@@ -831,19 +821,12 @@ cudaError_t attn_step_launch(const float *qkv, const float *q_norm, const float 
     a.nkv = nkv;
     a.smax = S;
     a.scale = scale;
-    a.rope = rope;
-    a.n_rot = n_rot;
-    a.eps = eps;
-    for (int r = 0; r < 3; ++r) {
-        a.pf[r] = pf ? pf[r] : nullptr;
-        a.pf_bytes[r] = a.pf[r] ? pf_bytes[r] : 0;
-    }
-    const size_t smem = attn_step_smem_bytes(nq / nkv, hd);
-    const dim3 grid(nkv, S);
+    const size_t smem = attn_batch_smem_bytes(nq / nkv, hd);
+    const dim3 grid(nkv, S, n_tok);
     switch (hd) {
-        case 64: return launch_pdl(k_attn_step<2>, grid, dim3(256), smem, st, a);
-        case 128: return launch_pdl(k_attn_step<4>, grid, dim3(256), smem, st, a);
-        case 256: return launch_pdl(k_attn_step<8>, grid, dim3(256), smem, st, a);
+        case 64: return launch_pdl(k_attn_batch<2>, grid, dim3(256), smem, st, a);
+        case 128: return launch_pdl(k_attn_batch<4>, grid, dim3(256), smem, st, a);
+        case 256: return launch_pdl(k_attn_batch<8>, grid, dim3(256), smem, st, a);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -857,8 +840,8 @@ cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float the
 cudaError_t attn_prepare() {
     cudaError_t e = cudaSuccess;
     for (cudaError_t r : {attn_opt_in<1>(), attn_opt_in<2>(), attn_opt_in<3>(), attn_opt_in<4>(), attn_opt_in<5>(),
-                          attn_opt_in<6>(), attn_opt_in<7>(), attn_opt_in<8>(), attn_step_opt_in<2>(),
-                          attn_step_opt_in<4>(), attn_step_opt_in<8>()})
+                          attn_opt_in<6>(), attn_opt_in<7>(), attn_opt_in<8>(), attn_batch_opt_in<2>(),
+                          attn_batch_opt_in<4>(), attn_batch_opt_in<8>()})
         if (r != cudaSuccess) e = r;
     return e;
 }

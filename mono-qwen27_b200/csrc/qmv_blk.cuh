@@ -699,6 +699,28 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
                 }
             }
         }
+        if constexpr (EPI == EPI_SWIGLU && NT == 1) {
+            // q8_K of the SwiGLU rows for the next matvec (a.q8out set): the
+            // warp that stores the last 8-row group of a 256-row block (an
+            // arrival count per block) quantizes the block from L2, with the
+            // routine and codes of m27b_act_quant, and resets the count
+            if (a.q8out && (split == 1 || warp == 0)) {
+                const int grp = wg + g * W, blk = grp >> 5;
+                __threadfence();
+                __syncwarp();
+                unsigned prev = 0u;
+                if (lane == 0) prev = atomicAdd(a.q8cnt + blk, 1u);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == 31u) {
+                    if (lane == 0) a.q8cnt[blk] = 0u;
+                    __threadfence();
+                    const float4 *src = (const float4 *)(a.y + (size_t)blk * 256 + lane * 8);
+                    const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
+                    float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                    quant_q8K_warp(v, lane, (m27b_block_q8_K *)a.q8out + blk);
+                }
+            }
+        }
 #pragma unroll
         for (int m = 0; m < NM; ++m)
 #pragma unroll

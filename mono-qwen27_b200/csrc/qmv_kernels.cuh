@@ -49,6 +49,10 @@ struct QmvArgs {
     int xnorm_on;
     const float *xnorm;        // RMSNorm weights (may be null: 1.0)
     float eps;
+    // SWIGLU, one token, rows a multiple of 256: also write the rows as q8_K
+    // blocks (the next matvec's input); q8cnt holds one zeroed word per block
+    void *q8out;
+    unsigned *q8cnt;
 };
 
 // EPI_PUSH row store: one epoch-tagged value to every rank's receive window.

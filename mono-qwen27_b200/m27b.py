@@ -63,7 +63,10 @@ def lib():
         "m27b_qmv_f32": (b, [wvp, vp, i32, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_qmv_f32_rmsnorm": (b, [wvp, wvp, vp, i32, vp, fp, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
-        "m27b_hbm_read_probe": (b, [vp, sz, vp, i32, vp, cp, sz]),
+        "m27b_hbm_read_probe": (b, [vp, sz, vp, cp, sz]),
+        "m27b_qmv_q6k_ksplit_part_bytes": (sz, [wvp]),
+        "m27b_qmv_q6k_ksplit_count_bytes": (sz, [wvp]),
+        "m27b_qmv_q6k_ksplit": (b, [wvp, vp, i32, vp, i32, vp, vp, vp, vp, cp, sz]),
         "m27b_allreduce_norm_quant": (b, [vp, i32, i32, vp, vp, vp, fp, i32, vp, vp, ctypes.c_ulonglong, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
@@ -191,11 +194,29 @@ def allreduce_norm_quant(words, nsrc, src_stride, ss_words, epoch, k, x_out, xq,
     return xq
 
 
-def hbm_read_probe(buf, sink, ctas_per_sm=2, stream=None):
+def qmv_q6k_ksplit(w, xq, n_tok, y, residual=None, part=None, count=None, stream=None, ldy=None):
+    """q6_K x n_tok (5..16) tokens with K split across CTAs (m27b_qmv_q6k_ksplit);
+    part / count scratch are allocated here (counters zeroed) unless given."""
+    import torch
+    L = lib()
+    if part is None:
+        part = torch.empty(max(16, L.m27b_qmv_q6k_ksplit_part_bytes(ctypes.byref(w.view))), dtype=torch.uint8,
+                           device="cuda")
+    if count is None:
+        count = torch.zeros(max(16, L.m27b_qmv_q6k_ksplit_count_bytes(ctypes.byref(w.view))), dtype=torch.uint8,
+                            device="cuda")
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(L.m27b_qmv_q6k_ksplit(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(y),
+                                 ldy if ldy is not None else w.view.row_count, _ptr(residual), _ptr(part), _ptr(count),
+                                 _stream(stream), err, ERR_CAP), err, "m27b_qmv_q6k_ksplit")
+    return y
+
+
+def hbm_read_probe(buf, stream=None):
     """One streaming read of the device tensor `buf` (see m27b_hbm_read_probe)."""
     err = ctypes.create_string_buffer(ERR_CAP)
-    _check(lib().m27b_hbm_read_probe(_ptr(buf), buf.numel() * buf.element_size(), _ptr(sink), ctas_per_sm,
-                                     _stream(stream), err, ERR_CAP), err, "m27b_hbm_read_probe")
+    _check(lib().m27b_hbm_read_probe(_ptr(buf), buf.numel() * buf.element_size(), _stream(stream), err, ERR_CAP), err,
+           "m27b_hbm_read_probe")
 
 
 def act_quant_swiglu(gate, up, act_type, out=None, stream=None):
@@ -378,7 +399,6 @@ def _engine_lib():
         "m27b_engine_stream": (vp, [vp]),
         "m27b_engine_destroy": (None, [vp]),
         "m27b_engine_create_sharing": (b, [vp, i32, ctypes.POINTER(vp), cp, sz]),
-        "m27b_engine_set_l2_prefetch": (b, [vp, ctypes.c_ulonglong, cp, sz]),
         "m27b_engine_speculative_generate": (b, [vp, vp, vp, i32, i32, i32, vp, ctypes.POINTER(SpecStats), cp, sz]),
     }
     for name, (res, args) in sig.items():
@@ -435,10 +455,6 @@ class Engine:
         """Load a .m27b blob's entries of `source` (a Blob, or a path)."""
         b = blob if isinstance(blob, Blob) else Blob(blob)
         engine_load_blob(self, b, source)
-
-    def set_l2_prefetch(self, nbytes):
-        """Bytes of the following weights the attention kernel prefetches into L2 (before the first step)."""
-        self._call("m27b_engine_set_l2_prefetch", self.h, ctypes.c_ulonglong(int(nbytes)))
 
     def random_weights(self, seed=0, sigma=0.02):
         self._call("m27b_engine_random_weights", self.h, seed, ctypes.c_float(sigma))

@@ -149,6 +149,23 @@ def rms_scaled(x, w, eps):
     return (x * (np.float32(1.0) / np.sqrt(ms + np.float32(eps)))) * w
 
 
+def q8K_tie_margin(x):
+    """Smallest distance of a q8_K code's unrounded value x * (-127 / max) to
+    a rounding tie (k + 0.5), relative to max(|value|, 1), over the 256-value
+    blocks of the fp32 vector x (ggml's quantize_row_q8_K rounds that value to
+    nearest).  Another fp32 summation order moves an activation by a few ulps:
+    a margin below ~1e-6 means the code may come out the other way."""
+    best = np.inf
+    x = np.asarray(x, dtype=np.float32).reshape(-1, 256)
+    for blk in x:
+        mx = blk[np.argmax(np.abs(blk))]
+        if mx == 0:
+            continue
+        v = ((np.float32(-127.0) / mx) * blk).astype(np.float32)
+        best = min(best, float((np.abs(v - np.floor(v) - 0.5) / np.maximum(np.abs(v), 1)).min()))
+    return best
+
+
 def rope(x, pos, n_rot, theta):
     half = n_rot // 2
     p = np.arange(half, dtype=np.float64)
@@ -202,8 +219,11 @@ class RefDecoder:
                 wd=col_slice(tq("ffn_down"), g("ffn_down"), p["f_lo"], p["n_f"]),
                 kc=np.zeros((max_ctx, p["n_kv"], hd), np.float32), vc=np.zeros((max_ctx, p["n_kv"], hd), np.float32)))
         self.hidden = None
+        self.tie_margin = np.inf  # q8K_tie_margin over the last step's q8_K activations
 
     def _mv(self, qtype, w, k, x):
+        if self.orc.act_type_for(qtype) == self.orc.Q8_K:
+            self.tie_margin = min(self.tie_margin, q8K_tie_margin(x))
         return self.orc.matvec(qtype, w, k, self.orc.quantize_act(qtype, x[None]))[0]
 
     def _ffn(self, Ly, h2, p, r0):
@@ -259,6 +279,7 @@ class RefDecoder:
     def step(self, token, pos):
         """Returns (local logits, hidden state before the output norm)."""
         orc, c, p = self.orc, self.c, self.p
+        self.tie_margin = np.inf
         hd, D, eps = c["head_dim"], c["hidden"], c["rms_eps"]
         r0 = self.rank == 0
         h = orc.dequantize(self.qt["token_embd.weight"], self.embd[token:token + 1], D)[0]

@@ -5,13 +5,20 @@ from device memory, argmax, embed, free_weights before free_state).
 
 The model is a GGUF-style tensor table of a tiny model quantized by the
 oracle (tests/_decode_ref.py).  Checked: the inferred shape, every step's
-logits against the decode reference (the structure test_hybrid_gpu.py
-explains: most steps at fp32 rounding level, a lone step within 2e-2 where a
-q8_K code rounds the other way) and bit for
-bit against the engine loaded tensor by tensor (the same kernels), the argmax
+logits against the decode reference at fp32 rounding level (rel-L2 <= 1e-4)
+and bit for bit against the engine loaded tensor by tensor (the same
+kernels), the argmax
 entry against the logits' first maximum, the embedding row bit for bit
 against the oracle's dequantization (a zero row for an out-of-range token),
-and that freed weights are refused."""
+and that freed weights are refused.
+
+Each model's seed is one whose activations keep every q8_K code at least 1e-6
+(relative) away from a rounding tie on every step (asserted from the decode
+reference): a code within fp32 rounding of a tie can come out the other way
+on one side, and where that code feeds the KV cache or a recurrent state the
+logits of every later step move by ~1e-2 (seed 5 of the hybrid model has an
+exact tie at step 4), which would hide a real error.  With no such code the
+two sides agree to fp32 rounding on every step."""
 import os
 import struct
 import subprocess
@@ -27,7 +34,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 DRIVER = os.path.join(ROOT, "tests", "abi", "api_driver.cpp")
 LIBDIR = os.path.join(ROOT, "mono-qwen27_b200", "lib")
 TOKENS = [7, 70, 700, 77, 707, 17, 170, 901]
-STEP_TOL, MEDIAN_TOL, RUN_TOL = 2e-2, 1e-5, 1e-4
+RUN_TOL, TIE_MARGIN = 1e-4, 1e-6
+SEEDS = dict(attention=11, hybrid=10)
 HYB = dict(R.TINY, n_layers=4, attn_interval=2, ssm_d_inner=512, ssm_d_state=128, ssm_dt_rank=4, ssm_n_group=2,
            ssm_conv_kern=4)
 
@@ -73,7 +81,7 @@ def _engine_logits(m27b, cfg, model):
 @pytest.mark.parametrize("kind", ["attention", "hybrid"])
 def test_reference_api_decode(orc, m27b, driver, tmp_path, kind):
     cfg = R.TINY if kind == "attention" else HYB
-    model = R.make_model(orc, cfg, seed=5)
+    model = R.make_model(orc, cfg, seed=SEEDS[kind])
     path, out = str(tmp_path / "model.m27t"), str(tmp_path / "out.bin")
     _write_model(path, model)
     r = subprocess.run([driver, path, out, "32"] + [str(t) for t in TOKENS], capture_output=True, text=True,
@@ -91,14 +99,13 @@ def test_reference_api_decode(orc, m27b, driver, tmp_path, kind):
     # the same kernels as the engine's own API: identical logits
     np.testing.assert_array_equal(logits, _engine_logits(m27b, cfg, model))
     ref = R.RefDecoder(orc, model, cfg)
-    errs = [orc.rel_l2(logits[pos], ref.step(t, pos)[0]) for pos, t in enumerate(TOKENS)]
+    errs, margins = [], []
+    for pos, t in enumerate(TOKENS):
+        errs.append(orc.rel_l2(logits[pos], ref.step(t, pos)[0]))
+        margins.append(ref.tie_margin)
     print(kind, "rel-L2 per step:", ["%.2e" % x for x in errs])
-    # an activation within fp32 rounding of a q8_K tie may take the other code
-    # on one side (both sides' fp32 sums run in different orders), moving one
-    # step's logits by up to ~1e-2; a wrong result would persist
-    assert max(errs) <= STEP_TOL, errs
-    assert float(np.median(errs)) <= MEDIAN_TOL, errs
-    assert not any(a > RUN_TOL and b > RUN_TOL for a, b in zip(errs, errs[1:])), errs
+    assert min(margins) >= TIE_MARGIN, margins  # the model keeps clear of q8_K ties
+    assert max(errs) <= RUN_TOL, errs
     for pos in range(n):
         assert am[pos] == int(np.argmax(logits[pos])), pos
     qt, k, rows, w = model["token_embd.weight"]
