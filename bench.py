@@ -51,6 +51,11 @@ for _p in (ROOT, PKG, os.path.join(ROOT, "tests")):
 Q8_0, Q4_K, Q6_K, Q8_K = 8, 12, 14, 15
 BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34)}
 GRAPH_STEPS = 16
+# read-probe copy shapes: (warps per CTA, copies in flight per warp, bytes per
+# copy, CTAs per SM); the first is the matvec kernel's own (8 warps, two
+# 4608-byte q4_K items each, two CTAs per SM)
+PROBE_SHAPES = [(8, 2, 4608, 2), (8, 3, 4608, 2), (8, 3, 8192, 1), (4, 3, 8192, 2), (16, 2, 4096, 1),
+                (8, 6, 4096, 1), (1, 6, 32768, 1), (2, 6, 16384, 1)]
 
 
 def wbytes(qt, rows, k):
@@ -444,6 +449,22 @@ def decode_bench(args, world, rank, dev, dist, uuid):
         e.close()
 
 
+def decode_launches_per_token(layers, p2p, hybrid):
+    """This library's kernel launches in one decode step (NCCL's own kernels
+    not counted).  Per attention layer: the qkv projection (RMSNorm + q8_K in
+    its prologue), the two attention kernels (norm/RoPE/KV append/split
+    attention; reduction + gate + q8_K), o_proj, gate/up (SwiGLU and the
+    down projection's q8_K input in its epilogue), down = 6; with the fused
+    NVLink all-reduce, o_proj and down push into the peers' windows and a
+    consumer kernel follows each = 8.  Per DeltaNet layer (one GPU): RMSNorm,
+    three projections, conv, delta rule, ssm_out, gate/up, down = 9.  Per
+    step: the embedding row, the rotary table, the output RMSNorm + q8_K
+    (before the first layer's projection with the fused all-reduce), lm_head
+    + argmax, the token/position advance = 5."""
+    n_attn = sum((l + 1) % 4 == 0 for l in range(layers)) if hybrid else layers
+    return (8 if p2p else 6) * n_attn + 9 * (layers - n_attn) + 5
+
+
 def decode_main(args, world, rank, dev, dist, uuid, tp_parity=None):
     """--workload decode: the decode figures as the line's own metric."""
     import m27b
@@ -462,7 +483,8 @@ def decode_main(args, world, rank, dev, dist, uuid, tp_parity=None):
                          "frac": d["roofline_frac"], "traffic": None, "kernel": "whole decode step (weight bytes / time)",
                          "peak_kind": d["peak_kind"]},
             "e2e": {"value": d["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 8},
-            "gpu_launches": ((10 if world > 1 and args.comm == "p2p" else 11) * args.layers + 3) * args.gen,
+            "gpu_launches": decode_launches_per_token(args.layers, world > 1 and args.comm == "p2p",
+                                                      bool(getattr(args, "hybrid", False))) * args.gen,
             "clocks": d["clocks"], "cpu_baseline": None,
             "device_status": m27b.device_status(clear=True), "decode": d, "tp_parity": tp_parity,
         }
@@ -913,17 +935,24 @@ def main():
 
     # the read ceiling for launches of this size: the same bytes per launch
     # streamed into shared memory by bulk copies, nothing computed, same
-    # rotation and graph structure
+    # rotation and graph structure; the fastest of several copy shapes
     probe = None
     if wl.name == "cfg0":
         bufs = [torch.empty(wbytes(Q4_K, wl.rows, wl.k), dtype=torch.uint8, device=dev) for _ in range(wl.copies)]
-        fn = lambda: [wl.m27b.hbm_read_probe(b) for b in bufs]
-        run_steps(fn, GRAPH_STEPS)
-        pms, _ = timed(fn, args.steps, warm)
-        us = pms * 1e3 / (args.steps * wl.copies)
-        probe = {"gbs": round(bufs[0].numel() / (us * 1e-6) / 1e9, 1), "launch_us": round(us, 3),
-                 "bytes_per_launch": bufs[0].numel(),
-                 "kernel": "m27b_hbm_read_probe (bulk copies into shared memory, nothing computed)"}
+        shapes = []
+        for shape in PROBE_SHAPES:
+            fn = lambda shape=shape: [wl.m27b.hbm_read_probe(b, shape) for b in bufs]
+            run_steps(fn, GRAPH_STEPS)
+            pms, _ = timed(fn, args.steps, warm)
+            us = pms * 1e3 / (args.steps * wl.copies)
+            shapes.append({"shape": list(shape), "launch_us": round(us, 3),
+                           "gbs": round(bufs[0].numel() / (us * 1e-6) / 1e9, 1)})
+        best = max(shapes, key=lambda r: r["gbs"])
+        probe = {"gbs": best["gbs"], "launch_us": best["launch_us"], "bytes_per_launch": bufs[0].numel(),
+                 "shape": best["shape"], "shape_keys": "warps per CTA, copies in flight per warp, bytes per copy, "
+                                                       "CTAs per SM",
+                 "shapes": shapes,
+                 "kernel": "m27b_hbm_read_probe_shape (bulk copies into shared memory, nothing computed)"}
         del bufs
         graphs.clear()
 

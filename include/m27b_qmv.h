@@ -206,10 +206,19 @@ M27B_API bool m27b_dequant_rows(const struct WeightView *w, const int32_t *rows,
 
 /* Measurement support (no counterpart in the reference): stream `bytes`
  * (16-byte aligned, a multiple of 16) from device memory p into shared memory
- * with bulk asynchronous copies on one CTA per SM (six 32 KB copies in
- * flight each), nothing computed.  The time of one launch is the read
- * ceiling a weight-streaming launch of that size can reach.  A wait that
- * runs out records status 6 (m27b_device_status). */
+ * with bulk asynchronous copies, nothing computed.  The time of one launch is
+ * the read ceiling a weight-streaming launch of that size can reach.  Shape:
+ * `ctas_per_sm` CTAs on every SM, `warps` issuing warps per CTA (1-16), each
+ * streaming its contiguous share of the buffer in `chunk`-byte copies
+ * (16-65536, a multiple of 16) with `stages` copies in flight (1-8).  Launched
+ * with programmatic dependent launch, like the matvec kernels: back-to-back
+ * probes overlap one launch's start with the previous one's drain.  A shape
+ * whose CTAs do not fit `ctas_per_sm` to an SM is refused.  A wait that runs
+ * out records status 6 (m27b_device_status). */
+M27B_API bool m27b_hbm_read_probe_shape(const void *p, size_t bytes, int warps, int stages, int chunk, int ctas_per_sm,
+                                        cudaStream_t stream, char *err, size_t err_cap);
+/* m27b_hbm_read_probe_shape with one warp per CTA, six 32 KB copies in flight,
+ * one CTA per SM. */
 M27B_API bool m27b_hbm_read_probe(const void *p, size_t bytes, cudaStream_t stream, char *err, size_t err_cap);
 
 /* Packed argmax key helpers (host side). */

@@ -319,13 +319,19 @@ M27B_DI void norm_rope_warp(const float *src, const float *nw, float *dst, float
 // active split only: that CTA also normalises and rotates kv head j's k,
 // appends k and v at position L - 1 of the caches, and reads them back like
 // any other position (no other CTA touches it).  Then as k_attn_partial.
+//
+// Before griddepcontrol.wait the kernel reads only what the launch order has
+// already completed (when this grid starts, its predecessor — the qkv
+// projection — has passed its own wait, so every earlier kernel of the step,
+// the position advance and the rotary table included, is done): the
+// position, and the K/V rows of this warp's first two positions unless one
+// of them is the newest (appended below).  Those rows are in flight while
+// the projection drains.
 template <int DPL>
 __global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, const float *q_norm, const float *k_norm,
                                                           float *kc, float *vc, float *part, const int *pos_p, int nq,
                                                           int nkv, float scale, const float2 *rope, int n_rot,
                                                           float eps) {
-    pdl_wait();
-    pdl_trigger();
     constexpr int hd = DPL * 32, rec = hd + 4;
     const int j = blockIdx.x, s = blockIdx.y;
     const int G = nq / nkv;
@@ -334,6 +340,21 @@ __global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, cons
     if (s >= S) return;
     const int p0 = (int)(((long)L * s) / S), p1 = (int)(((long)L * (s + 1)) / S);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // two K/V rows per warp in registers: buffer A holds positions pA, pA+16,
+    // ..., buffer B positions pA+8, pA+24, ...
+    const int pA = p0 + warp, pB = pA + 8;
+    float ka[DPL], va[DPL], kb[DPL], vb[DPL];
+    const bool fA = pA < p1 && pA != pos, fB = pB < p1 && pB != pos;
+    if (fA) {
+        ld_dims<DPL>(kc + ((size_t)pA * nkv + j) * hd + lane * DPL, ka);
+        ld_dims<DPL>(vc + ((size_t)pA * nkv + j) * hd + lane * DPL, va);
+    }
+    if (fB) {
+        ld_dims<DPL>(kc + ((size_t)pB * nkv + j) * hd + lane * DPL, kb);
+        ld_dims<DPL>(vc + ((size_t)pB * nkv + j) * hd + lane * DPL, vb);
+    }
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) float sh[];  // q [G][hd] (pre-scaled), then [8 warps][G][rec]
     float *qs = sh;
     float *cb = sh + G * hd;
@@ -360,23 +381,17 @@ __global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, cons
 #pragma unroll
         for (int i = 0; i < DPL; ++i) acc[g][i] = 0.0f;
     }
-    // software pipeline: the next position's K/V rows are in flight while
-    // the current one is scored (one memory latency per warp, not one per position)
-    float kv[DPL], vv[DPL], kn[DPL], vn[DPL];
-    if (p0 + warp < p1) {
-        ld_dims<DPL>(kc + ((size_t)(p0 + warp) * nkv + j) * hd + lane * DPL, kn);
-        ld_dims<DPL>(vc + ((size_t)(p0 + warp) * nkv + j) * hd + lane * DPL, vn);
+    // the newest position's rows (written above) are read after the barrier
+    if (pA < p1 && !fA) {
+        ld_dims<DPL>(kc + ((size_t)pA * nkv + j) * hd + lane * DPL, ka);
+        ld_dims<DPL>(vc + ((size_t)pA * nkv + j) * hd + lane * DPL, va);
     }
-    for (int p = p0 + warp; p < p1; p += 8) {
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-            kv[i] = kn[i];
-            vv[i] = vn[i];
-        }
-        if (p + 8 < p1) {
-            ld_dims<DPL>(kc + ((size_t)(p + 8) * nkv + j) * hd + lane * DPL, kn);
-            ld_dims<DPL>(vc + ((size_t)(p + 8) * nkv + j) * hd + lane * DPL, vn);
-        }
+    if (pB < p1 && !fB) {
+        ld_dims<DPL>(kc + ((size_t)pB * nkv + j) * hd + lane * DPL, kb);
+        ld_dims<DPL>(vc + ((size_t)pB * nkv + j) * hd + lane * DPL, vb);
+    }
+    // score one position into the running (max, sum, acc) of every query head
+    auto score = [&](const float (&kv)[DPL], const float (&vv)[DPL]) {
 #pragma unroll
         for (int g = 0; g < ATT_G; ++g) {
             if (g < G) {
@@ -392,6 +407,22 @@ __global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, cons
 #pragma unroll
                 for (int i = 0; i < DPL; ++i) acc[g][i] = acc[g][i] * a + b * vv[i];
                 m[g] = mn;
+            }
+        }
+    };
+    // positions in order pA, pA+8, pA+16, ...: each buffer is refilled
+    // 16 positions ahead as soon as it has been scored
+    for (int p = pA; p < p1; p += 16) {
+        score(ka, va);
+        if (p + 16 < p1) {
+            ld_dims<DPL>(kc + ((size_t)(p + 16) * nkv + j) * hd + lane * DPL, ka);
+            ld_dims<DPL>(vc + ((size_t)(p + 16) * nkv + j) * hd + lane * DPL, va);
+        }
+        if (p + 8 < p1) {
+            score(kb, vb);
+            if (p + 24 < p1) {
+                ld_dims<DPL>(kc + ((size_t)(p + 24) * nkv + j) * hd + lane * DPL, kb);
+                ld_dims<DPL>(vc + ((size_t)(p + 24) * nkv + j) * hd + lane * DPL, vb);
             }
         }
     }
@@ -437,14 +468,21 @@ __global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, cons
 template <int DPL>
 __global__ void __launch_bounds__(256) k_attn_reduce_gate_q8K(const float *part, const float *qkv, void *xq,
                                                               const int *pos_p, int nq, int smax) {
-    pdl_wait();
-    pdl_trigger();
     constexpr int hd = DPL * 32, rec = hd + 4, hpb = 256 / hd;
     __shared__ __align__(16) float red[8][rec];
     __shared__ float wmax[8];
     __shared__ __align__(16) float xs[256];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // the gate inputs come from the qkv projection, two launches back (done
+    // when this grid starts): read before the wait for the split records
+    float gv[hpb];
+#pragma unroll
+    for (int hh = 0; hh < hpb; ++hh)
+        gv[hh] = threadIdx.x < hd ? qkv[(size_t)(blockIdx.x * hpb + hh) * 2 * hd + hd + threadIdx.x] : 0.0f;
     const int S = att_splits(*pos_p + 1, smax);
+    pdl_wait();
+    pdl_trigger();
+#pragma unroll
     for (int hh = 0; hh < hpb; ++hh) {
         const int h = blockIdx.x * hpb + hh;
         float M = -INFINITY;
@@ -471,15 +509,15 @@ __global__ void __launch_bounds__(256) k_attn_reduce_gate_q8K(const float *part,
         for (int i = 0; i < DPL; ++i) red[warp][lane * DPL + i] = A[i];
         if (lane == 0) red[warp][hd] = Ls;
         __syncthreads();
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        if (threadIdx.x < hd) {  // hd <= 256 = blockDim.x: one value per thread
+            const int d = threadIdx.x;
             float o = 0.0f, L = 0.0f;
 #pragma unroll
             for (int w = 0; w < 8; ++w) {
                 o += red[w][d];
                 L += red[w][hd];
             }
-            const float g = qkv[(size_t)h * 2 * hd + hd + d];
-            xs[hh * hd + d] = (o / L) * (1.0f / (1.0f + expf(-g)));
+            xs[hh * hd + d] = (o / L) * (1.0f / (1.0f + expf(-gv[hh])));
         }
         __syncthreads();
     }

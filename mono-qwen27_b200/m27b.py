@@ -64,6 +64,7 @@ def lib():
         "m27b_qmv_f32_rmsnorm": (b, [wvp, wvp, vp, i32, vp, fp, i32, vp, vp, i32, vp, vp, cp, sz]),
         "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
         "m27b_hbm_read_probe": (b, [vp, sz, vp, cp, sz]),
+        "m27b_hbm_read_probe_shape": (b, [vp, sz, i32, i32, i32, i32, vp, cp, sz]),
         "m27b_qmv_q6k_ksplit_part_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_ksplit_count_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_ksplit": (b, [wvp, vp, i32, vp, i32, vp, vp, vp, vp, cp, sz]),
@@ -212,11 +213,17 @@ def qmv_q6k_ksplit(w, xq, n_tok, y, residual=None, part=None, count=None, stream
     return y
 
 
-def hbm_read_probe(buf, stream=None):
-    """One streaming read of the device tensor `buf` (see m27b_hbm_read_probe)."""
+def hbm_read_probe(buf, shape=None, stream=None):
+    """One streaming read of the device tensor `buf` (see
+    m27b_hbm_read_probe_shape); shape = (warps, stages, chunk, ctas_per_sm)
+    or None for the default one."""
     err = ctypes.create_string_buffer(ERR_CAP)
-    _check(lib().m27b_hbm_read_probe(_ptr(buf), buf.numel() * buf.element_size(), _stream(stream), err, ERR_CAP), err,
-           "m27b_hbm_read_probe")
+    n = buf.numel() * buf.element_size()
+    if shape is None:
+        ok = lib().m27b_hbm_read_probe(_ptr(buf), n, _stream(stream), err, ERR_CAP)
+    else:
+        ok = lib().m27b_hbm_read_probe_shape(_ptr(buf), n, *[int(v) for v in shape], _stream(stream), err, ERR_CAP)
+    _check(ok, err, "m27b_hbm_read_probe")
 
 
 def act_quant_swiglu(gate, up, act_type, out=None, stream=None):
