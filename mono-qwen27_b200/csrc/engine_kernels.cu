@@ -108,6 +108,37 @@ M27B_DI void ld_dims(const float *p, float (&v)[DPL]) {
     }
 }
 
+// Asynchronous global -> shared copies (cp.async; completion by
+// cp_async_wait_all in the issuing thread).
+M27B_DI void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+M27B_DI void cp_async8(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+                 : "memory");
+}
+M27B_DI void cp_async4(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+                 : "memory");
+}
+M27B_DI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// A lane's DPL consecutive floats of a row (16-, 8- or 4-byte aligned as DPL allows).
+template <int DPL>
+M27B_DI void cp_async_dims(float *dst, const float *src) {
+    if constexpr (DPL % 4 == 0) {
+#pragma unroll
+        for (int c = 0; c < DPL / 4; ++c) cp_async16(dst + 4 * c, src + 4 * c);
+    } else if constexpr (DPL == 2) {
+        cp_async8(dst, src);
+    } else {
+#pragma unroll
+        for (int c = 0; c < DPL; ++c) cp_async4(dst + c, src + c);
+    }
+}
+
 template <int DPL>
 __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const float *kc, const float *vc, float *part,
                                                       const int *pos_p, int nq, int nkv, float scale, int q_stride,
@@ -313,57 +344,121 @@ M27B_DI void norm_rope_warp(const float *src, const float *nw, float *dst, float
 }
 
 // Split attention with the q/k norm, RoPE and KV-cache append folded in.
-// grid (nkv, splits), 256 threads.  qkv = [nq heads of (q, gate) | nkv k
-// heads | nkv v heads].  Warp g normalises and rotates query head j*G + g
-// into shared memory.  The newest position L - 1 (= *pos) lies in the last
-// active split only: that CTA also normalises and rotates kv head j's k,
-// appends k and v at position L - 1 of the caches, and reads them back like
-// any other position (no other CTA touches it).  Then as k_attn_partial.
+// grid (nkv, splits), 256 threads, G = nq / nkv query heads per kv head (a
+// template parameter: the heads' arithmetic is unrolled and interleaved).
+// qkv = [nq heads of (q, gate) | nkv k heads | nkv v heads].  Warp g < G
+// normalises and rotates query head j*G + g into shared memory.  The newest
+// position L - 1 (= *pos) lies in the last active split only: there warp G
+// (warp 0 after its query head when G = 8) also normalises and rotates kv
+// head j's k and appends k and v at position L - 1 of the caches, which the
+// CTA reads back after a barrier (no other CTA touches it).  Warp w scores
+// positions p0 + w, p0 + w + 8, ...: the G dot products of a position are
+// reduced over the lanes in interleaved butterflies, then the running (max,
+// sum, acc) of each head is updated.  The warps' records
+// are combined with per-(warp, head) scale factors computed once.
 //
 // Before griddepcontrol.wait the kernel reads only what the launch order has
 // already completed (when this grid starts, its predecessor — the qkv
 // projection — has passed its own wait, so every earlier kernel of the step,
 // the position advance and the rotary table included, is done): the
-// position, and the K/V rows of this warp's first two positions unless one
-// of them is the newest (appended below).  Those rows are in flight while
-// the projection drains.
+// position, the K/V rows of this warp's first two positions unless one of
+// them is the newest (appended below), and (into shared memory, once per
+// CTA) the q/k norm weights and the rotary factors.  All of it is in flight
+// while the projection drains; after the wait only the q (and k, v) rows
+// are read.
+// As norm_rope_warp, with the norm weights (nw, hd values) and the rotary
+// factors (rope, n_rot / 2 pairs) already in shared memory.
 template <int DPL>
-__global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, const float *q_norm, const float *k_norm,
-                                                          float *kc, float *vc, float *part, const int *pos_p, int nq,
-                                                          int nkv, float scale, const float2 *rope, int n_rot,
-                                                          float eps) {
+M27B_DI void norm_rope_apply(const float *src, const float *nw, const float2 *rope, float *dst, float mul, int n_rot,
+                             float eps, int lane) {
+    constexpr int hd = DPL * 32;
+    float v[DPL];
+    ld_dims<DPL>(src + lane * DPL, v);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) ss = fmaf(v[i], v[i], ss);
+    ss = warp_sum(ss);
+    const float sc = rsqrtf(ss / (float)hd + eps);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+        v[i] = v[i] * sc * nw[lane * DPL + i];
+        dst[lane * DPL + i] = v[i];
+    }
+    __syncwarp();
+    const int half = n_rot / 2;
+    float out[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+        const int d = lane * DPL + i;
+        out[i] = v[i];
+        if (d < n_rot) {
+            const float2 r = rope[d < half ? d : d - half];
+            out[i] = d < half ? v[i] * r.x - dst[d + half] * r.y : dst[d - half] * r.y + v[i] * r.x;
+        }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) dst[lane * DPL + i] = out[i] * mul;
+    __syncwarp();
+}
+
+constexpr int ATT_SLOTS = 4;  // positions per warp whose K/V rows are copied before the wait
+
+size_t attn_qkv_smem_bytes(int G, int hd) {
+    // q [G][hd] | k scratch / warp records [8][G][hd] | (m, l) [8][G][2] |
+    // scale factors [8][G] | q_norm, k_norm [hd] each | rotary pairs (<= hd
+    // floats) | K/V slots [8][ATT_SLOTS][2][hd]
+    return (size_t)(G * hd + 8 * G * hd + 8 * G * 2 + 8 * G + 3 * hd + 8 * ATT_SLOTS * 2 * hd) * sizeof(float);
+}
+
+template <int DPL, int G>
+__global__ void __launch_bounds__(256, 2) k_attn_partial_qkv(const float *qkv, const float *q_norm, const float *k_norm,
+                                                             float *kc, float *vc, float *part, const int *pos_p,
+                                                             int nq, int nkv, float scale, const float2 *rope,
+                                                             int n_rot, float eps) {
     constexpr int hd = DPL * 32, rec = hd + 4;
     const int j = blockIdx.x, s = blockIdx.y;
-    const int G = nq / nkv;
     const int pos = *pos_p, L = pos + 1;
     const int S = att_splits(L, gridDim.y);
     if (s >= S) return;
     const int p0 = (int)(((long)L * s) / S), p1 = (int)(((long)L * (s + 1)) / S);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // two K/V rows per warp in registers: buffer A holds positions pA, pA+16,
-    // ..., buffer B positions pA+8, pA+24, ...
-    const int pA = p0 + warp, pB = pA + 8;
-    float ka[DPL], va[DPL], kb[DPL], vb[DPL];
-    const bool fA = pA < p1 && pA != pos, fB = pB < p1 && pB != pos;
-    if (fA) {
-        ld_dims<DPL>(kc + ((size_t)pA * nkv + j) * hd + lane * DPL, ka);
-        ld_dims<DPL>(vc + ((size_t)pA * nkv + j) * hd + lane * DPL, va);
+    const bool appender = s == S - 1;
+    const int kwarp = G < 8 ? G : 0;  // the warp that appends k, v (last split)
+    extern __shared__ __align__(16) float sh[];
+    float *qs = sh;                      // [G][hd] queries, normalised, rotated, times scale
+    float *cb = sh + G * hd;             // k scratch, then the warps' records [8][G][hd]
+    float *mlw = cb + 8 * G * hd;        // [8][G][2] (max, sum) per warp and head
+    float *fw = mlw + 8 * G * 2;         // [8][G] scale factor of each warp's record
+    float *wq = fw + 8 * G;              // q_norm [hd]
+    float *wk = wq + hd;                 // k_norm [hd]
+    float2 *rp = (float2 *)(wk + hd);    // rotary pairs [n_rot / 2]
+    float *kvs = wk + 2 * hd;            // [8 warps][ATT_SLOTS][K, V][hd] prefetched rows
+    // warp w's positions are pA + 8i; the first ATT_SLOTS of them (other
+    // than the newest, appended below) are copied into its slots now
+    const int pA = p0 + warp;
+    float *myk = kvs + (size_t)warp * ATT_SLOTS * 2 * hd;
+#pragma unroll
+    for (int i = 0; i < ATT_SLOTS; ++i) {
+        const int p = pA + 8 * i;
+        if (p < p1 && p != pos) {
+            cp_async_dims<DPL>(myk + (2 * i) * hd + lane * DPL, kc + ((size_t)p * nkv + j) * hd + lane * DPL);
+            cp_async_dims<DPL>(myk + (2 * i + 1) * hd + lane * DPL, vc + ((size_t)p * nkv + j) * hd + lane * DPL);
+        }
     }
-    if (fB) {
-        ld_dims<DPL>(kc + ((size_t)pB * nkv + j) * hd + lane * DPL, kb);
-        ld_dims<DPL>(vc + ((size_t)pB * nkv + j) * hd + lane * DPL, vb);
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        wq[i] = q_norm ? q_norm[i] : 1.0f;
+        wk[i] = k_norm ? k_norm[i] : 1.0f;
     }
+    for (int i = threadIdx.x; i < n_rot / 2; i += blockDim.x) rp[i] = rope[i];
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
-    extern __shared__ __align__(16) float sh[];  // q [G][hd] (pre-scaled), then [8 warps][G][rec]
-    float *qs = sh;
-    float *cb = sh + G * hd;
     if (warp < G)
-        norm_rope_warp<DPL>(qkv + (size_t)(j * G + warp) * 2 * hd, q_norm, qs + warp * hd, scale, rope, n_rot, eps,
-                            lane);
-    if (s == S - 1 && warp == 0) {
+        norm_rope_apply<DPL>(qkv + (size_t)(j * G + warp) * 2 * hd, wq, rp, qs + warp * hd, scale, n_rot, eps, lane);
+    if (appender && warp == kwarp) {
         const size_t off = ((size_t)pos * nkv + j) * hd;
-        norm_rope_warp<DPL>(qkv + (size_t)nq * 2 * hd + (size_t)j * hd, k_norm, cb, 1.0f, rope, n_rot, eps, lane);
+        norm_rope_apply<DPL>(qkv + (size_t)nq * 2 * hd + (size_t)j * hd, wk, rp, cb, 1.0f, n_rot, eps, lane);
         const float *vsrc = qkv + (size_t)nq * 2 * hd + (size_t)nkv * hd + (size_t)j * hd;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
@@ -372,105 +467,118 @@ __global__ void __launch_bounds__(256) k_attn_partial_qkv(const float *qkv, cons
             vc[off + d] = vsrc[d];
         }
     }
-    __syncthreads();  // q in shared memory; the appended k/v visible to this CTA
-    float acc[ATT_G][DPL], m[ATT_G], l[ATT_G];
+    cp_async_wait_all();  // this lane's slot rows (it reads only its own dims of them)
+    __syncthreads();      // q in shared memory; the appended k/v visible to this CTA
+    float acc[G][DPL], m[G], l[G];
 #pragma unroll
-    for (int g = 0; g < ATT_G; ++g) {
+    for (int g = 0; g < G; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.0f;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) acc[g][i] = 0.0f;
     }
-    // the newest position's rows (written above) are read after the barrier
-    if (pA < p1 && !fA) {
-        ld_dims<DPL>(kc + ((size_t)pA * nkv + j) * hd + lane * DPL, ka);
-        ld_dims<DPL>(vc + ((size_t)pA * nkv + j) * hd + lane * DPL, va);
-    }
-    if (pB < p1 && !fB) {
-        ld_dims<DPL>(kc + ((size_t)pB * nkv + j) * hd + lane * DPL, kb);
-        ld_dims<DPL>(vc + ((size_t)pB * nkv + j) * hd + lane * DPL, vb);
-    }
-    // score one position into the running (max, sum, acc) of every query head
-    auto score = [&](const float (&kv)[DPL], const float (&vv)[DPL]) {
+    // row r (0 = K, 1 = V) of position p = pA + 8i: from the warp's slot when
+    // it was prefetched, else (the newest position, or beyond the slots) from
+    // global memory
+    auto row = [&](int i, int p, int r, float (&out)[DPL]) {
+        if (i < ATT_SLOTS && p != pos)
+            ld_dims<DPL>(myk + (2 * i + r) * hd + lane * DPL, out);
+        else
+            ld_dims<DPL>((r ? vc : kc) + ((size_t)p * nkv + j) * hd + lane * DPL, out);
+    };
+    auto update = [&](int g, float d, const float (&vv)[DPL]) {
+        const float mn = fmaxf(m[g], d);
+        const float a = expf(m[g] - mn), b = expf(d - mn);
+        l[g] = l[g] * a + b;
 #pragma unroll
-        for (int g = 0; g < ATT_G; ++g) {
-            if (g < G) {
+        for (int i = 0; i < DPL; ++i) acc[g][i] = acc[g][i] * a + b * vv[i];
+        m[g] = mn;
+    };
+    // one position per step: G dot products, their lane sums in interleaved
+    // butterflies, then each head's running update
+    for (int i = 0; pA + 8 * i < p1; ++i) {
+        const int p = pA + 8 * i;
+        float dq[G];
+        {
+            float kr[DPL];
+            row(i, p, 0, kr);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
                 float qv[DPL];
                 ld_dims<DPL>(qs + g * hd + lane * DPL, qv);
-                float d = 0.0f;
+                float x = 0.0f;
 #pragma unroll
-                for (int i = 0; i < DPL; ++i) d = fmaf(qv[i], kv[i], d);
-                d = warp_sum(d);
-                const float mn = fmaxf(m[g], d);
-                const float a = expf(m[g] - mn), b = expf(d - mn);
-                l[g] = l[g] * a + b;
-#pragma unroll
-                for (int i = 0; i < DPL; ++i) acc[g][i] = acc[g][i] * a + b * vv[i];
-                m[g] = mn;
+                for (int d = 0; d < DPL; ++d) x = fmaf(qv[d], kr[d], x);
+                dq[g] = x;
             }
         }
-    };
-    // positions in order pA, pA+8, pA+16, ...: each buffer is refilled
-    // 16 positions ahead as soon as it has been scored
-    for (int p = pA; p < p1; p += 16) {
-        score(ka, va);
-        if (p + 16 < p1) {
-            ld_dims<DPL>(kc + ((size_t)(p + 16) * nkv + j) * hd + lane * DPL, ka);
-            ld_dims<DPL>(vc + ((size_t)(p + 16) * nkv + j) * hd + lane * DPL, va);
-        }
-        if (p + 8 < p1) {
-            score(kb, vb);
-            if (p + 24 < p1) {
-                ld_dims<DPL>(kc + ((size_t)(p + 24) * nkv + j) * hd + lane * DPL, kb);
-                ld_dims<DPL>(vc + ((size_t)(p + 24) * nkv + j) * hd + lane * DPL, vb);
-            }
-        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < G; ++g) dq[g] += __shfl_xor_sync(0xffffffffu, dq[g], o);
+        float vv[DPL];
+        row(i, p, 1, vv);
+#pragma unroll
+        for (int g = 0; g < G; ++g) update(g, dq[g], vv);
     }
     __syncthreads();  // the k scratch in cb is reused below
 #pragma unroll
-    for (int g = 0; g < ATT_G; ++g) {
-        if (g < G) {
-            float *r = cb + ((size_t)warp * G + g) * rec;
+    for (int g = 0; g < G; ++g) {
+        float *r = cb + ((size_t)warp * G + g) * hd;
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) r[lane * DPL + i] = acc[g][i];
-            if (lane == 0) {
-                r[hd] = m[g];
-                r[hd + 1] = l[g];
+        for (int i = 0; i < DPL; ++i) r[lane * DPL + i] = acc[g][i];
+    }
+    if (lane < G) {
+        // lane g publishes head g's (max, sum); the compile-time index keeps them in registers
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            if (lane == g) {
+                mlw[(warp * G + g) * 2] = m[g];
+                mlw[(warp * G + g) * 2 + 1] = l[g];
             }
+    }
+    __syncthreads();
+    // scale factor of warp w's record of head g against the heads' maximum
+    if (threadIdx.x < 8 * G) {
+        const int w = threadIdx.x / G, g = threadIdx.x - w * G;
+        float M = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) M = fmaxf(M, mlw[(u * G + g) * 2]);
+        const float mw = mlw[(w * G + g) * 2];
+        fw[w * G + g] = mw == -INFINITY ? 0.0f : expf(mw - M);
+        if (w == 0) {
+            float Lsum = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float mu = mlw[(u * G + g) * 2];
+                Lsum += mlw[(u * G + g) * 2 + 1] * (mu == -INFINITY ? 0.0f : expf(mu - M));
+            }
+            float *o = part + ((size_t)s * nq + j * G + g) * rec;
+            o[hd] = M;
+            o[hd + 1] = Lsum;
         }
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
         const int g = idx / hd, dd = idx - g * hd;
-        float M = -INFINITY;
+        float A = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) M = fmaxf(M, cb[((size_t)w * G + g) * rec + hd]);
-        float Lsum = 0.0f, A = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            const float *r = cb + ((size_t)w * G + g) * rec;
-            const float f = r[hd] == -INFINITY ? 0.0f : expf(r[hd] - M);
-            Lsum += r[hd + 1] * f;
-            A += r[dd] * f;
-        }
-        float *o = part + ((size_t)s * nq + j * G + g) * rec;
-        o[dd] = A;
-        if (dd == 0) {
-            o[hd] = M;
-            o[hd + 1] = Lsum;
-        }
+        for (int w = 0; w < 8; ++w) A += cb[((size_t)w * G + g) * hd + dd] * fw[w * G + g];
+        part[((size_t)s * nq + j * G + g) * rec + dd] = A;
     }
 }
 
 // Split reduction + sigmoid gate + q8_K quantization: grid nq*hd/256 (hd
 // divides 256), 256 threads; CTA b produces q8_K block b of the gated
 // attention output o * sigmoid(gate) (heads b*256/hd ..), the input of o_proj.
+// Warp w folds splits w, w + 8, ... into a running (max, sum, acc) in one
+// pass over the records (the loads of a warp's splits are independent), then
+// the 8 warps' results are combined against their common maximum.
 template <int DPL>
 __global__ void __launch_bounds__(256) k_attn_reduce_gate_q8K(const float *part, const float *qkv, void *xq,
                                                               const int *pos_p, int nq, int smax) {
     constexpr int hd = DPL * 32, rec = hd + 4, hpb = 256 / hd;
     __shared__ __align__(16) float red[8][rec];
-    __shared__ float wmax[8];
     __shared__ __align__(16) float xs[256];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     // the gate inputs come from the qkv projection, two launches back (done
@@ -485,37 +593,40 @@ __global__ void __launch_bounds__(256) k_attn_reduce_gate_q8K(const float *part,
 #pragma unroll
     for (int hh = 0; hh < hpb; ++hh) {
         const int h = blockIdx.x * hpb + hh;
-        float M = -INFINITY;
-#pragma unroll 4
-        for (int s = warp; s < S; s += 8) M = fmaxf(M, part[((size_t)s * nq + h) * rec + hd]);
-        if (lane == 0) wmax[warp] = M;
-        __syncthreads();
-#pragma unroll
-        for (int w = 0; w < 8; ++w) M = fmaxf(M, wmax[w]);
-        float A[DPL], Ls = 0.0f;
+        float M = -INFINITY, Ls = 0.0f, A[DPL];
 #pragma unroll
         for (int i = 0; i < DPL; ++i) A[i] = 0.0f;
 #pragma unroll 4
         for (int s = warp; s < S; s += 8) {
             const float *r = part + ((size_t)s * nq + h) * rec;
-            const float f = expf(r[hd] - M);
-            Ls = fmaf(f, r[hd + 1], Ls);
             float v[DPL];
             ld_dims<DPL>(r + lane * DPL, v);
+            const float mr = r[hd], lr = r[hd + 1];  // every active split holds at least one position
+            const float mn = fmaxf(M, mr);
+            const float a = expf(M - mn), b = expf(mr - mn);
+            Ls = Ls * a + lr * b;
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) A[i] = fmaf(f, v[i], A[i]);
+            for (int i = 0; i < DPL; ++i) A[i] = A[i] * a + b * v[i];
+            M = mn;
         }
 #pragma unroll
         for (int i = 0; i < DPL; ++i) red[warp][lane * DPL + i] = A[i];
-        if (lane == 0) red[warp][hd] = Ls;
+        if (lane == 0) {
+            red[warp][hd] = M;
+            red[warp][hd + 1] = Ls;
+        }
         __syncthreads();
         if (threadIdx.x < hd) {  // hd <= 256 = blockDim.x: one value per thread
             const int d = threadIdx.x;
+            float Mx = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) Mx = fmaxf(Mx, red[w][hd]);
             float o = 0.0f, L = 0.0f;
 #pragma unroll
             for (int w = 0; w < 8; ++w) {
-                o += red[w][d];
-                L += red[w][hd];
+                const float f = red[w][hd] == -INFINITY ? 0.0f : expf(red[w][hd] - Mx);  // a warp with no split
+                o += red[w][d] * f;
+                L += red[w][hd + 1] * f;
             }
             xs[hh * hd + d] = (o / L) * (1.0f / (1.0f + expf(-gv[hh])));
         }
@@ -544,21 +655,49 @@ static cudaError_t attn_run(const float *q, const float *kc, const float *vc, fl
                       part_stride, q_stride);
 }
 
+template <int DPL, int G>
+static cudaError_t attn_qkv_opt_in() {
+    return cudaFuncSetAttribute(k_attn_partial_qkv<DPL, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)attn_qkv_smem_bytes(G, DPL * 32));
+}
+
 template <int DPL>
 static cudaError_t attn_opt_in() {
     const int smem = (int)attn_smem_bytes(ATT_G, DPL * 32);
     const cudaError_t e = cudaFuncSetAttribute(k_attn_partial<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess || (DPL != 1 && DPL != 2 && DPL != 4 && DPL != 8)) return e;
-    return cudaFuncSetAttribute(k_attn_partial_qkv<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if constexpr (DPL == 1 || DPL == 2 || DPL == 4 || DPL == 8) {
+        for (cudaError_t r : {attn_qkv_opt_in<DPL, 1>(), attn_qkv_opt_in<DPL, 2>(), attn_qkv_opt_in<DPL, 3>(),
+                              attn_qkv_opt_in<DPL, 4>(), attn_qkv_opt_in<DPL, 5>(), attn_qkv_opt_in<DPL, 6>(),
+                              attn_qkv_opt_in<DPL, 7>(), attn_qkv_opt_in<DPL, 8>()})
+            if (r != cudaSuccess) return r;
+    }
+    return cudaSuccess;
+}
+
+template <int DPL, int G>
+static cudaError_t attn_partial_qkv_run(const float *qkv, const float *q_norm, const float *k_norm, float *kc,
+                                        float *vc, float *part, const int *pos, int nq, int nkv, int S, float scale,
+                                        const float2 *rope, int n_rot, float eps, cudaStream_t st) {
+    return launch_pdl(k_attn_partial_qkv<DPL, G>, dim3(nkv, S), dim3(256), attn_qkv_smem_bytes(G, DPL * 32), st, qkv,
+                      q_norm, k_norm, kc, vc, part, pos, nq, nkv, scale, rope, n_rot, eps);
 }
 
 template <int DPL>
 static cudaError_t attn_fused_run(const float *qkv, const float *q_norm, const float *k_norm, float *kc, float *vc,
                                   float *part, void *xq, const int *pos, int nq, int nkv, int S, float scale,
                                   const float2 *rope, int n_rot, float eps, cudaStream_t st) {
-    const size_t smem = attn_smem_bytes(nq / nkv, DPL * 32);
-    cudaError_t e = launch_pdl(k_attn_partial_qkv<DPL>, dim3(nkv, S), dim3(256), smem, st, qkv, q_norm, k_norm, kc, vc,
-                               part, pos, nq, nkv, scale, rope, n_rot, eps);
+    cudaError_t e;
+    switch (nq / nkv) {
+#define M27B_ATT_G(GG)                                                                                                 \
+    case GG:                                                                                                           \
+        e = attn_partial_qkv_run<DPL, GG>(qkv, q_norm, k_norm, kc, vc, part, pos, nq, nkv, S, scale, rope, n_rot, eps, \
+                                          st);                                                                         \
+        break;
+        M27B_ATT_G(1) M27B_ATT_G(2) M27B_ATT_G(3) M27B_ATT_G(4) M27B_ATT_G(5) M27B_ATT_G(6) M27B_ATT_G(7) M27B_ATT_G(8)
+#undef M27B_ATT_G
+        default: return cudaErrorInvalidValue;
+    }
     if (e != cudaSuccess) return e;
     return launch_pdl(k_attn_reduce_gate_q8K<DPL>, dim3(nq * DPL * 32 / 256), dim3(256), 0, st, (const float *)part, qkv,
                       xq, pos, nq, S);
@@ -616,13 +755,7 @@ struct AttnBatchArgs {
 };
 
 // 16 bytes global -> shared without a register round trip (L2 only).
-M27B_DI void cp_async16(void *smem, const void *gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
-                 "l"(gmem)
-                 : "memory");
-}
 // This thread's asynchronous copies have landed.
-M27B_DI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 M27B_DI int abt_splits(int L, int smax) {
     const int s = (L + ABT_CH - 1) / ABT_CH;

@@ -122,8 +122,6 @@ __global__ void __launch_bounds__(KSP_WARPS * 32, 1)
     for (int s = 0; s < 8; ++s)
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[s][t] = 0.0f;
-    const int s_lo = 2 * rr, s_hi = 2 * rr + 4;
-    const int sc_byte = 8 * half + 2 * rr + lsub;
     bool ok = true;
     int cs = 0, ci = 0;
     uint32_t cph = 0;
@@ -150,41 +148,7 @@ __global__ void __launch_bounds__(KSP_WARPS * 32, 1)
                     bhi[t] = (int)(int16_t)(pr >> 16);
                     dx[t] = xd[t * nbr + bl];
                 }
-#pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const uint8_t *tl = it + s * Q6T_TILE;
-                    const uint4 ql = *(const uint4 *)(tl + qd * 128 + 16 * c);
-                    const uint4 qh = *(const uint4 *)(tl + 512 + qd * 64 + 16 * (2 * half + lsub));
-                    const uint4 scw = *(const uint4 *)(tl + 768 + qd * 16);
-                    const float dw = h2f(*(const uint32_t *)(tl + 832 + qd * 4));
-                    const uint32_t sw_lo = sc_byte < 4 ? scw.x : sc_byte < 8 ? scw.y : sc_byte < 12 ? scw.z : scw.w;
-                    const uint32_t sw_hi = sc_byte < 4 ? scw.y : sc_byte < 8 ? scw.z : scw.w;
-                    const int scl = (int)(int8_t)((sw_lo >> (8 * (sc_byte & 3))) & 0xffu);
-                    const int sch = (int)(int8_t)((sw_hi >> (8 * (sc_byte & 3))) & 0xffu);
-                    uint32_t lo[4], hi[4];
-                    lo[0] = (ql.x & 0x0f0f0f0fu) | (((qh.x >> s_lo) & 0x03030303u) << 4);
-                    lo[1] = (ql.y & 0x0f0f0f0fu) | (((qh.y >> s_lo) & 0x03030303u) << 4);
-                    lo[2] = (ql.z & 0x0f0f0f0fu) | (((qh.z >> s_lo) & 0x03030303u) << 4);
-                    lo[3] = (ql.w & 0x0f0f0f0fu) | (((qh.w >> s_lo) & 0x03030303u) << 4);
-                    hi[0] = ((ql.x >> 4) & 0x0f0f0f0fu) | (((qh.x >> s_hi) & 0x03030303u) << 4);
-                    hi[1] = ((ql.y >> 4) & 0x0f0f0f0fu) | (((qh.y >> s_hi) & 0x03030303u) << 4);
-                    hi[2] = ((ql.z >> 4) & 0x0f0f0f0fu) | (((qh.z >> s_hi) & 0x03030303u) << 4);
-                    hi[3] = ((ql.w >> 4) & 0x0f0f0f0fu) | (((qh.w >> s_hi) & 0x03030303u) << 4);
-#pragma unroll
-                    for (int t = 0; t < NT; ++t) {
-                        int dl = dp4a_us(lo[0], xa[t].x, 0);
-                        dl = dp4a_us(lo[1], xa[t].y, dl);
-                        dl = dp4a_us(lo[2], xa[t].z, dl);
-                        dl = dp4a_us(lo[3], xa[t].w, dl);
-                        int dh = dp4a_us(hi[0], xh[t].x, 0);
-                        dh = dp4a_us(hi[1], xh[t].y, dh);
-                        dh = dp4a_us(hi[2], xh[t].z, dh);
-                        dh = dp4a_us(hi[3], xh[t].w, dh);
-                        // codes are stored +32: <q-32, x> = <q, x> - 32 * bsum
-                        const int isum = scl * (dl - 32 * blo[t]) + sch * (dh - 32 * bhi[t]);
-                        acc[s][t] = fmaf(dw * dx[t], (float)isum, acc[s][t]);
-                    }
-                }
+                q6t_item_mac<NT>(it, qd, c, half, rr, lsub, xa, xh, blo, bhi, dx, acc);
             }
             __syncwarp();  // every lane is done with this stage before it is refilled
             issue_item();
