@@ -174,6 +174,24 @@ M27B_API bool m27b_qmv_q6k_ksplit(const struct WeightView *w, const void *xq, in
                                   const float *residual, void *part, void *count, cudaStream_t stream, char *err,
                                   size_t err_cap);
 
+/* q6_K matvec for ONE token over a matrix of few, long rows (a decode step's
+ * ffn_down, 5120 x 17408), y = W.xq (+ residual): the (8-row group, 4-block
+ * tile) items are cut into equal runs, one per warp of a one-CTA-per-SM grid,
+ * so that no SM carries more row groups than another; a group shared by
+ * several runs is summed by the run that finishes it last, in run order
+ * (deterministic; within fp32 rounding of m27b_qmv).  Needs the repacked
+ * q6_K layout and rows of at most 609 blocks (the staged activation row must
+ * leave room for 4 warps' stages); the caller passes
+ * m27b_qmv_q6k_stream_part_bytes of scratch for partial sums and
+ * m27b_qmv_q6k_stream_count_bytes of counters that must be zero before the
+ * first call (each call leaves them zero).  Calls overlapping on the GPU
+ * with the same scratch race.  Replaces, for one token, the reference's
+ * k_q6k_mv_q8_dp4a (src/mono27b_executor.cu:630-645). */
+M27B_API size_t m27b_qmv_q6k_stream_part_bytes(const struct WeightView *w);
+M27B_API size_t m27b_qmv_q6k_stream_count_bytes(const struct WeightView *w);
+M27B_API bool m27b_qmv_q6k_stream(const struct WeightView *w, const void *xq, float *y, const float *residual,
+                                  void *part, void *count, cudaStream_t stream, char *err, size_t err_cap);
+
 /* fp32 activations in, like the reference's l_mv_quant(W, x, y)
  * (src/mono27b_executor.cu:2033-2050, its quantizer k_quant_q8_1 :84-107):
  * x rows (n_tok of them, stride ldx floats) are quantized to q8_K / q8_0 and

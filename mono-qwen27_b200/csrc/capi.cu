@@ -306,6 +306,42 @@ bool qmv_common(int epi, const WeightView *w0, const WeightView *w1, const void 
 }  // namespace
 
 namespace m27b {
+size_t q6k_stream_part_floats(int rows, int rb);
+size_t q6k_stream_count_words(int rows);
+bool q6k_stream_applies(int k);
+cudaError_t launch_q6k_stream(const QmvArgs &a, float *part, unsigned *count, int sm_count, cudaStream_t st);
+
+// q6_K x one token with the (row group, tile) items cut evenly over the
+// grid's warps (ffn_down in a decode step): part holds
+// q6k_stream_part_floats(rows, rb) floats, count one zeroed word per 8-row
+// group.  q8_K activations xq, or fp32 x quantized in the prologue.
+bool qmv_q6k_stream(const WeightView *w, const void *xq, const float *xf, float *y, const float *residual, float *part,
+                    unsigned *count, cudaStream_t stream, char *err, size_t cap) {
+    const char *what = "qmv_q6k_stream";
+    WDesc d{};
+    if (!describe(w, d, what, err, cap)) return false;
+    if (d.kind != W_Q6KP) return fail(err, cap, "%s: repacked q6_K weights only", what);
+    if ((!xq && !xf) || !y || !part || !count) return fail(err, cap, "%s: null pointer", what);
+    if (!q6k_stream_applies(d.k)) return fail(err, cap, "%s: rows of %d values are too long to stage", what, d.k);
+    const int sms = sm_count_current();
+    int *status = status_ptr_current();
+    if (sms <= 0 || !status) return fail(err, cap, "%s: no CUDA device", what);
+    QmvArgs a{};
+    a.w0 = (const uint8_t *)w->ptr;
+    a.xq = xq;
+    a.xf = xf;
+    a.ldxf = d.k;
+    a.y = y;
+    a.residual = residual;
+    a.row_stride = d.row_stride;
+    a.ldy = (int)w->row_count;
+    a.rows = (int)w->row_count;
+    a.rb = (int)w->row_blocks;
+    a.k = d.k;
+    a.status = status;
+    return cuda_ok(launch_q6k_stream(a, part, count, sms, stream), what, err, cap) && ok(err, cap);
+}
+
 int q6k_ksplit_ranges(int rb);
 size_t q6k_ksplit_part_floats(int rows, int ks);
 cudaError_t launch_q6k_ksplit(const QmvArgs &a_in, int n_tok, float *part, unsigned *count, int sm_count,
@@ -578,6 +614,24 @@ size_t m27b_qmv_q6k_ksplit_part_bytes(const WeightView *w) {
 size_t m27b_qmv_q6k_ksplit_count_bytes(const WeightView *w) {
     if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
     return q6k_ksplit_ranges((int)w->row_blocks) ? (size_t)((w->row_count + 7) / 8) * sizeof(unsigned) : 0;
+}
+
+size_t m27b_qmv_q6k_stream_part_bytes(const WeightView *w) {
+    if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
+    return q6k_stream_part_floats((int)w->row_count, (int)w->row_blocks) * sizeof(float);
+}
+
+size_t m27b_qmv_q6k_stream_count_bytes(const WeightView *w) {
+    if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
+    return q6k_stream_count_words((int)w->row_count) * sizeof(unsigned);
+}
+
+bool m27b_qmv_q6k_stream(const WeightView *w, const void *xq, float *y, const float *residual, void *part, void *count,
+                         cudaStream_t stream, char *err, size_t err_cap) {
+    if (((uintptr_t)part & 15) || ((uintptr_t)count & 3))
+        return fail(err, err_cap, "m27b_qmv_q6k_stream: misaligned scratch");
+    if (!xq) return fail(err, err_cap, "m27b_qmv_q6k_stream: null pointer");
+    return qmv_q6k_stream(w, xq, nullptr, y, residual, (float *)part, (unsigned *)count, stream, err, err_cap);
 }
 
 bool m27b_qmv_q6k_ksplit(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,

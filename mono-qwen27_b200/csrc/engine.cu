@@ -59,6 +59,11 @@ bool qmv_q6k_ksplit(const WeightView *w, const void *xq, int n_tok, float *y, in
 bool qmv_swiglu_q8(const WeightView *gate, const WeightView *up, const void *xq, const float *xf, const float *norm_w,
                    float eps, float *y, void *q8out, unsigned *q8cnt, cudaStream_t stream, char *err, size_t cap);
 int q6k_ksplit_ranges(int rb);
+size_t q6k_stream_part_floats(int rows, int rb);
+size_t q6k_stream_count_words(int rows);
+bool q6k_stream_applies(int k);
+bool qmv_q6k_stream(const WeightView *w, const void *xq, const float *xf, float *y, const float *residual, float *part,
+                    unsigned *count, cudaStream_t stream, char *err, size_t cap);
 size_t q6k_ksplit_part_floats(int rows, int ks);
 // Gated DeltaNet block (ssm.cu)
 cudaError_t ssm_rmsnorm_launch(const float *x, const float *w, float eps, int n, float *y, cudaStream_t st);
@@ -271,6 +276,17 @@ bool mv(M27BEngine *e, const QMat &m, const uint8_t *xq, float *y, const float *
     return m27b_qmv(&m.v, xq, 1, y, m.rows, res, e->st, err, err_cap);
 }
 
+// The down projection of one token (rows = hidden, long rows): a repacked
+// q6_K matrix goes to the kernel that cuts its items evenly over the warps
+// (its few row groups do not spread evenly over the SMs as whole groups),
+// anything else to the one-pass matvec.
+bool down_mv(M27BEngine *e, const QMat &m, const uint8_t *xq, float *y, const float *res, char *err, size_t err_cap) {
+    if (e->sk_part && m.v.ggml_type == (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) && m.rows <= e->c.hidden &&
+        (int)m.v.row_blocks <= e->F / 256 + 1 && q6k_stream_applies((int)m.v.row_blocks * 256))
+        return qmv_q6k_stream(&m.v, xq, nullptr, y, res, e->sk_part, e->sk_count, e->st, err, err_cap);
+    return mv(e, m, xq, y, res, err, err_cap);
+}
+
 bool allreduce_hidden(M27BEngine *e, float *buf, char *err, size_t err_cap) {
     if (e->c.tp_size == 1) return true;
     ENCCL(ncclAllReduce(buf, buf, (size_t)e->c.hidden, ncclFloat32, ncclSum, e->comm, e->st));
@@ -370,13 +386,13 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
             if (ffn_q8(Ly)) {
                 ECALL(qmv_swiglu_q8(&Ly.wg.v, &Ly.wu.v, nullptr, e->h2, Ly.post_norm, c.rms_eps, e->a, e->xq2,
                                     e->ffn_cnt, e->st, err, err_cap));
-                ECALL(mv(e, Ly.wd, e->xq2, e->h, e->h2, err, err_cap));
+                ECALL(down_mv(e, Ly.wd, e->xq2, e->h, e->h2, err, err_cap));
                 continue;
             }
             ECALL(m27b_qmv_f32_rmsnorm(&Ly.wg.v, &Ly.wu.v, e->h2, c.hidden, Ly.post_norm, c.rms_eps, 1, e->xq, e->a, e->F,
                                        nullptr, e->st, err, err_cap));
             ECALL(m27b_act_quant(e->a, e->F, 1, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
-            ECALL(mv(e, Ly.wd, e->xq, e->h, e->h2, err, err_cap));
+            ECALL(down_mv(e, Ly.wd, e->xq, e->h, e->h2, err, err_cap));
             continue;
         }
         if (p2p)
@@ -430,7 +446,7 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
             ECALL(qmv_push(&Ly.wd.v, dxq, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), e->st, err, err_cap));
             ECALL(consume(e, 1, 2u * l + 1u, next_norm, e->h, err, err_cap));
         } else {
-            ECALL(mv(e, Ly.wd, dxq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
+            ECALL(down_mv(e, Ly.wd, dxq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
             ECALL(allreduce_hidden(e, e->h, err, err_cap));
         }
     }
@@ -731,7 +747,10 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
               cudaMemset(e->ffn_cnt, 0, (size_t)(e->F / 256 + 1) * sizeof(unsigned)) == cudaSuccess &&
               A((void **)&e->ksp_part, q6k_ksplit_part_floats(c.hidden, 4) * sizeof(float)) &&
               A((void **)&e->ksp_count, (size_t)(c.hidden / 8) * sizeof(unsigned)) &&
-              cudaMemset(e->ksp_count, 0, (size_t)(c.hidden / 8) * sizeof(unsigned)) == cudaSuccess;
+              cudaMemset(e->ksp_count, 0, (size_t)(c.hidden / 8) * sizeof(unsigned)) == cudaSuccess &&
+              A((void **)&e->sk_part, q6k_stream_part_floats(c.hidden, e->F / 256 + 1) * sizeof(float)) &&
+              A((void **)&e->sk_count, q6k_stream_count_words(c.hidden) * sizeof(unsigned)) &&
+              cudaMemset(e->sk_count, 0, q6k_stream_count_words(c.hidden) * sizeof(unsigned)) == cudaSuccess;
     for (int l = 0; ok && l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
         if (Ly.ssm) {

@@ -65,6 +65,9 @@ def lib():
         "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
         "m27b_hbm_read_probe": (b, [vp, sz, vp, cp, sz]),
         "m27b_hbm_read_probe_shape": (b, [vp, sz, i32, i32, i32, i32, vp, cp, sz]),
+        "m27b_qmv_q6k_stream_part_bytes": (sz, [wvp]),
+        "m27b_qmv_q6k_stream_count_bytes": (sz, [wvp]),
+        "m27b_qmv_q6k_stream": (b, [wvp, vp, vp, vp, vp, vp, vp, cp, sz]),
         "m27b_qmv_q6k_ksplit_part_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_ksplit_count_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_ksplit": (b, [wvp, vp, i32, vp, i32, vp, vp, vp, vp, cp, sz]),
@@ -210,6 +213,24 @@ def qmv_q6k_ksplit(w, xq, n_tok, y, residual=None, part=None, count=None, stream
     _check(L.m27b_qmv_q6k_ksplit(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(y),
                                  ldy if ldy is not None else w.view.row_count, _ptr(residual), _ptr(part), _ptr(count),
                                  _stream(stream), err, ERR_CAP), err, "m27b_qmv_q6k_ksplit")
+    return y
+
+
+def qmv_q6k_stream(w, xq, y, residual=None, part=None, count=None, stream=None):
+    """q6_K x one token with the items cut evenly over warps
+    (m27b_qmv_q6k_stream); part / count scratch are allocated here (counters
+    zeroed) unless given."""
+    import torch
+    L = lib()
+    if part is None:
+        part = torch.empty(max(16, L.m27b_qmv_q6k_stream_part_bytes(ctypes.byref(w.view))), dtype=torch.uint8,
+                           device="cuda")
+    if count is None:
+        count = torch.zeros(max(16, L.m27b_qmv_q6k_stream_count_bytes(ctypes.byref(w.view))), dtype=torch.uint8,
+                            device="cuda")
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(L.m27b_qmv_q6k_stream(ctypes.byref(w.view), _ptr(xq), _ptr(y), _ptr(residual), _ptr(part), _ptr(count),
+                                 _stream(stream), err, ERR_CAP), err, "m27b_qmv_q6k_stream")
     return y
 
 
