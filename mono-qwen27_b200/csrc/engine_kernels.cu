@@ -12,6 +12,7 @@
 #include "m27b_device.cuh"
 #include "m27b_launch.cuh"
 #include "q8k_warp.cuh"
+#include "attn_common.cuh"
 
 namespace m27b {
 
@@ -80,65 +81,6 @@ __global__ void k_qk_norm_rope_cache(const float *qkv, const float *q_norm, cons
 // acc[hd], max, sum (record stride hd + 4 keeps records 16-byte aligned).
 // k_attn_reduce: grid nq, 256 threads: warp w combines splits w, w+8, ...
 // rescaled to the global max, then the 8 warps are summed in shared memory.
-constexpr int ATT_G = 8;         // most query heads per kv head
-constexpr int ATT_MIN_POS = 16;  // fewest positions per split
-
-M27B_DI int att_splits(int L, int smax) {
-    const int s = (L + ATT_MIN_POS - 1) / ATT_MIN_POS;
-    return s < smax ? s : smax;
-}
-
-template <int DPL>
-M27B_DI void ld_dims(const float *p, float (&v)[DPL]) {
-    if constexpr (DPL % 4 == 0) {
-#pragma unroll
-        for (int c = 0; c < DPL / 4; ++c) {
-            const float4 t = reinterpret_cast<const float4 *>(p)[c];
-            v[4 * c] = t.x; v[4 * c + 1] = t.y; v[4 * c + 2] = t.z; v[4 * c + 3] = t.w;
-        }
-    } else if constexpr (DPL % 2 == 0) {
-#pragma unroll
-        for (int c = 0; c < DPL / 2; ++c) {
-            const float2 t = reinterpret_cast<const float2 *>(p)[c];
-            v[2 * c] = t.x; v[2 * c + 1] = t.y;
-        }
-    } else {
-#pragma unroll
-        for (int c = 0; c < DPL; ++c) v[c] = p[c];
-    }
-}
-
-// Asynchronous global -> shared copies (cp.async; completion by
-// cp_async_wait_all in the issuing thread).
-M27B_DI void cp_async16(void *smem, const void *gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
-                 "l"(gmem)
-                 : "memory");
-}
-M27B_DI void cp_async8(void *smem, const void *gmem) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
-                 : "memory");
-}
-M27B_DI void cp_async4(void *smem, const void *gmem) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
-                 : "memory");
-}
-M27B_DI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-// A lane's DPL consecutive floats of a row (16-, 8- or 4-byte aligned as DPL allows).
-template <int DPL>
-M27B_DI void cp_async_dims(float *dst, const float *src) {
-    if constexpr (DPL % 4 == 0) {
-#pragma unroll
-        for (int c = 0; c < DPL / 4; ++c) cp_async16(dst + 4 * c, src + 4 * c);
-    } else if constexpr (DPL == 2) {
-        cp_async8(dst, src);
-    } else {
-#pragma unroll
-        for (int c = 0; c < DPL; ++c) cp_async4(dst + c, src + c);
-    }
-}
-
 template <int DPL>
 __global__ void __launch_bounds__(256) k_attn_partial(const float *q, const float *kc, const float *vc, float *part,
                                                       const int *pos_p, int nq, int nkv, float scale, int q_stride,
@@ -366,42 +308,6 @@ M27B_DI void norm_rope_warp(const float *src, const float *nw, float *dst, float
 // CTA) the q/k norm weights and the rotary factors.  All of it is in flight
 // while the projection drains; after the wait only the q (and k, v) rows
 // are read.
-// As norm_rope_warp, with the norm weights (nw, hd values) and the rotary
-// factors (rope, n_rot / 2 pairs) already in shared memory.
-template <int DPL>
-M27B_DI void norm_rope_apply(const float *src, const float *nw, const float2 *rope, float *dst, float mul, int n_rot,
-                             float eps, int lane) {
-    constexpr int hd = DPL * 32;
-    float v[DPL];
-    ld_dims<DPL>(src + lane * DPL, v);
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) ss = fmaf(v[i], v[i], ss);
-    ss = warp_sum(ss);
-    const float sc = rsqrtf(ss / (float)hd + eps);
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-        v[i] = v[i] * sc * nw[lane * DPL + i];
-        dst[lane * DPL + i] = v[i];
-    }
-    __syncwarp();
-    const int half = n_rot / 2;
-    float out[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-        const int d = lane * DPL + i;
-        out[i] = v[i];
-        if (d < n_rot) {
-            const float2 r = rope[d < half ? d : d - half];
-            out[i] = d < half ? v[i] * r.x - dst[d + half] * r.y : dst[d - half] * r.y + v[i] * r.x;
-        }
-    }
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) dst[lane * DPL + i] = out[i] * mul;
-    __syncwarp();
-}
-
 constexpr int ATT_SLOTS = 4;  // positions per warp whose K/V rows are copied before the wait
 
 size_t attn_qkv_smem_bytes(int G, int hd) {

@@ -139,16 +139,16 @@ M27B_DI void stage_x_blk(const QmvArgs &a, uint8_t *xrec, float *xd) {
     const uint8_t *src = (const uint8_t *)a.xq;  // NT*nb blocks of 292 bytes
     for (int i = threadIdx.x; i < NT * nb * 64; i += blockDim.x) {
         const int blk = i >> 6, w = i & 63;
-        ((uint32_t *)(xrec + (size_t)blk * BLK_XREC))[w] = ((const uint32_t *)(src + (size_t)blk * 292 + 4))[w];
+        ((uint32_t *)(xrec + (size_t)blk * BLK_XREC))[w] = __ldcg((const unsigned *)(src + (size_t)blk * 292 + 4) + w);
     }
     for (int i = threadIdx.x; i < NT * nb * 9; i += blockDim.x) {
         const int blk = i / 9, j = i - blk * 9;
         const uint8_t *sb = src + (size_t)blk * 292;
         if (j < 8) {
             const int16_t *bs = (const int16_t *)(sb + 260);
-            ((int16_t *)(xrec + (size_t)blk * BLK_XREC + 256))[j] = (int16_t)(bs[2 * j] + bs[2 * j + 1]);
+            ((int16_t *)(xrec + (size_t)blk * BLK_XREC + 256))[j] = (int16_t)(__ldcg(bs + 2 * j) + __ldcg(bs + 2 * j + 1));
         } else {
-            xd[blk] = *(const float *)sb;
+            xd[blk] = __ldcg((const float *)sb);
         }
     }
 }
@@ -191,7 +191,7 @@ M27B_DI void quant_x_blk(const QmvArgs &a, uint8_t *xrec, float *xd, float *red)
             if (i < total) {
                 const int t = i / nb, b = i - t * nb;
                 const float4 *xr = (const float4 *)(a.xf + (size_t)t * a.ldxf + b * 256 + lane * 8);
-                const float4 p0 = xr[0], p1 = xr[1];
+                const float4 p0 = __ldcg(xr), p1 = __ldcg(xr + 1);
                 v[r][0] = p0.x; v[r][1] = p0.y; v[r][2] = p0.z; v[r][3] = p0.w;
                 v[r][4] = p1.x; v[r][5] = p1.y; v[r][6] = p1.z; v[r][7] = p1.w;
             }
@@ -277,7 +277,7 @@ M27B_DI void quant_x_blk(const QmvArgs &a, uint8_t *xrec, float *xd, float *red)
     for (int i = warp; i < total; i += nw) {
         const int t = i / nb, b = i - t * nb;
         const float4 *xr = (const float4 *)(a.xf + (size_t)t * a.ldxf + b * 256 + lane * 8);
-        const float4 p0 = xr[0], p1 = xr[1];
+        const float4 p0 = __ldcg(xr), p1 = __ldcg(xr + 1);
         float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
         if (a.xnorm_on) {
             float nst = ns[0];

@@ -76,7 +76,7 @@ M27B_DI void stage_x_q6t(const QmvArgs &a, uint8_t *xrec, float *xd) {
         const int blk = i >> 6, r = i & 63;
         const int hi = r >> 5, c = (r >> 2) & 7, w = r & 3;
         const int e = 128 * (c >> 2) + 32 * ((c >> 1) & 1) + 16 * (c & 1) + 64 * hi + 4 * w;
-        const uint32_t v = *(const uint32_t *)(src + (size_t)blk * 292 + 4 + e);
+        const uint32_t v = __ldcg((const unsigned *)(src + (size_t)blk * 292 + 4 + e));
         ((uint32_t *)(xrec + (size_t)blk * Q6T_XREC))[hi * 32 + c * 4 + w] = v;
     }
     for (int i = threadIdx.x; i < NT * nb * 9; i += blockDim.x) {
@@ -86,9 +86,9 @@ M27B_DI void stage_x_q6t(const QmvArgs &a, uint8_t *xrec, float *xd) {
             const int16_t *bs = (const int16_t *)(sb + 260);
             const int g = 8 * (j >> 2) + 2 * ((j >> 1) & 1) + (j & 1);  // 16-value group of chunk j's low half
             ((uint32_t *)(xrec + (size_t)blk * Q6T_XREC + 256))[j] =
-                (uint32_t)(uint16_t)bs[g] | ((uint32_t)(uint16_t)bs[g + 4] << 16);
+                (uint32_t)(uint16_t)__ldcg(bs + g) | ((uint32_t)(uint16_t)__ldcg(bs + g + 4) << 16);
         } else {
-            xd[blk] = *(const float *)sb;
+            xd[blk] = __ldcg((const float *)sb);
         }
     }
 }
@@ -118,7 +118,7 @@ M27B_DI void quant_x_q6t(const QmvArgs &a, uint8_t *xrec, float *xd) {
             if (i < total) {
                 const int t = i / nb, b = i - t * nb;
                 const float4 *xr = (const float4 *)(a.xf + (size_t)t * a.ldxf + b * 256 + lane * 8);
-                const float4 p0 = xr[0], p1 = xr[1];
+                const float4 p0 = __ldcg(xr), p1 = __ldcg(xr + 1);
                 v[r][0] = p0.x; v[r][1] = p0.y; v[r][2] = p0.z; v[r][3] = p0.w;
                 v[r][4] = p1.x; v[r][5] = p1.y; v[r][6] = p1.z; v[r][7] = p1.w;
             }
