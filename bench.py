@@ -208,9 +208,16 @@ class Workload:
                                "rows": rows, "k": k, "ntok": n, "matvecs_per_step": copies,
                                "bytes_per_matvec": self.mv_bytes, "l2": l2,
                                "int_ops_per_matvec": 2 * rows * k * n}
-                self.kernel = ("k_qmv_q4k_mma<%d> (tcgen05 kind::i8)" % (8 if n <= 8 else 16)) if n >= 5 else \
+                self.kernel = ("k_qmv_q4k_mma<%d> (tcgen05 kind::i8, K split across CTAs: m27b_qmv_mma_split, "
+                               "the verify pass's entry)" % (8 if n <= 8 else 16)) if n >= 5 else \
                     "k_qmv_q4k_blk<%d,STORE>" % n
                 self.profile = "qmv_q4K_mma_cfg2.md"
+                if n >= 5:
+                    L = m27b.lib()
+                    self.split = [(torch.empty(L.m27b_qmv_mma_split_part_bytes(m27b.ctypes.byref(W.view), n),
+                                               dtype=torch.uint8, device=dev),
+                                   torch.zeros(L.m27b_qmv_mma_split_count_bytes(m27b.ctypes.byref(W.view)),
+                                               dtype=torch.uint8, device=dev)) for W in self.W]
             self.fused = w == "cfg0"  # quantize in the matvec prologue (m27b_qmv_f32)
             self.launches_per_step = copies if self.fused else 2 * copies
             self.copies, self.rows, self.k = copies, rows, k
@@ -270,6 +277,9 @@ class Workload:
         m = self.m27b
         if self.name == "cfg1":
             m.qmv_argmax(self.W[c], self.xq[c], 1, self.best, logits=self.y[c])
+        elif getattr(self, "split", None):
+            part, count = self.split[c]
+            m.qmv_mma_split(self.W[c], self.xq[c], self.n, self.y[c], part=part, count=count)
         else:
             m.qmv(self.W[c], self.xq[c], self.n, self.y[c])
 

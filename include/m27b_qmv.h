@@ -174,6 +174,24 @@ M27B_API bool m27b_qmv_q6k_ksplit(const struct WeightView *w, const void *xq, in
                                   const float *residual, void *part, void *count, cudaStream_t stream, char *err,
                                   size_t err_cap);
 
+/* q4_K matvec for 5..16 tokens on the tensor cores (as m27b_qmv does for
+ * them) with each 128-row tile's K dimension cut into ranges handled by
+ * different CTAs, two CTAs per SM at up to 8 tokens: more, shorter
+ * block-column chains in flight than the one-unit-per-tile launch (17408
+ * rows are only 136 tiles for 148 SMs).  The ranges' partial sums are added
+ * in range order by the last-arriving range of each 32-row slice
+ * (deterministic; within fp32 rounding of m27b_qmv).  The caller passes
+ * m27b_qmv_mma_split_part_bytes of scratch and m27b_qmv_mma_split_count_bytes
+ * of counters that must be zero before the first call (each call leaves them
+ * zero); calls overlapping on the GPU with the same scratch race.  Replaces,
+ * for a verify pass, the reference's per-token k_q4k_mv_q8_dp4a
+ * (src/mono27b_executor.cu:320-364). */
+M27B_API size_t m27b_qmv_mma_split_part_bytes(const struct WeightView *w, int n_tok);
+M27B_API size_t m27b_qmv_mma_split_count_bytes(const struct WeightView *w);
+M27B_API bool m27b_qmv_mma_split(const struct WeightView *w, const void *xq, int n_tok, float *y, int ldy,
+                                 const float *residual, void *part, void *count, cudaStream_t stream, char *err,
+                                 size_t err_cap);
+
 /* q6_K matvec for ONE token over a matrix of few, long rows (a decode step's
  * ffn_down, 5120 x 17408), y = W.xq (+ residual): the (8-row group, 4-block
  * tile) items are cut into equal runs, one per warp of a one-CTA-per-SM grid,

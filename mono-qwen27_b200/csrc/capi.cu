@@ -342,6 +342,38 @@ bool qmv_q6k_stream(const WeightView *w, const void *xq, const float *xf, float 
     return cuda_ok(launch_q6k_stream(a, part, count, sms, stream), what, err, cap) && ok(err, cap);
 }
 
+// q4_K x 5..16 tokens on the tensor cores with K split across CTAs (the
+// verify pass's q4_K projections): part holds q4k_mma_split_part_floats
+// floats, count q4k_mma_split_count_words zeroed words.
+bool qmv_mma_split(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                   float *part, unsigned *count, cudaStream_t stream, char *err, size_t cap) {
+    const char *what = "qmv_mma_split";
+    WDesc d{};
+    if (!describe(w, d, what, err, cap)) return false;
+    if (d.kind != W_Q4K) return fail(err, cap, "%s: q4_K weights only", what);
+    if (!xq || !y || !part || !count) return fail(err, cap, "%s: null pointer", what);
+    if (!q4k_mma_supported((int)w->row_blocks, n_tok))
+        return fail(err, cap, "%s: %d tokens x %u blocks per row are not served by the tensor-core kernel", what, n_tok,
+                    w->row_blocks);
+    if (n_tok > 1 && ldy < (int)w->row_count) return fail(err, cap, "%s: ldy (%d) < row_count (%u)", what, ldy, w->row_count);
+    const int sms = sm_count_current();
+    int *status = status_ptr_current();
+    if (sms <= 0 || !status) return fail(err, cap, "%s: no CUDA device", what);
+    QmvArgs a{};
+    a.w0 = (const uint8_t *)w->ptr;
+    a.xq = xq;
+    a.y = y;
+    a.residual = residual;
+    a.row_stride = d.row_stride;
+    a.ldy = ldy;
+    a.rows = (int)w->row_count;
+    a.rb = (int)w->row_blocks;
+    a.k = d.k;
+    a.passes = d.passes;
+    a.status = status;
+    return cuda_ok(launch_q4k_mma(a, n_tok, sms, stream, part, count), what, err, cap) && ok(err, cap);
+}
+
 int q6k_ksplit_ranges(int rb);
 size_t q6k_ksplit_part_floats(int rows, int ks);
 cudaError_t launch_q6k_ksplit(const QmvArgs &a_in, int n_tok, float *part, unsigned *count, int sm_count,
@@ -614,6 +646,23 @@ size_t m27b_qmv_q6k_ksplit_part_bytes(const WeightView *w) {
 size_t m27b_qmv_q6k_ksplit_count_bytes(const WeightView *w) {
     if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
     return q6k_ksplit_ranges((int)w->row_blocks) ? (size_t)((w->row_count + 7) / 8) * sizeof(unsigned) : 0;
+}
+
+size_t m27b_qmv_mma_split_part_bytes(const WeightView *w, int n_tok) {
+    if (!w || w->ggml_type != M27B_TYPE_Q4_K || n_tok < 5 || n_tok > 16) return 0;
+    return q4k_mma_split_part_floats((int)w->row_count, (int)w->row_blocks, n_tok) * sizeof(float);
+}
+
+size_t m27b_qmv_mma_split_count_bytes(const WeightView *w) {
+    if (!w || w->ggml_type != M27B_TYPE_Q4_K) return 0;
+    return q4k_mma_split_count_words((int)w->row_count) * sizeof(unsigned);
+}
+
+bool m27b_qmv_mma_split(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                        void *part, void *count, cudaStream_t stream, char *err, size_t err_cap) {
+    if (((uintptr_t)part & 15) || ((uintptr_t)count & 3))
+        return fail(err, err_cap, "m27b_qmv_mma_split: misaligned scratch");
+    return qmv_mma_split(w, xq, n_tok, y, ldy, residual, (float *)part, (unsigned *)count, stream, err, err_cap);
 }
 
 size_t m27b_qmv_q6k_stream_part_bytes(const WeightView *w) {

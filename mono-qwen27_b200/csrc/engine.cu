@@ -59,6 +59,11 @@ bool qmv_q6k_ksplit(const WeightView *w, const void *xq, int n_tok, float *y, in
 bool qmv_swiglu_q8(const WeightView *gate, const WeightView *up, const void *xq, const float *xf, const float *norm_w,
                    float eps, float *y, void *q8out, unsigned *q8cnt, cudaStream_t stream, char *err, size_t cap);
 int q6k_ksplit_ranges(int rb);
+bool q4k_mma_supported(int rb, int n_tok);
+size_t q4k_mma_split_part_floats(int rows, int rb, int n_tok);
+size_t q4k_mma_split_count_words(int rows);
+bool qmv_mma_split(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                   float *part, unsigned *count, cudaStream_t stream, char *err, size_t cap);
 size_t q6k_stream_part_floats(int rows, int rb);
 size_t q6k_stream_count_words(int rows);
 bool q6k_stream_applies(int k);
@@ -276,6 +281,34 @@ bool mv(M27BEngine *e, const QMat &m, const uint8_t *xq, float *y, const float *
     return m27b_qmv(&m.v, xq, 1, y, m.rows, res, e->st, err, err_cap);
 }
 
+// Most rows of the verify pass's q4_K projections (qkv, o_proj, gate/up).
+int mma_rows_max(const M27BEngine *e) {
+    const int qkv_rows = (2 * e->H + 2 * e->KV) * e->c.head_dim;
+    return std::max(std::max(e->c.hidden, e->F), qkv_rows);
+}
+
+// Scratch of the verify pass's K-split tensor-core projections: the largest
+// of qkv, o_proj and gate/up at 16 tokens.
+size_t mma_scratch_floats(const M27BEngine *e) {
+    const M27BModelConfig &c = e->c;
+    const int hd = c.head_dim, qkv_rows = (2 * e->H + 2 * e->KV) * hd;
+    size_t m = q4k_mma_split_part_floats(qkv_rows, c.hidden / 256, 16);
+    m = std::max(m, q4k_mma_split_part_floats(c.hidden, std::max(1, e->H * hd / 256), 16));
+    m = std::max(m, q4k_mma_split_part_floats(e->F, c.hidden / 256, 16));
+    return m;
+}
+
+// A q4_K projection of a verify pass (5..16 tokens): on the tensor cores
+// with K split across CTAs where the kernel serves the shape, else m27b_qmv.
+bool vmv(M27BEngine *e, const QMat &m, const uint8_t *xq, int n, float *y, int ldy, const float *res, char *err,
+         size_t err_cap) {
+    if (e->mma_part && m.v.ggml_type == M27B_TYPE_Q4_K && q4k_mma_supported((int)m.v.row_blocks, n) &&
+        q4k_mma_split_part_floats(m.rows, (int)m.v.row_blocks, n) <= mma_scratch_floats(e) &&
+        m.rows <= mma_rows_max(e))
+        return qmv_mma_split(&m.v, xq, n, y, ldy, res, e->mma_part, e->mma_count, e->st, err, err_cap);
+    return m27b_qmv(&m.v, xq, n, y, ldy, res, e->st, err, err_cap);
+}
+
 // The down projection of one token (rows = hidden, long rows): a repacked
 // q6_K matrix goes to the kernel that cuts its items evenly over the warps
 // (its few row groups do not spread evenly over the SMs as whole groups),
@@ -485,8 +518,15 @@ bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
     ECALL(m27b_dequant_rows(&e->embd.v, e->vtok, n, e->h, D, e->st, err, err_cap));
     for (int l = 0; l < c.n_layers; ++l) {
         Layer &Ly = e->L[l];
-        ECALL(m27b_qmv_f32_rmsnorm(&Ly.wqkv.v, nullptr, e->h, D, Ly.attn_norm, c.rms_eps, n, e->xq, e->qkv, qkv_rows,
-                                   nullptr, e->st, err, err_cap));
+        if (n >= 5 && Ly.wqkv.v.ggml_type == M27B_TYPE_Q4_K) {
+            // quantize once, then the tensor cores with K split across CTAs
+            ECALL(m27b_act_quant_rmsnorm(e->h, Ly.attn_norm, c.rms_eps, D, n, D, M27B_TYPE_Q8_K, e->xq, e->st, err,
+                                         err_cap));
+            ECALL(vmv(e, Ly.wqkv, e->xq, n, e->qkv, qkv_rows, nullptr, err, err_cap));
+        } else {
+            ECALL(m27b_qmv_f32_rmsnorm(&Ly.wqkv.v, nullptr, e->h, D, Ly.attn_norm, c.rms_eps, n, e->xq, e->qkv,
+                                       qkv_rows, nullptr, e->st, err, err_cap));
+        }
         ECUDA(launch_pdl(k_qk_norm_rope_cache, dim3(e->H + e->KV, n), dim3(hd), (size_t)(hd + 32) * 4, e->st,
                          (const float *)e->qkv, (const float *)Ly.q_norm, (const float *)Ly.k_norm, e->q, e->gate, Ly.kc,
                          Ly.vc, pos, e->H, e->KV, hd, c.n_rot, c.rope_theta, c.rms_eps, qkv_rows, e->H * hd));
@@ -500,14 +540,14 @@ bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
             ECALL(m27b_act_quant_gated(e->o, e->gate, e->H * hd, n, e->H * hd, act_type_of(Ly.wo.type), e->xq, e->st,
                                        err, err_cap));
         }
-        ECALL(m27b_qmv(&Ly.wo.v, e->xq, n, e->h2, D, r0 ? e->h : nullptr, e->st, err, err_cap));
+        ECALL(vmv(e, Ly.wo, e->xq, n, e->h2, D, r0 ? e->h : nullptr, err, err_cap));
         if (c.tp_size > 1) ENCCL(ncclAllReduce(e->h2, e->h2, (size_t)n * D, ncclFloat32, ncclSum, e->comm, e->st));
         if (n >= 5 && Ly.wg.type == M27B_TYPE_Q4_K) {
             // 5+ tokens: gate and up on the tensor cores, then silu(gate) * up -> q8 for down
             ECALL(m27b_act_quant_rmsnorm(e->h2, Ly.post_norm, c.rms_eps, D, n, D, M27B_TYPE_Q8_K, e->xq, e->st, err,
                                          err_cap));
-            ECALL(m27b_qmv(&Ly.wg.v, e->xq, n, e->a, e->F, nullptr, e->st, err, err_cap));
-            ECALL(m27b_qmv(&Ly.wu.v, e->xq, n, e->a2, e->F, nullptr, e->st, err, err_cap));
+            ECALL(vmv(e, Ly.wg, e->xq, n, e->a, e->F, nullptr, err, err_cap));
+            ECALL(vmv(e, Ly.wu, e->xq, n, e->a2, e->F, nullptr, err, err_cap));
             ECALL(m27b_act_quant_swiglu(e->a, e->a2, e->F, n, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err,
                                         err_cap));
         } else {
@@ -748,6 +788,10 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
               A((void **)&e->ksp_part, q6k_ksplit_part_floats(c.hidden, 4) * sizeof(float)) &&
               A((void **)&e->ksp_count, (size_t)(c.hidden / 8) * sizeof(unsigned)) &&
               cudaMemset(e->ksp_count, 0, (size_t)(c.hidden / 8) * sizeof(unsigned)) == cudaSuccess &&
+              A((void **)&e->mma_part, mma_scratch_floats(e) * sizeof(float)) &&
+              A((void **)&e->mma_count, q4k_mma_split_count_words(mma_rows_max(e)) * sizeof(unsigned)) &&
+              cudaMemset(e->mma_count, 0, q4k_mma_split_count_words(mma_rows_max(e)) * sizeof(unsigned)) ==
+                  cudaSuccess &&
               A((void **)&e->sk_part, q6k_stream_part_floats(c.hidden, e->F / 256 + 1) * sizeof(float)) &&
               A((void **)&e->sk_count, q6k_stream_count_words(c.hidden) * sizeof(unsigned)) &&
               cudaMemset(e->sk_count, 0, q6k_stream_count_words(c.hidden) * sizeof(unsigned)) == cudaSuccess;

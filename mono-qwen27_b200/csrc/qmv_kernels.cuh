@@ -424,6 +424,10 @@ cudaError_t launch_qmv(int wt, int epi, QmvArgs a, int nt, int sm_count, cudaStr
 cudaError_t launch_qmv_float(int wt, const QmvArgs &a, int nt, int sm_count, cudaStream_t st);
 // q4_K x 5..16 tokens on the tensor cores (qmv_q4k_mma.cu), store epilogue.
 bool q4k_mma_supported(int rb, int n_tok);
-cudaError_t launch_q4k_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st);
+// part / count (nullable): scratch for K split across CTAs (q4k_mma_split_*).
+cudaError_t launch_q4k_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st, float *part = nullptr,
+                           unsigned *count = nullptr);
+size_t q4k_mma_split_part_floats(int rows, int rb, int n_tok);
+size_t q4k_mma_split_count_words(int rows);
 
 }  // namespace m27b

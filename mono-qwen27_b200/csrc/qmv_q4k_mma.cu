@@ -56,16 +56,34 @@ constexpr int MMA_PRODUCER = MMA_ISSUER + 1;                    // warp 13: TMA 
 constexpr int MMA_ISSUER2 = MMA_PRODUCER + 1;                   // warp 14: MMAs of second half-blocks
 constexpr int MMA_THREADS = (MMA_ISSUER2 + 1) * 32;
 constexpr int MMA_RAW_BYTES = MMA_ROWS * 144;    // one TMA box: 128 rows x one q4_K block
-constexpr int MMA_TMEM_COLS = 512;               // D: 2 blocks x 8 sub-blocks x 16; A: 2 x 32
-constexpr int MMA_ACOL = 256;                    // first TMEM column of the A buffers
 constexpr int MMA_NA = 2;                        // A buffers: one per half-block position (= issuing warp)
 constexpr size_t MMA_SMEM_LIMIT = 227 * 1024;
-// Every CTA asks for more than half of an SM's shared memory, so no two CTAs
-// of this kernel (of one launch, or of two launches that programmatic
-// dependent launch overlaps) are ever resident on one SM: each allocates all
-// 512 TMEM columns, and tcgen05.alloc has no bounded form — a second
-// allocator on the SM would wait for the first CTA to exit, unbounded.
+// TMEM per CTA: D = 2 blocks x 8 sub-blocks x NB columns, then the two A
+// buffers of 32 columns.  NB = 16: 320 columns -> all 512, and every CTA
+// asks for more than half of an SM's shared memory (MMA_SMEM_MIN), so no two
+// CTAs of this kernel (of one launch, or of two launches that programmatic
+// dependent launch overlaps) are ever resident on one SM — tcgen05.alloc has
+// no bounded form.  NB = 8: 192 columns -> 256, two CTAs per SM (each with at
+// most MMA_SMEM_PAIR and at least MMA_SMEM_PAIR_MIN of shared memory, so a
+// third never fits): their allocations add up to the SM's 512 columns.
+template <int NB> constexpr int mma_dbuf() { return 8 * NB; }                 // columns per block buffer
+template <int NB> constexpr int mma_acol() { return 2 * mma_dbuf<NB>(); }     // first A column
+template <int NB> constexpr int mma_tcols() { return mma_acol<NB>() + 2 * 32 <= 256 ? 256 : 512; }
+template <int NB> constexpr int mma_ctas_per_sm() { return mma_tcols<NB>() == 256 ? 2 : 1; }
 constexpr size_t MMA_SMEM_MIN = 116 * 1024;
+constexpr size_t MMA_SMEM_PAIR = 112 * 1024;
+constexpr size_t MMA_SMEM_PAIR_MIN = 80 * 1024;
+
+// K split across CTAs (verify pass): ks ranges of rb / ks blocks per 128-row
+// tile; unit u = tile * ks + range; the ranges' partial sums go to
+// part[((tile * ks + range) * NB + token) * 128 + row] and the epilogue warp
+// that arrives last at count[tile * 8 + epilogue warp] adds its 32-row slice
+// over the ranges in range order (ks = 1: no scratch, rows written directly).
+struct MmaSplit {
+    float *part;
+    unsigned *count;
+    int ks;
+};
 
 struct MmaLayout {
     size_t b, dx, bs, raw, bar, flag, total;
@@ -94,10 +112,12 @@ __host__ __device__ inline MmaLayout mma_layout(int rb, int nb_tok, int stages) 
     return L;
 }
 
-// Most stages (up to 4) that fit; 0 if not even two do.
-inline int mma_stages(int rb, int nb_tok) {
+// Most stages (up to 4) that fit the CTA's shared-memory budget (pair: two
+// CTAs per SM); 0 if not even two do.
+inline int mma_stages(int rb, int nb_tok, bool pair = false) {
+    const size_t lim = pair ? MMA_SMEM_PAIR : MMA_SMEM_LIMIT;
     for (int s = 4; s >= 2; --s)
-        if (mma_layout(rb, nb_tok, s).total + 1024 <= MMA_SMEM_LIMIT) return s;
+        if (mma_layout(rb, nb_tok, s).total + 1024 <= lim) return s;
     return 0;
 }
 
@@ -195,8 +215,10 @@ M27B_DI bool warp_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *ab
 }
 
 template <int NB>
-__global__ void __launch_bounds__(MMA_THREADS, 1)
-    k_qmv_q4k_mma(const QmvArgs a, const __grid_constant__ CUtensorMap tm, int n_tok, int stages) {
+__global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
+    k_qmv_q4k_mma(const QmvArgs a, const __grid_constant__ CUtensorMap tm, int n_tok, int stages, uint32_t tcols,
+                  const MmaSplit sp) {
+    constexpr int DBUF = mma_dbuf<NB>(), ACOL = mma_acol<NB>();
     extern __shared__ __align__(1024) uint8_t mma_smem[];
     uint8_t *smem = mma_smem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -216,10 +238,16 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     volatile int *abort = (volatile int *)(smem + L.flag);
     uint32_t *tslot = (uint32_t *)(smem + L.flag + 8);
 
-    const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS;
-    const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int nblk = my_tiles * rb;  // block items of this CTA
-    const int J = 2 * nblk;          // half-block items
+    // units (tile, K range) of this CTA: u = blockIdx.x + i * gridDim.x,
+    // tile u / ks, blocks [range * bpu, (range + 1) * bpu) of its rows
+    const int ks = sp.ks, bpu = rb / ks;
+    const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS, nunits = ntiles * ks;
+    const int my_units = (int)blockIdx.x < nunits ? (nunits - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int nblk = my_units * bpu;  // block items of this CTA
+    const int J = 2 * nblk;           // half-block items
+    // block item bi -> unit, tile, range and block index k within the row
+    auto unit_of = [&](int bi) { return (int)blockIdx.x + (bi / bpu) * (int)gridDim.x; };
+    auto k_of = [&](int bi) { return (unit_of(bi) % ks) * bpu + bi % bpu; };
 
     if (tid == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -239,7 +267,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
         fence_mbar_init();
     }
     if (warp == 0) {
-        tmem_alloc(tslot, MMA_TMEM_COLS);
+        tmem_alloc(tslot, tcols);
         tmem_relinquish();
     }
     __syncthreads();
@@ -249,8 +277,8 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     // the readers' generic loads of a stage are ordered before its refill by
     // the empty barrier (arrive-release, wait-acquire) that the producer waits on
     auto issue_block = [&](int bi) {
-        const int tl = bi / rb, k = bi - tl * rb;
-        const int row0 = ((int)blockIdx.x + tl * (int)gridDim.x) * MMA_ROWS;
+        const int k = k_of(bi);
+        const int row0 = (unit_of(bi) / ks) * MMA_ROWS;
         uint64_t *b = &full[bi % stages];
         mbar_arrive_expect_tx(b, MMA_RAW_BYTES);
         tma_load_2d(raw + (size_t)(bi % stages) * MMA_RAW_BYTES, &tm, k * 36, row0, b);
@@ -312,12 +340,12 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
                 if (bi >= 2 && !wait_or_abort(&d_free[db], (uint32_t)(((bi - 2) >> 1) & 1), abort, a.status)) break;
                 if (!wait_or_abort(&a_full[q], (uint32_t)(bi & 1), abort, a.status)) break;
                 tc_fence_after();
-                const int k = bi % rb;
+                const int k = k_of(bi);
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
                     const uint64_t bd = umma_desc(b_base + (uint32_t)((k * 8 + 4 * q + s) * NB * 32));
-                    umma_i8_ts(tmem + (uint32_t)(db * 128 + (4 * q + s) * 16),
-                               tmem + (uint32_t)(MMA_ACOL + q * 32 + s * 8), bd, idesc, 0u);
+                    umma_i8_ts(tmem + (uint32_t)(db * DBUF + (4 * q + s) * NB),
+                               tmem + (uint32_t)(ACOL + q * 32 + s * 8), bd, idesc, 0u);
                 }
                 umma_commit(&mma_done[q]);
                 umma_commit(&blk_done[db]);  // with the other warp's commit: the block's accumulators are final
@@ -355,7 +383,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
                 break;
             tc_fence_after();
             const uint8_t *rw = raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144;
-            const uint32_t acol = tmem + lane_base + (uint32_t)(MMA_ACOL + ab * 32);
+            const uint32_t acol = tmem + lane_base + (uint32_t)(ACOL + ab * 32);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 // qs group g = 2q + h: low nibbles are sub-block 2g, high 2g+1,
@@ -389,7 +417,7 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < TPT; ++i) acc[i] = 0.0f;
         for (int bi = 0; bi < nblk; ++bi) {
-            const int tl = bi / rb, k = bi - tl * rb;
+            const int u = unit_of(bi), k = k_of(bi);
             // the block header of row r (scales, mins), read before the stage is handed back
             if (!warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) break;
             const uint4 hd = *(const uint4 *)(raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144);
@@ -403,11 +431,11 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
             if (!warp_wait_or_abort(&blk_done[bi & 1], (uint32_t)((bi >> 1) & 1), abort, a.status)) break;
             tc_fence_after();
             int v[8][TPT];
-            const uint32_t dcol = tmem + lane_base + (uint32_t)((bi & 1) * 128 + toff);
+            const uint32_t dcol = tmem + lane_base + (uint32_t)((bi & 1) * DBUF + toff);
 #pragma unroll
             for (int s = 0; s < 8; ++s) {
-                if constexpr (TPT == 8) tmem_ld8(dcol + (uint32_t)(s * 16), v[s]);
-                else tmem_ld4(dcol + (uint32_t)(s * 16), v[s]);
+                if constexpr (TPT == 8) tmem_ld8(dcol + (uint32_t)(s * NB), v[s]);
+                else tmem_ld4(dcol + (uint32_t)(s * NB), v[s]);
             }
             tmem_wait_ld();
             tc_fence_before();
@@ -431,9 +459,37 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
                 acc[i] = fmaf(dw * dx, (float)isum, acc[i]);
                 acc[i] = fmaf(-(dmw * dx), (float)msum, acc[i]);
             }
-            if (k == rb - 1) {  // the tile's last block: write its rows
-                const int row = ((int)blockIdx.x + tl * (int)gridDim.x) * MMA_ROWS + r;
-                if (row < a.rows) {
+            if (bi % bpu == bpu - 1) {  // the unit's last block
+                const int tile = u / ks, range = u % ks;
+                const int row = tile * MMA_ROWS + r;
+                bool write = true;
+                if (ks > 1) {
+                    // this range's partial sums; the warp arriving last for its
+                    // 32-row slice of the tile adds the ranges in range order
+                    float *pt = sp.part + ((size_t)(tile * ks + range) * NB + toff) * MMA_ROWS + r;
+#pragma unroll
+                    for (int i = 0; i < TPT; ++i) pt[(size_t)i * MMA_ROWS] = acc[i];
+                    __threadfence();
+                    __syncwarp();
+                    unsigned prev = 0u;
+                    unsigned *cnt = sp.count + (size_t)tile * 8 + e;
+                    if (lane == 0) prev = atomicAdd(cnt, 1u);
+                    prev = __shfl_sync(0xffffffffu, prev, 0);
+                    write = prev == (unsigned)(ks - 1);
+                    if (write) {
+                        if (lane == 0) *cnt = 0u;
+                        __threadfence();
+#pragma unroll
+                        for (int i = 0; i < TPT; ++i) {
+                            float v2 = 0.0f;
+                            for (int q2 = 0; q2 < ks; ++q2)
+                                v2 += q2 == range ? acc[i]
+                                                  : __ldcg(sp.part + ((size_t)(tile * ks + q2) * NB + toff + i) * MMA_ROWS + r);
+                            acc[i] = v2;
+                        }
+                    }
+                }
+                if (write && row < a.rows) {
 #pragma unroll
                     for (int i = 0; i < TPT; ++i) {
                         const int t = toff + i;
@@ -452,15 +508,35 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, MMA_TMEM_COLS);
+        tmem_dealloc(tmem, tcols);
     }
+}
+
+// K ranges per tile: the most (a divisor of rb, at most 8) that keep one
+// unit per CTA slot; 1 without scratch.
+static int mma_ks(int ntiles, int rb, int slots) {
+    int best = 1;
+    for (int k = 2; k <= 8; ++k)
+        if (rb % k == 0 && rb / k >= 2 && ntiles * k <= slots) best = k;
+    return best;
+}
+
+// Whether NB-token tiles run two CTAs per SM (256 TMEM columns each) for rows
+// of rb blocks, and with how many stages.
+template <int NB>
+static bool mma_pair(int rb, int *stages) {
+    const int ps = NB == 8 ? mma_stages(rb, NB, true) : 0;
+    *stages = ps > 0 ? ps : mma_stages(rb, NB);
+    return ps > 0;
 }
 
 // 1: launched; 0: shape not supported by this kernel (caller falls back).
 template <int NB>
-static cudaError_t run_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st, bool *launched) {
+static cudaError_t run_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st, bool *launched, float *part,
+                           unsigned *count) {
     *launched = false;
-    const int stages = mma_stages(a.rb, NB);
+    int stages = 0;
+    const bool pair = mma_pair<NB>(a.rb, &stages);
     if (stages == 0) return cudaSuccess;
     const MmaLayout L = mma_layout(a.rb, NB, stages);
     int dev = 0;
@@ -475,20 +551,38 @@ static cudaError_t run_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream
     CUtensorMap tm;
     if (!encode_rows_u32(&tm, a.w0, a.row_stride, a.rows, 36, MMA_ROWS)) return cudaErrorInvalidValue;
     const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS;
-    const int grid = ntiles < sm_count ? ntiles : sm_count;
-    const size_t smem = L.total > MMA_SMEM_MIN ? L.total : MMA_SMEM_MIN;
+    const int slots = sm_count * (pair ? 2 : 1);
+    const int ks = part && count ? mma_ks(ntiles, a.rb, slots) : 1;
+    const int units = ntiles * ks;
+    const int grid = units < slots ? units : slots;
+    const size_t smem = pair ? (L.total > MMA_SMEM_PAIR_MIN ? L.total : MMA_SMEM_PAIR_MIN)
+                             : (L.total > MMA_SMEM_MIN ? L.total : MMA_SMEM_MIN);
     *launched = true;
-    return launch_pdl(k_qmv_q4k_mma<NB>, dim3(grid), dim3(MMA_THREADS), smem, st, a, tm, n_tok, stages);
+    return launch_pdl(k_qmv_q4k_mma<NB>, dim3(grid), dim3(MMA_THREADS), smem, st, a, tm, n_tok, stages,
+                      (uint32_t)(pair ? 256 : 512), MmaSplit{part, count, ks});
 }
 
 bool q4k_mma_supported(int rb, int n_tok) {
     return n_tok >= 5 && n_tok <= 16 && mma_stages(rb, n_tok <= 8 ? 8 : 16) > 0;
 }
 
-cudaError_t launch_q4k_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st) {
+// Scratch of the K-split tensor-core path for `rows` x rb q4_K and n_tok
+// tokens (an upper bound: the split the launch picks never needs more).
+size_t q4k_mma_split_part_floats(int rows, int rb, int n_tok) {
+    const int NB = n_tok <= 8 ? 8 : 16, ntiles = (rows + MMA_ROWS - 1) / MMA_ROWS;
+    int k = 1;
+    for (int c = 2; c <= 8; ++c)
+        if (rb % c == 0 && rb / c >= 2) k = c;
+    return (size_t)ntiles * k * NB * MMA_ROWS;
+}
+size_t q4k_mma_split_count_words(int rows) { return (size_t)((rows + MMA_ROWS - 1) / MMA_ROWS) * 8; }
+
+// part / count null: one unit per tile (no scratch).
+cudaError_t launch_q4k_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st, float *part,
+                           unsigned *count) {
     bool launched = false;
-    const cudaError_t e = n_tok <= 8 ? run_mma<8>(a, n_tok, sm_count, st, &launched)
-                                     : run_mma<16>(a, n_tok, sm_count, st, &launched);
+    const cudaError_t e = n_tok <= 8 ? run_mma<8>(a, n_tok, sm_count, st, &launched, part, count)
+                                     : run_mma<16>(a, n_tok, sm_count, st, &launched, part, count);
     if (e != cudaSuccess) return e;
     return launched ? cudaSuccess : cudaErrorInvalidValue;
 }

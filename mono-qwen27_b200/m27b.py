@@ -65,6 +65,9 @@ def lib():
         "m27b_dequant_rows": (b, [wvp, vp, i32, vp, i32, vp, cp, sz]),
         "m27b_hbm_read_probe": (b, [vp, sz, vp, cp, sz]),
         "m27b_hbm_read_probe_shape": (b, [vp, sz, i32, i32, i32, i32, vp, cp, sz]),
+        "m27b_qmv_mma_split_part_bytes": (sz, [wvp, i32]),
+        "m27b_qmv_mma_split_count_bytes": (sz, [wvp]),
+        "m27b_qmv_mma_split": (b, [wvp, vp, i32, vp, i32, vp, vp, vp, vp, cp, sz]),
         "m27b_qmv_q6k_stream_part_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_stream_count_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_stream": (b, [wvp, vp, vp, vp, vp, vp, vp, cp, sz]),
@@ -213,6 +216,25 @@ def qmv_q6k_ksplit(w, xq, n_tok, y, residual=None, part=None, count=None, stream
     _check(L.m27b_qmv_q6k_ksplit(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(y),
                                  ldy if ldy is not None else w.view.row_count, _ptr(residual), _ptr(part), _ptr(count),
                                  _stream(stream), err, ERR_CAP), err, "m27b_qmv_q6k_ksplit")
+    return y
+
+
+def qmv_mma_split(w, xq, n_tok, y, residual=None, part=None, count=None, stream=None, ldy=None):
+    """q4_K x n_tok (5..16) tokens on the tensor cores with K split across CTAs
+    (m27b_qmv_mma_split); part / count scratch are allocated here (counters
+    zeroed) unless given."""
+    import torch
+    L = lib()
+    if part is None:
+        part = torch.empty(max(16, L.m27b_qmv_mma_split_part_bytes(ctypes.byref(w.view), n_tok)), dtype=torch.uint8,
+                           device="cuda")
+    if count is None:
+        count = torch.zeros(max(16, L.m27b_qmv_mma_split_count_bytes(ctypes.byref(w.view))), dtype=torch.uint8,
+                            device="cuda")
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(L.m27b_qmv_mma_split(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(y),
+                                ldy if ldy is not None else w.view.row_count, _ptr(residual), _ptr(part), _ptr(count),
+                                _stream(stream), err, ERR_CAP), err, "m27b_qmv_mma_split")
     return y
 
 
