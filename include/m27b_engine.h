@@ -170,8 +170,10 @@ M27B_API bool m27b_engine_decode_step(M27BEngine *e, int token, int pos, int *ne
  * position; tokens a caller rejects leave K/V behind that later steps simply
  * overwrite).  q4_K matrices run 5+ tokens on the tensor cores.  logits
  * (tp_size 1 only, may be NULL) receive n rows of vocab floats.  The pass is
- * captured into a CUDA graph per n on first use; not with the fused NVLink
- * all-reduce (NCCL or tp_size 1).  Synchronises before returning. */
+ * captured into a CUDA graph per n on first use.  At tp_size > 1 its
+ * all-reduces (n rows each) run on the engine's NCCL communicator, also when
+ * the decode step uses the fused NVLink all-reduce.  Synchronises before
+ * returning. */
 M27B_API bool m27b_engine_verify(M27BEngine *e, const int *tokens, int n, int pos, int *next, float *logits, char *err,
                                  size_t err_cap);
 

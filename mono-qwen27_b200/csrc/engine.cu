@@ -508,7 +508,10 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
 
 // Enqueue a verify pass over n tokens (device e->vtok, positions ctl[1] ..
 // ctl[1]+n-1): the same layer arithmetic as enqueue_step on n rows, with the
-// unfused attention (each token at its own position) and the NCCL all-reduce.
+// unfused attention (each token at its own position) and the NCCL all-reduce
+// of n rows at once — also on an engine whose decode step uses the fused
+// NVLink all-reduce (it has the communicator; the verify pass leaves the
+// fused path's step counter, ctl[3], alone).
 bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
     const M27BModelConfig &c = e->c;
     const int hd = c.head_dim, D = c.hidden;
@@ -1203,7 +1206,6 @@ bool m27b_engine_verify(M27BEngine *e, const int *tokens, int n, int pos, int *n
                         size_t err_cap) {
     if (!e || !tokens || !next) return efail(err, err_cap, "m27b_engine_verify: null argument");
     if (n < 1 || n > M27B_VERIFY_MAX) return efail(err, err_cap, "m27b_engine_verify: n must be in [1, %d]", M27B_VERIFY_MAX);
-    if (e->p2p) return efail(err, err_cap, "m27b_engine_verify: not with the fused NVLink all-reduce");
     if (e->n_ssm)
         return efail(err, err_cap,
                      "m27b_engine_verify: not for hybrid models (the DeltaNet state cannot be rolled back after a "

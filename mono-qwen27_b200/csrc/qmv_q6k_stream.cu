@@ -8,9 +8,11 @@
 // two CTAs per SM also stage the 17408-value activation row twice, which
 // leaves room for six warps each.  Here one CTA per SM stages the row once,
 // next to the stages of up to 15 warps, and the items (row group, tile) are
-// numbered group-major and cut into one contiguous run per warp of the grid
-// (runs differ by at most one item; with fewer items than warps, one item
-// per run and the other warps idle).  A warp accumulates the 8 rows of a
+// numbered group-major and cut into one contiguous run per warp of the grid:
+// with at least as many warps as row groups, each group into 3-4 equal runs
+// of its own (every warp in one group), else into runs of equal item counts
+// across group boundaries (with fewer items than warps, one item per run and
+// the other warps idle).  A warp accumulates the 8 rows of a
 // group over the tiles of its run; when the run leaves the group (or ends)
 // it reduces over its lanes.  A group that lies inside one run is written
 // directly; otherwise the run's partial row sums go to slot (warp - first
@@ -58,11 +60,41 @@ __global__ void __launch_bounds__(Q6S_MAX_WARPS * 32, 1)
     const int nb = a.rb;
     // runs: Wt = min(warps of the grid, items), so that no run is empty (a
     // group's contributors are then consecutive runs); run r belongs to warp
-    // r / gridDim.x of CTA r % gridDim.x (consecutive runs on different SMs)
+    // r / gridDim.x of CTA r % gridDim.x (consecutive runs on different SMs).
+    // With at least as many runs as groups every group gets kg = Wt / G or
+    // Wt / G + 1 runs of equal tile counts (each run inside one group: one
+    // hand-off per warp); otherwise the items are cut into equal runs
+    // regardless of group boundaries.
     const long long T = (long long)ngroups * P;
     const long long Wt = (long long)gridDim.x * nwarps < T ? (long long)gridDim.x * nwarps : T;
     const int gw = warp * (int)gridDim.x + (int)blockIdx.x;
-    const long long i_lo = gw < Wt ? gw * T / Wt : 0, i_hi = gw < Wt ? (gw + 1) * T / Wt : 0;
+    const bool aligned = Wt >= ngroups && Wt / ngroups <= P;
+    long long i_lo = 0, i_hi = 0;
+    int a_first = 0, a_n = 0;  // aligned: this run's group's first run and run count
+    if (gw < Wt) {
+        if (aligned) {
+            const int k = (int)(Wt / ngroups), m = (int)(Wt % ngroups);  // m groups take k + 1 runs
+            int g, p, kg;
+            if (gw < m * (k + 1)) {
+                g = gw / (k + 1);
+                p = gw - g * (k + 1);
+                kg = k + 1;
+                a_first = g * (k + 1);
+            } else {
+                const int r = gw - m * (k + 1);
+                g = m + r / k;
+                p = r - (g - m) * k;
+                kg = k;
+                a_first = m * (k + 1) + (g - m) * k;
+            }
+            a_n = kg;
+            i_lo = (long long)g * P + (long long)p * P / kg;
+            i_hi = (long long)g * P + (long long)(p + 1) * P / kg;
+        } else {
+            i_lo = gw * T / Wt;
+            i_hi = (gw + 1) * T / Wt;
+        }
+    }
 
     // [stages of all warps | activation records | block scales | barriers]
     uint8_t *stage0 = q6s_smem + (size_t)warp * Q6T_STAGES * Q6T_ITEM;
@@ -147,7 +179,8 @@ __global__ void __launch_bounds__(Q6S_MAX_WARPS * 32, 1)
             acc[s][0] = 0.0f;
         }
         const int row = grp * 8 + lane;
-        const int w_first = q6s_warp_of(g_lo, T, Wt), w_last = q6s_warp_of(g_end - 1, T, Wt);
+        const int w_first = aligned ? a_first : q6s_warp_of(g_lo, T, Wt);
+        const int w_last = aligned ? a_first + a_n - 1 : q6s_warp_of(g_end - 1, T, Wt);
         if (w_first == w_last) {
             // the whole group lies in this run
             if (lane < 8 && row < a.rows) a.y[row] = a.residual ? fin + a.residual[row] : fin;

@@ -8,7 +8,10 @@ state after the last all-reduce is replicated on every rank and must match the
 reference within the matvec tolerance, all ranks must return the same greedy
 tokens, and the two all-reduce paths must agree (both add the same two
 partials; their RMSNorm reductions run in different orders, so a q8_K code
-can round the other way: 1e-4)."""
+can round the other way: 1e-4).  A verify pass over the generated
+continuation (its all-reduces on NCCL, also on the engine that decodes with
+the fused path) must return the greedy continuation on every rank, and the
+fused decode step must carry on after it."""
 import os
 import time
 
@@ -61,7 +64,13 @@ def _rank(rank, world, out_dir, comm):
             toks.append(e.decode_step(t, pos))
             hid.append(e.hidden())
         gen = e.generate(toks[-1], len(PROMPT), N_GEN)
-        np.savez(os.path.join(out_dir, f"{comm}_rank{rank}.npz"), hidden=np.array(hid), toks=np.array(toks), gen=gen)
+        # a verify pass over the generated continuation (its all-reduces on
+        # NCCL in both modes): the greedy token after each drafted token
+        vt = [int(toks[-1])] + [int(x) for x in gen[:N_GEN - 1]]
+        vnext = e.verify(vt, len(PROMPT))
+        after = e.decode_step(int(gen[-1]), len(PROMPT) + N_GEN)  # the fused step still works afterwards
+        np.savez(os.path.join(out_dir, f"{comm}_rank{rank}.npz"), hidden=np.array(hid), toks=np.array(toks), gen=gen,
+                 vnext=np.array(vnext), after=np.array([after]))
     finally:
         e.close()
 
@@ -93,3 +102,8 @@ def test_tp2_decode(orc, tmp_path):
     for pos in range(len(PROMPT)):
         assert orc.rel_l2(b["hidden"][pos], a["hidden"][pos]) <= 1e-4, pos
     assert (a["toks"] == b["toks"]).all() and (a["gen"] == b["gen"]).all()
+    for comm, r in res.items():
+        # verify agrees with the greedy continuation and across ranks, on both paths
+        assert (r[0]["vnext"] == r[1]["vnext"]).all() and (r[0]["after"] == r[1]["after"]).all(), comm
+        assert (r[0]["vnext"] == r[0]["gen"]).all(), (comm, r[0]["vnext"], r[0]["gen"])
+    assert (a["after"] == b["after"]).all()
