@@ -427,7 +427,7 @@ def decode_bench(args, world, rank, dev, dist, uuid):
         ms_e2e, gen_e2e, _ = timed(host_loop)
         # speculative verification: one pass over n drafted tokens (tensor cores for the q4_K matrices)
         verify = {}
-        if (world == 1 or args.comm == "nccl") and not hybrid:
+        if not hybrid:
             vt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.vocab, 16)]
             for n in (8, 16):
                 e.verify(vt[:n], p0)  # capture

@@ -660,9 +660,6 @@ struct AttnBatchArgs {
     float scale;
 };
 
-// 16 bytes global -> shared without a register round trip (L2 only).
-// This thread's asynchronous copies have landed.
-
 M27B_DI int abt_splits(int L, int smax) {
     const int s = (L + ABT_CH - 1) / ABT_CH;
     return s < smax ? s : smax;
@@ -672,16 +669,18 @@ size_t attn_batch_smem_bytes(int G, int hd) {
     return (size_t)(G * hd + 2 * ABT_CH * hd + ATT_G * ABT_CH + 4 * ATT_G) * sizeof(float);
 }
 
-template <int DPL>
+template <int DPL, int G>
 __global__ void __launch_bounds__(256) k_attn_batch(const AttnBatchArgs a) {
-    pdl_wait();
-    pdl_trigger();
     constexpr int hd = DPL * 32, rec = hd + 4, CH = ABT_CH, Q4 = hd / 4;
-    constexpr int NO = ATT_G * hd / 256;  // output values per thread, at most
+    constexpr int NO = (G * hd + 255) / 256;  // output values per thread, at most
     const int j = blockIdx.x, s = blockIdx.y, tok = blockIdx.z;
-    const int nq = a.nq, nkv = a.nkv, G = nq / nkv;
+    const int nq = a.nq, nkv = a.nkv;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, t = threadIdx.x;
-    const int L = *a.pos_p + tok + 1;
+    // the pass's first position is set before the pass starts; cache rows
+    // below it are older than this launch, those at or past it are appended
+    // by the previous kernel
+    const int pos0 = *a.pos_p;
+    const int L = pos0 + tok + 1;
     const int S = abt_splits(L, a.smax);
     if (s >= S) return;
     float *part = a.part + (size_t)tok * a.smax * nq * rec;
@@ -704,7 +703,13 @@ __global__ void __launch_bounds__(256) k_attn_batch(const AttnBatchArgs a) {
             cp_async16(vs + p * hd + 4 * c4, a.vc + o);
         }
     };
-    stage(p0, p1 - p0 < CH ? p1 - p0 : CH);
+    // the first chunk's copies go out before the wait when all its rows are old
+    const int n0 = p1 - p0 < CH ? p1 - p0 : CH;
+    const bool early = p0 + n0 <= pos0;
+    if (early) stage(p0, n0);
+    pdl_wait();
+    pdl_trigger();
+    if (!early) stage(p0, n0);
     const float *qrow = a.q + (size_t)tok * nq * hd;
     if (warp < G) {
         float qv[DPL];
@@ -728,17 +733,24 @@ __global__ void __launch_bounds__(256) k_attn_batch(const AttnBatchArgs a) {
         for (int p = warp; p < n; p += 8) {
             float kv[DPL];
             ld_dims<DPL>(ks + p * hd + lane * DPL, kv);
+            float d[G];
 #pragma unroll
-            for (int g = 0; g < ATT_G; ++g) {
-                if (g < G) {
-                    float qv[DPL];
-                    ld_dims<DPL>(qs + g * hd + lane * DPL, qv);
-                    float d = 0.0f;
+            for (int g = 0; g < G; ++g) {
+                float qv[DPL];
+                ld_dims<DPL>(qs + g * hd + lane * DPL, qv);
+                float x = 0.0f;
 #pragma unroll
-                    for (int i = 0; i < DPL; ++i) d = fmaf(qv[i], kv[i], d);
-                    d = warp_sum(d);
-                    if (lane == 0) sc[g * CH + p] = d;
-                }
+                for (int i = 0; i < DPL; ++i) x = fmaf(qv[i], kv[i], x);
+                d[g] = x;
+            }
+            // the G lane sums in interleaved butterflies
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
+            if (lane == 0) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) sc[g * CH + p] = d[g];
             }
         }
         __syncthreads();
@@ -865,10 +877,20 @@ __global__ void __launch_bounds__(256) k_attn_batch(const AttnBatchArgs a) {
     }
 }
 
-template <int DPL>
-static cudaError_t attn_batch_opt_in() {
-    return cudaFuncSetAttribute(k_attn_batch<DPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)attn_batch_smem_bytes(ATT_G, DPL * 32));
+// The (head_dim, heads per kv head) pairs the batch kernel is built for:
+// whole q8_K blocks per kv group, (G * hd) % 256 == 0.
+#define M27B_ABT_SHAPES(X)                                                                                             \
+    X(2, 4) X(2, 8) X(4, 2) X(4, 4) X(4, 6) X(4, 8) X(8, 1) X(8, 2) X(8, 3) X(8, 4) X(8, 5) X(8, 6) X(8, 7) X(8, 8)
+
+static cudaError_t attn_batch_opt_in_all() {
+    cudaError_t e = cudaSuccess;
+#define M27B_ABT_OPT(D, GG)                                                                                            \
+    if (e == cudaSuccess)                                                                                              \
+        e = cudaFuncSetAttribute(k_attn_batch<D, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize,                     \
+                                 (int)attn_batch_smem_bytes(ATT_G, D * 32));
+    M27B_ABT_SHAPES(M27B_ABT_OPT)
+#undef M27B_ABT_OPT
+    return e;
 }
 
 // head_dim 64 / 128 / 256, a kv group's heads filling whole q8_K blocks, and
@@ -900,12 +922,12 @@ cudaError_t attn_batch_launch(const float *q, const float *gate, const float *kc
     a.scale = scale;
     const size_t smem = attn_batch_smem_bytes(nq / nkv, hd);
     const dim3 grid(nkv, S, n_tok);
-    switch (hd) {
-        case 64: return launch_pdl(k_attn_batch<2>, grid, dim3(256), smem, st, a);
-        case 128: return launch_pdl(k_attn_batch<4>, grid, dim3(256), smem, st, a);
-        case 256: return launch_pdl(k_attn_batch<8>, grid, dim3(256), smem, st, a);
-        default: return cudaErrorInvalidValue;
-    }
+    const int dpl = hd / 32, G = nq / nkv;
+#define M27B_ABT_RUN(D, GG)                                                                                            \
+    if (dpl == D && G == GG) return launch_pdl(k_attn_batch<D, GG>, grid, dim3(256), smem, st, a);
+    M27B_ABT_SHAPES(M27B_ABT_RUN)
+#undef M27B_ABT_RUN
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float theta, cudaStream_t st) {
@@ -917,8 +939,7 @@ cudaError_t rope_table_launch(float2 *rope, const int *pos, int n_rot, float the
 cudaError_t attn_prepare() {
     cudaError_t e = cudaSuccess;
     for (cudaError_t r : {attn_opt_in<1>(), attn_opt_in<2>(), attn_opt_in<3>(), attn_opt_in<4>(), attn_opt_in<5>(),
-                          attn_opt_in<6>(), attn_opt_in<7>(), attn_opt_in<8>(), attn_batch_opt_in<2>(),
-                          attn_batch_opt_in<4>(), attn_batch_opt_in<8>()})
+                          attn_opt_in<6>(), attn_opt_in<7>(), attn_opt_in<8>(), attn_batch_opt_in_all()})
         if (r != cudaSuccess) e = r;
     return e;
 }
