@@ -892,6 +892,9 @@ def main():
         return g
 
     graphs = {}
+    # graphs are replayed, and timed, on a stream of their own (not the legacy
+    # default stream)
+    run_st = torch.cuda.Stream()
 
     def run_steps(fn, n):
         full, rem = divmod(n, GRAPH_STEPS)
@@ -899,10 +902,11 @@ def main():
             graphs[(fn, GRAPH_STEPS)] = capture(fn, GRAPH_STEPS)
         if rem and (fn, rem) not in graphs:
             graphs[(fn, rem)] = capture(fn, rem)
-        for _ in range(full):
-            graphs[(fn, GRAPH_STEPS)].replay()
-        if rem:
-            graphs[(fn, rem)].replay()
+        with torch.cuda.stream(run_st):
+            for _ in range(full):
+                graphs[(fn, GRAPH_STEPS)].replay()
+            if rem:
+                graphs[(fn, rem)].replay()
 
     def timed(fn, steps, warmup, sampler=None):
         run_steps(fn, warmup)
@@ -912,9 +916,9 @@ def main():
         if sampler:
             sampler.start()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        e0.record(run_st)
         run_steps(fn, steps)
-        e1.record()
+        e1.record(run_st)
         torch.cuda.synchronize()
         clocks = sampler.stop() if sampler else None
         barrier()

@@ -192,6 +192,33 @@ M27B_API bool m27b_qmv_mma_split(const struct WeightView *w, const void *xq, int
                                  const float *residual, void *part, void *count, cudaStream_t stream, char *err,
                                  size_t err_cap);
 
+/* q6_K matvec for 1..8 tokens on the tensor cores (tcgen05 kind::i8, one
+ * MMA per 16-value group: each 32-value slice is multiplied with either
+ * group's codes zeroed), y = W.xq (+ residual): the speculative verify
+ * pass's ffn_down.  Integer sums per super-block exactly as ggml's
+ * vec_dot_q6_K_q8_K, fp32 combine per block (within fp32 rounding of
+ * m27b_qmv).  Needs the repacked q6_K layout.  With part / count (both
+ * non-NULL: m27b_qmv_q6k_mma_part_bytes of scratch, m27b_qmv_q6k_mma_count_bytes
+ * of counters zero before the first call, left zero by every call) a matrix
+ * of few row tiles has its K dimension split across CTAs, the ranges' partial
+ * sums added in range order (deterministic); calls overlapping on the GPU
+ * with the same scratch race.  Replaces, for a verify pass, the reference's
+ * per-token k_q6k_mv_q8_dp4a (src/mono27b_executor.cu:630-645). */
+M27B_API size_t m27b_qmv_q6k_mma_part_bytes(const struct WeightView *w);
+M27B_API size_t m27b_qmv_q6k_mma_count_bytes(const struct WeightView *w);
+M27B_API bool m27b_qmv_q6k_mma(const struct WeightView *w, const void *xq, int n_tok, float *y, int ldy,
+                               const float *residual, void *part, void *count, cudaStream_t stream, char *err,
+                               size_t err_cap);
+
+/* The same kernel with m27b_qmv_argmax's epilogue (best[t] receives token
+ * t's packed key; logits, may be NULL, with stride ldl): the
+ * verify pass's lm_head for up to 8 tokens in one weight pass.  Replaces the
+ * reference's lm_head block + k_argmax (src/mono27b_executor.cu:2577-2593,
+ * :209-239) for the drafted tokens. */
+M27B_API bool m27b_qmv_q6k_mma_argmax(const struct WeightView *w, const void *xq, int n_tok, float *logits, int ldl,
+                                      unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
+                                      size_t err_cap);
+
 /* q6_K matvec for ONE token over a matrix of few, long rows (a decode step's
  * ffn_down, 5120 x 17408), y = W.xq (+ residual): the (8-row group, 4-block
  * tile) items are cut into equal runs, one per warp of a one-CTA-per-SM grid,

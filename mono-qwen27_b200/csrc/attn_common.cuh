@@ -35,23 +35,6 @@ M27B_DI void ld_dims(const float *p, float (&v)[DPL]) {
     }
 }
 
-// Asynchronous global -> shared copies (cp.async; completion by
-// cp_async_wait_all in the issuing thread).
-M27B_DI void cp_async16(void *smem, const void *gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
-                 "l"(gmem)
-                 : "memory");
-}
-M27B_DI void cp_async8(void *smem, const void *gmem) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
-                 : "memory");
-}
-M27B_DI void cp_async4(void *smem, const void *gmem) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
-                 : "memory");
-}
-M27B_DI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
 // A lane's DPL consecutive floats of a row (16-, 8- or 4-byte aligned as DPL allows).
 template <int DPL>
 M27B_DI void cp_async_dims(float *dst, const float *src) {

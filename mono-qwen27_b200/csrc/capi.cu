@@ -309,19 +309,20 @@ namespace m27b {
 size_t q6k_stream_part_floats(int rows, int rb);
 size_t q6k_stream_count_words(int rows);
 bool q6k_stream_applies(int k);
-cudaError_t launch_q6k_stream(const QmvArgs &a, float *part, unsigned *count, int sm_count, cudaStream_t st);
+cudaError_t launch_q6k_stream(const QmvArgs &a, float *part, unsigned *count, int sm_count, cudaStream_t st,
+                              int epi);
 
 // q6_K x one token with the (row group, tile) items cut evenly over the
 // grid's warps (ffn_down in a decode step): part holds
 // q6k_stream_part_floats(rows, rb) floats, count one zeroed word per 8-row
 // group.  q8_K activations xq, or fp32 x quantized in the prologue.
 bool qmv_q6k_stream(const WeightView *w, const void *xq, const float *xf, float *y, const float *residual, float *part,
-                    unsigned *count, cudaStream_t stream, char *err, size_t cap) {
+                    unsigned *count, cudaStream_t stream, char *err, size_t cap, const PushArgs *push) {
     const char *what = "qmv_q6k_stream";
     WDesc d{};
     if (!describe(w, d, what, err, cap)) return false;
     if (d.kind != W_Q6KP) return fail(err, cap, "%s: repacked q6_K weights only", what);
-    if ((!xq && !xf) || !y || !part || !count) return fail(err, cap, "%s: null pointer", what);
+    if ((!xq && !xf) || (!y && !push) || !part || !count) return fail(err, cap, "%s: null pointer", what);
     if (!q6k_stream_applies(d.k)) return fail(err, cap, "%s: rows of %d values are too long to stage", what, d.k);
     const int sms = sm_count_current();
     int *status = status_ptr_current();
@@ -339,7 +340,9 @@ bool qmv_q6k_stream(const WeightView *w, const void *xq, const float *xf, float 
     a.rb = (int)w->row_blocks;
     a.k = d.k;
     a.status = status;
-    return cuda_ok(launch_q6k_stream(a, part, count, sms, stream), what, err, cap) && ok(err, cap);
+    if (push) a.push = *push;
+    return cuda_ok(launch_q6k_stream(a, part, count, sms, stream, push ? EPI_PUSH : EPI_STORE), what, err, cap) &&
+           ok(err, cap);
 }
 
 // q4_K x 5..16 tokens on the tensor cores with K split across CTAs (the
@@ -372,6 +375,54 @@ bool qmv_mma_split(const WeightView *w, const void *xq, int n_tok, float *y, int
     a.passes = d.passes;
     a.status = status;
     return cuda_ok(launch_q4k_mma(a, n_tok, sms, stream, part, count), what, err, cap) && ok(err, cap);
+}
+
+bool q6k_mma_supported(int rows, int rb, int n_tok, bool split, int sm_count);
+size_t q6k_mma_part_floats(int rows);
+size_t q6k_mma_count_words(int rows);
+cudaError_t launch_q6k_mma(const QmvArgs &a, int n_tok, int epi, float *part, unsigned *count, int sm_count,
+                           cudaStream_t st);
+
+// q6_K x 1..8 tokens on the tensor cores (the verify pass's ffn_down and
+// lm_head): EPI_STORE writes y (+ residual), EPI_ARGMAX sets best[t] to the
+// packed argmax key of token t (logits into y when non-null).  part / count: K-split scratch
+// (q6k_mma_part_floats floats, q6k_mma_count_words zeroed words) or null.
+bool qmv_q6k_mma(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                 unsigned long long *best, uint32_t row_offset, int epi, float *part, unsigned *count,
+                 cudaStream_t stream, char *err, size_t cap) {
+    const char *what = epi == EPI_ARGMAX ? "qmv_q6k_mma_argmax" : "qmv_q6k_mma";
+    WDesc d{};
+    if (!describe(w, d, what, err, cap)) return false;
+    if (d.kind != W_Q6KP) return fail(err, cap, "%s: repacked q6_K weights only", what);
+    if (!xq || (epi == EPI_STORE && !y) || (epi == EPI_ARGMAX && !best))
+        return fail(err, cap, "%s: null pointer", what);
+    if ((part == nullptr) != (count == nullptr)) return fail(err, cap, "%s: part and count go together", what);
+    const int sms = sm_count_current();
+    int *status = status_ptr_current();
+    if (sms <= 0 || !status) return fail(err, cap, "%s: no CUDA device", what);
+    if (!q6k_mma_supported((int)w->row_count, (int)w->row_blocks, n_tok, part != nullptr, sms))
+        return fail(err, cap, "%s: %d tokens x %u blocks per row are not served by the tensor-core kernel", what, n_tok,
+                    w->row_blocks);
+    if (n_tok > 1 && y && ldy < (int)w->row_count)
+        return fail(err, cap, "%s: ldy (%d) < row_count (%u)", what, ldy, w->row_count);
+    QmvArgs a{};
+    a.w0 = (const uint8_t *)w->ptr;
+    a.xq = xq;
+    a.y = y;
+    a.residual = epi == EPI_STORE ? residual : nullptr;
+    a.best = best;
+    a.row_offset = row_offset;
+    a.row_stride = d.row_stride;
+    a.ldy = y ? ldy : (int)w->row_count;
+    a.rows = (int)w->row_count;
+    a.rb = (int)w->row_blocks;
+    a.k = d.k;
+    a.status = status;
+    if (epi == EPI_ARGMAX) {
+        const cudaError_t e = cudaMemsetAsync(best, 0, sizeof(unsigned long long) * (size_t)n_tok, stream);
+        if (e != cudaSuccess) return cuda_ok(e, what, err, cap);
+    }
+    return cuda_ok(launch_q6k_mma(a, n_tok, epi, part, count, sms, stream), what, err, cap) && ok(err, cap);
 }
 
 int q6k_ksplit_ranges(int rb);
@@ -665,6 +716,31 @@ bool m27b_qmv_mma_split(const WeightView *w, const void *xq, int n_tok, float *y
     return qmv_mma_split(w, xq, n_tok, y, ldy, residual, (float *)part, (unsigned *)count, stream, err, err_cap);
 }
 
+size_t m27b_qmv_q6k_mma_part_bytes(const WeightView *w) {
+    if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
+    return q6k_mma_part_floats((int)w->row_count) * sizeof(float);
+}
+
+size_t m27b_qmv_q6k_mma_count_bytes(const WeightView *w) {
+    if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
+    return q6k_mma_count_words((int)w->row_count) * sizeof(unsigned);
+}
+
+bool m27b_qmv_q6k_mma(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                      void *part, void *count, cudaStream_t stream, char *err, size_t err_cap) {
+    if (((uintptr_t)part & 15) || ((uintptr_t)count & 3))
+        return fail(err, err_cap, "m27b_qmv_q6k_mma: misaligned scratch");
+    return qmv_q6k_mma(w, xq, n_tok, y, ldy, residual, nullptr, 0u, EPI_STORE, (float *)part, (unsigned *)count,
+                       stream, err, err_cap);
+}
+
+bool m27b_qmv_q6k_mma_argmax(const WeightView *w, const void *xq, int n_tok, float *logits, int ldl,
+                             unsigned long long *best, uint32_t row_offset, cudaStream_t stream, char *err,
+                             size_t err_cap) {
+    return qmv_q6k_mma(w, xq, n_tok, logits, ldl, nullptr, best, row_offset, EPI_ARGMAX, nullptr, nullptr, stream, err,
+                       err_cap);
+}
+
 size_t m27b_qmv_q6k_stream_part_bytes(const WeightView *w) {
     if (!w || (w->ggml_type & M27B_TYPE_MASK) != M27B_TYPE_Q6_K) return 0;
     return q6k_stream_part_floats((int)w->row_count, (int)w->row_blocks) * sizeof(float);
@@ -680,7 +756,8 @@ bool m27b_qmv_q6k_stream(const WeightView *w, const void *xq, float *y, const fl
     if (((uintptr_t)part & 15) || ((uintptr_t)count & 3))
         return fail(err, err_cap, "m27b_qmv_q6k_stream: misaligned scratch");
     if (!xq) return fail(err, err_cap, "m27b_qmv_q6k_stream: null pointer");
-    return qmv_q6k_stream(w, xq, nullptr, y, residual, (float *)part, (unsigned *)count, stream, err, err_cap);
+    return qmv_q6k_stream(w, xq, nullptr, y, residual, (float *)part, (unsigned *)count, stream, err, err_cap,
+                          nullptr);
 }
 
 bool m27b_qmv_q6k_ksplit(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,

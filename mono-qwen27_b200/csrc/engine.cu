@@ -68,8 +68,15 @@ size_t q6k_stream_part_floats(int rows, int rb);
 size_t q6k_stream_count_words(int rows);
 bool q6k_stream_applies(int k);
 bool qmv_q6k_stream(const WeightView *w, const void *xq, const float *xf, float *y, const float *residual, float *part,
-                    unsigned *count, cudaStream_t stream, char *err, size_t cap);
+                    unsigned *count, cudaStream_t stream, char *err, size_t cap, const PushArgs *push);
 size_t q6k_ksplit_part_floats(int rows, int ks);
+// q6_K on the tensor cores (qmv_q6k_mma.cu, capi.cu)
+bool q6k_mma_supported(int rows, int rb, int n_tok, bool split, int sm_count);
+size_t q6k_mma_part_floats(int rows);
+size_t q6k_mma_count_words(int rows);
+bool qmv_q6k_mma(const WeightView *w, const void *xq, int n_tok, float *y, int ldy, const float *residual,
+                 unsigned long long *best, uint32_t row_offset, int epi, float *part, unsigned *count,
+                 cudaStream_t stream, char *err, size_t cap);
 // Gated DeltaNet block (ssm.cu)
 cudaError_t ssm_rmsnorm_launch(const float *x, const float *w, float eps, int n, float *y, cudaStream_t st);
 cudaError_t ssm_conv_launch(const float *x, const float *w, float *cstate, float *out, const float *ba,
@@ -309,15 +316,37 @@ bool vmv(M27BEngine *e, const QMat &m, const uint8_t *xq, int n, float *y, int l
     return m27b_qmv(&m.v, xq, n, y, ldy, res, e->st, err, err_cap);
 }
 
+// A repacked q6_K matrix of a verify pass (ffn_down with K split, lm_head
+// without) that the tensor-core kernel serves for chunks of up to 8 tokens.
+bool q6_verify_mma(const M27BEngine *e, const QMat &m, int n, bool split) {
+    if (m.v.ggml_type != (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) || (split && !e->q6m_part)) return false;
+    if (split && (size_t)m.rows > (size_t)e->c.hidden) return false;  // the scratch is sized for hidden rows
+    for (int t0 = 0; t0 < n; t0 += 8)
+        if (!q6k_mma_supported(m.rows, (int)m.v.row_blocks, std::min(8, n - t0), split, e->sms)) return false;
+    return true;
+}
+
 // The down projection of one token (rows = hidden, long rows): a repacked
 // q6_K matrix goes to the kernel that cuts its items evenly over the warps
 // (its few row groups do not spread evenly over the SMs as whole groups),
 // anything else to the one-pass matvec.
+bool down_stream_ok(const M27BEngine *e, const QMat &m) {
+    return e->sk_part && m.v.ggml_type == (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) && m.rows <= e->c.hidden &&
+           (int)m.v.row_blocks <= e->F / 256 + 1 && q6k_stream_applies((int)m.v.row_blocks * 256);
+}
+
 bool down_mv(M27BEngine *e, const QMat &m, const uint8_t *xq, float *y, const float *res, char *err, size_t err_cap) {
-    if (e->sk_part && m.v.ggml_type == (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) && m.rows <= e->c.hidden &&
-        (int)m.v.row_blocks <= e->F / 256 + 1 && q6k_stream_applies((int)m.v.row_blocks * 256))
-        return qmv_q6k_stream(&m.v, xq, nullptr, y, res, e->sk_part, e->sk_count, e->st, err, err_cap);
+    if (down_stream_ok(e, m))
+        return qmv_q6k_stream(&m.v, xq, nullptr, y, res, e->sk_part, e->sk_count, e->st, err, err_cap, nullptr);
     return mv(e, m, xq, y, res, err, err_cap);
+}
+
+// The same into every rank's window (the fused all-reduce's producer).
+bool down_push(M27BEngine *e, const QMat &m, const uint8_t *xq, const float *res, const PushArgs &push, char *err,
+               size_t err_cap) {
+    if (down_stream_ok(e, m))
+        return qmv_q6k_stream(&m.v, xq, nullptr, nullptr, res, e->sk_part, e->sk_count, e->st, err, err_cap, &push);
+    return qmv_push(&m.v, xq, res, push, e->st, err, err_cap);
 }
 
 bool allreduce_hidden(M27BEngine *e, float *buf, char *err, size_t err_cap) {
@@ -476,7 +505,7 @@ bool enqueue_step(M27BEngine *e, char *err, size_t err_cap) {
         // next layer's input RMSNorm (the output norm after the last layer) -> xq
         const float *next_norm = l + 1 < c.n_layers ? e->L[l + 1].attn_norm : e->out_norm;
         if (p2p) {
-            ECALL(qmv_push(&Ly.wd.v, dxq, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), e->st, err, err_cap));
+            ECALL(down_push(e, Ly.wd, dxq, r0 ? e->h2 : nullptr, push_args(e, 1, 2u * l + 1u), err, err_cap));
             ECALL(consume(e, 1, 2u * l + 1u, next_norm, e->h, err, err_cap));
         } else {
             ECALL(down_mv(e, Ly.wd, dxq, e->h, r0 ? e->h2 : nullptr, err, err_cap));
@@ -558,8 +587,17 @@ bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
                                        nullptr, e->st, err, err_cap));
             ECALL(m27b_act_quant(e->a, e->F, n, e->F, act_type_of(Ly.wd.type), e->xq, e->st, err, err_cap));
         }
-        if (n >= 5 && Ly.wd.v.ggml_type == (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) &&
-            q6k_ksplit_ranges((int)Ly.wd.v.row_blocks) > 0 && Ly.wd.rows == D)
+        if (n >= 5 && q6_verify_mma(e, Ly.wd, n, true)) {
+            // 5+ tokens of a q6_K down: the tensor cores, K split across CTAs, up to 8 tokens per weight pass
+            const size_t xrow = m27b_act_bytes(M27B_TYPE_Q8_K, e->F);
+            for (int t0 = 0; t0 < n; t0 += 8) {
+                const int nt = std::min(8, n - t0);
+                ECALL(qmv_q6k_mma(&Ly.wd.v, e->xq + t0 * xrow, nt, e->h + (size_t)t0 * D, D,
+                                  r0 ? e->h2 + (size_t)t0 * D : nullptr, nullptr, 0u, EPI_STORE, e->q6m_part,
+                                  e->q6m_count, e->st, err, err_cap));
+            }
+        } else if (n >= 5 && Ly.wd.v.ggml_type == (M27B_TYPE_Q6_K | M27B_LAYOUT_PLANAR) &&
+                   q6k_ksplit_ranges((int)Ly.wd.v.row_blocks) > 0 && Ly.wd.rows == D)
             // 5+ tokens of a q6_K down: K split across CTAs, 8 tokens per weight pass
             ECALL(qmv_q6k_ksplit(&Ly.wd.v, e->xq, n, e->h, D, r0 ? e->h2 : nullptr, e->ksp_part, e->ksp_count, e->st,
                                  err, err_cap));
@@ -569,7 +607,16 @@ bool enqueue_verify(M27BEngine *e, int n, char *err, size_t err_cap) {
     }
     ECALL(m27b_act_quant_rmsnorm(e->h, e->out_norm, c.rms_eps, D, n, D, act_type_of(e->lmh.type), e->xq, e->st, err,
                                  err_cap));
-    ECALL(m27b_qmv_argmax(&e->lmh.v, e->xq, n, e->logits, e->V, e->best, (uint32_t)e->v_lo, e->st, err, err_cap));
+    if (n >= 5 && q6_verify_mma(e, e->lmh, n, false)) {
+        // 5+ tokens: lm_head on the tensor cores, up to 8 tokens per weight pass
+        const size_t xrow = m27b_act_bytes(M27B_TYPE_Q8_K, D);
+        for (int t0 = 0; t0 < n; t0 += 8)
+            ECALL(qmv_q6k_mma(&e->lmh.v, e->xq + t0 * xrow, std::min(8, n - t0), e->logits + (size_t)t0 * e->V, e->V,
+                              nullptr, e->best + t0, (uint32_t)e->v_lo, EPI_ARGMAX, nullptr, nullptr, e->st, err,
+                              err_cap));
+    } else {
+        ECALL(m27b_qmv_argmax(&e->lmh.v, e->xq, n, e->logits, e->V, e->best, (uint32_t)e->v_lo, e->st, err, err_cap));
+    }
     if (c.tp_size > 1) ENCCL(ncclAllReduce(e->best, e->best, (size_t)n, ncclUint64, ncclMax, e->comm, e->st));
     return true;
 }
@@ -751,7 +798,9 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
         m27b_engine_destroy(e);
         return false;
     };
-    if (cudaGetDevice(&e->dev) != cudaSuccess) return bail(efail(err, err_cap, "no CUDA device"));
+    if (cudaGetDevice(&e->dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&e->sms, cudaDevAttrMultiProcessorCount, e->dev) != cudaSuccess)
+        return bail(efail(err, err_cap, "no CUDA device"));
     e->H = pt.n_q;
     e->q_lo = pt.q_lo;
     e->KV = pt.n_kv;
@@ -795,6 +844,9 @@ bool m27b_engine_create(const M27BModelConfig *cfg, M27BEngine **out, char *err,
               A((void **)&e->mma_count, q4k_mma_split_count_words(mma_rows_max(e)) * sizeof(unsigned)) &&
               cudaMemset(e->mma_count, 0, q4k_mma_split_count_words(mma_rows_max(e)) * sizeof(unsigned)) ==
                   cudaSuccess &&
+              A((void **)&e->q6m_part, q6k_mma_part_floats(c.hidden) * sizeof(float)) &&
+              A((void **)&e->q6m_count, q6k_mma_count_words(c.hidden) * sizeof(unsigned)) &&
+              cudaMemset(e->q6m_count, 0, q6k_mma_count_words(c.hidden) * sizeof(unsigned)) == cudaSuccess &&
               A((void **)&e->sk_part, q6k_stream_part_floats(c.hidden, e->F / 256 + 1) * sizeof(float)) &&
               A((void **)&e->sk_count, q6k_stream_count_words(c.hidden) * sizeof(unsigned)) &&
               cudaMemset(e->sk_count, 0, q6k_stream_count_words(c.hidden) * sizeof(unsigned)) == cudaSuccess;

@@ -120,4 +120,51 @@ M27B_DI uint2 wait_word(const uint2 *p, uint2 w, uint32_t ep, int *status, int c
     }
 }
 
+// ---- prologue gathers ----
+// A q8_K activation record (fp32 d, 256 codes, 16 int16 sub-block sums:
+// 292 bytes) in 32-bit words, and the two signed halves of a word.
+constexpr int Q8K_WORDS = 73;
+M27B_DI int s16_lo(uint32_t v) { return (int)(int16_t)(v & 0xffffu); }
+M27B_DI int s16_hi(uint32_t v) { return (int)(int16_t)(v >> 16); }
+
+// Element i of n goes from global src(i) to shared dst(i, value), read
+// through L2 (the previous kernel wrote it).  Each thread issues R loads
+// before any of its stores: the compiler does not move a global load above a
+// store through a generic pointer, so a plain load-store loop pays one L2
+// round trip per iteration.
+template <int R, class T, class Src, class Dst>
+M27B_DI void gather_l2(int n, Src src, Dst dst) {
+    for (int i0 = threadIdx.x; i0 < n; i0 += R * (int)blockDim.x) {
+        T v[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = i0 + r * (int)blockDim.x;
+            if (i < n) v[r] = __ldcg(src(i));
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = i0 + r * (int)blockDim.x;
+            if (i < n) dst(i, v[r]);
+        }
+    }
+}
+
+// ---- asynchronous copies ----
+// Asynchronous global -> shared copies (cp.async; completion by
+// cp_async_wait_all in the issuing thread).
+M27B_DI void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+M27B_DI void cp_async8(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+                 : "memory");
+}
+M27B_DI void cp_async4(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+                 : "memory");
+}
+M27B_DI void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 }  // namespace m27b

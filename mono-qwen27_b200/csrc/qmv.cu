@@ -51,15 +51,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows, int box_u32, int box_rows) {
+bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows, int box_u32, int box_rows,
+                     int swizzle) {
     auto enc = tensor_map_encoder();
     if (!enc || (row_bytes & 15) != 0 || ((uintptr_t)w & 15) != 0) return false;
+    const CUtensorMapSwizzle sw = swizzle == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : swizzle == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                  : swizzle == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
+    if (swizzle && box_u32 * 4 > swizzle) return false;
     const cuuint64_t gdim[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)rows};
     const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
     const cuuint32_t box[2] = {(cuuint32_t)box_u32, (cuuint32_t)box_rows};
     const cuuint32_t estride[2] = {1, 1};
     return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(w), gdim, gstride, box, estride,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

@@ -137,20 +137,15 @@ template <int NT>
 M27B_DI void stage_x_blk(const QmvArgs &a, uint8_t *xrec, float *xd) {
     const int nb = a.k / 256;
     const uint8_t *src = (const uint8_t *)a.xq;  // NT*nb blocks of 292 bytes
-    for (int i = threadIdx.x; i < NT * nb * 64; i += blockDim.x) {
-        const int blk = i >> 6, w = i & 63;
-        ((uint32_t *)(xrec + (size_t)blk * BLK_XREC))[w] = __ldcg((const unsigned *)(src + (size_t)blk * 292 + 4) + w);
-    }
-    for (int i = threadIdx.x; i < NT * nb * 9; i += blockDim.x) {
-        const int blk = i / 9, j = i - blk * 9;
-        const uint8_t *sb = src + (size_t)blk * 292;
-        if (j < 8) {
-            const int16_t *bs = (const int16_t *)(sb + 260);
-            ((int16_t *)(xrec + (size_t)blk * BLK_XREC + 256))[j] = (int16_t)(__ldcg(bs + 2 * j) + __ldcg(bs + 2 * j + 1));
-        } else {
-            xd[blk] = __ldcg((const float *)sb);
-        }
-    }
+    // a record is 73 words: d, 64 code words, 8 words of two bsums each
+    gather_l2<8, unsigned>(NT * nb * Q8K_WORDS, [&](int i) { return (const unsigned *)src + i; },
+                           [&](int i, unsigned v) {
+                               const int blk = i / Q8K_WORDS, o = i - blk * Q8K_WORDS;
+                               uint8_t *rec = xrec + (size_t)blk * BLK_XREC;
+                               if (o == 0) xd[blk] = __uint_as_float(v);
+                               else if (o <= 64) ((uint32_t *)rec)[o - 1] = v;
+                               else ((int16_t *)(rec + 256))[o - 65] = (int16_t)(s16_lo(v) + s16_hi(v));
+                           });
 }
 
 // The same records built from fp32 activations in the prologue (the fused

@@ -253,13 +253,13 @@ M27B_DI XStage stage_x(const QmvArgs &a, uint8_t *smem) {
         int8_t *q = (int8_t *)smem;
         float *d = (float *)(smem + (size_t)NT * a.k);
         const uint16_t *src = (const uint16_t *)a.xq;  // 17 halfwords per block
-        const int total = NT * nb * 17;
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            const int blk = i / 17, o = i - blk * 17;
-            const uint16_t hw = src[i];
-            if (o == 0) d[blk] = h2f(hw);
-            else *(uint16_t *)(q + (size_t)blk * 32 + 2 * (o - 1)) = hw;
-        }
+        gather_l2<8, unsigned short>(
+            NT * nb * 17, [&](int i) { return (const unsigned short *)src + i; },
+            [&](int i, unsigned short hw) {
+                const int blk = i / 17, o = i - blk * 17;
+                if (o == 0) d[blk] = h2f(hw);
+                else *(uint16_t *)(q + (size_t)blk * 32 + 2 * (o - 1)) = hw;
+            });
         xs.q = q;
         xs.pk = nullptr;
         xs.d = d;
@@ -272,16 +272,17 @@ M27B_DI XStage stage_x(const QmvArgs &a, uint8_t *smem) {
         float *d = (float *)(smem + (size_t)NT * a.k + (size_t)NT * nb * 32);
         const uint8_t *src = (const uint8_t *)a.xq;  // 292-byte blocks
         const int total = NT * nb * 65;                // d + 64 code words per block
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            const int blk = i / 65, o = i - blk * 65;
-            const uint32_t w = ((const uint32_t *)(src + (size_t)blk * 292))[o];
-            if (o == 0) d[blk] = __uint_as_float(w);
-            else ((uint32_t *)q)[(size_t)blk * 64 + (o - 1)] = w;
-        }
+        gather_l2<8, unsigned>(
+            total, [&](int i) { return (const unsigned *)(src + (size_t)(i / 65) * 292) + (i % 65); },
+            [&](int i, unsigned w) {
+                const int blk = i / 65, o = i - blk * 65;
+                if (o == 0) d[blk] = __uint_as_float(w);
+                else ((uint32_t *)q)[(size_t)blk * 64 + (o - 1)] = w;
+            });
         for (int i = threadIdx.x; i < NT * nb * 8; i += blockDim.x) {
             const int blk = i >> 3, c = i & 7, lo = T::bsum_lo(c);
             const int16_t *bs = (const int16_t *)(src + (size_t)blk * 292 + 260);
-            pk[i] = (uint32_t)(uint16_t)bs[lo] | ((uint32_t)(uint16_t)bs[lo + T::BSUM_GAP] << 16);
+            pk[i] = (uint32_t)(uint16_t)__ldcg(bs + lo) | ((uint32_t)(uint16_t)__ldcg(bs + lo + T::BSUM_GAP) << 16);
         }
         xs.q = q;
         xs.pk = pk;

@@ -13,7 +13,12 @@ size_t qmv_smem_bytes(int wtype, int k, int ntok);
 
 // Tensor map over weight rows viewed as [rows][row_bytes/4] uint32 with a box
 // of box_rows rows x box_u32 words (one TMA copy per (row group, tile)).
-bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows, int box_u32, int box_rows = 8);
+// 2-D map over rows of uint32 words, box of box_u32 words x box_rows rows;
+// swizzle 0 (none) or 32 / 64 / 128: the shared-memory swizzle span in bytes
+// (16-byte chunk c of row r lands at chunk c ^ (r mod span / 16) for the
+// 128-byte pattern; the box row must fit in the span).
+bool encode_rows_u32(CUtensorMap *tm, const void *w, size_t row_bytes, int rows, int box_u32, int box_rows = 8,
+                     int swizzle = 0);
 
 template <int WT, int NT, int EPI, int PS>
 cudaError_t run_qmv(const QmvArgs &a, int sm_count, cudaStream_t st) {

@@ -42,7 +42,7 @@
 // pairs.  Every wait is bounded (2 s); a timeout records status 5 and raises
 // the CTA's abort flag, every role leaves its loop, the issuing thread waits
 // (bounded) for its own copies and MMAs, and the CTA frees its TMEM.
-#include "qmv_blk.cuh"
+#include "tc05.cuh"
 #include "m27b_launch.cuh"
 #include "qmv_launch.cuh"
 
@@ -56,35 +56,26 @@ constexpr int MMA_PRODUCER = MMA_ISSUER + 1;                    // warp 13: TMA 
 constexpr int MMA_ISSUER2 = MMA_PRODUCER + 1;                   // warp 14: MMAs of second half-blocks
 constexpr int MMA_THREADS = (MMA_ISSUER2 + 1) * 32;
 constexpr int MMA_RAW_BYTES = MMA_ROWS * 144;    // one TMA box: 128 rows x one q4_K block
-constexpr int MMA_NA = 2;                        // A buffers: one per half-block position (= issuing warp)
-constexpr size_t MMA_SMEM_LIMIT = 227 * 1024;
-// TMEM per CTA: D = 2 blocks x 8 sub-blocks x NB columns, then the two A
-// buffers of 32 columns.  NB = 16: 320 columns -> all 512, and every CTA
-// asks for more than half of an SM's shared memory (MMA_SMEM_MIN), so no two
-// CTAs of this kernel (of one launch, or of two launches that programmatic
-// dependent launch overlaps) are ever resident on one SM — tcgen05.alloc has
-// no bounded form.  NB = 8: 192 columns -> 256, two CTAs per SM (each with at
-// most MMA_SMEM_PAIR and at least MMA_SMEM_PAIR_MIN of shared memory, so a
-// third never fits): their allocations add up to the SM's 512 columns.
+constexpr int MMA_NA = 4;                        // A buffers: the half-blocks of two blocks
+// TMEM per CTA: D = 2 blocks x 8 sub-blocks x NB columns, then the four A
+// buffers of 32 columns.  NB = 16: 384 columns -> all 512, and every CTA
+// asks for more shared memory (MMA_SMEM_MIN) than an SM has beside one CTA
+// of MMA_SMEM_PAIR_MIN, so no other CTA of a tensor-core matvec (of one
+// launch, or of two launches that programmatic dependent launch overlaps) is
+// ever resident beside it — tcgen05.alloc has no bounded form.  NB = 8: 256
+// columns, two CTAs per SM (each with at most MMA_SMEM_PAIR and at least
+// MMA_SMEM_PAIR_MIN of shared memory, so a third never fits): their
+// allocations add up to the SM's 512 columns.
 template <int NB> constexpr int mma_dbuf() { return 8 * NB; }                 // columns per block buffer
 template <int NB> constexpr int mma_acol() { return 2 * mma_dbuf<NB>(); }     // first A column
-template <int NB> constexpr int mma_tcols() { return mma_acol<NB>() + 2 * 32 <= 256 ? 256 : 512; }
+template <int NB> constexpr int mma_tcols() { return mma_acol<NB>() + MMA_NA * 32 <= 256 ? 256 : 512; }
 template <int NB> constexpr int mma_ctas_per_sm() { return mma_tcols<NB>() == 256 ? 2 : 1; }
-constexpr size_t MMA_SMEM_MIN = 116 * 1024;
-constexpr size_t MMA_SMEM_PAIR = 112 * 1024;
-constexpr size_t MMA_SMEM_PAIR_MIN = 80 * 1024;
 
 // K split across CTAs (verify pass): ks ranges of rb / ks blocks per 128-row
 // tile; unit u = tile * ks + range; the ranges' partial sums go to
 // part[((tile * ks + range) * NB + token) * 128 + row] and the epilogue warp
 // that arrives last at count[tile * 8 + epilogue warp] adds its 32-row slice
 // over the ranges in range order (ks = 1: no scratch, rows written directly).
-struct MmaSplit {
-    float *part;
-    unsigned *count;
-    int ks;
-};
-
 struct MmaLayout {
     size_t b, dx, bs, raw, bar, flag, total;
     int stages;
@@ -121,98 +112,6 @@ inline int mma_stages(int rb, int nb_tok, bool pair = false) {
     return 0;
 }
 
-// ---- tcgen05 helpers ----
-M27B_DI void tmem_alloc(uint32_t *slot, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
-                 : "memory");
-}
-M27B_DI void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
-M27B_DI void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-M27B_DI void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-M27B_DI void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// D[tmem] (+)= A[tmem] * B[smem desc]^T, s8 x s8 -> s32, one thread.
-M27B_DI void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
-        : "memory");
-}
-// The MMAs issued so far by this thread arrive on `bar` when they complete.
-M27B_DI void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-// Eight consecutive 32-bit TMEM columns of this thread's lane.
-M27B_DI void tmem_ld8(uint32_t taddr, int (&v)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                 : "r"(taddr)
-                 : "memory");
-}
-// Four consecutive 32-bit TMEM columns of this thread's lane.
-M27B_DI void tmem_ld4(uint32_t taddr, int (&v)[4]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-                 : "r"(taddr)
-                 : "memory");
-}
-M27B_DI void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// Eight consecutive 32-bit TMEM columns of this thread's lane.
-M27B_DI void tmem_st8(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, uint32_t v4, uint32_t v5,
-                      uint32_t v6, uint32_t v7) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(v0),
-                 "r"(v1), "r"(v2), "r"(v3), "r"(v4), "r"(v5), "r"(v6), "r"(v7)
-                 : "memory");
-}
-M27B_DI void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major, no swizzle, core matrices of
-// 8 rows x 16 bytes; 128 bytes between the two 16-byte K halves of a 32-byte
-// K slice (leading offset), 256 bytes between 8-row groups (stride offset).
-M27B_DI uint64_t umma_desc(uint32_t saddr) {
-    return (uint64_t)((saddr & 0x3ffffu) >> 4) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
-           ((uint64_t)1 << 46);
-}
-
-// Instruction descriptor: D s32, A s8 (the planes are 0..105), B s8, both
-// K-major, M = 128, N = NB.
-template <int NB>
-constexpr uint32_t umma_idesc_i8() {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(MMA_ROWS >> 4) << 24);
-}
-
-M27B_DI void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Bounded wait that gives up at once when the CTA's abort flag is raised, and
-// raises it (recording status 5) when its own 2 s run out.
-M27B_DI bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort, int *status) {
-    if (*abort) return false;
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = global_ns();
-    for (;;) {
-        for (int i = 0; i < 8; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (*abort) return false;
-        if (global_ns() - t0 > M27B_WAIT_NS) {
-            *abort = 1;
-            if (status) atomicCAS(status, 0, 5);
-            return false;
-        }
-    }
-}
-
-// The same wait for a whole worker warp: every lane leaves with one answer,
-// so a warp never runs its .sync.aligned TMEM accesses with lanes missing.
-M27B_DI bool warp_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort, int *status) {
-    return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort, status)) != 0;
-}
 
 template <int NB>
 __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
@@ -288,49 +187,34 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
     if (warp == MMA_PRODUCER && lane == 0)
         for (; issued < stages && issued < nblk; ++issued) issue_block(issued);
 
-    // activations: codes into the UMMA layout (tokens >= n_tok are zero),
-    // block scales and sub-block bsum pairs
+    // activations, record by record (73 words: d, 64 code words, 8 words of
+    // two sub-block sums each): the block scale to dxs, the codes into the
+    // UMMA layout (code word wi, in 16-byte chunk ch = wi / 4, goes to K
+    // slice ch / 2, half ch % 2 of the token's 8-token core matrix), the
+    // sums of sub-block pairs (2m, 2m + 1) to halfword m of bss; tokens
+    // >= n_tok are zero
     pdl_wait();
-    {
-        const uint8_t *xq = (const uint8_t *)a.xq;
-        const int nchunk = NB * rb * 16;  // 16-byte chunks of codes
-        for (int c = tid; c < nchunk; c += MMA_THREADS) {
-            const int t = c / (rb * 16), rem = c - t * rb * 16, blk = rem >> 4, ch = rem & 15;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (t < n_tok) {
-                const uint32_t *src = (const uint32_t *)(xq + ((size_t)t * rb + blk) * 292 + 4 + 16 * ch);
-                v = make_uint4(src[0], src[1], src[2], src[3]);
+    gather_records<NB == 8 ? 9 : 8>(
+        n_tok, NB, rb, [&](int t, int blk) { return (const unsigned *)a.xq + ((size_t)t * rb + blk) * Q8K_WORDS; },
+        [&](int t, int blk, int o, unsigned v) {
+            if (o == 0) {
+                dxs[t * rb + blk] = __uint_as_float(v);
+            } else if (o <= 64) {
+                const int wi = o - 1, ch = wi >> 2;
+                ((uint32_t *)(bsm + ((size_t)(blk * 8 + (ch >> 1)) * (NB / 8) + (t >> 3)) * 256 + (ch & 1) * 128 +
+                              (t & 7) * 16))[wi & 3] = v;
+            } else {
+                ((int16_t *)&bss[t * rb + blk])[o - 65] = (int16_t)(s16_lo(v) + s16_hi(v));
             }
-            const int s = ch >> 1, j = ch & 1;
-            *(uint4 *)(bsm + ((size_t)(blk * 8 + s) * (NB / 8) + (t >> 3)) * 256 + j * 128 + (t & 7) * 16) = v;
-        }
-        for (int c = tid; c < NB * rb; c += MMA_THREADS) {
-            const int t = c / rb, blk = c - t * rb;
-            float d = 0.0f;
-            int4 p = make_int4(0, 0, 0, 0);
-            if (t < n_tok) {
-                const uint8_t *sb = xq + ((size_t)t * rb + blk) * 292;
-                d = *(const float *)sb;
-                const int16_t *bs = (const int16_t *)(sb + 260);
-                int w[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int lo = bs[4 * q] + bs[4 * q + 1], hi = bs[4 * q + 2] + bs[4 * q + 3];
-                    w[q] = (lo & 0xffff) | (hi << 16);
-                }
-                p = make_int4(w[0], w[1], w[2], w[3]);
-            }
-            dxs[c] = d;
-            bss[c] = p;
-        }
-    }
+        });
     pdl_trigger();
     fence_proxy_async();  // the codes are read by the tensor cores (async proxy)
     __syncthreads();
 
     if (warp == MMA_ISSUER || warp == MMA_ISSUER2) {
         if (lane == 0) {
-            // half-block q of every block: A buffer q, sub-blocks 4q .. 4q+3
+            // half-block q of every block (sub-blocks 4q .. 4q+3); half-block
+            // j = 2 bi + q sits in A buffer j % MMA_NA
             const int q = warp == MMA_ISSUER ? 0 : 1;
             constexpr uint32_t idesc = umma_idesc_i8<NB>();
             const uint32_t b_base = smem_u32(bsm);
@@ -338,16 +222,17 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
                 const int db = bi & 1;
                 // the block's MMAs overwrite accumulators whose epilogue (block bi - 2) is done
                 if (bi >= 2 && !wait_or_abort(&d_free[db], (uint32_t)(((bi - 2) >> 1) & 1), abort, a.status)) break;
-                if (!wait_or_abort(&a_full[q], (uint32_t)(bi & 1), abort, a.status)) break;
+                const int j = 2 * bi + q, ab = j % MMA_NA;
+                if (!wait_or_abort(&a_full[ab], (uint32_t)((j / MMA_NA) & 1), abort, a.status)) break;
                 tc_fence_after();
                 const int k = k_of(bi);
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
                     const uint64_t bd = umma_desc(b_base + (uint32_t)((k * 8 + 4 * q + s) * NB * 32));
                     umma_i8_ts(tmem + (uint32_t)(db * DBUF + (4 * q + s) * NB),
-                               tmem + (uint32_t)(ACOL + q * 32 + s * 8), bd, idesc, 0u);
+                               tmem + (uint32_t)(ACOL + ab * 32 + s * 8), bd, idesc, 0u);
                 }
-                umma_commit(&mma_done[q]);
+                umma_commit(&mma_done[ab]);
                 umma_commit(&blk_done[db]);  // with the other warp's commit: the block's accumulators are final
             }
             // drain: every MMA issued above (bounded, even after an abort)

@@ -49,8 +49,18 @@ struct StreamArgs {
 // The warp (of Wt) whose run holds item i of T: runs are [w*T/Wt, (w+1)*T/Wt).
 M27B_DI int q6s_warp_of(long long i, long long T, long long Wt) { return (int)(((i + 1) * Wt - 1) / T); }
 
+// EPI_STORE: y[row] = sum (+ residual); EPI_PUSH: the same value as an
+// epoch-tagged word into every rank's receive window (the fused all-reduce).
+template <int EPI>
 __global__ void __launch_bounds__(Q6S_MAX_WARPS * 32, 1)
     k_qmv_q6k_stream(const QmvArgs a, const __grid_constant__ CUtensorMap tm, const StreamArgs sa) {
+    auto out = [&](int row, float v) {
+        const float r = a.residual ? v + a.residual[row] : v;
+        if constexpr (EPI == EPI_PUSH)
+            push_row(a.push, (size_t)row, r);
+        else
+            a.y[row] = r;
+    };
     extern __shared__ __align__(128) uint8_t q6s_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int qd = lane >> 3, c = lane & 7;
@@ -183,7 +193,7 @@ __global__ void __launch_bounds__(Q6S_MAX_WARPS * 32, 1)
         const int w_last = aligned ? a_first + a_n - 1 : q6s_warp_of(g_end - 1, T, Wt);
         if (w_first == w_last) {
             // the whole group lies in this run
-            if (lane < 8 && row < a.rows) a.y[row] = a.residual ? fin + a.residual[row] : fin;
+            if (lane < 8 && row < a.rows) out(row, fin);
             continue;
         }
         const int n = w_last - w_first + 1;
@@ -201,7 +211,7 @@ __global__ void __launch_bounds__(Q6S_MAX_WARPS * 32, 1)
             if (lane < 8 && row < a.rows) {
                 float v = 0.0f;
                 for (int k = 0; k < n; ++k) v += __ldcg(gp + k * 8 + lane);
-                a.y[row] = a.residual ? v + a.residual[row] : v;
+                out(row, v);
             }
         }
     }
@@ -223,7 +233,8 @@ size_t q6k_stream_count_words(int rows) { return (size_t)(rows + 7) / 8; }
 // staged activation row leaves room for Q6S_MIN_WARPS warps).
 bool q6k_stream_applies(int k) { return q6s_warps(k) >= Q6S_MIN_WARPS; }
 
-cudaError_t launch_q6k_stream(const QmvArgs &a, float *part, unsigned *count, int sm_count, cudaStream_t st) {
+template <int EPI>
+static cudaError_t launch_stream_epi(const QmvArgs &a, float *part, unsigned *count, int sm_count, cudaStream_t st) {
     const int nw = q6s_warps(a.k);
     if (nw < Q6S_MIN_WARPS || !part || !count) return cudaErrorInvalidValue;
     const size_t smem = q6s_smem_for(nw, a.k);
@@ -232,14 +243,22 @@ cudaError_t launch_q6k_stream(const QmvArgs &a, float *part, unsigned *count, in
     if (e != cudaSuccess) return e;
     static size_t opted[64] = {0};
     if (dev >= 64 || smem > opted[dev]) {
-        e = cudaFuncSetAttribute(k_qmv_q6k_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaFuncSetAttribute(k_qmv_q6k_stream<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         if (dev < 64) opted[dev] = smem;
     }
     CUtensorMap tm;
     if (!encode_rows_u32(&tm, a.w0, a.row_stride, a.rows, Q6T_TILE / 4)) return cudaErrorInvalidValue;
     const StreamArgs sa{part, count};
-    return launch_pdl(k_qmv_q6k_stream, dim3(sm_count), dim3(nw * 32), smem, st, a, tm, sa);
+    return launch_pdl(k_qmv_q6k_stream<EPI>, dim3(sm_count), dim3(nw * 32), smem, st, a, tm, sa);
+}
+
+// epi: EPI_STORE or EPI_PUSH (a.push set).
+cudaError_t launch_q6k_stream(const QmvArgs &a, float *part, unsigned *count, int sm_count, cudaStream_t st,
+                              int epi) {
+    if (epi == EPI_PUSH) return launch_stream_epi<EPI_PUSH>(a, part, count, sm_count, st);
+    if (epi == EPI_STORE) return launch_stream_epi<EPI_STORE>(a, part, count, sm_count, st);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace m27b

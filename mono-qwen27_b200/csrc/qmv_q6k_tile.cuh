@@ -71,26 +71,32 @@ M27B_DI void stage_x_q6t(const QmvArgs &a, uint8_t *xrec, float *xd) {
     const uint8_t *src = (const uint8_t *)a.xq;  // NT*nb blocks of 292 bytes
     // codes: 64 words per block; word w of chunk c (lo/hi) comes from element
     // e_lo(c) (+64 for hi) + 4w
-#pragma unroll 8
-    for (int i = threadIdx.x; i < NT * nb * 64; i += blockDim.x) {
-        const int blk = i >> 6, r = i & 63;
-        const int hi = r >> 5, c = (r >> 2) & 7, w = r & 3;
-        const int e = 128 * (c >> 2) + 32 * ((c >> 1) & 1) + 16 * (c & 1) + 64 * hi + 4 * w;
-        const uint32_t v = __ldcg((const unsigned *)(src + (size_t)blk * 292 + 4 + e));
-        ((uint32_t *)(xrec + (size_t)blk * Q6T_XREC))[hi * 32 + c * 4 + w] = v;
-    }
-    for (int i = threadIdx.x; i < NT * nb * 9; i += blockDim.x) {
-        const int blk = i / 9, j = i - blk * 9;
-        const uint8_t *sb = src + (size_t)blk * 292;
-        if (j < 8) {
-            const int16_t *bs = (const int16_t *)(sb + 260);
-            const int g = 8 * (j >> 2) + 2 * ((j >> 1) & 1) + (j & 1);  // 16-value group of chunk j's low half
-            ((uint32_t *)(xrec + (size_t)blk * Q6T_XREC + 256))[j] =
-                (uint32_t)(uint16_t)__ldcg(bs + g) | ((uint32_t)(uint16_t)__ldcg(bs + g + 4) << 16);
-        } else {
-            xd[blk] = __ldcg((const float *)sb);
-        }
-    }
+    // a record is 73 words: d, 64 code words, 8 words of two bsums each.
+    // Code element e = 4 (o - 1) goes to word hi * 32 + c * 4 + w of the
+    // staged record, where e = 128 (c / 4) + 32 ((c / 2) % 2) + 16 (c % 2)
+    // + 64 hi + 4 w; pack word j holds the sums of 16-value groups
+    // g(j) = 8 (j / 4) + 2 ((j / 2) % 2) + j % 2 (low half) and g(j) + 4.
+    gather_l2<8, unsigned>(NT * nb * Q8K_WORDS, [&](int i) { return (const unsigned *)src + i; },
+                           [&](int i, unsigned v) {
+                               const int blk = i / Q8K_WORDS, o = i - blk * Q8K_WORDS;
+                               uint8_t *rec = xrec + (size_t)blk * Q6T_XREC;
+                               if (o == 0) {
+                                   xd[blk] = __uint_as_float(v);
+                               } else if (o <= 64) {
+                                   const int e = 4 * (o - 1), hi = (e >> 6) & 1, w = (e >> 2) & 3;
+                                   const int c = 4 * (e >> 7) + 2 * ((e >> 5) & 1) + ((e >> 4) & 1);
+                                   ((uint32_t *)rec)[hi * 32 + c * 4 + w] = v;
+                               } else {
+                                   uint16_t *pk = (uint16_t *)(rec + 256);
+#pragma unroll
+                                   for (int h = 0; h < 2; ++h) {
+                                       const int b = 2 * (o - 65) + h;          // bsum index 0..15
+                                       const int hb = (b >> 2) & 1, g = b - 4 * hb;  // high half of g's word?
+                                       const int j = g < 4 ? g : g - 4;
+                                       pk[2 * j + hb] = (uint16_t)(h ? (v >> 16) : v);
+                                   }
+                               }
+                           });
 }
 
 // The same records built from fp32 activations (the fused quantize + matvec

@@ -68,6 +68,10 @@ def lib():
         "m27b_qmv_mma_split_part_bytes": (sz, [wvp, i32]),
         "m27b_qmv_mma_split_count_bytes": (sz, [wvp]),
         "m27b_qmv_mma_split": (b, [wvp, vp, i32, vp, i32, vp, vp, vp, vp, cp, sz]),
+        "m27b_qmv_q6k_mma_part_bytes": (sz, [wvp]),
+        "m27b_qmv_q6k_mma_count_bytes": (sz, [wvp]),
+        "m27b_qmv_q6k_mma": (b, [wvp, vp, i32, vp, i32, vp, vp, vp, vp, cp, sz]),
+        "m27b_qmv_q6k_mma_argmax": (b, [wvp, vp, i32, vp, i32, vp, u32, vp, cp, sz]),
         "m27b_qmv_q6k_stream_part_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_stream_count_bytes": (sz, [wvp]),
         "m27b_qmv_q6k_stream": (b, [wvp, vp, vp, vp, vp, vp, vp, cp, sz]),
@@ -236,6 +240,34 @@ def qmv_mma_split(w, xq, n_tok, y, residual=None, part=None, count=None, stream=
                                 ldy if ldy is not None else w.view.row_count, _ptr(residual), _ptr(part), _ptr(count),
                                 _stream(stream), err, ERR_CAP), err, "m27b_qmv_mma_split")
     return y
+
+
+def qmv_q6k_mma(w, xq, n_tok, y, residual=None, part=None, count=None, stream=None, ldy=None, split=True):
+    """q6_K x n_tok (1..8) tokens on the tensor cores (m27b_qmv_q6k_mma); with
+    split, K-split scratch is allocated here (counters zeroed) unless given."""
+    import torch
+    L = lib()
+    if split and part is None:
+        part = torch.empty(max(16, L.m27b_qmv_q6k_mma_part_bytes(ctypes.byref(w.view))), dtype=torch.uint8,
+                           device="cuda")
+    if split and count is None:
+        count = torch.zeros(max(16, L.m27b_qmv_q6k_mma_count_bytes(ctypes.byref(w.view))), dtype=torch.uint8,
+                            device="cuda")
+    err = ctypes.create_string_buffer(ERR_CAP)
+    _check(L.m27b_qmv_q6k_mma(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(y),
+                              ldy if ldy is not None else w.view.row_count, _ptr(residual), _ptr(part), _ptr(count),
+                              _stream(stream), err, ERR_CAP), err, "m27b_qmv_q6k_mma")
+    return y
+
+
+def qmv_q6k_mma_argmax(w, xq, n_tok, best, logits=None, row_offset=0, stream=None, ldl=None):
+    """q6_K x n_tok (1..8) tokens on the tensor cores with the argmax epilogue
+    (m27b_qmv_q6k_mma_argmax)."""
+    err = ctypes.create_string_buffer(ERR_CAP)
+    ldl = ldl if ldl is not None else w.rows
+    _check(lib().m27b_qmv_q6k_mma_argmax(ctypes.byref(w.view), _ptr(xq), n_tok, _ptr(logits), ldl, _ptr(best),
+                                         row_offset, _stream(stream), err, ERR_CAP), err, "m27b_qmv_q6k_mma_argmax")
+    return best
 
 
 def qmv_q6k_stream(w, xq, y, residual=None, part=None, count=None, stream=None):
