@@ -896,12 +896,16 @@ def main():
     # default stream)
     run_st = torch.cuda.Stream()
 
-    def run_steps(fn, n):
+    def ensure_graphs(fn, n):
         full, rem = divmod(n, GRAPH_STEPS)
         if full and (fn, GRAPH_STEPS) not in graphs:
             graphs[(fn, GRAPH_STEPS)] = capture(fn, GRAPH_STEPS)
         if rem and (fn, rem) not in graphs:
             graphs[(fn, rem)] = capture(fn, rem)
+
+    def run_steps(fn, n):
+        ensure_graphs(fn, n)
+        full, rem = divmod(n, GRAPH_STEPS)
         with torch.cuda.stream(run_st):
             for _ in range(full):
                 graphs[(fn, GRAPH_STEPS)].replay()
@@ -909,6 +913,7 @@ def main():
                 graphs[(fn, rem)].replay()
 
     def timed(fn, steps, warmup, sampler=None):
+        ensure_graphs(fn, steps)  # no capture inside the timed region
         run_steps(fn, warmup)
         torch.cuda.synchronize()
         barrier()

@@ -23,13 +23,13 @@
 // Pipeline per CTA (one 128-row tile at a time, persistent over tiles, one
 // CTA per SM), warp-specialized and synchronised only by mbarriers:
 //   * warp 13 streams the weights: one TMA copy of a raw 128-row x 144-byte
-//     block column per stage (2-D tensor map, no multicast), refilling a
-//     stage once every reader has handed it back;
+//     block column per stage (2-D tensor map, no multicast; up to 10 stages
+//     in flight), refilling a stage once every reader has handed it back;
 //   * warps 12 and 14 issue the MMAs, one per half-block of every block
-//     (4 sub-blocks: 4 MMAs plus two commits) — nothing else, since the
-//     issuing threads' instruction rate bounds the whole pipeline;
-//   * warps 0-3 unpack: thread r (TMEM lane r) writes row r's half-block
-//     into one of two TMEM A buffers;
+//     (4 sub-blocks: 4 MMAs plus two commits);
+//   * warps 0-3 unpack: thread r (TMEM lane r) writes row r's block into
+//     two of eight TMEM A buffers (one per half-block), a block per
+//     tcgen05.wait::st;
 //   * warps 4-11 run the epilogue, concurrently with the unpacking of the
 //     next block: two warps per TMEM lane quarter, each for half of the
 //     tokens (tcgen05.ld of the block's 8 accumulators, one row per thread);
@@ -37,9 +37,9 @@
 //     read the nibbles and the epilogue warps the block header), A buffer
 //     full -> half-block MMAs done (the buffer is free again), block MMAs
 //     done (its accumulators are final) -> accumulators free (epilogue read).
-// The activations (all K, all tokens) are staged once per CTA in the
-// canonical K-major no-swizzle UMMA layout, with their scales and bsum
-// pairs.  Every wait is bounded (2 s); a timeout records status 5 and raises
+// The activations of the CTA's K range (all tokens) are staged once per CTA
+// in the canonical K-major no-swizzle UMMA layout, with their scales and
+// bsum pairs.  Every wait is bounded (2 s); a timeout records status 5 and raises
 // the CTA's abort flag, every role leaves its loop, the issuing thread waits
 // (bounded) for its own copies and MMAs, and the CTA frees its TMEM.
 #include "tc05.cuh"
@@ -55,24 +55,33 @@ constexpr int MMA_ISSUER = MMA_UNPACK_WARPS + MMA_EPI_WARPS;  // warp 12: MMAs o
 constexpr int MMA_PRODUCER = MMA_ISSUER + 1;                    // warp 13: TMA weight copies
 constexpr int MMA_ISSUER2 = MMA_PRODUCER + 1;                   // warp 14: MMAs of second half-blocks
 constexpr int MMA_THREADS = (MMA_ISSUER2 + 1) * 32;
-constexpr int MMA_RAW_BYTES = MMA_ROWS * 144;    // one TMA box: 128 rows x one q4_K block
-constexpr int MMA_NA = 4;                        // A buffers: the half-blocks of two blocks
-// TMEM per CTA: D = 2 blocks x 8 sub-blocks x NB columns, then the four A
-// buffers of 32 columns.  NB = 16: 384 columns -> all 512, and every CTA
-// asks for more shared memory (MMA_SMEM_MIN) than an SM has beside one CTA
-// of MMA_SMEM_PAIR_MIN, so no other CTA of a tensor-core matvec (of one
-// launch, or of two launches that programmatic dependent launch overlaps) is
-// ever resident beside it — tcgen05.alloc has no bounded form.  NB = 8: 256
-// columns, two CTAs per SM (each with at most MMA_SMEM_PAIR and at least
-// MMA_SMEM_PAIR_MIN of shared memory, so a third never fits): their
-// allocations add up to the SM's 512 columns.
+// One stage = one TMA box: 128 rows x MMA_SB consecutive q4_K blocks (432
+// bytes per row).  Rows of several blocks cut the number of row requests the
+// TMA unit issues per byte (a 144-byte row per request bounded the stream),
+// and the 432-byte row stride (108 words, 12 mod 32) puts the 8 rows a
+// quarter-warp reads on distinct banks.
+constexpr int MMA_SB = 3;
+constexpr int MMA_RS = 144 * MMA_SB;               // bytes per row in a stage
+constexpr int MMA_RAW_BYTES = MMA_ROWS * MMA_RS;
+constexpr int MMA_NA = 8;                        // A buffers: the half-blocks of four blocks
+constexpr int MMA_MAX_STAGES = 10;
+constexpr int MMA_MAX_KS = 8;
+constexpr uint32_t MMA_TCOLS = 512;
+// TMEM per CTA: D = 2 blocks x 8 sub-blocks x NB columns, then the eight A
+// buffers of 32 columns (384 of the 512 columns at NB = 8, all 512 at 16).
+// One CTA per SM: every CTA asks for at least MMA_SMEM_MIN of shared memory,
+// more than an SM has beside any other tensor-core CTA (of one launch, or of
+// two launches that programmatic dependent launch overlaps), so its
+// tcgen05.alloc of all columns never contends — the instruction has no
+// bounded form.
 template <int NB> constexpr int mma_dbuf() { return 8 * NB; }                 // columns per block buffer
 template <int NB> constexpr int mma_acol() { return 2 * mma_dbuf<NB>(); }     // first A column
-template <int NB> constexpr int mma_tcols() { return mma_acol<NB>() + MMA_NA * 32 <= 256 ? 256 : 512; }
-template <int NB> constexpr int mma_ctas_per_sm() { return mma_tcols<NB>() == 256 ? 2 : 1; }
+static_assert(mma_acol<16>() + MMA_NA * 32 <= (int)MMA_TCOLS, "TMEM plan");
 
-// K split across CTAs (verify pass): ks ranges of rb / ks blocks per 128-row
-// tile; unit u = tile * ks + range; the ranges' partial sums go to
+// K split across CTAs (verify pass, few row tiles): ks ranges of blocks per
+// 128-row tile, unit u = tile * ks + range, the grid a multiple of ks so that
+// all units of a CTA lie in one range and the CTA stages only that range's
+// activations; the ranges' partial sums go to
 // part[((tile * ks + range) * NB + token) * 128 + row] and the epilogue warp
 // that arrives last at count[tile * 8 + epilogue warp] adds its 32-row slice
 // over the ranges in range order (ks = 1: no scratch, rows written directly).
@@ -81,7 +90,8 @@ struct MmaLayout {
     int stages;
 };
 
-// Shared memory plan for K = 256 * rb values and an MMA N of nb_tok (8 or 16).
+// Shared memory plan for nbmax blocks of staged activations (a K range) and
+// an MMA N of nb_tok (8 or 16).
 __host__ __device__ inline MmaLayout mma_layout(int rb, int nb_tok, int stages) {
     MmaLayout L;
     size_t off = 0;
@@ -103,26 +113,25 @@ __host__ __device__ inline MmaLayout mma_layout(int rb, int nb_tok, int stages) 
     return L;
 }
 
-// Most stages (up to 4) that fit the CTA's shared-memory budget (pair: two
-// CTAs per SM); 0 if not even two do.
-inline int mma_stages(int rb, int nb_tok, bool pair = false) {
-    const size_t lim = pair ? MMA_SMEM_PAIR : MMA_SMEM_LIMIT;
-    for (int s = 4; s >= 2; --s)
-        if (mma_layout(rb, nb_tok, s).total + 1024 <= lim) return s;
+// Most stages (up to MMA_MAX_STAGES) that fit beside nbmax blocks of
+// activations; 0 if not even two do.
+inline int mma_stages(int nbmax, int nb_tok) {
+    for (int s = MMA_MAX_STAGES; s >= 2; --s)
+        if (mma_layout(nbmax, nb_tok, s).total + 1024 <= MMA_SMEM_LIMIT) return s;
     return 0;
 }
 
 
 template <int NB>
-__global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
-    k_qmv_q4k_mma(const QmvArgs a, const __grid_constant__ CUtensorMap tm, int n_tok, int stages, uint32_t tcols,
+__global__ void __launch_bounds__(MMA_THREADS, 1)
+    k_qmv_q4k_mma(const QmvArgs a, const __grid_constant__ CUtensorMap tm, int n_tok, int stages, int nbmax,
                   const MmaSplit sp) {
     constexpr int DBUF = mma_dbuf<NB>(), ACOL = mma_acol<NB>();
     extern __shared__ __align__(1024) uint8_t mma_smem[];
     uint8_t *smem = mma_smem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rb = a.rb;
-    const MmaLayout L = mma_layout(rb, NB, stages);
+    const MmaLayout L = mma_layout(nbmax, NB, stages);
     uint8_t *bsm = smem + L.b;
     float *dxs = (float *)(smem + L.dx);
     int4 *bss = (int4 *)(smem + L.bs);
@@ -137,16 +146,18 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
     volatile int *abort = (volatile int *)(smem + L.flag);
     uint32_t *tslot = (uint32_t *)(smem + L.flag + 8);
 
-    // units (tile, K range) of this CTA: u = blockIdx.x + i * gridDim.x,
-    // tile u / ks, blocks [range * bpu, (range + 1) * bpu) of its rows
-    const int ks = sp.ks, bpu = rb / ks;
+    // units of this CTA: u = blockIdx.x + i * gridDim.x, tile u / ks, range
+    // u % ks = blockIdx.x % ks (gridDim.x is a multiple of ks): blocks
+    // [k0, k0 + nbr) of the tile's rows
+    const int ks = sp.ks, range = (int)blockIdx.x % ks;
+    const int k0 = range * rb / ks, nbr = (range + 1) * rb / ks - k0;
     const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS, nunits = ntiles * ks;
     const int my_units = (int)blockIdx.x < nunits ? (nunits - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int nblk = my_units * bpu;  // block items of this CTA
-    const int J = 2 * nblk;           // half-block items
-    // block item bi -> unit, tile, range and block index k within the row
-    auto unit_of = [&](int bi) { return (int)blockIdx.x + (bi / bpu) * (int)gridDim.x; };
-    auto k_of = [&](int bi) { return (unit_of(bi) % ks) * bpu + bi % bpu; };
+    const int nblk = my_units * nbr;  // block items of this CTA
+    const int ng = (nbr + MMA_SB - 1) / MMA_SB, nitem = my_units * ng;  // stage items: MMA_SB blocks of a unit
+    auto tile_of = [&](int bi) { return ((int)blockIdx.x + (bi / nbr) * (int)gridDim.x) / ks; };
+    auto item_of = [&](int bi) { return (bi / nbr) * ng + (bi % nbr) / MMA_SB; };
+    auto item_last = [&](int bi) { const int kl = bi % nbr; return kl % MMA_SB == MMA_SB - 1 || kl == nbr - 1; };
 
     if (tid == 0) {
         for (int s = 0; s < stages; ++s) {
@@ -166,7 +177,7 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
         fence_mbar_init();
     }
     if (warp == 0) {
-        tmem_alloc(tslot, tcols);
+        tmem_alloc(tslot, MMA_TCOLS);
         tmem_relinquish();
     }
     __syncthreads();
@@ -175,37 +186,29 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
 
     // the readers' generic loads of a stage are ordered before its refill by
     // the empty barrier (arrive-release, wait-acquire) that the producer waits on
-    auto issue_block = [&](int bi) {
-        const int k = k_of(bi);
-        const int row0 = (unit_of(bi) / ks) * MMA_ROWS;
-        uint64_t *b = &full[bi % stages];
+    // item it: blocks k0 + MMA_SB g .. of unit it / ng, g = it % ng (a box
+    // reaching past the range reads blocks no one uses; past the row, zeros)
+    auto issue_item = [&](int it) {
+        const int k = k0 + (it % ng) * MMA_SB;
+        const int row0 = (((int)blockIdx.x + (it / ng) * (int)gridDim.x) / ks) * MMA_ROWS;
+        uint64_t *b = &full[it % stages];
         mbar_arrive_expect_tx(b, MMA_RAW_BYTES);
-        tma_load_2d(raw + (size_t)(bi % stages) * MMA_RAW_BYTES, &tm, k * 36, row0, b);
+        tma_load_2d(raw + (size_t)(it % stages) * MMA_RAW_BYTES, &tm, k * 36, row0, b);
     };
     // the first raw block columns go out at once: weights do not depend on the previous kernel
     int issued = 0;
     if (warp == MMA_PRODUCER && lane == 0)
-        for (; issued < stages && issued < nblk; ++issued) issue_block(issued);
+        for (; issued < stages && issued < nitem; ++issued) issue_item(issued);
 
-    // activations, record by record (73 words: d, 64 code words, 8 words of
-    // two sub-block sums each): the block scale to dxs, the codes into the
-    // UMMA layout (code word wi, in 16-byte chunk ch = wi / 4, goes to K
-    // slice ch / 2, half ch % 2 of the token's 8-token core matrix), the
-    // sums of sub-block pairs (2m, 2m + 1) to halfword m of bss; tokens
-    // >= n_tok are zero
+    // activations of this CTA's range: the codes into the UMMA layout, the
+    // block scales to dxs, the sums of sub-block pairs (2m, 2m + 1) to
+    // halfword m of bss; tokens >= n_tok zero
     pdl_wait();
-    gather_records<NB == 8 ? 9 : 8>(
-        n_tok, NB, rb, [&](int t, int blk) { return (const unsigned *)a.xq + ((size_t)t * rb + blk) * Q8K_WORDS; },
-        [&](int t, int blk, int o, unsigned v) {
-            if (o == 0) {
-                dxs[t * rb + blk] = __uint_as_float(v);
-            } else if (o <= 64) {
-                const int wi = o - 1, ch = wi >> 2;
-                ((uint32_t *)(bsm + ((size_t)(blk * 8 + (ch >> 1)) * (NB / 8) + (t >> 3)) * 256 + (ch & 1) * 128 +
-                              (t & 7) * 16))[wi & 3] = v;
-            } else {
-                ((int16_t *)&bss[t * rb + blk])[o - 65] = (int16_t)(s16_lo(v) + s16_hi(v));
-            }
+    gather_tiles<2, NB>(
+        n_tok, nbr, bsm, [&](int t, int kl) { return (const unsigned *)a.xq + ((size_t)t * rb + k0 + kl) * Q8K_WORDS; },
+        [&](int t, int kl, unsigned v) { dxs[t * nbmax + kl] = __uint_as_float(v); },
+        [&](int t, int kl, int m, unsigned v) {
+            ((int16_t *)&bss[t * nbmax + kl])[m] = (int16_t)(s16_lo(v) + s16_hi(v));
         });
     pdl_trigger();
     fence_proxy_async();  // the codes are read by the tensor cores (async proxy)
@@ -225,10 +228,10 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
                 const int j = 2 * bi + q, ab = j % MMA_NA;
                 if (!wait_or_abort(&a_full[ab], (uint32_t)((j / MMA_NA) & 1), abort, a.status)) break;
                 tc_fence_after();
-                const int k = k_of(bi);
+                const int kl = bi % nbr;
 #pragma unroll
                 for (int s = 0; s < 4; ++s) {
-                    const uint64_t bd = umma_desc(b_base + (uint32_t)((k * 8 + 4 * q + s) * NB * 32));
+                    const uint64_t bd = umma_desc(b_base + (uint32_t)((kl * 8 + 4 * q + s) * NB * 32));
                     umma_i8_ts(tmem + (uint32_t)(db * DBUF + (4 * q + s) * NB),
                                tmem + (uint32_t)(ACOL + ab * 32 + s * 8), bd, idesc, 0u);
                 }
@@ -244,50 +247,61 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
         if (lane == 0) {
             // block bi goes into the stage block bi - stages used, once every
             // unpacking and epilogue warp has handed that one back
-            for (; issued < nblk; ++issued) {
-                const int bi = issued;
-                if (!wait_or_abort(&empty[bi % stages], (uint32_t)((bi / stages - 1) & 1), abort, a.status)) break;
-                issue_block(bi);
+            for (; issued < nitem; ++issued) {
+                const int it = issued;
+                if (!wait_or_abort(&empty[it % stages], (uint32_t)((it / stages - 1) & 1), abort, a.status)) break;
+                issue_item(it);
             }
             // every copy still in flight lands before the CTA's shared memory is released (bounded)
-            for (int bi = issued - stages < 0 ? 0 : issued - stages; bi < issued; ++bi)
-                mbar_wait_bounded(&full[bi % stages], (uint32_t)((bi / stages) & 1), a.status, 5);
+            for (int it = issued - stages < 0 ? 0 : issued - stages; it < issued; ++it)
+                mbar_wait_bounded(&full[it % stages], (uint32_t)((it / stages) & 1), a.status, 5);
         }
         __syncwarp();
     } else if (warp < MMA_UNPACK_WARPS) {
         // A operand: thread r = TMEM lane r = row r of the tile
         const int r = tid;
         const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-        for (int j = 0; j < J; ++j) {
-            const int bi = j >> 1, q = j & 1, ab = j % MMA_NA;
-            if (q == 0 && !warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status))
+        // a whole block per pass (both half-blocks into their A buffers): one
+        // tcgen05.wait::st per block, whose latency bounded the per-half loop
+        for (int bi = 0; bi < nblk; ++bi) {
+            const int j0 = 2 * bi, ab0 = j0 % MMA_NA, ab1 = (j0 + 1) % MMA_NA, it = item_of(bi);
+            if ((bi % nbr) % MMA_SB == 0 &&
+                !warp_wait_or_abort(&full[it % stages], (uint32_t)((it / stages) & 1), abort, a.status))
                 break;
             // A buffer ab is free once the MMAs of half-block j - MMA_NA are done
-            if (j >= MMA_NA &&
-                !warp_wait_or_abort(&mma_done[ab], (uint32_t)(((j - MMA_NA) / MMA_NA) & 1), abort, a.status))
+            if (j0 >= MMA_NA &&
+                !warp_wait_or_abort(&mma_done[ab0], (uint32_t)(((j0 - MMA_NA) / MMA_NA) & 1), abort, a.status))
+                break;
+            if (j0 + 1 >= MMA_NA &&
+                !warp_wait_or_abort(&mma_done[ab1], (uint32_t)(((j0 + 1 - MMA_NA) / MMA_NA) & 1), abort, a.status))
                 break;
             tc_fence_after();
-            const uint8_t *rw = raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144;
-            const uint32_t acol = tmem + lane_base + (uint32_t)(ACOL + ab * 32);
+            const uint8_t *rw =
+                raw + (size_t)(it % stages) * MMA_RAW_BYTES + (size_t)r * MMA_RS + ((bi % nbr) % MMA_SB) * 144;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                // qs group g = 2q + h: low nibbles are sub-block 2g, high 2g+1,
-                // i.e. sub-blocks 2h and 2h + 1 of the half-block
-                const int g = 2 * q + h;
-                const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
-                tmem_st8(acol + 16 * h, qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu,
-                         qa.w & 0x0f0f0f0fu, qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu,
-                         qb.w & 0x0f0f0f0fu);
-                tmem_st8(acol + 16 * h + 8, (qa.x >> 4) & 0x0f0f0f0fu, (qa.y >> 4) & 0x0f0f0f0fu,
-                         (qa.z >> 4) & 0x0f0f0f0fu, (qa.w >> 4) & 0x0f0f0f0fu, (qb.x >> 4) & 0x0f0f0f0fu,
-                         (qb.y >> 4) & 0x0f0f0f0fu, (qb.z >> 4) & 0x0f0f0f0fu, (qb.w >> 4) & 0x0f0f0f0fu);
+            for (int q = 0; q < 2; ++q) {
+                const uint32_t acol = tmem + lane_base + (uint32_t)(ACOL + (q ? ab1 : ab0) * 32);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    // qs group g = 2q + h: low nibbles are sub-block 2g, high 2g+1,
+                    // i.e. sub-blocks 2h and 2h + 1 of half-block q
+                    const int g = 2 * q + h;
+                    const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
+                    tmem_st8(acol + 16 * h, qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu,
+                             qa.w & 0x0f0f0f0fu, qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu,
+                             qb.w & 0x0f0f0f0fu);
+                    tmem_st8(acol + 16 * h + 8, (qa.x >> 4) & 0x0f0f0f0fu, (qa.y >> 4) & 0x0f0f0f0fu,
+                             (qa.z >> 4) & 0x0f0f0f0fu, (qa.w >> 4) & 0x0f0f0f0fu, (qb.x >> 4) & 0x0f0f0f0fu,
+                             (qb.y >> 4) & 0x0f0f0f0fu, (qb.z >> 4) & 0x0f0f0f0fu, (qb.w >> 4) & 0x0f0f0f0fu);
+                }
             }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&a_full[ab]);
-                if (q == 1) mbar_arrive(&empty[bi % stages]);  // this warp is done with the raw stage
+                mbar_arrive(&a_full[ab0]);
+                mbar_arrive(&a_full[ab1]);
+                if (item_last(bi)) mbar_arrive(&empty[it % stages]);  // this warp is done with the stage
             }
         }
     } else {
@@ -302,12 +316,16 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
 #pragma unroll
         for (int i = 0; i < TPT; ++i) acc[i] = 0.0f;
         for (int bi = 0; bi < nblk; ++bi) {
-            const int u = unit_of(bi), k = k_of(bi);
+            const int kl = bi % nbr;
             // the block header of row r (scales, mins), read before the stage is handed back
-            if (!warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) break;
-            const uint4 hd = *(const uint4 *)(raw + (size_t)(bi % stages) * MMA_RAW_BYTES + (size_t)r * 144);
+            const int it = item_of(bi);
+            if (kl % MMA_SB == 0 &&
+                !warp_wait_or_abort(&full[it % stages], (uint32_t)((it / stages) & 1), abort, a.status))
+                break;
+            const uint4 hd = *(const uint4 *)(raw + (size_t)(it % stages) * MMA_RAW_BYTES + (size_t)r * MMA_RS +
+                                              (kl % MMA_SB) * 144);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[bi % stages]);
+            if (lane == 0 && item_last(bi)) mbar_arrive(&empty[it % stages]);
             const float dw = h2f(hd.x), dmw = h2f(hd.x >> 16);
             const uint32_t sc03 = hd.y & 0x3f3f3f3fu, mn03 = hd.z & 0x3f3f3f3fu;
             const uint32_t sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
@@ -335,17 +353,17 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
                     isum += sc * v[s][i];
                 }
                 const int t = toff + i;
-                const int4 bs = bss[t * rb + k];
+                const int4 bs = bss[t * nbmax + kl];
                 int msum = __dp2a_lo(bs.x, (int)mn03, 0);
                 msum = __dp2a_hi(bs.y, (int)mn03, msum);
                 msum = __dp2a_lo(bs.z, (int)mn47, msum);
                 msum = __dp2a_hi(bs.w, (int)mn47, msum);
-                const float dx = dxs[t * rb + k];
+                const float dx = dxs[t * nbmax + kl];
                 acc[i] = fmaf(dw * dx, (float)isum, acc[i]);
                 acc[i] = fmaf(-(dmw * dx), (float)msum, acc[i]);
             }
-            if (bi % bpu == bpu - 1) {  // the unit's last block
-                const int tile = u / ks, range = u % ks;
+            if (kl == nbr - 1) {  // the unit's last block
+                const int tile = tile_of(bi);
                 const int row = tile * MMA_ROWS + r;
                 bool write = true;
                 if (ks > 1) {
@@ -393,26 +411,18 @@ __global__ void __launch_bounds__(MMA_THREADS, mma_ctas_per_sm<NB>())
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, tcols);
+        tmem_dealloc(tmem, MMA_TCOLS);
     }
 }
 
-// K ranges per tile: the most (a divisor of rb, at most 8) that keep one
-// unit per CTA slot; 1 without scratch.
-static int mma_ks(int ntiles, int rb, int slots) {
+// K ranges per tile: 1 when the tiles fill the SMs, else the most (at most
+// MMA_MAX_KS, ranges of at least 2 blocks) that keep one unit per SM.
+static int mma_ks(int ntiles, int rb, int sm_count) {
+    if (ntiles >= sm_count) return 1;
     int best = 1;
-    for (int k = 2; k <= 8; ++k)
-        if (rb % k == 0 && rb / k >= 2 && ntiles * k <= slots) best = k;
+    for (int k = 2; k <= MMA_MAX_KS; ++k)
+        if (rb / k >= 2 && ntiles * k <= sm_count) best = k;
     return best;
-}
-
-// Whether NB-token tiles run two CTAs per SM (256 TMEM columns each) for rows
-// of rb blocks, and with how many stages.
-template <int NB>
-static bool mma_pair(int rb, int *stages) {
-    const int ps = NB == 8 ? mma_stages(rb, NB, true) : 0;
-    *stages = ps > 0 ? ps : mma_stages(rb, NB);
-    return ps > 0;
 }
 
 // 1: launched; 0: shape not supported by this kernel (caller falls back).
@@ -420,10 +430,12 @@ template <int NB>
 static cudaError_t run_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream_t st, bool *launched, float *part,
                            unsigned *count) {
     *launched = false;
-    int stages = 0;
-    const bool pair = mma_pair<NB>(a.rb, &stages);
+    const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS;
+    const int ks = part && count ? mma_ks(ntiles, a.rb, sm_count) : 1;
+    const int nbmax = (a.rb + ks - 1) / ks;
+    const int stages = mma_stages(nbmax, NB);
     if (stages == 0) return cudaSuccess;
-    const MmaLayout L = mma_layout(a.rb, NB, stages);
+    const MmaLayout L = mma_layout(nbmax, NB, stages);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -434,19 +446,17 @@ static cudaError_t run_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream
         if (dev < 64) opted[dev] = true;
     }
     CUtensorMap tm;
-    if (!encode_rows_u32(&tm, a.w0, a.row_stride, a.rows, 36, MMA_ROWS)) return cudaErrorInvalidValue;
-    const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS;
-    const int slots = sm_count * (pair ? 2 : 1);
-    const int ks = part && count ? mma_ks(ntiles, a.rb, slots) : 1;
+    if (!encode_rows_u32(&tm, a.w0, a.row_stride, a.rows, 36 * MMA_SB, MMA_ROWS)) return cudaErrorInvalidValue;
     const int units = ntiles * ks;
-    const int grid = units < slots ? units : slots;
-    const size_t smem = pair ? (L.total > MMA_SMEM_PAIR_MIN ? L.total : MMA_SMEM_PAIR_MIN)
-                             : (L.total > MMA_SMEM_MIN ? L.total : MMA_SMEM_MIN);
+    const int grid = ks > 1 ? units : (units < sm_count ? units : sm_count);
+    const size_t smem = L.total > MMA_SMEM_MIN ? L.total : MMA_SMEM_MIN;
     *launched = true;
-    return launch_pdl(k_qmv_q4k_mma<NB>, dim3(grid), dim3(MMA_THREADS), smem, st, a, tm, n_tok, stages,
-                      (uint32_t)(pair ? 256 : 512), MmaSplit{part, count, ks});
+    return launch_pdl(k_qmv_q4k_mma<NB>, dim3(grid), dim3(MMA_THREADS), smem, st, a, tm, n_tok, stages, nbmax,
+                      MmaSplit{part, count, ks});
 }
 
+// Whether 5..16 tokens over rows of rb blocks are served without a K split
+// (the whole row's activations and two stages fit).
 bool q4k_mma_supported(int rb, int n_tok) {
     return n_tok >= 5 && n_tok <= 16 && mma_stages(rb, n_tok <= 8 ? 8 : 16) > 0;
 }
@@ -454,11 +464,9 @@ bool q4k_mma_supported(int rb, int n_tok) {
 // Scratch of the K-split tensor-core path for `rows` x rb q4_K and n_tok
 // tokens (an upper bound: the split the launch picks never needs more).
 size_t q4k_mma_split_part_floats(int rows, int rb, int n_tok) {
+    (void)rb;
     const int NB = n_tok <= 8 ? 8 : 16, ntiles = (rows + MMA_ROWS - 1) / MMA_ROWS;
-    int k = 1;
-    for (int c = 2; c <= 8; ++c)
-        if (rb % c == 0 && rb / c >= 2) k = c;
-    return (size_t)ntiles * k * NB * MMA_ROWS;
+    return (size_t)ntiles * MMA_MAX_KS * NB * MMA_ROWS;
 }
 size_t q4k_mma_split_count_words(int rows) { return (size_t)((rows + MMA_ROWS - 1) / MMA_ROWS) * 8; }
 

@@ -210,25 +210,13 @@ __global__ void __launch_bounds__(Q6M_THREADS, 1)
         tmem_wait_st();
     }
 
-    // activations of this CTA's range, record by record (73 words: d, 64 code
-    // words, 8 words of two bsums): the block scale to dxs, the codes into the
-    // UMMA layout (code word wi, in 16-byte chunk ch = wi / 4, to K slice
-    // ch / 2, half ch % 2 of the token's 8-token core matrix), the bsum words
-    // as they are; tokens >= n_tok are zero
+    // activations of this CTA's range: the codes into the UMMA layout, the
+    // block scales to dxs, the bsum words as they are; tokens >= n_tok zero
     pdl_wait();
-    gather_records<13>(
-        n_tok, NB, nbr, [&](int t, int kl) { return (const unsigned *)a.xq + ((size_t)t * rb + k0 + kl) * Q8K_WORDS; },
-        [&](int t, int kl, int o, unsigned v) {
-            if (o == 0) {
-                dxs[t * nbmax + kl] = __uint_as_float(v);
-            } else if (o <= 64) {
-                const int wi = o - 1, ch = wi >> 2;
-                ((uint32_t *)(bsm + ((size_t)(kl * 8 + (ch >> 1)) * (NB / 8) + (t >> 3)) * 256 + (ch & 1) * 128 +
-                              (t & 7) * 16))[wi & 3] = v;
-            } else {
-                bss[(t * nbmax + kl) * 8 + (o - 65)] = v;
-            }
-        });
+    gather_tiles<2, NB>(
+        n_tok, nbr, bsm, [&](int t, int kl) { return (const unsigned *)a.xq + ((size_t)t * rb + k0 + kl) * Q8K_WORDS; },
+        [&](int t, int kl, unsigned v) { dxs[t * nbmax + kl] = __uint_as_float(v); },
+        [&](int t, int kl, int m, unsigned v) { bss[(t * nbmax + kl) * 8 + m] = v; });
     pdl_trigger();
     fence_proxy_async();  // the codes are read by the tensor cores (async proxy)
     tc_fence_before();
@@ -280,38 +268,47 @@ __global__ void __launch_bounds__(Q6M_THREADS, 1)
         const int r = tid;
         const uint32_t lb = (uint32_t)(32 * warp) << 16;
         const int sw_ql = r & 7, sw_qh = (r >> 1) & 3;  // swizzle of row r's 16-byte chunks
-        for (int j = 0; j < J; ++j) {
-            const int bi = j >> 1, q = j & 1, ab = j % Q6M_NA;
-            if (q == 0 && !warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status))
+        // a whole block per pass (both half-blocks into their A buffers): one
+        // tcgen05.wait::st per block
+        for (int bi = 0; bi < nblk; ++bi) {
+            const int j0 = 2 * bi, ab0 = j0 % Q6M_NA, ab1 = (j0 + 1) % Q6M_NA;
+            if (!warp_wait_or_abort(&full[bi % stages], (uint32_t)((bi / stages) & 1), abort, a.status)) break;
+            if (j0 >= Q6M_NA &&
+                !warp_wait_or_abort(&mma_done[ab0], (uint32_t)(((j0 - Q6M_NA) / Q6M_NA) & 1), abort, a.status))
                 break;
-            if (j >= Q6M_NA &&
-                !warp_wait_or_abort(&mma_done[ab], (uint32_t)(((j - Q6M_NA) / Q6M_NA) & 1), abort, a.status))
+            if (j0 + 1 >= Q6M_NA &&
+                !warp_wait_or_abort(&mma_done[ab1], (uint32_t)(((j0 + 1 - Q6M_NA) / Q6M_NA) & 1), abort, a.status))
                 break;
             tc_fence_after();
             const uint8_t *st = raw + (size_t)(bi % stages) * Q6M_RAW;
             const uint8_t *qlr = st + Q6M_QL + r * 128, *qhr = st + Q6M_QH + r * 64;
-            // half q: ql bytes 64q .. 64q + 63 (chunks 4q .. 4q + 3), qh bytes 32q .. 32q + 31
-            uint4 l[4], h[2];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) l[c] = *(const uint4 *)(qlr + 16 * ((4 * q + c) ^ sw_ql));
+            for (int q = 0; q < 2; ++q) {
+                // half q: ql bytes 64q .. 64q + 63 (chunks 4q .. 4q + 3), qh bytes 32q .. 32q + 31
+                uint4 l[4], h[2];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) h[c] = *(const uint4 *)(qhr + 16 * ((2 * q + c) ^ sw_qh));
-            const uint32_t acol = tmem + lb + (uint32_t)(Q6M_ACOL + ab * 64);
+                for (int c = 0; c < 4; ++c) l[c] = *(const uint4 *)(qlr + 16 * ((4 * q + c) ^ sw_ql));
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                // values 32 m + [0, 16) of the half: ql bytes [0, 16) (or [32, 48)), qh bytes [0, 16)
-                const uint4 a0 = l[0], a1 = l[1], b0 = l[2], b1 = l[3];
-                tmem_st4(acol + 16 * m, q6_code_word(a0.x, b0.x, h[0].x, m), q6_code_word(a0.y, b0.y, h[0].y, m),
-                         q6_code_word(a0.z, b0.z, h[0].z, m), q6_code_word(a0.w, b0.w, h[0].w, m));
-                tmem_st4(acol + 16 * m + 12, q6_code_word(a1.x, b1.x, h[1].x, m), q6_code_word(a1.y, b1.y, h[1].y, m),
-                         q6_code_word(a1.z, b1.z, h[1].z, m), q6_code_word(a1.w, b1.w, h[1].w, m));
+                for (int c = 0; c < 2; ++c) h[c] = *(const uint4 *)(qhr + 16 * ((2 * q + c) ^ sw_qh));
+                const uint32_t acol = tmem + lb + (uint32_t)(Q6M_ACOL + (q ? ab1 : ab0) * 64);
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    // values 32 m + [0, 16) of the half: ql bytes [0, 16) (or [32, 48)), qh bytes [0, 16)
+                    const uint4 a0 = l[0], a1 = l[1], b0 = l[2], b1 = l[3];
+                    tmem_st4(acol + 16 * m, q6_code_word(a0.x, b0.x, h[0].x, m), q6_code_word(a0.y, b0.y, h[0].y, m),
+                             q6_code_word(a0.z, b0.z, h[0].z, m), q6_code_word(a0.w, b0.w, h[0].w, m));
+                    tmem_st4(acol + 16 * m + 12, q6_code_word(a1.x, b1.x, h[1].x, m),
+                             q6_code_word(a1.y, b1.y, h[1].y, m), q6_code_word(a1.z, b1.z, h[1].z, m),
+                             q6_code_word(a1.w, b1.w, h[1].w, m));
+                }
             }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&a_full[ab]);
-                if (q == 1) mbar_arrive(&empty[bi % stages]);  // this warp is done with the stage
+                mbar_arrive(&a_full[ab0]);
+                mbar_arrive(&a_full[ab1]);
+                mbar_arrive(&empty[bi % stages]);  // this warp is done with the stage
             }
         }
     } else {

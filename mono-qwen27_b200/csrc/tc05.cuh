@@ -12,14 +12,12 @@ namespace m27b {
 // TMEM residency.  tcgen05.alloc has no bounded form, so the CTAs of the
 // tensor-core matvecs that can be resident on one SM at once (of one launch,
 // or of launches that programmatic dependent launch overlaps) never ask for
-// more than the SM's 512 columns together.  Shared memory enforces it: a CTA
-// of 512 columns asks for at least MMA_SMEM_MIN, more than an SM has beside
-// any other such CTA; a CTA of 256 columns asks for MMA_SMEM_PAIR_MIN ..
-// MMA_SMEM_PAIR, so at most two fit.
+// more than the SM's 512 columns together.  Shared memory enforces it: every
+// such CTA allocates all 512 columns and asks for at least MMA_SMEM_MIN of
+// shared memory, more than half of what an SM has, so no two are resident
+// on one SM.
 constexpr size_t MMA_SMEM_LIMIT = 227 * 1024;
-constexpr size_t MMA_SMEM_MIN = 148 * 1024;
-constexpr size_t MMA_SMEM_PAIR = 112 * 1024;
-constexpr size_t MMA_SMEM_PAIR_MIN = 80 * 1024;
+constexpr size_t MMA_SMEM_MIN = 116 * 1024;
 
 // ---- tcgen05 helpers ----
 M27B_DI void tmem_alloc(uint32_t *slot, uint32_t ncols) {
@@ -114,46 +112,48 @@ M27B_DI bool warp_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *ab
     return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort, status)) != 0;
 }
 
-// The tokens' q8_K records of a tensor-core matvec's K range, a warp per
-// record: record rec = t * nb + kl (token t < n_tok, local block kl < nb) is
-// read from src(t, kl) (73 words, through L2) and word o of it handed to
-// put(t, kl, o, value); lane l takes words l, l + 32 and l + 64 (l < 9).  A
-// warp issues the loads of R records before any store, and the address
-// arithmetic is per record, not per word.  Records of tokens n_tok .. NB-1
-// are put as zeros.
-template <int R, class Src, class Put>
-M27B_DI void gather_records(int n_tok, int NB, int nb, Src src, Put put) {
+// The tokens' q8_K activations of a tensor-core matvec's K range (nb blocks)
+// into shared memory: the codes into the canonical K-major no-swizzle UMMA
+// layout of B (`bsm`: per block and 32-value slice s, NB / 8 core-matrix
+// groups of 8 tokens x 2 K halves x 16 bytes), the block scale and the
+// bsum words through the callbacks.  A warp task is (block kl, group of 8
+// tokens): lane l takes token 8 g + l / 4 and word l % 4 of each 16-byte code
+// chunk, so a store instruction covers 8 tokens x 16 bytes = 128 consecutive
+// bytes (no bank conflict); its loads (16 chunk words, the scale on lanes
+// l % 4 == 0, bsum words 65 + l % 4 and 69 + l % 4) all go out before its
+// stores, R tasks at a time.  Tokens n_tok .. NB-1 are zero.  src(t, kl)
+// points at token t's record of block kl (73 words: d, 64 code words, 8
+// words of two bsums each), read through L2.
+template <int R, int NB, class Src, class PutD, class PutBs>
+M27B_DI void gather_tiles(int n_tok, int nb, uint8_t *bsm, Src src, PutD put_d, PutBs put_bs) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int nrec = n_tok * nb;
-    for (int r0 = warp; r0 < nrec; r0 += R * nw) {
-        unsigned v[R][3];
+    const int tl = lane >> 2, w = lane & 3;
+    const int ntask = nb * (NB / 8);
+    for (int k0 = warp; k0 < ntask; k0 += R * nw) {
+        uint32_t v[R][16], dv[R], b0[R], b1[R];
 #pragma unroll
-        for (int j = 0; j < R; ++j) {
-            const int rec = r0 + j * nw;
-            if (rec < nrec) {
-                const int t = rec / nb;
-                const unsigned *p = src(t, rec - t * nb);
-                v[j][0] = __ldcg(p + lane);
-                v[j][1] = __ldcg(p + 32 + lane);
-                v[j][2] = lane < Q8K_WORDS - 64 ? __ldcg(p + 64 + lane) : 0u;
-            }
+        for (int r = 0; r < R; ++r) {
+            const int task = k0 + r * nw, kl = task / (NB / 8), t = (task % (NB / 8)) * 8 + tl;
+            const bool on = task < ntask && t < n_tok;
+            const unsigned *p = on ? src(t, kl) : nullptr;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) v[r][c] = on ? __ldcg(p + 1 + 4 * c + w) : 0u;
+            dv[r] = on && w == 0 ? __ldcg(p) : 0u;
+            b0[r] = on ? __ldcg(p + 65 + w) : 0u;
+            b1[r] = on ? __ldcg(p + 69 + w) : 0u;
         }
 #pragma unroll
-        for (int j = 0; j < R; ++j) {
-            const int rec = r0 + j * nw;
-            if (rec < nrec) {
-                const int t = rec / nb, kl = rec - t * nb;
-                put(t, kl, lane, v[j][0]);
-                put(t, kl, 32 + lane, v[j][1]);
-                if (lane < Q8K_WORDS - 64) put(t, kl, 64 + lane, v[j][2]);
-            }
+        for (int r = 0; r < R; ++r) {
+            const int task = k0 + r * nw, kl = task / (NB / 8), g = task % (NB / 8), t = g * 8 + tl;
+            if (task >= ntask) continue;
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+                *(uint32_t *)(bsm + ((size_t)(kl * 8 + (c >> 1)) * (NB / 8) + g) * 256 + (c & 1) * 128 + tl * 16 +
+                              w * 4) = v[r][c];
+            if (w == 0) put_d(t, kl, dv[r]);
+            put_bs(t, kl, w, b0[r]);
+            put_bs(t, kl, 4 + w, b1[r]);
         }
-    }
-    for (int rec = nrec + warp; rec < NB * nb; rec += nw) {
-        const int t = rec / nb, kl = rec - t * nb;
-        put(t, kl, lane, 0u);
-        put(t, kl, 32 + lane, 0u);
-        if (lane < Q8K_WORDS - 64) put(t, kl, 64 + lane, 0u);
     }
 }
 
