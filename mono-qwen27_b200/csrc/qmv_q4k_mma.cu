@@ -55,12 +55,12 @@ constexpr int MMA_ISSUER = MMA_UNPACK_WARPS + MMA_EPI_WARPS;  // warp 12: MMAs o
 constexpr int MMA_PRODUCER = MMA_ISSUER + 1;                    // warp 13: TMA weight copies
 constexpr int MMA_ISSUER2 = MMA_PRODUCER + 1;                   // warp 14: MMAs of second half-blocks
 constexpr int MMA_THREADS = (MMA_ISSUER2 + 1) * 32;
-// One stage = one TMA box: 128 rows x MMA_SB consecutive q4_K blocks (432
-// bytes per row).  Rows of several blocks cut the number of row requests the
-// TMA unit issues per byte (a 144-byte row per request bounded the stream),
-// and the 432-byte row stride (108 words, 12 mod 32) puts the 8 rows a
-// quarter-warp reads on distinct banks.
-constexpr int MMA_SB = 3;
+// One stage = one TMA box: 128 rows x MMA_SB consecutive q4_K blocks.  Row
+// strides of 144 and 432 bytes (36 and 108 words) both put the 8 rows a
+// quarter-warp reads on distinct banks; one-block stages (10 in flight)
+// measured faster than three-block ones (3 in flight): the per-block chain
+// of roles, not the copies, bounds the kernel.
+constexpr int MMA_SB = 1;
 constexpr int MMA_RS = 144 * MMA_SB;               // bytes per row in a stage
 constexpr int MMA_RAW_BYTES = MMA_ROWS * MMA_RS;
 constexpr int MMA_NA = 8;                        // A buffers: the half-blocks of four blocks
