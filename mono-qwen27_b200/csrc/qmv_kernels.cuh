@@ -175,16 +175,18 @@ struct WQ6KP {
         const int sc_hi = (int)(int8_t)((v[2].y >> sb) & 0xffu);
         const float dw = h2f(v[2].z);
         const uint4 ql = v[0], qh = v[1];
-        const int s_lo = 2 * rr, s_hi = 2 * rr + 4;
+        // qh bits 2rr, 2rr + 1 (low nibbles) and 2rr + 4, 2rr + 5 (high) to
+        // bits 4-5 of each byte with one shift inside the byte
+        const int sl = 4 - 2 * rr, sh = 2 * rr;
         uint4 lo, hi;
-        lo.x = (ql.x & 0x0f0f0f0fu) | (((qh.x >> s_lo) & 0x03030303u) << 4);
-        lo.y = (ql.y & 0x0f0f0f0fu) | (((qh.y >> s_lo) & 0x03030303u) << 4);
-        lo.z = (ql.z & 0x0f0f0f0fu) | (((qh.z >> s_lo) & 0x03030303u) << 4);
-        lo.w = (ql.w & 0x0f0f0f0fu) | (((qh.w >> s_lo) & 0x03030303u) << 4);
-        hi.x = ((ql.x >> 4) & 0x0f0f0f0fu) | (((qh.x >> s_hi) & 0x03030303u) << 4);
-        hi.y = ((ql.y >> 4) & 0x0f0f0f0fu) | (((qh.y >> s_hi) & 0x03030303u) << 4);
-        hi.z = ((ql.z >> 4) & 0x0f0f0f0fu) | (((qh.z >> s_hi) & 0x03030303u) << 4);
-        hi.w = ((ql.w >> 4) & 0x0f0f0f0fu) | (((qh.w >> s_hi) & 0x03030303u) << 4);
+        lo.x = (ql.x & 0x0f0f0f0fu) | ((qh.x << sl) & 0x30303030u);
+        lo.y = (ql.y & 0x0f0f0f0fu) | ((qh.y << sl) & 0x30303030u);
+        lo.z = (ql.z & 0x0f0f0f0fu) | ((qh.z << sl) & 0x30303030u);
+        lo.w = (ql.w & 0x0f0f0f0fu) | ((qh.w << sl) & 0x30303030u);
+        hi.x = ((ql.x >> 4) & 0x0f0f0f0fu) | ((qh.x >> sh) & 0x30303030u);
+        hi.y = ((ql.y >> 4) & 0x0f0f0f0fu) | ((qh.y >> sh) & 0x30303030u);
+        hi.z = ((ql.z >> 4) & 0x0f0f0f0fu) | ((qh.z >> sh) & 0x30303030u);
+        hi.w = ((ql.w >> 4) & 0x0f0f0f0fu) | ((qh.w >> sh) & 0x30303030u);
         const int e_lo = b * 256 + 128 * half + 32 * rr + 16 * lsub;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {

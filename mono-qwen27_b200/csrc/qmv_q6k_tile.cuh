@@ -157,7 +157,10 @@ template <int NT>
 M27B_DI void q6t_item_mac(const uint8_t *it, int qd, int c, int half, int rr, int lsub, const int4 (&xa)[NT],
                           const int4 (&xh)[NT], const int (&blo)[NT], const int (&bhi)[NT], const float (&dx)[NT],
                           float (&acc)[8][NT]) {
-    const int s_lo = 2 * rr, s_hi = 2 * rr + 4;
+    // the code's two high bits (qh bits 2rr, 2rr + 1 for the low nibbles,
+    // 2rr + 4, 2rr + 5 for the high ones) moved to bits 4-5 of each byte
+    // with one shift inside the byte: << (4 - 2rr), >> 2rr
+    const int sl = 4 - 2 * rr, sh = 2 * rr;
     const int sc_byte = 8 * half + 2 * rr + lsub;  // scale of the low chunk; the high one is +4
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
@@ -171,14 +174,14 @@ M27B_DI void q6t_item_mac(const uint8_t *it, int qd, int c, int half, int rr, in
         const int scl = (int)(int8_t)((sw_lo >> (8 * (sc_byte & 3))) & 0xffu);
         const int sch = (int)(int8_t)((sw_hi >> (8 * (sc_byte & 3))) & 0xffu);
         uint32_t lo[4], hi[4];
-        lo[0] = (ql.x & 0x0f0f0f0fu) | (((qh.x >> s_lo) & 0x03030303u) << 4);
-        lo[1] = (ql.y & 0x0f0f0f0fu) | (((qh.y >> s_lo) & 0x03030303u) << 4);
-        lo[2] = (ql.z & 0x0f0f0f0fu) | (((qh.z >> s_lo) & 0x03030303u) << 4);
-        lo[3] = (ql.w & 0x0f0f0f0fu) | (((qh.w >> s_lo) & 0x03030303u) << 4);
-        hi[0] = ((ql.x >> 4) & 0x0f0f0f0fu) | (((qh.x >> s_hi) & 0x03030303u) << 4);
-        hi[1] = ((ql.y >> 4) & 0x0f0f0f0fu) | (((qh.y >> s_hi) & 0x03030303u) << 4);
-        hi[2] = ((ql.z >> 4) & 0x0f0f0f0fu) | (((qh.z >> s_hi) & 0x03030303u) << 4);
-        hi[3] = ((ql.w >> 4) & 0x0f0f0f0fu) | (((qh.w >> s_hi) & 0x03030303u) << 4);
+        lo[0] = (ql.x & 0x0f0f0f0fu) | ((qh.x << sl) & 0x30303030u);
+        lo[1] = (ql.y & 0x0f0f0f0fu) | ((qh.y << sl) & 0x30303030u);
+        lo[2] = (ql.z & 0x0f0f0f0fu) | ((qh.z << sl) & 0x30303030u);
+        lo[3] = (ql.w & 0x0f0f0f0fu) | ((qh.w << sl) & 0x30303030u);
+        hi[0] = ((ql.x >> 4) & 0x0f0f0f0fu) | ((qh.x >> sh) & 0x30303030u);
+        hi[1] = ((ql.y >> 4) & 0x0f0f0f0fu) | ((qh.y >> sh) & 0x30303030u);
+        hi[2] = ((ql.z >> 4) & 0x0f0f0f0fu) | ((qh.z >> sh) & 0x30303030u);
+        hi[3] = ((ql.w >> 4) & 0x0f0f0f0fu) | ((qh.w >> sh) & 0x30303030u);
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             int dl = dp4a_us(lo[0], xa[t].x, 0);
