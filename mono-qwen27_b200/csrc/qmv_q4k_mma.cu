@@ -55,28 +55,28 @@ constexpr int MMA_ISSUER = MMA_UNPACK_WARPS + MMA_EPI_WARPS;  // warp 12: MMAs o
 constexpr int MMA_PRODUCER = MMA_ISSUER + 1;                    // warp 13: TMA weight copies
 constexpr int MMA_ISSUER2 = MMA_PRODUCER + 1;                   // warp 14: MMAs of second half-blocks
 constexpr int MMA_THREADS = (MMA_ISSUER2 + 1) * 32;
-// One stage = one TMA box: 128 rows x MMA_SB consecutive q4_K blocks.  Row
-// strides of 144 and 432 bytes (36 and 108 words) both put the 8 rows a
-// quarter-warp reads on distinct banks; one-block stages (10 in flight)
-// measured faster than three-block ones (3 in flight): the per-block chain
-// of roles, not the copies, bounds the kernel.
-constexpr int MMA_SB = 1;
-constexpr int MMA_RS = 144 * MMA_SB;               // bytes per row in a stage
-constexpr int MMA_RAW_BYTES = MMA_ROWS * MMA_RS;
-constexpr int MMA_NA = 8;                        // A buffers: the half-blocks of four blocks
 constexpr int MMA_MAX_STAGES = 10;
 constexpr int MMA_MAX_KS = 8;
 constexpr uint32_t MMA_TCOLS = 512;
-// TMEM per CTA: D = 2 blocks x 8 sub-blocks x NB columns, then the eight A
-// buffers of 32 columns (384 of the 512 columns at NB = 8, all 512 at 16).
-// One CTA per SM: every CTA asks for at least MMA_SMEM_MIN of shared memory,
-// more than an SM has beside any other tensor-core CTA (of one launch, or of
-// two launches that programmatic dependent launch overlaps), so its
-// tcgen05.alloc of all columns never contends — the instruction has no
-// bounded form.
-template <int NB> constexpr int mma_dbuf() { return 8 * NB; }                 // columns per block buffer
-template <int NB> constexpr int mma_acol() { return 2 * mma_dbuf<NB>(); }     // first A column
-static_assert(mma_acol<16>() + MMA_NA * 32 <= (int)MMA_TCOLS, "TMEM plan");
+// Work moves through the roles in items of PB consecutive blocks of a unit
+// (PB = 2 at 8 tokens, 1 at 16): one TMA stage (a 128-row box of PB blocks),
+// one unpack pass with one tcgen05.wait::st, one A-buffer hand-off, one MMA
+// commit, one accumulator hand-off per item — every mbarrier hand-off costs
+// ~0.2 us of wake-up latency, which bounded the one-block pipeline.
+// TMEM per CTA (all 512 columns): a ring of 2 accumulator items (PB blocks x
+// 8 sub-blocks x NB columns: 256 together) and a ring of NAI A items (2 PB
+// half-blocks of 32 columns each: 256 together).  One CTA per SM: every CTA
+// asks for at least MMA_SMEM_MIN of shared memory, more than an SM has beside
+// any other tensor-core CTA (of one launch, or of two launches that
+// programmatic dependent launch overlaps), so its tcgen05.alloc of all
+// columns never contends — the instruction has no bounded form.
+template <int NB> constexpr int mma_pb() { return NB == 8 ? 2 : 1; }
+template <int NB> constexpr int mma_ditem() { return mma_pb<NB>() * 8 * NB; }   // accumulator columns per item
+template <int NB> constexpr int mma_aitem() { return mma_pb<NB>() * 64; }       // A columns per item
+template <int NB> constexpr int mma_nai() { return 256 / mma_aitem<NB>(); }     // A ring slots
+constexpr int MMA_ACOL = 256;                                                    // first A column
+static_assert(2 * mma_ditem<8>() == MMA_ACOL && 2 * mma_ditem<16>() == MMA_ACOL, "TMEM plan");
+__host__ __device__ constexpr int mma_raw_bytes(int nb_tok) { return MMA_ROWS * 144 * (nb_tok <= 8 ? 2 : 1); }  // one stage
 
 // K split across CTAs (verify pass, few row tiles): ks ranges of blocks per
 // 128-row tile, unit u = tile * ks + range, the grid a multiple of ks so that
@@ -103,9 +103,9 @@ __host__ __device__ inline MmaLayout mma_layout(int rb, int nb_tok, int stages) 
     off += (size_t)nb_tok * rb * 16;                         // bsum pairs
     off = (off + 127) & ~(size_t)127;
     L.raw = off;
-    off += (size_t)stages * MMA_RAW_BYTES;
-    L.bar = off;  // full[stages], empty[stages], a_full[NA], mma_done[NA], blk_done[2], d_free[2], drain
-    off += (size_t)(2 * stages + 2 * MMA_NA + 5) * 8;
+    off += (size_t)stages * mma_raw_bytes(nb_tok);
+    L.bar = off;  // full[stages], empty[stages], a_full[NAI], idone[NAI], d_free[2], drain
+    off += (size_t)(2 * stages + 2 * 4 + 3) * 8;
     L.flag = off;  // abort flag, TMEM address slot
     off += 16;
     L.total = off;
@@ -126,7 +126,8 @@ template <int NB>
 __global__ void __launch_bounds__(MMA_THREADS, 1)
     k_qmv_q4k_mma(const QmvArgs a, const __grid_constant__ CUtensorMap tm, int n_tok, int stages, int nbmax,
                   const MmaSplit sp) {
-    constexpr int DBUF = mma_dbuf<NB>(), ACOL = mma_acol<NB>();
+    constexpr int PB = mma_pb<NB>(), DITEM = mma_ditem<NB>(), AITEM = mma_aitem<NB>(), NAI = mma_nai<NB>();
+    constexpr int RS = 144 * PB, RAW = MMA_ROWS * RS;  // stage row stride, stage bytes
     extern __shared__ __align__(1024) uint8_t mma_smem[];
     uint8_t *smem = mma_smem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -138,10 +139,9 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     uint8_t *raw = smem + L.raw;
     uint64_t *full = (uint64_t *)(smem + L.bar);
     uint64_t *empty = full + stages;
-    uint64_t *a_full = empty + stages;      // [MMA_NA]
-    uint64_t *mma_done = a_full + MMA_NA;   // [MMA_NA]: one half-block's MMAs
-    uint64_t *blk_done = mma_done + MMA_NA; // [2]: all MMAs of a block (accumulator buffer bi & 1)
-    uint64_t *d_free = blk_done + 2;        // [2]
+    uint64_t *a_full = empty + stages;   // [NAI]: an item's A operand written
+    uint64_t *idone = a_full + NAI;      // [NAI]: an item's MMAs complete (accumulators final, A slot free)
+    uint64_t *d_free = idone + NAI;      // [2]: an accumulator item read by the epilogue
     uint64_t *drain = d_free + 2;
     volatile int *abort = (volatile int *)(smem + L.flag);
     uint32_t *tslot = (uint32_t *)(smem + L.flag + 8);
@@ -153,25 +153,22 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
     const int k0 = range * rb / ks, nbr = (range + 1) * rb / ks - k0;
     const int ntiles = (a.rows + MMA_ROWS - 1) / MMA_ROWS, nunits = ntiles * ks;
     const int my_units = (int)blockIdx.x < nunits ? (nunits - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int nblk = my_units * nbr;  // block items of this CTA
-    const int ng = (nbr + MMA_SB - 1) / MMA_SB, nitem = my_units * ng;  // stage items: MMA_SB blocks of a unit
-    auto tile_of = [&](int bi) { return ((int)blockIdx.x + (bi / nbr) * (int)gridDim.x) / ks; };
-    auto item_of = [&](int bi) { return (bi / nbr) * ng + (bi % nbr) / MMA_SB; };
-    auto item_last = [&](int bi) { const int kl = bi % nbr; return kl % MMA_SB == MMA_SB - 1 || kl == nbr - 1; };
+    // items: PB consecutive blocks of a unit, ng per unit (the last may be short)
+    const int ng = (nbr + PB - 1) / PB, nitem = my_units * ng;
+    auto item_tile = [&](int it) { return ((int)blockIdx.x + (it / ng) * (int)gridDim.x) / ks; };
+    auto item_kl0 = [&](int it) { return (it % ng) * PB; };                         // first block in the range
+    auto item_nb = [&](int it) { const int k = nbr - item_kl0(it); return k < PB ? k : PB; };
 
     if (tid == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], MMA_UNPACK_WARPS + MMA_EPI_WARPS);
         }
-        for (int b = 0; b < MMA_NA; ++b) {
+        for (int b = 0; b < NAI; ++b) {
             mbar_init(&a_full[b], MMA_UNPACK_WARPS);
-            mbar_init(&mma_done[b], 1);
+            mbar_init(&idone[b], 1);  // one issuing thread per item
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&blk_done[b], 2);  // both issuing warps commit
-            mbar_init(&d_free[b], MMA_EPI_WARPS);
-        }
+        for (int b = 0; b < 2; ++b) mbar_init(&d_free[b], MMA_EPI_WARPS);
         mbar_init(drain, 2);
         *abort = 0;
         fence_mbar_init();
@@ -186,14 +183,12 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
 
     // the readers' generic loads of a stage are ordered before its refill by
     // the empty barrier (arrive-release, wait-acquire) that the producer waits on
-    // item it: blocks k0 + MMA_SB g .. of unit it / ng, g = it % ng (a box
-    // reaching past the range reads blocks no one uses; past the row, zeros)
+    // item it: blocks k0 + PB (it % ng) .. of unit it / ng (a box reaching
+    // past the range reads blocks no one uses; past the row, zeros)
     auto issue_item = [&](int it) {
-        const int k = k0 + (it % ng) * MMA_SB;
-        const int row0 = (((int)blockIdx.x + (it / ng) * (int)gridDim.x) / ks) * MMA_ROWS;
         uint64_t *b = &full[it % stages];
-        mbar_arrive_expect_tx(b, MMA_RAW_BYTES);
-        tma_load_2d(raw + (size_t)(it % stages) * MMA_RAW_BYTES, &tm, k * 36, row0, b);
+        mbar_arrive_expect_tx(b, RAW);
+        tma_load_2d(raw + (size_t)(it % stages) * RAW, &tm, (k0 + item_kl0(it)) * 36, item_tile(it) * MMA_ROWS, b);
     };
     // the first raw block columns go out at once: weights do not depend on the previous kernel
     int issued = 0;
@@ -216,27 +211,27 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
 
     if (warp == MMA_ISSUER || warp == MMA_ISSUER2) {
         if (lane == 0) {
-            // half-block q of every block (sub-blocks 4q .. 4q+3); half-block
-            // j = 2 bi + q sits in A buffer j % MMA_NA
-            const int q = warp == MMA_ISSUER ? 0 : 1;
+            // whole items, alternating between the two issuing threads: item
+            // it accumulates into accumulator item it & 1 from A slot it % NAI
+            const int w = warp == MMA_ISSUER ? 0 : 1;
             constexpr uint32_t idesc = umma_idesc_i8<NB>();
             const uint32_t b_base = smem_u32(bsm);
-            for (int bi = 0; bi < nblk; ++bi) {
-                const int db = bi & 1;
-                // the block's MMAs overwrite accumulators whose epilogue (block bi - 2) is done
-                if (bi >= 2 && !wait_or_abort(&d_free[db], (uint32_t)(((bi - 2) >> 1) & 1), abort, a.status)) break;
-                const int j = 2 * bi + q, ab = j % MMA_NA;
-                if (!wait_or_abort(&a_full[ab], (uint32_t)((j / MMA_NA) & 1), abort, a.status)) break;
+            for (int it = w; it < nitem; it += 2) {
+                const int ds = it & 1, as = it % NAI;
+                // the item's MMAs overwrite accumulators whose epilogue (item it - 2) is done
+                if (it >= 2 && !wait_or_abort(&d_free[ds], (uint32_t)(((it - 2) >> 1) & 1), abort, a.status)) break;
+                if (!wait_or_abort(&a_full[as], (uint32_t)((it / NAI) & 1), abort, a.status)) break;
                 tc_fence_after();
-                const int kl = bi % nbr;
+                const int kl0 = item_kl0(it), nb = item_nb(it);
+                for (int b = 0; b < nb; ++b)
 #pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const uint64_t bd = umma_desc(b_base + (uint32_t)((kl * 8 + 4 * q + s) * NB * 32));
-                    umma_i8_ts(tmem + (uint32_t)(db * DBUF + (4 * q + s) * NB),
-                               tmem + (uint32_t)(ACOL + ab * 32 + s * 8), bd, idesc, 0u);
-                }
-                umma_commit(&mma_done[ab]);
-                umma_commit(&blk_done[db]);  // with the other warp's commit: the block's accumulators are final
+                    for (int s8 = 0; s8 < 8; ++s8) {
+                        const uint64_t bd = umma_desc(b_base + (uint32_t)(((kl0 + b) * 8 + s8) * NB * 32));
+                        umma_i8_ts(tmem + (uint32_t)(ds * DITEM + (8 * b + s8) * NB),
+                                   tmem + (uint32_t)(MMA_ACOL + as * AITEM + (2 * b + (s8 >> 2)) * 32 + (s8 & 3) * 8),
+                                   bd, idesc, 0u);
+                    }
+                umma_commit(&idone[as]);
             }
             // drain: every MMA issued above (bounded, even after an abort)
             umma_commit(drain);
@@ -261,47 +256,41 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
         // A operand: thread r = TMEM lane r = row r of the tile
         const int r = tid;
         const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-        // a whole block per pass (both half-blocks into their A buffers): one
-        // tcgen05.wait::st per block, whose latency bounded the per-half loop
-        for (int bi = 0; bi < nblk; ++bi) {
-            const int j0 = 2 * bi, ab0 = j0 % MMA_NA, ab1 = (j0 + 1) % MMA_NA, it = item_of(bi);
-            if ((bi % nbr) % MMA_SB == 0 &&
-                !warp_wait_or_abort(&full[it % stages], (uint32_t)((it / stages) & 1), abort, a.status))
-                break;
-            // A buffer ab is free once the MMAs of half-block j - MMA_NA are done
-            if (j0 >= MMA_NA &&
-                !warp_wait_or_abort(&mma_done[ab0], (uint32_t)(((j0 - MMA_NA) / MMA_NA) & 1), abort, a.status))
-                break;
-            if (j0 + 1 >= MMA_NA &&
-                !warp_wait_or_abort(&mma_done[ab1], (uint32_t)(((j0 + 1 - MMA_NA) / MMA_NA) & 1), abort, a.status))
+        for (int it = 0; it < nitem; ++it) {
+            const int as = it % NAI;
+            if (!warp_wait_or_abort(&full[it % stages], (uint32_t)((it / stages) & 1), abort, a.status)) break;
+            // A slot as is free once the MMAs of item it - NAI are done
+            if (it >= NAI && !warp_wait_or_abort(&idone[as], (uint32_t)(((it - NAI) / NAI) & 1), abort, a.status))
                 break;
             tc_fence_after();
-            const uint8_t *rw =
-                raw + (size_t)(it % stages) * MMA_RAW_BYTES + (size_t)r * MMA_RS + ((bi % nbr) % MMA_SB) * 144;
+            const uint8_t *rw0 = raw + (size_t)(it % stages) * RAW + (size_t)r * RS;
+            const int nb = item_nb(it);
+            for (int b = 0; b < nb; ++b) {
+                const uint8_t *rw = rw0 + b * 144;
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const uint32_t acol = tmem + lane_base + (uint32_t)(ACOL + (q ? ab1 : ab0) * 32);
+                for (int q = 0; q < 2; ++q) {
+                    const uint32_t acol = tmem + lane_base + (uint32_t)(MMA_ACOL + as * AITEM + (2 * b + q) * 32);
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    // qs group g = 2q + h: low nibbles are sub-block 2g, high 2g+1,
-                    // i.e. sub-blocks 2h and 2h + 1 of half-block q
-                    const int g = 2 * q + h;
-                    const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
-                    tmem_st8(acol + 16 * h, qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu,
-                             qa.w & 0x0f0f0f0fu, qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu,
-                             qb.w & 0x0f0f0f0fu);
-                    tmem_st8(acol + 16 * h + 8, (qa.x >> 4) & 0x0f0f0f0fu, (qa.y >> 4) & 0x0f0f0f0fu,
-                             (qa.z >> 4) & 0x0f0f0f0fu, (qa.w >> 4) & 0x0f0f0f0fu, (qb.x >> 4) & 0x0f0f0f0fu,
-                             (qb.y >> 4) & 0x0f0f0f0fu, (qb.z >> 4) & 0x0f0f0f0fu, (qb.w >> 4) & 0x0f0f0f0fu);
+                    for (int h = 0; h < 2; ++h) {
+                        // qs group g = 2q + h: low nibbles are sub-block 2g, high 2g+1,
+                        // i.e. sub-blocks 2h and 2h + 1 of half-block q
+                        const int g = 2 * q + h;
+                        const uint4 qa = *(const uint4 *)(rw + 16 + 32 * g), qb = *(const uint4 *)(rw + 32 + 32 * g);
+                        tmem_st8(acol + 16 * h, qa.x & 0x0f0f0f0fu, qa.y & 0x0f0f0f0fu, qa.z & 0x0f0f0f0fu,
+                                 qa.w & 0x0f0f0f0fu, qb.x & 0x0f0f0f0fu, qb.y & 0x0f0f0f0fu, qb.z & 0x0f0f0f0fu,
+                                 qb.w & 0x0f0f0f0fu);
+                        tmem_st8(acol + 16 * h + 8, (qa.x >> 4) & 0x0f0f0f0fu, (qa.y >> 4) & 0x0f0f0f0fu,
+                                 (qa.z >> 4) & 0x0f0f0f0fu, (qa.w >> 4) & 0x0f0f0f0fu, (qb.x >> 4) & 0x0f0f0f0fu,
+                                 (qb.y >> 4) & 0x0f0f0f0fu, (qb.z >> 4) & 0x0f0f0f0fu, (qb.w >> 4) & 0x0f0f0f0fu);
+                    }
                 }
             }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&a_full[ab0]);
-                mbar_arrive(&a_full[ab1]);
-                if (item_last(bi)) mbar_arrive(&empty[it % stages]);  // this warp is done with the stage
+                mbar_arrive(&a_full[as]);
+                mbar_arrive(&empty[it % stages]);  // this warp is done with the stage
             }
         }
     } else {
@@ -315,55 +304,62 @@ __global__ void __launch_bounds__(MMA_THREADS, 1)
         float acc[TPT];
 #pragma unroll
         for (int i = 0; i < TPT; ++i) acc[i] = 0.0f;
-        for (int bi = 0; bi < nblk; ++bi) {
-            const int kl = bi % nbr;
-            // the block header of row r (scales, mins), read before the stage is handed back
-            const int it = item_of(bi);
-            if (kl % MMA_SB == 0 &&
-                !warp_wait_or_abort(&full[it % stages], (uint32_t)((it / stages) & 1), abort, a.status))
-                break;
-            const uint4 hd = *(const uint4 *)(raw + (size_t)(it % stages) * MMA_RAW_BYTES + (size_t)r * MMA_RS +
-                                              (kl % MMA_SB) * 144);
-            __syncwarp();
-            if (lane == 0 && item_last(bi)) mbar_arrive(&empty[it % stages]);
-            const float dw = h2f(hd.x), dmw = h2f(hd.x >> 16);
-            const uint32_t sc03 = hd.y & 0x3f3f3f3fu, mn03 = hd.z & 0x3f3f3f3fu;
-            const uint32_t sc47 = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
-            const uint32_t mn47 = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
-            // the block's MMAs (both half-blocks)
-            if (!warp_wait_or_abort(&blk_done[bi & 1], (uint32_t)((bi >> 1) & 1), abort, a.status)) break;
-            tc_fence_after();
-            int v[8][TPT];
-            const uint32_t dcol = tmem + lane_base + (uint32_t)((bi & 1) * DBUF + toff);
+        for (int it = 0; it < nitem; ++it) {
+            const int kl0 = item_kl0(it), nb = item_nb(it), ds = it & 1;
+            // the block headers of row r (scales, mins), read before the stage is handed back
+            if (!warp_wait_or_abort(&full[it % stages], (uint32_t)((it / stages) & 1), abort, a.status)) break;
+            uint4 hd[PB];
 #pragma unroll
-            for (int s = 0; s < 8; ++s) {
-                if constexpr (TPT == 8) tmem_ld8(dcol + (uint32_t)(s * NB), v[s]);
-                else tmem_ld4(dcol + (uint32_t)(s * NB), v[s]);
-            }
+            for (int b = 0; b < PB; ++b)
+                hd[b] = b < nb ? *(const uint4 *)(raw + (size_t)(it % stages) * RAW + (size_t)r * RS + b * 144)
+                               : make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[it % stages]);
+            // the item's MMAs
+            if (!warp_wait_or_abort(&idone[it % NAI], (uint32_t)((it / NAI) & 1), abort, a.status)) break;
+            tc_fence_after();
+            int v[PB][8][TPT];
+            const uint32_t dcol = tmem + lane_base + (uint32_t)(ds * DITEM + toff);
+#pragma unroll
+            for (int b = 0; b < PB; ++b)
+#pragma unroll
+                for (int s8 = 0; s8 < 8; ++s8) {
+                    if constexpr (TPT == 8) tmem_ld8(dcol + (uint32_t)((8 * b + s8) * NB), v[b][s8]);
+                    else tmem_ld4(dcol + (uint32_t)((8 * b + s8) * NB), v[b][s8]);
+                }
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&d_free[bi & 1]);  // the accumulators are in registers
+            if (lane == 0) mbar_arrive(&d_free[ds]);  // the accumulators are in registers
 #pragma unroll
-            for (int i = 0; i < TPT; ++i) {
-                int isum = 0;
+            for (int b = 0; b < PB; ++b) {
+                if (b >= nb) continue;
+                const int kl = kl0 + b;
+                const float dw = h2f(hd[b].x), dmw = h2f(hd[b].x >> 16);
+                const uint32_t sc03 = hd[b].y & 0x3f3f3f3fu, mn03 = hd[b].z & 0x3f3f3f3fu;
+                const uint32_t sc47 = (hd[b].w & 0x0f0f0f0fu) | ((hd[b].y >> 2) & 0x30303030u);
+                const uint32_t mn47 = ((hd[b].w >> 4) & 0x0f0f0f0fu) | ((hd[b].z >> 2) & 0x30303030u);
 #pragma unroll
-                for (int s = 0; s < 8; ++s) {
-                    const int sc = (int)(((s < 4 ? sc03 : sc47) >> (8 * (s & 3))) & 0xffu);
-                    isum += sc * v[s][i];
+                for (int i = 0; i < TPT; ++i) {
+                    int isum = 0;
+#pragma unroll
+                    for (int s8 = 0; s8 < 8; ++s8) {
+                        const int sc = (int)(((s8 < 4 ? sc03 : sc47) >> (8 * (s8 & 3))) & 0xffu);
+                        isum += sc * v[b][s8][i];
+                    }
+                    const int t = toff + i;
+                    const int4 bs = bss[t * nbmax + kl];
+                    int msum = __dp2a_lo(bs.x, (int)mn03, 0);
+                    msum = __dp2a_hi(bs.y, (int)mn03, msum);
+                    msum = __dp2a_lo(bs.z, (int)mn47, msum);
+                    msum = __dp2a_hi(bs.w, (int)mn47, msum);
+                    const float dx = dxs[t * nbmax + kl];
+                    acc[i] = fmaf(dw * dx, (float)isum, acc[i]);
+                    acc[i] = fmaf(-(dmw * dx), (float)msum, acc[i]);
                 }
-                const int t = toff + i;
-                const int4 bs = bss[t * nbmax + kl];
-                int msum = __dp2a_lo(bs.x, (int)mn03, 0);
-                msum = __dp2a_hi(bs.y, (int)mn03, msum);
-                msum = __dp2a_lo(bs.z, (int)mn47, msum);
-                msum = __dp2a_hi(bs.w, (int)mn47, msum);
-                const float dx = dxs[t * nbmax + kl];
-                acc[i] = fmaf(dw * dx, (float)isum, acc[i]);
-                acc[i] = fmaf(-(dmw * dx), (float)msum, acc[i]);
             }
-            if (kl == nbr - 1) {  // the unit's last block
-                const int tile = tile_of(bi);
+            if (kl0 + nb == nbr) {  // the unit's last item
+                const int tile = item_tile(it);
                 const int row = tile * MMA_ROWS + r;
                 bool write = true;
                 if (ks > 1) {
@@ -446,7 +442,7 @@ static cudaError_t run_mma(const QmvArgs &a, int n_tok, int sm_count, cudaStream
         if (dev < 64) opted[dev] = true;
     }
     CUtensorMap tm;
-    if (!encode_rows_u32(&tm, a.w0, a.row_stride, a.rows, 36 * MMA_SB, MMA_ROWS)) return cudaErrorInvalidValue;
+    if (!encode_rows_u32(&tm, a.w0, a.row_stride, a.rows, 36 * mma_pb<NB>(), MMA_ROWS)) return cudaErrorInvalidValue;
     const int units = ntiles * ks;
     const int grid = ks > 1 ? units : (units < sm_count ? units : sm_count);
     const size_t smem = L.total > MMA_SMEM_MIN ? L.total : MMA_SMEM_MIN;
