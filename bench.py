@@ -15,7 +15,9 @@ barrier and a synchronize.
            matvec's algorithmic bytes are W 50,135,040 + x 20,480 + y 69,632.
   e2e      the same through the C ABI with host buffers: per matvec a pinned
            host->device copy of x and a device->host copy of y are inside the
-           timed region.
+           timed region, on a copy stream beside the kernels (the inputs go
+           out at the start of the step, each result comes back while the
+           next matvec computes).
   roofline the step's kernel (for cfg0 the step is that one kernel; for
            cfg2 the matvec without the separate quantizer): bytes per launch
            / mean launch time, against the measured HBM copy bandwidth in
@@ -185,7 +187,9 @@ class Workload:
             self.host_w0 = random_valid_blocks(Q4_K, rows, k, 1000 * rank)
             self.W = [m27b.QWeight(self.host_w0 if c == 0 else random_valid_blocks(Q4_K, rows, k, 1000 * rank + c),
                                    Q4_K, k, rows) for c in range(copies)]
-            self.x = [torch.from_numpy(gen.standard_normal((n, k)).astype(np.float32)).to(dev) for _ in range(copies)]
+            # the step's activations in one buffer (one host->device copy per step)
+            self.x_all = torch.from_numpy(gen.standard_normal((copies, n, k)).astype(np.float32)).to(dev)
+            self.x = list(self.x_all.unbind(0))
             self.xq = [torch.empty(n * m27b.act_bytes(Q8_K, k), dtype=torch.uint8, device=dev) for _ in range(copies)]
             self.y = [torch.empty((n, rows), dtype=torch.float32, device=dev) for _ in range(copies)]
             self.mv_bytes = wbytes(Q4_K, rows, k) + n * (k * 4 + rows * 4)
@@ -271,6 +275,8 @@ class Workload:
             self.oh = [torch.empty((n, H), dtype=torch.float32).pin_memory() for _ in range(2)]
             self.h2d, self.d2h = 2 * n * H * 4, 2 * n * H * 4
             self.n = n
+        if w in ("cfg0", "cfg2"):
+            self.xh_all = self.x_all.cpu().pin_memory()
         if w in ("cfg0", "cfg1", "cfg2"):
             self.xh = [x.cpu().pin_memory() for x in self.x]
             self.yh = [torch.empty_like(y, device="cpu").pin_memory() for y in self.y]
@@ -331,14 +337,39 @@ class Workload:
                 self._ffn(c)
                 self.oh[c].copy_(self.out[c], non_blocking=True)
             return
+        # the host copies run on a copy stream beside the kernels, as a
+        # serving loop overlaps them: the step's activations go to the device
+        # in one copy at its start (cfg0/cfg2: one pinned buffer; cfg1 has
+        # one activation), and the copy of y[c] back to the host runs while
+        # matvec c+1 computes; the step ends when the last result is on the
+        # host
+        torch = self.torch
+        cur = torch.cuda.current_stream()
+        if not hasattr(self, "copy_st"):
+            self.copy_st = torch.cuda.Stream()
+            self.ev_in = torch.cuda.Event()
+            self.ev_out = [torch.cuda.Event() for _ in range(self.copies)]
+        cs = self.copy_st
+        cs.wait_stream(cur)
+        with torch.cuda.stream(cs):
+            if hasattr(self, "xh_all"):
+                self.x_all.copy_(self.xh_all, non_blocking=True)
+            else:
+                for c in range(self.copies):
+                    self.x[c].copy_(self.xh[c], non_blocking=True)
+            self.ev_in.record(cs)
+        cur.wait_event(self.ev_in)
         for c in range(self.copies):
-            self.x[c].copy_(self.xh[c], non_blocking=True)
             if getattr(self, "fused", False):
                 self.m27b.qmv_f32(self.W[c], self.x[c], self.n, self.y[c])
             else:
                 self.m27b.act_quant(self.x[c], Q8_K, out=self.xq[c])
                 self._mv(c)
-            self.yh[c].copy_(self.y[c], non_blocking=True)
+            self.ev_out[c].record(cur)
+            cs.wait_event(self.ev_out[c])
+            with torch.cuda.stream(cs):
+                self.yh[c].copy_(self.y[c], non_blocking=True)
+        cur.wait_stream(cs)
 
     def kernel_bytes(self):
         return self.step_bytes / (1 if self.name == "cfg3" else self.copies)

@@ -42,11 +42,22 @@
 
 namespace m27b {
 
+#ifndef M27B_BLK_STAGES
+#define M27B_BLK_STAGES 2
+#endif
+#ifndef M27B_BLK_WARPS
+#define M27B_BLK_WARPS 8
+#endif
+#ifndef M27B_BLK_CTAS
+#define M27B_BLK_CTAS 2
+#endif
 constexpr int BLK_XREC = 272;                 // bytes per staged (token, block) activation record
-constexpr int BLK_STAGES = 2;                 // stages per warp
-constexpr int BLK_WARPS = 8;                  // most warps per CTA (two CTAs per SM)
+constexpr int BLK_STAGES = M27B_BLK_STAGES;   // stages per warp
+constexpr int BLK_WARPS = M27B_BLK_WARPS;     // most warps per CTA
+constexpr int BLK_CTAS = M27B_BLK_CTAS;       // resident CTAs per SM the launch plans for
 constexpr int BLK_THREADS = BLK_WARPS * 32;
-constexpr size_t BLK_SMEM_MAX = 112 * 1024;   // two CTAs per SM within the 228 KB of shared memory
+// the CTAs of an SM share its 228 KB of shared memory (1 KB reserved per CTA)
+constexpr size_t BLK_SMEM_MAX = BLK_CTAS == 1 ? 226 * 1024 : 112 * 1024;
 
 // One item: 8 rows x 4 consecutive blocks of `bytes` bytes (q4_K: 4608).
 constexpr int blk_item(int bytes) { return 8 * 4 * bytes; }
@@ -746,21 +757,21 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
 }
 
 template <int NT, int EPI>
-__global__ void __launch_bounds__(BLK_THREADS, 2)
+__global__ void __launch_bounds__(BLK_THREADS, BLK_CTAS)
     k_qmv_q4k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
                   int split) {
     qmv_kblk_body<BlkQ4K, NT, EPI>(a, &tm0, &tm1, split);
 }
 
 template <int NT, int EPI>
-__global__ void __launch_bounds__(BLK_THREADS, 2)
+__global__ void __launch_bounds__(BLK_THREADS, BLK_CTAS)
     k_qmv_q5k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
                   int split) {
     qmv_kblk_body<BlkQ5K, NT, EPI>(a, &tm0, &tm1, split);
 }
 
 template <int NT, int EPI>
-__global__ void __launch_bounds__(BLK_THREADS, 2)
+__global__ void __launch_bounds__(BLK_THREADS, BLK_CTAS)
     k_qmv_iq4xs_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
                     int split) {
     qmv_kblk_body<BlkIQ4XS, NT, EPI>(a, &tm0, &tm1, split);

@@ -30,10 +30,10 @@ cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         if (dev < 64) opted[dev] = smem;
     }
-    // two resident CTAs per SM by construction (shared memory <= 112 KB each)
+    // BLK_CTAS resident CTAs per SM by construction (shared memory <= BLK_SMEM_MAX each)
     const long groups = (a.rows + 7) / 8;
     const int P = (a.rb + 3) / 4;
-    const long slots = (long)sm_count * 2;
+    const long slots = (long)sm_count * BLK_CTAS;
     int split, nthreads;
     long grid;
     size_t smem_launch;
