@@ -46,10 +46,10 @@ namespace m27b {
 #define M27B_BLK_STAGES 2
 #endif
 #ifndef M27B_BLK_WARPS
-#define M27B_BLK_WARPS 8
+#define M27B_BLK_WARPS 16
 #endif
 #ifndef M27B_BLK_CTAS
-#define M27B_BLK_CTAS 2
+#define M27B_BLK_CTAS 1
 #endif
 constexpr int BLK_XREC = 272;                 // bytes per staged (token, block) activation record
 constexpr int BLK_STAGES = M27B_BLK_STAGES;   // stages per warp
@@ -566,11 +566,13 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
     const int P = (a.rb + 3) >> 2;  // passes per row
     const int nb = a.rb;
 
-    // split == 1: warp wg owns groups wg, wg+W, ...; all passes of each.
+    // split == 1: warp wg owns groups wg, wg+W, ...; all passes of each
     // split == nwarps: the CTA owns groups blockIdx.x, +gridDim.x, ...; warp
     // w takes passes [w*P/split, (w+1)*P/split) of each and the partial sums
     // are combined in warp order (deterministic).
-    const int wg = split == 1 ? blockIdx.x * nwarps + warp : blockIdx.x;
+    // (warp-major: the groups go round the CTAs first, so that every CTA,
+    // and every SM, carries the same number of groups within one)
+    const int wg = split == 1 ? warp * gridDim.x + blockIdx.x : blockIdx.x;
     const int W = split == 1 ? gridDim.x * nwarps : gridDim.x;
     const int my_groups = wg < ngroups ? (ngroups - 1 - wg) / W + 1 : 0;
     const int p_lo = split == 1 ? 0 : (warp * P) / split;

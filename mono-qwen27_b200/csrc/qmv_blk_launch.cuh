@@ -38,22 +38,23 @@ cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     long grid;
     size_t smem_launch;
     if (2 * groups >= slots * nw || P < 2) {
-        // every warp streams whole row groups: the fewest groups per warp
-        // that the resident warps allow, then just enough warps
+        // every warp streams whole row groups, one CTA per resident slot
+        // (fewer only for a one-pass matrix with fewer groups than slots);
+        // the kernel deals the groups warp-major, so the CTAs (and SMs)
+        // differ by at most one group per warp index
         split = 1;
-        const long max_warps = slots * nw;
-        const long gpw = (groups + max_warps - 1) / max_warps;
-        const long warps = (groups + gpw - 1) / gpw;
-        grid = (warps + nw - 1) / nw;
+        grid = groups < slots ? groups : slots;
         nthreads = nw * 32;
         smem_launch = smem;
     } else {
         // few row groups: the warps of a CTA split each group's passes
         split = P < nw ? P : nw;
-        // one CTA per resident slot; CTA c takes groups c, c + grid, ...: the
-        // two CTAs an SM holds then carry (nearly) the same number of groups,
-        // and the SMs differ by at most one group
-        grid = groups < slots ? groups : slots;
+        // one CTA per resident slot — two per SM while a CTA has at most 8
+        // warps (registers and shared memory hold two); CTA c takes groups
+        // c, c + grid, ...: the CTAs an SM holds then carry (nearly) the
+        // same number of groups, and the SMs differ by at most one group
+        const long split_slots = (long)sm_count * (split <= 8 ? 2 : 1);
+        grid = groups < split_slots ? groups : split_slots;
         nthreads = split * 32;
         smem_launch = blk_smem_for(split, a.k, NT, BT::BYTES);
     }
