@@ -21,7 +21,7 @@
 // the weight rows, no multicast) that completes on the stage's mbarrier.
 // Rows past the end and blocks past the end of a row read as zeros (the
 // tensor map's bounds), so ragged tails need no special case; the copies of item i+1 are in flight while item i is
-// multiplied (two stages per warp; the block is copied to registers and the
+// multiplied (two stages per warp, or all of a warp's items for matrices with few row groups; the block is copied to registers and the
 // stage handed back before the math).  Every mbarrier wait is bounded by the
 // global timer (M27B_WAIT_NS); a wait that runs out records an error in the
 // library's device status word and the kernel drains its own copies before
@@ -62,7 +62,12 @@ constexpr size_t BLK_SMEM_MAX = BLK_CTAS == 1 ? 226 * 1024 : 112 * 1024;
 // One item: 8 rows x 4 consecutive blocks of `bytes` bytes (q4_K: 4608).
 constexpr int blk_item(int bytes) { return 8 * 4 * bytes; }
 // stages + barriers of one warp
-constexpr size_t blk_warp_bytes(int bytes) { return (size_t)BLK_STAGES * blk_item(bytes) + (size_t)BLK_STAGES * 8; }
+// most stages per warp: a matrix with few row groups streams each group
+// with one warp that has all of the group's items in flight at once
+constexpr int BLK_MAX_STAGES = 8;
+constexpr size_t blk_warp_bytes(int bytes, int nst = BLK_STAGES) {
+    return (size_t)nst * blk_item(bytes) + (size_t)nst * 8;
+}
 
 inline size_t blk_x_bytes(int k, int nt) { return (size_t)nt * ((size_t)k / 256) * (BLK_XREC + 4); }
 
@@ -77,8 +82,8 @@ inline int blk_warps(int k, int nt, int bytes = 144) {
     return (int)(w < (size_t)BLK_WARPS ? w : (size_t)BLK_WARPS);
 }
 
-inline size_t blk_smem_for(int nwarps, int k, int nt, int bytes = 144) {
-    return (size_t)nwarps * blk_warp_bytes(bytes) + blk_x_bytes(k, nt) + blk_part_bytes(nt) + 16;
+inline size_t blk_smem_for(int nwarps, int k, int nt, int bytes = 144, int nst = BLK_STAGES) {
+    return (size_t)nwarps * blk_warp_bytes(bytes, nst) + blk_x_bytes(k, nt) + blk_part_bytes(nt) + 16;
 }
 inline size_t blk_smem_bytes(int k, int nt, int bytes = 144) {
     return blk_smem_for(blk_warps(k, nt, bytes), k, nt, bytes);
@@ -554,7 +559,7 @@ struct BlkIQ4XS {
 // Work of a warp: items (group, pass, matrix) in that order, matrix fastest
 // (SWIGLU streams the gate blocks, then the up blocks, of the same pass).
 template <class BT, int NT, int EPI>
-M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUtensorMap *tm1, int split) {
+M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUtensorMap *tm1, int split, int nst) {
     constexpr int NM = EPI == EPI_SWIGLU ? 2 : 1;
     constexpr int ITEM = blk_item(BT::BYTES);
     extern __shared__ __align__(128) uint8_t kblk_smem[];
@@ -579,19 +584,19 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
     const int my_passes = (split == 1 ? P : ((warp + 1) * P) / split) - p_lo;
 
     // [stages of all warps | activation records | block scales | partials | barriers]
-    uint8_t *stage0 = smem + (size_t)warp * BLK_STAGES * ITEM;
-    uint8_t *xrec = smem + (size_t)nwarps * BLK_STAGES * ITEM;
+    uint8_t *stage0 = smem + (size_t)warp * nst * ITEM;
+    uint8_t *xrec = smem + (size_t)nwarps * nst * ITEM;
     float *xd = (float *)(xrec + (size_t)NT * nb * BLK_XREC);
     float *part = (float *)(((uintptr_t)(xd + NT * nb) + 15) & ~(uintptr_t)15);  // [BLK_WARPS][8][2][NT]
-    uint64_t *bar = (uint64_t *)(part + (size_t)BLK_WARPS * 8 * 2 * NT) + (size_t)warp * BLK_STAGES;
+    uint64_t *bar = (uint64_t *)(part + (size_t)BLK_WARPS * 8 * 2 * NT) + (size_t)warp * nst;
     if (lane == 0) {
-        for (int s = 0; s < BLK_STAGES; ++s) mbar_init(&bar[s], 1);
+        for (int s = 0; s < nst; ++s) mbar_init(&bar[s], 1);
         fence_mbar_init();
     }
     __syncwarp();
 
     // copy cursor: lane 0 issues one tensor copy per item; all lanes track it
-    int lg = 0, lp = 0, lm = 0, li = 0, ls = 0;  // ls = li % BLK_STAGES
+    int lg = 0, lp = 0, lm = 0, li = 0, ls = 0;  // ls = li % nst
     auto issue_item = [&]() {
         if (lg < my_groups && my_passes > 0) {
             if (lane == 0) {
@@ -602,7 +607,7 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
                             (wg + lg * W) * 8, b);
             }
             ++li;
-            if (++ls == BLK_STAGES) ls = 0;
+            if (++ls == nst) ls = 0;
             if (++lm == NM) {
                 lm = 0;
                 if (++lp == my_passes) { lp = 0; ++lg; }
@@ -611,7 +616,7 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
     };
 
     // the stages' copies go out before the activations are staged
-    for (int i = 0; i < BLK_STAGES; ++i) issue_item();
+    for (int i = 0; i < nst; ++i) issue_item();
     // the weights are not produced by the previous kernel: their copies are
     // already in flight; the activations (and every global write) wait for it
     pdl_wait();
@@ -631,7 +636,7 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
 #pragma unroll
     for (int t = 0; t < NT; ++t) best[t] = 0ull;
 
-    int ci = 0, cs = 0;  // items consumed; cs = ci % BLK_STAGES
+    int ci = 0, cs = 0;  // items consumed; cs = ci % nst
     uint32_t cph = 0;     // phase parity of stage cs
     bool ok = true;
     int g = 0;
@@ -651,7 +656,7 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
                 __syncwarp();
                 issue_item();
                 ++ci;
-                if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
+                if (++cs == nst) { cs = 0; cph ^= 1u; }
                 if (row < a.rows && b < nb) BT::template mac<NT>(v, xrec + (size_t)b * BLK_XREC, xd + b, nb, acc[m]);
             }
             if (!ok) break;
@@ -739,7 +744,7 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
         // before the CTA's shared memory is released
         for (; ci < li; ++ci) {
             mbar_wait_bounded(&bar[cs], cph, a.status, 2);
-            if (++cs == BLK_STAGES) { cs = 0; cph ^= 1u; }
+            if (++cs == nst) { cs = 0; cph ^= 1u; }
         }
         // keep the CTA-wide barriers of the cooperative split balanced
         if (split > 1)
@@ -761,22 +766,22 @@ M27B_DI void qmv_kblk_body(const QmvArgs &a, const CUtensorMap *tm0, const CUten
 template <int NT, int EPI>
 __global__ void __launch_bounds__(BLK_THREADS, BLK_CTAS)
     k_qmv_q4k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
-                  int split) {
-    qmv_kblk_body<BlkQ4K, NT, EPI>(a, &tm0, &tm1, split);
+                  int split, int nst) {
+    qmv_kblk_body<BlkQ4K, NT, EPI>(a, &tm0, &tm1, split, nst);
 }
 
 template <int NT, int EPI>
 __global__ void __launch_bounds__(BLK_THREADS, BLK_CTAS)
     k_qmv_q5k_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
-                  int split) {
-    qmv_kblk_body<BlkQ5K, NT, EPI>(a, &tm0, &tm1, split);
+                  int split, int nst) {
+    qmv_kblk_body<BlkQ5K, NT, EPI>(a, &tm0, &tm1, split, nst);
 }
 
 template <int NT, int EPI>
 __global__ void __launch_bounds__(BLK_THREADS, BLK_CTAS)
     k_qmv_iq4xs_blk(const QmvArgs a, const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1,
-                    int split) {
-    qmv_kblk_body<BlkIQ4XS, NT, EPI>(a, &tm0, &tm1, split);
+                    int split, int nst) {
+    qmv_kblk_body<BlkIQ4XS, NT, EPI>(a, &tm0, &tm1, split, nst);
 }
 
 }  // namespace m27b

@@ -34,9 +34,17 @@ cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     const long groups = (a.rows + 7) / 8;
     const int P = (a.rb + 3) / 4;
     const long slots = (long)sm_count * BLK_CTAS;
-    int split, nthreads;
+    int split, nthreads, nst = BLK_STAGES;
     long grid;
     size_t smem_launch;
+    // few row groups: one warp per group, every item of the group in flight
+    // from the start (a stage per item), the warps spread over all SMs —
+    // while that fits the shared memory the kernel is opted in for
+    const int items = P * (EPI == EPI_SWIGLU ? 2 : 1);
+    const long wpc = (groups + sm_count - 1) / sm_count;  // warps per CTA
+    const bool all_in_flight = !(2 * groups >= slots * nw || P < 2) && groups >= 2L * sm_count &&
+                               items <= BLK_MAX_STAGES && wpc <= nw &&
+                               blk_smem_for((int)wpc, a.k, NT, BT::BYTES, items) <= smem;
     if (2 * groups >= slots * nw || P < 2) {
         // every warp streams whole row groups, one CTA per resident slot
         // (fewer only for a one-pass matrix with fewer groups than slots);
@@ -46,6 +54,12 @@ cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
         grid = groups < slots ? groups : slots;
         nthreads = nw * 32;
         smem_launch = smem;
+    } else if (all_in_flight) {
+        split = 1;
+        nst = items;
+        grid = sm_count;
+        nthreads = (int)wpc * 32;
+        smem_launch = blk_smem_for((int)wpc, a.k, NT, BT::BYTES, nst);
     } else {
         // few row groups: the warps of a CTA split each group's passes
         split = P < nw ? P : nw;
@@ -66,7 +80,7 @@ cudaError_t run_blk(const QmvArgs &a, int sm_count, cudaStream_t st) {
     } else {
         tm1 = tm0;
     }
-    return launch_pdl(kern, dim3((unsigned)grid), dim3(nthreads), smem_launch, st, a, tm0, tm1, split);
+    return launch_pdl(kern, dim3((unsigned)grid), dim3(nthreads), smem_launch, st, a, tm0, tm1, split, nst);
 }
 
 template <class BT, int EPI>
