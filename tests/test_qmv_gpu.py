@@ -92,7 +92,8 @@ def _act_close(orc, got, want, x):
 # matvec parity
 
 SHAPES = {
-    Q4_K: [(1, 256), (37, 1280), (300, 5120), (129, 6144), (64, 17408)],
+    # (5120, 6144): o_proj's shape, few row groups streamed with every item in flight
+    Q4_K: [(1, 256), (37, 1280), (300, 5120), (129, 6144), (64, 17408), (5120, 6144)],
     Q6_K: [(1, 256), (37, 1280), (300, 5120), (65, 17408)],
     Q8_0: [(1, 32), (37, 1056), (300, 1024), (129, 3072)],
 }
@@ -104,7 +105,7 @@ def _case(orc, qtype, rows, k, seed):
 
 
 @pytest.mark.parametrize("qtype", [Q4_K, Q6_K, Q8_0])
-@pytest.mark.parametrize("shape_i", range(5))
+@pytest.mark.parametrize("shape_i", range(6))
 @pytest.mark.parametrize("n", [1, 2, 4, 5])
 def test_qmv_parity(torch, orc, m27b, qtype, shape_i, n):
     if shape_i >= len(SHAPES[qtype]):
